@@ -1,0 +1,448 @@
+#!/usr/bin/env python3
+"""Benchmark of the Vox memory-bound operator path on B200 (one JSON line on rank 0).
+
+A step is one pass of the whole hot path over one batch of synthetic input at BASELINE's shapes ("vox-hotpath-suite"):
+  cfg1  RMSNorm x[512,1024] f32 (eps 1e-6, w ~N(1,0.02)) and SwiGLU silu(g)*u, g,u [512,3072] f32
+  cfg2  causal scaled softmax, scores [16,1024,1024] f32 ~N(0,3) x 1/sqrt(128)
+  cfg3  fused adaLN block, x/residual [8,2048,1024] bf16, shift/scale/gate [8,1024] bf16, eps 1e-6
+  cfg4  q8 and q4 dequant [4096,4096] (f16 scales, block 32) -> bf16; HiFT Snake x [16,512,24000] f32
+  cfg5  sweep per GPU: add / mul / GELU / row sum / row max / row L2 (rows of 4096) in f32 and bf16 over
+        --sweep-elems elements each, plus the deterministic global sum of the f32 tensor across all ranks
+        (slot partials -> one NCCL all-reduce of 840 f64 -> fixed-order fold).
+value = algorithmic bytes of all ranks (each input read once, each output written once) / step time (max over
+ranks, CUDA events). Scaling is weak: every rank runs the full per-GPU suite on its own shard of a global batch
+(inputs drawn from Philox counters offset by the rank), and only the global sum exchanges data.
+
+--impl reference times dariumi/Vox's own CPU operators (oracle/_ref/libvox_ref.so, compiled from the reference
+sources; the C restatement if that library is absent) on the host cores over a bounded sample of the same suite.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "HBM GB/s & % of B200 peak per op; elements/s at 1/2/4/8 GPUs vs host CPU"
+FALLBACK_HBM_GBS = 6650.0  # used only if MEASURED_PEAKS.json is absent
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------------- workload
+
+class Suite:
+    """Device buffers and the per-op launch list of one step. `ops` entries: (name, bytes, elements, fn)."""
+
+    def __init__(self, vox, torch, rank: int, world: int, sweep_elems: int, dist=None):
+        self.vox, self.t, self.rank, self.world, self.dist = vox, torch, rank, world, dist
+        dev = torch.device("cuda", torch.cuda.current_device())
+        f32, bf16 = torch.float32, torch.bfloat16
+        E = lambda *s, dt=f32: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
+        seed, c0 = 0, rank << 36  # shard k draws counters offset by k * 2^36: independent shards of one global batch
+        fill = lambda t, d, a, b, sid: vox.fill_philox(t, d, a, b, seed=seed, stream_id=sid, counter0=c0)  # noqa: E731
+        self.launches_per_step = 0
+        ops = []
+
+        # cfg1
+        x1, w1 = fill(E(512, 1024), 1, 0, 1, 1), fill(E(1024), 1, 1, 0.02, 2)
+        y1 = E(512, 1024)
+        g1, u1, h1 = fill(E(512, 3072), 1, 0, 1, 3), fill(E(512, 3072), 1, 0, 1, 4), E(512, 3072)
+        ops.append(("cfg1_rmsnorm_f32", 2 * 512 * 1024 * 4 + 1024 * 4, 512 * 1024, lambda: vox.rmsnorm(x1, w1, 1e-6, out=y1)))
+        ops.append(("cfg1_swiglu_f32", 3 * 512 * 3072 * 4, 512 * 3072, lambda: vox.silu_mul(g1, u1, out=h1)))
+        # cfg2
+        s2, p2 = fill(E(16, 1024, 1024), 1, 0, 3, 5), E(16, 1024, 1024)
+        sc2 = float(1.0 / np.sqrt(128.0))
+        ops.append(("cfg2_softmax_causal_f32", 16 * 1024 * 1025 // 2 * 4 + 16 * 1024 * 1024 * 4, 16 * 1024 * 1024,
+                    lambda: vox.softmax_rows(s2, sc2, 1024, 0, out=p2)))
+        # cfg3
+        B, T, D = 8, 2048, 1024
+        x3, r3, y3 = fill(E(B, T, D, dt=bf16), 1, 0, 1, 6), fill(E(B, T, D, dt=bf16), 1, 0, 1, 7), E(B, T, D, dt=bf16)
+        sh3, sc3, g3 = (fill(E(B, D, dt=bf16), 1, 0, 0.1, s) for s in (8, 9, 10))
+        ops.append(("cfg3_adaln_bf16", 3 * B * T * D * 2 + 3 * B * D * 2, B * T * D,
+                    lambda: vox.adaln(x3, sh3, sc3, 1e-6, g3, r3, out=y3)))
+        # cfg4
+        q8 = fill(E(4096, 4096, dt=torch.int8), 2, -128, 127, 11)
+        q4 = fill(E(4096, 2048, dt=torch.uint8), 3, 0, 0, 12)
+        s4 = fill(E(4096, 128), 0, 0.001, 0.05, 13).to(torch.float16)
+        o8, o4 = E(4096, 4096, dt=bf16), E(4096, 4096, dt=bf16)
+        ops.append(("cfg4_dequant_q8_bf16", 4096 * 4096 + 4096 * 128 * 2 + 4096 * 4096 * 2, 4096 * 4096,
+                    lambda: vox.dequant_q8(q8, s4, out=o8)))
+        ops.append(("cfg4_dequant_q4_bf16", 4096 * 2048 + 4096 * 128 * 2 + 4096 * 4096 * 2, 4096 * 4096,
+                    lambda: vox.dequant_q4(q4, s4, out=o4)))
+        xs, al = fill(E(16, 512, 24000), 1, 0, 1, 14), fill(E(512), 0, 0.2, 2.0, 15)
+        ys = E(16, 512, 24000)
+        ops.append(("cfg4_snake_hift_f32", 2 * 16 * 512 * 24000 * 4 + 512 * 4, 16 * 512 * 24000,
+                    lambda: vox.snake(xs, al, vox.SNAKE_HIFT, out=ys)))
+        # cfg5 sweep
+        n = sweep_elems
+        rows = n // 4096
+        sweep_in, sweep_out = [], []
+        for dt, tag, es in ((f32, "f32", 4), (bf16, "bf16", 2)):
+            a = fill(E(rows, 4096, dt=dt), 1, 0, 1, 16 if es == 4 else 17)
+            b = fill(E(rows, 4096, dt=dt), 1, 0, 1, 18 if es == 4 else 19)
+            y = E(rows, 4096, dt=dt)
+            rr = E(rows)
+            ops.append((f"cfg5_add_{tag}", 3 * n * es, n, lambda a=a, b=b, y=y: vox.add(a, b, out=y)))
+            ops.append((f"cfg5_mul_{tag}", 3 * n * es, n, lambda a=a, b=b, y=y: vox.mul(a, b, out=y)))
+            ops.append((f"cfg5_gelu_{tag}", 2 * n * es, n, lambda a=a, y=y: vox.gelu(a, vox.GELU_ERF, out=y)))
+            for op, nm in ((vox.REDUCE_SUM, "rowsum"), (vox.REDUCE_MAX, "rowmax"), (vox.REDUCE_L2, "rowl2")):
+                ops.append((f"cfg5_{nm}_{tag}", n * es + rows * 4, n, lambda a=a, op=op, rr=rr: vox.row_reduce(a, op, out=rr)))
+            if es == 4:
+                self.gsum_x = a
+            sweep_in += [a, b]
+            sweep_out += [y, rr]
+        from vox_b200.shard import shard_rows
+
+        self.g_rows_total = rows * world
+        self.g_row0, _ = shard_rows(self.g_rows_total, world, rank)
+        self.slots = E(840, dt=torch.float64)
+        self.gscratch = E(rows)
+        self.gout = E(1, dt=torch.float64)
+        ops.append(("cfg5_global_sum_f32", n * 4 + rows * 4, n, self.global_sum))
+        self.ops = ops
+        self.kernels = {nm: (3 if nm == "cfg5_global_sum_f32" else 1) for nm, *_ in ops}
+        self.bytes_per_step = sum(o[1] for o in ops)
+        self.elems_per_step = sum(o[2] for o in ops)
+        self.launches_per_step = sum(self.kernels.values())
+        self.outputs = [y1, h1, p2, y3, o8, o4, ys] + sweep_out
+        self.inputs = [x1, w1, g1, u1, s2, x3, r3, sh3, sc3, g3, q8, q4, s4, xs, al] + sweep_in
+
+    def global_sum(self):
+        v = self.vox
+        v.global_sum_partials(self.gsum_x, self.g_row0, self.g_rows_total, slots=self.slots, scratch=self.gscratch)
+        if self.world > 1:
+            self.dist.all_reduce(self.slots)
+        v.global_sum_finish(self.slots, out=self.gout)
+
+    def step(self, events=None):
+        for i, (_, _, _, fn) in enumerate(self.ops):
+            if events is not None:
+                events[i][0].record()
+            fn()
+            if events is not None:
+                events[i][1].record()
+
+
+# ---------------------------------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) during the timed region: median SM MHz under load and throttle reasons."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx, self.proc, self.lines = gpu_index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------- CPU reference
+
+def cpu_suite_sample(scale: float = 1.0):
+    """Bounded sample of the suite on the host, through the reference's own CPU operators. Returns (lib, kind, cores, ops)
+    with ops = [(name, bytes, elements, fn)]; byte model identical to the GPU arm's."""
+    from oracle.oracle import port, ref
+
+    R = ref()
+    P = port()
+    kind = "reference" if R is not None else "port"
+    if R is not None:
+        cores = R.set_threads(0)
+    else:
+        cores = 1
+    L = R if R is not None else P
+    f32 = np.float32
+    ops = []
+    x1, w1 = P.normal((512, 1024), sid=1), P.normal((1024,), 1, 0.02, sid=2)
+    g1, u1 = P.normal((512, 3072), sid=3), P.normal((512, 3072), sid=4)
+    ops.append(("cfg1_rmsnorm_f32", 2 * 512 * 1024 * 4 + 1024 * 4, 512 * 1024, lambda: L.rmsnorm(x1, w1, 1e-6)))
+    ops.append(("cfg1_swiglu_f32", 3 * 512 * 3072 * 4, 512 * 3072, lambda: L.silu_mul(g1, u1)))
+    hs = max(1, int(16 * scale))
+    s2 = P.normal((hs, 1024, 1024), 0, 3, sid=5)
+    ops.append(("cfg2_softmax_causal_f32", hs * (1024 * 1025 // 2 * 4 + 1024 * 1024 * 4), hs * 1024 * 1024,
+                lambda: L.softmax_rows(s2, float(1 / np.sqrt(128.0)), 1024, 0)))
+    Bs = max(1, int(8 * scale))
+    x3 = P.normal((Bs, 2048, 1024), sid=6)
+    r3 = P.normal((Bs, 2048, 1024), sid=7)
+    sh3, sc3, g3 = (P.normal((Bs, 1024), 0, 0.1, sid=s) for s in (8, 9, 10))
+    ops.append(("cfg3_adaln_bf16", Bs * (3 * 2048 * 1024 * 2 + 3 * 1024 * 2), Bs * 2048 * 1024,
+                lambda: L.adaln(x3, sh3, sc3, g3, r3)))
+    q8 = P.fill_i8((4096, 4096), -128, 127, sid=11)
+    q4 = P.fill_u8((4096, 2048), sid=12)
+    s4 = P.f16_to_f32(P.uniform_arr((4096, 128), 0.001, 0.05, sid=13).astype(np.float16).view(np.uint16))
+    if R is not None:
+        ops.append(("cfg4_dequant_q8_bf16", 4096 * 4096 * 3 + 4096 * 128 * 2, 4096 * 4096, lambda: P.bf16_round(R.mat_rows(q8, s4))))
+        ops.append(("cfg4_dequant_q4_bf16", 4096 * 2048 + 4096 * 4096 * 2 + 4096 * 128 * 2, 4096 * 4096,
+                    lambda: P.bf16_round(R.mat_rows(q4, s4, q4=True))))
+    else:
+        ops.append(("cfg4_dequant_q8_bf16", 4096 * 4096 * 3 + 4096 * 128 * 2, 4096 * 4096, lambda: P.bf16_round(P.dequant_q8(q8, s4))))
+        ops.append(("cfg4_dequant_q4_bf16", 4096 * 2048 + 4096 * 4096 * 2 + 4096 * 128 * 2, 4096 * 4096,
+                    lambda: P.bf16_round(P.dequant_q4(q4, s4))))
+    Cs = max(4, int(512 * scale / 8))  # snake rows sampled: one batch, Cs channels
+    xs, al = P.normal((1, Cs, 24000), sid=14), P.uniform_arr((Cs,), 0.2, 2.0, sid=15)
+    ops.append(("cfg4_snake_hift_f32", 2 * Cs * 24000 * 4 + Cs * 4, Cs * 24000, lambda: L.snake(xs, al, 0, inner=24000)))
+    n = int(2 ** 24 * scale)
+    a, b = P.normal((n // 4096, 4096), sid=16), P.normal((n // 4096, 4096), sid=18)
+    ops.append(("cfg5_add_f32", 3 * n * 4, n, lambda: L.add(a, b)))
+    ops.append(("cfg5_mul_f32", 3 * n * 4, n, lambda: L.mul(a, b)))
+    ops.append(("cfg5_gelu_f32", 2 * n * 4, n, (lambda: R.gelu_inplace(a)) if R is not None else (lambda: P.gelu(a, 0))))
+    if R is not None:
+        for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
+            ops.append((f"cfg5_{nm}_f32", n * 4 + n // 1024, n, lambda op=op: R.row_reduce(a, op)))
+    else:
+        for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
+            ops.append((f"cfg5_{nm}_f32", n * 4 + n // 1024, n, lambda op=op: P.row_reduce(a, op)))
+    return kind, cores, ops, f32
+
+
+def time_cpu(ops, reps: int = 1) -> tuple[float, int, int, dict]:
+    """Seconds, bytes and elements over `reps` passes of the sampled suite (after one untimed pass)."""
+    for *_, fn in ops:
+        fn()
+    per = {}
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        for nm, by, el, fn in ops:
+            s = time.perf_counter()
+            fn()
+            per[nm] = per.get(nm, 0.0) + time.perf_counter() - s
+    dt = time.perf_counter() - t0
+    return dt, reps * sum(o[1] for o in ops), reps * sum(o[2] for o in ops), per
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    kind, cores, ops, _ = cpu_suite_sample(1.0)
+    for _ in range(args.warmup):
+        for *_, fn in ops:
+            fn()
+    dt, by, el, per = time_cpu(ops, reps=args.steps)
+    value = by / dt / 1e9
+    sample = ("per step: cfg1-cfg4 at BASELINE shapes except Snake on 64 of 8192 rows; cfg5 f32 add/mul/GELU/row "
+              "sum/max/L2 on 2^24 elements; bf16 ops computed in f32 and rounded")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (Philox4x32-10 seed 0, BASELINE shapes)",
+        "config": {"workload": "vox-hotpath-suite", "sample": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "elements_per_s": round(el / dt, 1),
+        "ops": {nm: {"gb_s": round(b * args.steps / per[nm] / 1e9, 3)} for nm, b, _, _ in ops},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------------- GPU arm
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    import vox_b200 as vox
+
+    suite = Suite(vox, torch, rank, world, args.sweep_elems, dist if world > 1 else None)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        suite.step()
+    barrier()
+
+    nops = len(suite.ops)
+    ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(nops)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        t0.record()
+        for k in range(args.steps):
+            suite.step(ev[k])
+        t1.record()
+        barrier()
+    ms = t0.elapsed_time(t1)
+    per_op = np.array([[ev[k][i][0].elapsed_time(ev[k][i][1]) for i in range(nops)] for k in range(args.steps)])  # ms
+    op_ms = per_op.mean(0)
+    times = torch.tensor([ms] + list(op_ms), dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, op_ms = float(times[0]), times[1:].cpu().numpy()
+
+    # end to end through the public API with host buffers: pinned H2D of every input, the suite, D2H of every output
+    e2e = run_e2e(suite, torch, dist, world, max(1, min(args.steps, args.e2e_steps)))
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    step_s = ms / 1e3 / args.steps
+    value = suite.bytes_per_step * world / step_s / 1e9
+    ops = {}
+    for (nm, by, el, _), t in zip(suite.ops, op_ms):
+        gbs = by / (t / 1e3) / 1e9
+        ops[nm] = {"us": round(t * 1e3, 2), "gb_s": round(gbs, 1), "frac_of_peak": round(gbs / peak, 3),
+                   "elements_per_s": round(el / (t / 1e3), 1), "bytes": by}
+    dom_i = int(np.argmax(op_ms))
+    dom = suite.ops[dom_i]
+    achieved = dom[1] / (op_ms[dom_i] / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(dom[0])
+        except Exception:
+            traffic = None
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        kind, cores, cops, _ = cpu_suite_sample(1.0)
+        dt, by, el, _ = time_cpu(cops, reps=1)
+        cpu = {"value": round(by / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+               "sample": "one pass: cfg1-cfg4 at BASELINE shapes except Snake on 64 of 8192 rows; cfg5 f32 ops on 2^24 elements"}
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (Philox4x32-10 seed 0 on the device, BASELINE shapes and distributions)",
+        "config": {"workload": "vox-hotpath-suite", "sweep_elems_per_gpu": args.sweep_elems,
+                   "bytes_per_step_per_gpu": suite.bytes_per_step, "elements_per_step_per_gpu": suite.elems_per_step,
+                   "parallelism": f"row shards x{world}, NCCL all-reduce of 840 f64 slots for the global sum",
+                   "l2": "no flush: the step streams ~%.1f GB per GPU (> 126 MB L2), so every input is evicted by the other ops' "
+                         "traffic between its uses" % (suite.bytes_per_step / 1e9)},
+        "elements_per_s": round(suite.elems_per_step * world / step_s, 1),
+        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 3), "traffic": traffic, "peak_source": peak_kind},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": suite.launches_per_step * args.steps,
+        "clocks": clk.summary(), "ops": ops,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(suite, torch, dist, world, steps) -> dict:
+    """The suite through the public API with pinned host buffers: every step copies each op's inputs host->device,
+    runs the ops and copies each op's outputs device->host. Returns the same metric (algorithmic GB/s)."""
+    pin_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in suite.inputs]
+    pin_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in suite.outputs]
+    for p, t in zip(pin_in, suite.inputs):
+        p.copy_(t)
+    h2d = sum(p.numel() * p.element_size() for p in pin_in)
+    d2h = sum(p.numel() * p.element_size() for p in pin_out)
+    gback = torch.empty(1, dtype=torch.float64, pin_memory=True)
+    d2h += 8
+
+    def one():
+        for p, t in zip(pin_in, suite.inputs):
+            t.copy_(p, non_blocking=True)
+        suite.step()
+        for p, t in zip(pin_out, suite.outputs):
+            p.copy_(t, non_blocking=True)
+        gback.copy_(suite.gout, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    s = float(ms[0]) / 1e3 / steps
+    return {"value": round(suite.bytes_per_step * world / s / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--sweep-elems", type=int, default=1 << 27, help="per-GPU elements of each cfg5 tensor (multiple of 4096)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+/*
+ * vox_cuda.h — C ABI of the B200 (sm_100a) backend for Vox's memory-bound operator path.
+ *
+ * Every entry point here replaces an operator of Vox's CPU library (src/kernels.hpp, src/nn.hpp) or an
+ * elementwise dispatch of its Vulkan backend (src/gpu_f5.cpp, src/gpu_codec.cpp, src/gpu_vulkan.cpp).
+ * The citation above each declaration names the reference interface it stands in for (file:line within
+ * the dariumi/Vox project).
+ *
+ * Conventions (kept from Vox's GPU seam, src/gpu.hpp and src/gpu_vulkan.cpp):
+ *   - Return value is a status: 0 = OK, negative = one of the VOX_CUDA_ERR_* codes, whose values equal
+ *     Vox's vox_status codes (include/vox.h:48-55). No exception crosses this boundary.
+ *   - The message of the last failed call is kept per host thread: vox_cuda_last_error().
+ *   - All tensor pointers are DEVICE pointers owned by the caller and never retained after the call.
+ *   - Every call takes a CUDA stream (cudaStream_t passed as void*, NULL = legacy default stream) and is
+ *     asynchronous and stream-ordered. There is no global lock around launches: calls from several host
+ *     threads on distinct streams run concurrently.
+ *   - There is no CPU fallback. If the device cannot run the kernel the call fails with VOX_CUDA_ERR_DEVICE.
+ *   - "Activations" follow the call's dtype (VOX_CUDA_F32 or VOX_CUDA_BF16). Learned weight vectors that Vox
+ *     holds as `const float *` (norm weights and biases, Snake alpha/beta) are always f32. Per-batch
+ *     modulation vectors of adaLN (shift/scale/gate) follow the call's dtype.
+ *   - Arithmetic is f32 for every dtype; bf16 outputs are rounded to nearest-even once, at the store.
+ *   - Reductions use a fixed order (no floating-point atomics): results are bitwise reproducible run to run.
+ */
+#ifndef VOX_CUDA_H
+#define VOX_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VOX_CUDA_API __attribute__((visibility("default")))
+#else
+#define VOX_CUDA_API
+#endif
+
+/* Status codes: same numeric values as vox_status in include/vox.h:44-56. */
+#define VOX_CUDA_OK 0
+#define VOX_CUDA_ERR_DEVICE (-3)
+#define VOX_CUDA_ERR_OOM (-4)
+#define VOX_CUDA_ERR_ARG (-6)
+#define VOX_CUDA_ERR_UNSUPPORTED (-8)
+
+/* Element types of activations. */
+#define VOX_CUDA_F32 0
+#define VOX_CUDA_BF16 1
+#define VOX_CUDA_F16 2 /* only as a q8/q4 scale type */
+
+/* GELU forms. */
+#define VOX_CUDA_GELU_ERF 0  /* 0.5x(1+erf(x/sqrt2)): kernels.hpp:106 gelu_erf, nn.cpp:87-96 gelu_inplace */
+#define VOX_CUDA_GELU_TANH 1 /* 0.5x(1+tanh(sqrt(2/pi)(x+0.044715x^3))): f5.cpp:93-96, f5ew.comp mode 1 */
+
+/* Snake forms (all: y = x + coef[c] * s^2 with s = sin(arg[c] * x)). */
+#define VOX_CUDA_SNAKE_HIFT 0   /* coef = 1/(alpha+1e-9), arg = alpha, accurate sin: cosyvoice.cpp:239-248 */
+#define VOX_CUDA_SNAKE_BETA 1   /* coef = inv_b, arg = a (the precomputed Snake struct): qwen3.cpp:86-94 */
+#define VOX_CUDA_SNAKE_KOKORO 2 /* coef = 1/alpha, arg = alpha, Vox's fast_sin polynomial: kokoro.cpp:233-242 */
+
+/* Row reductions. */
+#define VOX_CUDA_REDUCE_SUM 0
+#define VOX_CUDA_REDUCE_MAX 1
+#define VOX_CUDA_REDUCE_L2 2 /* sqrt(sum of squares) */
+
+/* Slot count of the deterministic global sum: lcm(1..8), so every world size 1..8 owns whole slots. */
+#define VOX_CUDA_GLOBAL_SUM_SLOTS 840
+
+/* ---------------------------------------------------------------- service */
+
+/* Library version string, e.g. "vox-cuda 0.1.0 sm_100a". */
+VOX_CUDA_API const char *vox_cuda_version(void);
+/* Message of the last failed call on this host thread ("" if none). Mirrors vox_last_error(), include/vox.h:120. */
+VOX_CUDA_API const char *vox_cuda_last_error(void);
+/* Number of CUDA devices, written to *count. Mirrors gpu_enumerate(), src/gpu.hpp:35. */
+VOX_CUDA_API int vox_cuda_device_count(int *count);
+/* Compute capability of the current device as major*10+minor (100 for B200), written to *cc. */
+VOX_CUDA_API int vox_cuda_device_cc(int *cc);
+
+/* Seeded synthetic data with Vox's counter-based generator (Philox4x32-10, src/sampling.hpp:16-50).
+ * Element i uses counter {i lo, i hi, stream_id, draw}, key {seed lo, seed hi}.
+ *   dist 0 = uniform in [a, b): u = (r0 >> 8) * 2^-24 as DetRng::uniform (sampling.hpp:43-46), then a + (b-a)*u.
+ *   dist 1 = normal(mean a, std b): Box–Muller on element pairs p = i/2 as F5Model::noise (f5.cpp:402-414).
+ *   dist 2 = uniform integer codes in [a, b] (inclusive), written as int8 (dtype ignored): floor(u*(b-a+1)) + a.
+ *   dist 3 = uniform bytes (0..255), written as uint8 (dtype ignored): r0 & 0xFF.
+ * counter0 offsets the element index, so a shard of a larger tensor draws the same numbers as the whole. */
+VOX_CUDA_API int vox_cuda_fill_philox(void *out, int64_t n, int dist, float a, float b, uint64_t seed, uint32_t stream_id,
+                                      int64_t counter0, int dtype, void *stream);
+
+/* ---------------------------------------------------------------- normalisation */
+
+/* y[r] = w * (x[r] * 1/sqrt(mean(x[r]^2) + eps)) for r < rows; y may equal x.
+ * Replaces vox::rmsnorm(x, w, n, eps, out), src/kernels.hpp:103 (kernels.cpp:707-712), batched over rows;
+ * GPU twin of rmsnorm.comp (src/shaders/rmsnorm.comp:1-22). w: f32 [n]. */
+VOX_CUDA_API int vox_cuda_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int64_t n, float eps, int dtype,
+                                  void *stream);
+
+/* LayerNorm over rows of n. modulate = 0: y = (x-mean)*inv*w + b (w NULL: no scale, b NULL: no shift).
+ * modulate = 1: y = (x-mean)*inv*(1+w) + b, the AdaLayerNorm form (w and b required).
+ * Replaces vox::layernorm(x, w, b, n, eps, out), src/kernels.hpp:104 (kernels.cpp:714-723), and
+ * vox::nn::layer_norm(x, T, C, w, b, eps, modulate), src/nn.hpp:83 (nn.cpp:248-265). y may equal x. */
+VOX_CUDA_API int vox_cuda_layernorm(const void *x, const float *w, const float *b, void *y, int64_t rows, int64_t n, float eps,
+                                    int modulate, int dtype, void *stream);
+
+/* Fused adaLN block of the F5 DiT over x [B][T][D]:
+ *   m = LN(x[b][t]) * (1 + scale[b]) + shift[b]          (LN without affine, eps)
+ *   y = residual[b][t] + gate[b] * m                      (gate and residual given)
+ *   y = m                                                 (gate and residual NULL: Vox's modulate alone)
+ * shift/scale/gate: [B][D] in dtype. Replaces the modulate lambda f5.cpp:617-632 composed with the gated_add
+ * lambda f5.cpp:670-676; GPU twin of f5ln.comp mode 1 followed by f5ew.comp mode 0 (gpu_f5.cpp:295,312). */
+VOX_CUDA_API int vox_cuda_adaln(const void *x, const void *shift, const void *scale, const void *gate, const void *residual,
+                                void *y, int64_t B, int64_t T, int64_t D, float eps, int dtype, void *stream);
+
+/* h[b][t][d] += gate[b][d] * src[b][t][d]; gate [B][D] in dtype.
+ * Replaces the gated_add lambda f5.cpp:670-676 (B = 1) and f5ew.comp mode 0 (f5ew.comp:18-19). */
+VOX_CUDA_API int vox_cuda_gated_add(void *h, const void *gate, const void *src, int64_t B, int64_t T, int64_t D, int dtype,
+                                    void *stream);
+
+/* y[r][o] += b[o] for r < rows, o < D; b: f32 [D].
+ * Replaces the bias loop of vox::nn::linear, nn.cpp:148-155 (also Conv/ConvT bias nn.cpp:242-244), f5ew.comp mode 3. */
+VOX_CUDA_API int vox_cuda_bias_add(void *y, const float *b, int64_t rows, int64_t D, int dtype, void *stream);
+
+/* ---------------------------------------------------------------- softmax */
+
+/* Scaled row softmax, f32. Row r sees its first `visible` entries: visible = n when q_len == 0, else
+ * min(n, (r % q_len) + pos0 + 1) (causal: query i of a head at absolute position pos0+i sees keys 0..pos0+i).
+ * y[r][j] = exp(scale*x[r][j] - max) / sum for j < visible, 0 for j >= visible; x beyond visible is not read.
+ * y may equal x. Replaces the causal composition kernels.cpp:812-819 around vox::softmax_inplace(x, n),
+ * src/kernels.hpp:107 (kernels.cpp:725-732), and the softmax half of attention.comp:20-39. */
+VOX_CUDA_API int vox_cuda_softmax_rows(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len,
+                                       int64_t pos0, void *stream);
+
+/* ---------------------------------------------------------------- activations */
+
+/* h[i] = silu(g[i]) * u[i], silu(x) = x/(1+exp(-x)); h may equal g.
+ * Replaces the SwiGLU loop kernels.cpp:836 over vox::silu, src/kernels.hpp:105; silumul.comp:1-12. */
+VOX_CUDA_API int vox_cuda_silu_mul(const void *g, const void *u, void *h, int64_t n, int dtype, void *stream);
+
+/* Fused gate|up layout: gu [m][2I] -> h [m][I] = silu(gu[:, :I]) * gu[:, I:]. Replaces swiglu.comp:1-13. */
+VOX_CUDA_API int vox_cuda_swiglu_fused(const void *gu, void *h, int64_t m, int64_t I, int dtype, void *stream);
+
+/* y = gelu(x), kind = VOX_CUDA_GELU_*; y may equal x.
+ * Replaces vox::gelu_erf (kernels.hpp:106), vox::nn::gelu_inplace (nn.hpp:125, nn.cpp:87-96), F5's gelu_tanh
+ * (f5.cpp:93-96) and f5ew.comp mode 1. */
+VOX_CUDA_API int vox_cuda_gelu(const void *x, void *y, int64_t n, int kind, int dtype, void *stream);
+
+/* y = a + b and y = a * b, elementwise (the residual adds of kernels.cpp:830,840 and the sweep ops). */
+VOX_CUDA_API int vox_cuda_add(const void *a, const void *b, void *y, int64_t n, int dtype, void *stream);
+VOX_CUDA_API int vox_cuda_mul(const void *a, const void *b, void *y, int64_t n, int dtype, void *stream);
+
+/* Snake activation, f32, over n elements whose channel is c = (i / inner) % C:
+ *   inner = 1  -> Vox's time-major [T][C] layout;  inner = T -> channel-major [B][C][T].
+ * alpha: f32 [C]; beta: f32 [C] for VOX_CUDA_SNAKE_BETA (the Snake struct's inv_b), else NULL. y may equal x.
+ * Replaces snake_apply (qwen3.cpp:86-94), SnakeRes::snake (cosyvoice.cpp:239-248), the Kokoro snake
+ * (kokoro.cpp:233-242 with fast_sin, nn.hpp:26-40) and snake.comp:1-14. */
+VOX_CUDA_API int vox_cuda_snake(const float *x, const float *alpha, const float *beta, float *y, int64_t n, int64_t C,
+                                int64_t inner, int kind, void *stream);
+
+/* load_snake (qwen3.cpp:76-84) on the device: a[c] = exp(alpha[c]), inv_b[c] = 1/(exp(beta[c]) + 1e-9). */
+VOX_CUDA_API int vox_cuda_snake_beta_params(const float *alpha, const float *beta, float *a, float *inv_b, int64_t C,
+                                            void *stream);
+
+/* ---------------------------------------------------------------- block dequantisation */
+
+/* Q8: q int8 [rows][cols], scale [rows][cols/32] (scale_dtype VOX_CUDA_F32 = Vox's layout, or VOX_CUDA_F16);
+ * out[r][k] = float(q[r][k]) * scale[r][k/32], written as out_dtype (VOX_CUDA_F32 or VOX_CUDA_BF16, RNE).
+ * cols % 32 == 0. Bit-exact with vox::mat_row / mat_gather (kernels.cpp:446-452,468-471), Mat layout kernels.hpp:45. */
+VOX_CUDA_API int vox_cuda_dequant_q8(const int8_t *q, const void *scale, int scale_dtype, void *out, int out_dtype, int64_t rows,
+                                     int64_t cols, void *stream);
+
+/* Q4: packed [rows][cols/2] bytes, 16 bytes per 32-weight block; byte j of a block holds element j in its low nibble
+ * and element j+16 in its high nibble; value = (code - 8) * scale. Layout kernels.hpp:46-47, bit-exact with
+ * vox::mat_row Q4 (kernels.cpp:453-463). */
+VOX_CUDA_API int vox_cuda_dequant_q4(const uint8_t *q, const void *scale, int scale_dtype, void *out, int out_dtype, int64_t rows,
+                                     int64_t cols, void *stream);
+
+/* ---------------------------------------------------------------- reductions */
+
+/* out[r] = sum / max / sqrt(sum of squares) of row r of x [rows][n], f32 result.
+ * No single reference function: the same reductions sit inside vox::rmsnorm (kernels.cpp:709) and
+ * vox::softmax_inplace (kernels.cpp:727-729). Fixed order: lane l of a warp takes 4-wide vectors l, l+32, ...
+ * of the row, keeps one accumulator per vector component, folds them as (c0+c1)+(c2+c3) and the 32 lanes by an
+ * xor butterfly (16, 8, 4, 2, 1). */
+VOX_CUDA_API int vox_cuda_row_reduce(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, void *stream);
+
+/* Deterministic global sum across shards, step 1 of 2 (no reference counterpart: Vox has no multi-device code).
+ * The global tensor has total_rows rows of n; this shard holds rows [row0, row0 + rows). Slot s of
+ * VOX_CUDA_GLOBAL_SUM_SLOTS covers global rows [floor(s*R/S), floor((s+1)*R/S)). The shard's rows must be a whole
+ * number of slots. Writes slots[S] (f64): each owned slot = fixed-order sum of its row sums, every other slot 0.
+ * rowsum_scratch: device f32 [rows], caller-allocated scratch for the row sums.
+ * Summing the slot vectors of all shards element-wise (one NCCL all-reduce) is exact (x + 0 = x), so step 2 gives
+ * a result that is bitwise identical for any number of shards. */
+VOX_CUDA_API int vox_cuda_global_sum_partials(const void *x, int64_t rows, int64_t n, int64_t row0, int64_t total_rows,
+                                              float *rowsum_scratch, double *slots, int dtype, void *stream);
+
+/* Step 2: out[0] = fixed-order pairwise sum of slots[VOX_CUDA_GLOBAL_SUM_SLOTS] (f64). */
+VOX_CUDA_API int vox_cuda_global_sum_finish(const double *slots, double *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOX_CUDA_H */

@@ -1,0 +1,240 @@
+// ref_shim.cpp — TEST INFRASTRUCTURE, not product code.
+//
+// Links dariumi/Vox's own CPU operators, compiled from the reference sources where they lie (src/kernels.cpp,
+// src/nn.cpp, src/f5.cpp and the few files they need), into oracle/_ref/libvox_ref.so and exposes them with
+// extern "C" entry points, batched over rows and over Vox's own thread pool (vox::parallel_for) with Vox's own
+// grain sizes. It serves two purposes:
+//   1. pin the C restatement (vox_oracle.c) and generate the golden fixtures under tests/golden/;
+//   2. time the reference's CPU path on the host cores (bench.py --impl reference, the cpu_baseline leg).
+// Where Vox's code is not externally linkable (anonymous-namespace lambdas: the F5 modulate / gated_add, the Snake
+// loops) the loop is restated here, around the reference's own helpers (vox::nn::fast_sin, vox::silu, ...), with
+// the reference's grain, and cited.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "f5.hpp"
+#include "kernels.hpp"
+#include "nn.hpp"
+#include "sampling.hpp"
+
+namespace vox {
+// resources.cpp (which owns release_pages) is not linked: the mmap helpers that reference it are never called here.
+void release_pages(const void *, size_t) {}
+}  // namespace vox
+
+using namespace vox;
+
+#define VR_API extern "C" __attribute__((visibility("default")))
+
+VR_API void vr_set_threads(int n) { set_num_threads(n); }
+VR_API int vr_num_threads() { return num_threads(); }
+
+// ---------------------------------------------------------------- generator (sampling.hpp, f5.cpp:402-414)
+
+VR_API void vr_philox_block(const uint32_t c[4], const uint32_t k[2], uint32_t out[4]) {
+    auto r = Philox4x32::block({c[0], c[1], c[2], c[3]}, {k[0], k[1]});
+    for (int i = 0; i < 4; ++i) out[i] = r[size_t(i)];
+}
+VR_API float vr_uniform(uint64_t seed, uint64_t frame, uint32_t codebook, uint32_t draw) {
+    return DetRng(seed).uniform(frame, codebook, draw);
+}
+VR_API void vr_f5_noise(uint64_t seed, uint32_t chunk, int64_t n, float *out) { F5Model::noise(seed, chunk, size_t(n), out); }
+
+VR_API float vr_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+VR_API float vr_bf16_to_f32(uint16_t h) { return bf16_to_f32(h); }
+
+// ---------------------------------------------------------------- normalisation
+
+// vox::rmsnorm (kernels.cpp:707-712) per row: serially, as transformer_forward calls it (kernels.cpp:793), or over
+// parallel_for(rows, 16).
+VR_API void vr_rmsnorm_rows(const float *x, const float *w, int64_t rows, int64_t n, float eps, float *out, int par) {
+    if (!par) {
+        for (int64_t r = 0; r < rows; ++r) rmsnorm(x + r * n, w, n, eps, out + r * n);
+        return;
+    }
+    parallel_for(rows, 16, [&](int64_t a, int64_t b) {
+        for (int64_t r = a; r < b; ++r) rmsnorm(x + r * n, w, n, eps, out + r * n);
+    });
+}
+
+// vox::layernorm (kernels.cpp:714-723) per row over parallel_for(rows, 16), as ln_rows (f5.cpp:101-106).
+VR_API void vr_layernorm_rows(const float *x, const float *w, const float *b, int64_t rows, int64_t n, float eps, float *out) {
+    parallel_for(rows, 16, [&](int64_t a, int64_t e) {
+        for (int64_t r = a; r < e; ++r) layernorm(x + r * n, w, b, n, eps, out + r * n);
+    });
+}
+
+// vox::nn::layer_norm (nn.cpp:248-265), in place.
+VR_API void vr_nn_layer_norm(float *x, int T, int C, const float *w, const float *b, float eps, int modulate) {
+    nn::layer_norm(x, T, C, w, b, eps, modulate != 0);
+}
+
+// F5 adaLN: the modulate lambda (f5.cpp:617-632, parallel_for(R, 16)) then the gated_add lambda (f5.cpp:670-676,
+// parallel_for(R, 32)) with src = the modulated rows, per batch b of x [B][T][D]. Restated (lambdas).
+VR_API void vr_adaln(const float *x, const float *shift, const float *scale, const float *gate, const float *res, int64_t B,
+                     int64_t T, int64_t D, float *out) {
+    for (int64_t bb = 0; bb < B; ++bb) {
+        const float *sc = scale + bb * D, *sh = shift + bb * D;
+        const float *src = x + bb * T * D;
+        float *dst = out + bb * T * D;
+        parallel_for(T, 16, [&](int64_t r0, int64_t r1) {
+            for (int64_t r = r0; r < r1; ++r) {
+                const float *xr = src + size_t(r) * size_t(D);
+                double mean = 0;
+                for (int i = 0; i < D; ++i) mean += xr[i];
+                mean /= D;
+                double var = 0;
+                for (int i = 0; i < D; ++i) { const double dd = xr[i] - mean; var += dd * dd; }
+                var /= D;
+                const float inv = float(1.0 / std::sqrt(var + 1e-6));
+                float *yr = dst + size_t(r) * size_t(D);
+                for (int i = 0; i < D; ++i) yr[i] = (xr[i] - float(mean)) * inv * (1.0f + sc[i]) + sh[i];
+            }
+        });
+        if (gate) {
+            const float *g = gate + bb * D, *rb = res + bb * T * D;
+            parallel_for(T, 32, [&](int64_t r0, int64_t r1) {
+                for (int64_t r = r0; r < r1; ++r)
+                    for (int i = 0; i < D; ++i) {
+                        const float m = dst[size_t(r) * size_t(D) + size_t(i)];
+                        dst[size_t(r) * size_t(D) + size_t(i)] = rb[size_t(r) * size_t(D) + size_t(i)];
+                        dst[size_t(r) * size_t(D) + size_t(i)] += g[i] * m;
+                    }
+            });
+        }
+    }
+}
+
+// Broadcast bias-add over parallel_for(T, 64): the loop of vox::nn::linear (nn.cpp:148-155).
+VR_API void vr_bias_add(float *y, const float *b, int64_t T, int64_t O) {
+    parallel_for(T, 64, [&](int64_t a, int64_t e) {
+        for (int64_t t = a; t < e; ++t)
+            for (int64_t o = 0; o < O; ++o) y[t * O + o] += b[size_t(o)];
+    });
+}
+
+// ---------------------------------------------------------------- softmax
+
+// Causal composition of transformer_forward (kernels.cpp:812-819) around vox::softmax_inplace (fast = 0) or
+// vox::nn::softmax_fast (fast = 1), over parallel_for(rows, 8) (the F5 attention grain, f5.cpp:650).
+VR_API void vr_softmax_rows(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0, int fast) {
+    parallel_for(rows, 8, [&](int64_t a, int64_t e) {
+        for (int64_t r = a; r < e; ++r) {
+            int64_t vis = n;
+            if (q_len > 0) vis = std::min<int64_t>(n, (r % q_len) + pos0 + 1);
+            float *yr = y + r * n;
+            for (int64_t j = 0; j < vis; ++j) yr[j] = scale * x[r * n + j];
+            if (fast) nn::softmax_fast(yr, vis);
+            else softmax_inplace(yr, vis);
+            for (int64_t j = vis; j < n; ++j) yr[j] = 0.0f;
+        }
+    });
+}
+
+// ---------------------------------------------------------------- activations
+
+// g[i] = silu(g[i]) * u[i] (kernels.cpp:836) over parallel_for(n, 4096) (the map_inplace grain, nn.hpp:111).
+VR_API void vr_silu_mul(const float *g, const float *u, float *h, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t a, int64_t b) {
+        for (int64_t i = a; i < b; ++i) h[i] = silu(g[i]) * u[i];
+    });
+}
+VR_API void vr_gelu_erf(const float *x, float *y, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t a, int64_t b) {
+        for (int64_t i = a; i < b; ++i) y[i] = gelu_erf(x[i]);
+    });
+}
+// vox::nn::gelu_inplace (nn.cpp:87-96): the AVX2 erfc-polynomial path, parallel_for(n, 8192).
+VR_API void vr_gelu_inplace(float *x, int64_t n) { nn::gelu_inplace(x, n); }
+// F5 gelu_tanh (f5.cpp:93-96), restated (anonymous namespace), over parallel_for(n, 4096).
+VR_API void vr_gelu_tanh(const float *x, float *y, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t a, int64_t b) {
+        for (int64_t i = a; i < b; ++i) {
+            const float k = 0.7978845608028654f, v = x[i];
+            y[i] = 0.5f * v * (1.0f + std::tanh(k * (v + 0.044715f * v * v * v)));
+        }
+    });
+}
+VR_API void vr_add(const float *a, const float *b, float *y, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t s, int64_t e) {
+        for (int64_t i = s; i < e; ++i) y[i] = a[i] + b[i];
+    });
+}
+VR_API void vr_mul(const float *a, const float *b, float *y, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t s, int64_t e) {
+        for (int64_t i = s; i < e; ++i) y[i] = a[i] * b[i];
+    });
+}
+// Vox's own fast_sin (nn.hpp:26-40), linked from the header.
+VR_API float vr_fast_sin(float x) { return nn::fast_sin(x); }
+
+// Snake over rows of `inner` elements, channel (i / inner) % C, parallel_for(rows, 256) (cosyvoice.cpp:241,
+// kokoro.cpp:235). kind 0 HiFT (cosyvoice.cpp:239-248), 1 SnakeBeta (qwen3.cpp:86-94, a / inv_b given),
+// 2 Kokoro (kokoro.cpp:233-242). Restated loops (anonymous namespaces), reference helpers.
+VR_API void vr_snake(const float *x, const float *alpha, const float *beta, float *y, int64_t n, int64_t C, int64_t inner, int kind) {
+    const int64_t rows = (n + inner - 1) / inner;
+    parallel_for(rows, inner == 1 ? 256 * C : 256, [&](int64_t a, int64_t e) {
+        for (int64_t i = a * inner; i < std::min(n, e * inner); ++i) {
+            const int64_t c = (i / inner) % C;
+            const float v = x[i];
+            if (kind == 0) {
+                const float al = alpha[c], sn = std::sin(al * v);
+                y[i] = v + (1.0f / (al + 1e-9f)) * (sn * sn);
+            } else if (kind == 1) {
+                const float sn = std::sin(v * alpha[c]);
+                y[i] = v + beta[c] * sn * sn;
+            } else {
+                const float s = nn::fast_sin(alpha[c] * v);
+                y[i] = v + (1.0f / alpha[c]) * (s * s);
+            }
+        }
+    });
+}
+
+// ---------------------------------------------------------------- block dequantisation
+
+// vox::mat_gather (kernels.cpp:468-471) of every row of a Q8 (type 3) or Q4 (type 4) Mat, over parallel_for(rows, 16)
+// (the dequant grain of matmul, kernels.cpp:665); f32 scales [rows][cols/32].
+VR_API void vr_mat_rows(int type, const uint8_t *data, const float *scale, int64_t rows, int64_t cols, float *out) {
+    Mat M;
+    M.type = type == 4 ? WType::Q4 : WType::Q8;
+    M.data = data;
+    M.scale = scale;
+    M.rows = rows;
+    M.cols = cols;
+    parallel_for(rows, 16, [&](int64_t a, int64_t b) {
+        for (int64_t r = a; r < b; ++r) mat_gather(M, r, out + r * cols);
+    });
+}
+
+VR_API void vr_quantize_q8(const float *w, int64_t rows, int64_t cols, int8_t *q, float *scale) {
+    std::vector<int8_t> qq;
+    std::vector<float> ss;
+    quantize_q8(w, rows, cols, qq, ss);
+    std::memcpy(q, qq.data(), qq.size());
+    std::memcpy(scale, ss.data(), ss.size() * 4);
+}
+VR_API void vr_quantize_q4(const float *w, int64_t rows, int64_t cols, uint8_t *q, float *scale) {
+    std::vector<uint8_t> qq;
+    std::vector<float> ss;
+    quantize_q4(w, rows, cols, qq, ss);
+    std::memcpy(q, qq.data(), qq.size());
+    std::memcpy(scale, ss.data(), ss.size() * 4);
+}
+
+// ---------------------------------------------------------------- reductions (CPU baseline only)
+
+// Row sum / max / L2 over parallel_for(rows, 16), float accumulation in element order as inside vox::rmsnorm
+// (kernels.cpp:709) and softmax_inplace (kernels.cpp:727-729).
+VR_API void vr_row_reduce(const float *x, float *out, int64_t rows, int64_t n, int op) {
+    parallel_for(rows, 16, [&](int64_t a, int64_t b) {
+        for (int64_t r = a; r < b; ++r) {
+            const float *xr = x + r * n;
+            float acc = op == 1 ? -INFINITY : 0.f;
+            for (int64_t i = 0; i < n; ++i) acc = op == 1 ? std::max(acc, xr[i]) : op == 2 ? acc + xr[i] * xr[i] : acc + xr[i];
+            out[r] = op == 2 ? std::sqrt(acc) : acc;
+        }
+    });
+}

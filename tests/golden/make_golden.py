@@ -1,0 +1,103 @@
+"""Generate the golden fixtures of the Vox operator path from dariumi/Vox's own CPU code.
+
+Inputs come from the seeded Philox generator of the C restatement (oracle/vox_oracle.c, itself checked against
+the reference's DetRng and F5Model::noise in gen.npz); every output is computed by the reference library
+oracle/_ref/libvox_ref.so, which is compiled from the reference sources (make -C oracle ref REF=...). The fixtures
+let the tests pin the oracle and the CUDA kernels on machines where the reference sources are absent.
+
+Run from the repository root: ``python tests/golden/make_golden.py``.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+from oracle.oracle import port, ref  # noqa: E402
+
+OUT = Path(__file__).resolve().parent
+
+
+def main() -> None:
+    P, R = port(), ref()
+    if R is None:
+        raise SystemExit("oracle/_ref/libvox_ref.so is missing: build it with `make -C oracle ref REF=<reference root>`")
+
+    # -- generator: DetRng::uniform and F5Model::noise of the reference
+    frames = np.arange(256, dtype=np.uint64)
+    uni = np.array([[[R.uniform(s, int(f), 7, d) for f in frames] for d in (0, 1)] for s in (0, 42)], np.float32)
+    np.savez_compressed(OUT / "gen.npz", uniform_seeds=np.array([0, 42], np.uint64), uniform=uni,
+                        noise_0_0=R.f5_noise(0, 0, 1001), noise_12345_3=R.f5_noise(12345, 3, 513))
+
+    # -- normalisation
+    x = P.normal((6, 1024))
+    w = P.normal((1024,), 1.0, 0.02, sid=1)
+    b = P.normal((1024,), 0.0, 0.1, sid=2)
+    x33 = P.normal((3, 33), sid=7)
+    X = P.normal((2, 8, 1024), sid=8)
+    sh = P.normal((2, 1024), 0.0, 0.1, sid=3)
+    sc = P.normal((2, 1024), 0.0, 0.1, sid=4)
+    g = P.normal((2, 1024), 0.0, 0.1, sid=5)
+    res = P.normal((2, 8, 1024), sid=6)
+    np.savez_compressed(
+        OUT / "norm.npz", x=x, w=w, b=b, x33=x33, X=X, shift=sh, scale=sc, gate=g, res=res,
+        rmsnorm=R.rmsnorm(x, w, 1e-6), rmsnorm33=R.rmsnorm(x33, w[:33], 1e-6),
+        layernorm=R.layernorm(x, w, b, 1e-5), layernorm_nob=R.layernorm(x, w, None, 1e-5),
+        ln_modulate=R.nn_layer_norm(x, w, b, 1e-6, True), ln_plain=R.nn_layer_norm(x, None, None, 1e-6),
+        adaln_gated=R.adaln(X, sh, sc, g, res), adaln_modulate=R.adaln(X, sh, sc))
+
+    # -- softmax (Vox's causal composition of kernels.cpp:812-819)
+    s = P.normal((2, 64, 64), 0.0, 3.0, sid=10)
+    s2 = P.normal((2, 16, 40), 0.0, 3.0, sid=11)
+    k = np.float32(1.0 / np.sqrt(128.0))
+    np.savez_compressed(
+        OUT / "softmax.npz", s=s, s2=s2, scale=k,
+        causal=R.softmax_rows(s, k, 64, 0), full=R.softmax_rows(s, k, 0, 0),
+        causal_pos24=R.softmax_rows(s2, k, 16, 24), causal_fast=R.softmax_rows(s, k, 64, 0, fast=True))
+
+    # -- activations
+    gg = P.normal((4, 3072), sid=20)
+    uu = P.normal((4, 3072), sid=21)
+    xg = P.normal((4099,), 0.0, 2.0, sid=22)
+    al = P.uniform_arr((8,), 0.2, 2.0, sid=23)
+    xs = P.normal((2, 8, 100), sid=24)
+    ib = P.uniform_arr((8,), 0.5, 1.5, sid=25)
+    np.savez_compressed(
+        OUT / "act.npz", g=gg, u=uu, xg=xg, alpha=al, xs=xs, inv_b=ib,
+        silu_mul=R.silu_mul(gg, uu), gelu_erf=R.gelu_erf(xg), gelu_inplace=R.gelu_inplace(xg), gelu_tanh=R.gelu_tanh(xg),
+        snake_hift_cm=R.snake(xs, al, 0, inner=100), snake_hift_tm=R.snake(xs, al, 0, inner=1),
+        snake_kokoro_cm=R.snake(xs, al, 2, inner=100), snake_kokoro_tm=R.snake(xs, al, 2, inner=1),
+        snake_beta_tm=R.snake(xs, al, 1, ib, inner=1),
+        fast_sin_x=np.linspace(-60, 60, 2001, dtype=np.float32),
+        fast_sin=np.array([R.fast_sin(v) for v in np.linspace(-60, 60, 2001, dtype=np.float32)], np.float32))
+
+    # -- block dequantisation (f16 scale bits converted by the reference's f16_to_f32)
+    q8 = P.fill_i8((64, 256), -128, 127, sid=30)
+    q4 = P.fill_u8((64, 128), sid=31)
+    s16 = P.uniform_arr((64, 8), 0.001, 0.05, sid=32).astype(np.float16)
+    s16_bits = s16.view(np.uint16)
+    s32 = R.f16_to_f32(s16_bits)
+    wq = P.normal((16, 256), 0.0, 0.05, sid=33)
+    rq8, rs8 = R.quantize_q8(wq)
+    rq4, rs4 = R.quantize_q4(wq)
+    np.savez_compressed(
+        OUT / "dequant.npz", q8=q8, q4=q4, scale_f16_bits=s16_bits, scale_f32=s32,
+        q8_out=R.mat_rows(q8, s32), q4_out=R.mat_rows(q4, s32, q4=True),
+        wq=wq, quant_q8=rq8, quant_q8_scale=rs8, quant_q8_out=R.mat_rows(rq8, rs8),
+        quant_q4=rq4, quant_q4_scale=rs4, quant_q4_out=R.mat_rows(rq4, rs4, q4=True))
+
+    # -- broadcast bias-add
+    yb = P.normal((8, 100), sid=40)
+    bb = P.normal((100,), sid=41)
+    np.savez_compressed(OUT / "bias.npz", y=yb, b=bb, out=R.bias_add(yb, bb))
+    for f in sorted(OUT.glob("*.npz")):
+        print(f.name, f.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

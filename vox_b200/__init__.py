@@ -1,0 +1,361 @@
+"""vox_b200 — B200 (sm_100a) backend for Vox's memory-bound operator path, Python host side.
+
+This module binds the C ABI of ``libvox_cuda.so`` (declared in ``include/vox_cuda.h``) with ctypes and exposes
+one function per Vox operator, under the names of Vox's CPU operator API (``src/kernels.hpp``, ``src/nn.hpp``)
+but batched and on device tensors. torch is used only to hold device memory and to name the current CUDA stream;
+every operator runs a kernel of ``libvox_cuda.so``. There is no CPU fallback: if the library is missing or the
+tensors are not on a CUDA device the call raises.
+
+Errors of the library come back as :class:`VoxCudaError` carrying Vox's status code (``include/vox.h:48-55``)
+and the library's per-thread message.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+__all__ = [
+    "VoxCudaError", "lib", "lib_path", "version",
+    "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
+    "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
+    "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
+    "fill_philox", "F32", "BF16", "F16",
+]
+
+F32, BF16, F16 = 0, 1, 2
+GELU_ERF, GELU_TANH = 0, 1
+SNAKE_HIFT, SNAKE_BETA, SNAKE_KOKORO = 0, 1, 2
+REDUCE_SUM, REDUCE_MAX, REDUCE_L2 = 0, 1, 2
+GLOBAL_SUM_SLOTS = 840
+STATUS_NAMES = {-3: "VOX_ERR_DEVICE", -4: "VOX_ERR_OOM", -6: "VOX_ERR_ARG", -8: "VOX_ERR_UNSUPPORTED"}
+
+_DIR = Path(__file__).resolve().parent
+lib_path = Path(os.environ.get("VOX_CUDA_LIB", _DIR / "libvox_cuda.so"))
+
+
+class VoxCudaError(RuntimeError):
+    """A vox_cuda call returned a negative status."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+def _load() -> ctypes.CDLL:
+    if not lib_path.exists():
+        raise ImportError(f"{lib_path} is missing: build it with `python -m vox_b200.build` (nvcc, sm_100a)")
+    L = ctypes.CDLL(str(lib_path))
+    c_i64, c_int, c_f, c_p, c_u64, c_u32 = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint32
+    sigs = {
+        "vox_cuda_version": ([], ctypes.c_char_p),
+        "vox_cuda_last_error": ([], ctypes.c_char_p),
+        "vox_cuda_device_count": ([c_p], c_int),
+        "vox_cuda_device_cc": ([c_p], c_int),
+        "vox_cuda_fill_philox": ([c_p, c_i64, c_int, c_f, c_f, c_u64, c_u32, c_i64, c_int, c_p], c_int),
+        "vox_cuda_rmsnorm": ([c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
+        "vox_cuda_layernorm": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_int, c_p], c_int),
+        "vox_cuda_adaln": ([c_p, c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_f, c_int, c_p], c_int),
+        "vox_cuda_gated_add": ([c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_bias_add": ([c_p, c_p, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_softmax_rows": ([c_p, c_p, c_i64, c_i64, c_f, c_i64, c_i64, c_p], c_int),
+        "vox_cuda_silu_mul": ([c_p, c_p, c_p, c_i64, c_int, c_p], c_int),
+        "vox_cuda_swiglu_fused": ([c_p, c_p, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_gelu": ([c_p, c_p, c_i64, c_int, c_int, c_p], c_int),
+        "vox_cuda_add": ([c_p, c_p, c_p, c_i64, c_int, c_p], c_int),
+        "vox_cuda_mul": ([c_p, c_p, c_p, c_i64, c_int, c_p], c_int),
+        "vox_cuda_snake": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_snake_beta_params": ([c_p, c_p, c_p, c_p, c_i64, c_p], c_int),
+        "vox_cuda_dequant_q8": ([c_p, c_p, c_int, c_p, c_int, c_i64, c_i64, c_p], c_int),
+        "vox_cuda_dequant_q4": ([c_p, c_p, c_int, c_p, c_int, c_i64, c_i64, c_p], c_int),
+        "vox_cuda_row_reduce": ([c_p, c_p, c_i64, c_i64, c_int, c_int, c_p], c_int),
+        "vox_cuda_global_sum_partials": ([c_p, c_i64, c_i64, c_i64, c_i64, c_p, c_p, c_int, c_p], c_int),
+        "vox_cuda_global_sum_finish": ([c_p, c_p, c_p], c_int),
+    }
+    for name, (args, res) in sigs.items():
+        f = getattr(L, name)
+        f.argtypes, f.restype = args, res
+    return L
+
+
+lib = _load()
+
+
+def version() -> str:
+    return lib.vox_cuda_version().decode()
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise VoxCudaError(rc, lib.vox_cuda_last_error().decode(errors="replace"))
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _dev(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise VoxCudaError(-6, f"{name} must be a CUDA tensor (vox_b200 has no CPU path)")
+    if not t.is_contiguous():
+        raise VoxCudaError(-6, f"{name} must be contiguous")
+    return t
+
+
+def _act(t: torch.Tensor, name: str) -> int:
+    _dev(t, name)
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise VoxCudaError(-6, f"{name} must be float32 or bfloat16, got {t.dtype}")
+
+
+def _f32(t: torch.Tensor | None, name: str) -> int | None:
+    if t is None:
+        return None
+    _dev(t, name)
+    if t.dtype != torch.float32:
+        raise VoxCudaError(-6, f"{name} must be float32 (Vox keeps this vector as const float *)")
+    return t.data_ptr()
+
+
+def _same(a: torch.Tensor, b: torch.Tensor, na: str, nb: str) -> None:
+    if a.dtype != b.dtype or a.device != b.device:
+        raise VoxCudaError(-6, f"{na} and {nb} must share dtype and device")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+# ------------------------------------------------------------------ normalisation
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rows of x [..., n] -> w * x / sqrt(mean(x^2) + eps). vox::rmsnorm (kernels.hpp:103) batched; out may be x."""
+    dt = _act(x, "x")
+    n = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _same(x, out, "x", "out")
+    _check(lib.vox_cuda_rmsnorm(x.data_ptr(), _f32(w, "w"), out.data_ptr(), x.numel() // n, n, eps, dt, _stream(x)))
+    return out
+
+
+def layernorm(x, w=None, b=None, eps: float = 1e-5, modulate: bool = False, out=None) -> torch.Tensor:
+    """vox::layernorm (kernels.hpp:104) / vox::nn::layer_norm (nn.hpp:83) over the last dim; modulate = (1+w)·n + b."""
+    dt = _act(x, "x")
+    n = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _same(x, out, "x", "out")
+    _check(lib.vox_cuda_layernorm(x.data_ptr(), _f32(w, "w"), _f32(b, "b"), out.data_ptr(), x.numel() // n, n, eps,
+                                  int(modulate), dt, _stream(x)))
+    return out
+
+
+def layer_norm(x: torch.Tensor, w, b, eps: float, modulate: bool = False) -> torch.Tensor:
+    """In place, as vox::nn::layer_norm(x, T, C, w, b, eps, modulate) (nn.cpp:248-265)."""
+    return layernorm(x, w, b, eps, modulate, out=x)
+
+
+def adaln(x, shift, scale, eps: float = 1e-6, gate=None, residual=None, out=None) -> torch.Tensor:
+    """Fused F5 adaLN over x [B][T][D]: residual + gate * (LN(x)·(1+scale) + shift), or the modulate part alone.
+
+    shift/scale/gate: [B][D] in x's dtype. f5.cpp:617-632 (modulate) composed with f5.cpp:670-676 (gated_add).
+    """
+    dt = _act(x, "x")
+    B, T, D = x.shape
+    for t, nm in ((shift, "shift"), (scale, "scale"), (gate, "gate"), (residual, "residual")):
+        if t is not None:
+            _same(x, _dev(t, nm), "x", nm)
+    out = torch.empty_like(x) if out is None else out
+    _check(lib.vox_cuda_adaln(x.data_ptr(), shift.data_ptr(), scale.data_ptr(), _ptr(gate), _ptr(residual), out.data_ptr(),
+                              B, T, D, eps, dt, _stream(x)))
+    return out
+
+
+def gated_add(h: torch.Tensor, gate: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """h [B][T][D] += gate [B][D] * src, in place (F5 gated_add, f5.cpp:670-676)."""
+    dt = _act(h, "h")
+    _same(h, _dev(src, "src"), "h", "src")
+    _same(h, _dev(gate, "gate"), "h", "gate")
+    B, T, D = h.shape
+    _check(lib.vox_cuda_gated_add(h.data_ptr(), gate.data_ptr(), src.data_ptr(), B, T, D, dt, _stream(h)))
+    return h
+
+
+def bias_add(y: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """y [..., D] += b [D] in place (bias loop of vox::nn::linear, nn.cpp:148-155)."""
+    dt = _act(y, "y")
+    D = y.shape[-1]
+    _check(lib.vox_cuda_bias_add(y.data_ptr(), _f32(b, "b"), y.numel() // D, D, dt, _stream(y)))
+    return y
+
+
+# ------------------------------------------------------------------ softmax
+
+def softmax_rows(x: torch.Tensor, scale: float = 1.0, q_len: int = 0, pos0: int = 0, out=None) -> torch.Tensor:
+    """Scaled row softmax of f32 rows [..., n]; q_len > 0 applies Vox's causal truncation (kernels.cpp:812-819)."""
+    if _act(x, "x") != F32:
+        raise VoxCudaError(-6, "softmax_rows works on float32 scores")
+    n = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _same(x, out, "x", "out")
+    _check(lib.vox_cuda_softmax_rows(x.data_ptr(), out.data_ptr(), x.numel() // n, n, scale, q_len, pos0, _stream(x)))
+    return out
+
+
+# ------------------------------------------------------------------ activations
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor, out=None) -> torch.Tensor:
+    """silu(g) * u (the SwiGLU loop of kernels.cpp:836); out may be g."""
+    dt = _act(g, "g")
+    _same(g, _dev(u, "u"), "g", "u")
+    out = torch.empty_like(g) if out is None else out
+    _check(lib.vox_cuda_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), dt, _stream(g)))
+    return out
+
+
+def swiglu_fused(gu: torch.Tensor, out=None) -> torch.Tensor:
+    """gu [m][2I] -> silu(gu[:, :I]) * gu[:, I:] (swiglu.comp)."""
+    dt = _act(gu, "gu")
+    m, I2 = gu.shape
+    out = torch.empty((m, I2 // 2), dtype=gu.dtype, device=gu.device) if out is None else out
+    _check(lib.vox_cuda_swiglu_fused(gu.data_ptr(), out.data_ptr(), m, I2 // 2, dt, _stream(gu)))
+    return out
+
+
+def gelu(x: torch.Tensor, kind: int = GELU_ERF, out=None) -> torch.Tensor:
+    """GELU, erf form (vox::gelu_erf, nn::gelu_inplace) or tanh form (F5 gelu_tanh); out may be x."""
+    dt = _act(x, "x")
+    out = torch.empty_like(x) if out is None else out
+    _same(x, out, "x", "out")
+    _check(lib.vox_cuda_gelu(x.data_ptr(), out.data_ptr(), x.numel(), kind, dt, _stream(x)))
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor, out=None) -> torch.Tensor:
+    dt = _act(a, "a")
+    _same(a, _dev(b, "b"), "a", "b")
+    out = torch.empty_like(a) if out is None else out
+    _check(lib.vox_cuda_add(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), dt, _stream(a)))
+    return out
+
+
+def mul(a: torch.Tensor, b: torch.Tensor, out=None) -> torch.Tensor:
+    dt = _act(a, "a")
+    _same(a, _dev(b, "b"), "a", "b")
+    out = torch.empty_like(a) if out is None else out
+    _check(lib.vox_cuda_mul(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), dt, _stream(a)))
+    return out
+
+
+def snake(x: torch.Tensor, alpha: torch.Tensor, kind: int = SNAKE_HIFT, beta=None, channel_major: bool = True,
+          out=None) -> torch.Tensor:
+    """Snake over f32 x: channel_major -> x [..., C, T] (inner = T); else Vox's time-major [T][C] (inner = 1)."""
+    if _act(x, "x") != F32:
+        raise VoxCudaError(-6, "snake works on float32 activations")
+    C = alpha.numel()
+    inner = x.shape[-1] if channel_major else 1
+    out = torch.empty_like(x) if out is None else out
+    _check(lib.vox_cuda_snake(x.data_ptr(), _f32(alpha, "alpha"), _f32(beta, "beta"), out.data_ptr(), x.numel(), C, inner,
+                              kind, _stream(x)))
+    return out
+
+
+def load_snake(alpha: torch.Tensor, beta: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The Snake struct of load_snake (qwen3.cpp:76-84): a = exp(alpha), inv_b = 1/(exp(beta) + 1e-9)."""
+    a = torch.empty_like(alpha)
+    ib = torch.empty_like(beta)
+    _check(lib.vox_cuda_snake_beta_params(_f32(alpha, "alpha"), _f32(beta, "beta"), a.data_ptr(), ib.data_ptr(), alpha.numel(),
+                                          _stream(alpha)))
+    return a, ib
+
+
+# ------------------------------------------------------------------ dequantisation
+
+def _scale_dt(scale: torch.Tensor) -> int:
+    _dev(scale, "scale")
+    if scale.dtype == torch.float32:
+        return F32
+    if scale.dtype == torch.float16:
+        return F16
+    raise VoxCudaError(-6, "scale must be float32 (Vox's layout) or float16")
+
+
+def dequant_q8(q: torch.Tensor, scale: torch.Tensor, out_dtype=torch.bfloat16, out=None) -> torch.Tensor:
+    """int8 q [rows][cols] * scale [rows][cols/32] -> out (vox::mat_row Q8, kernels.cpp:446-452)."""
+    _dev(q, "q")
+    rows, cols = q.shape
+    out = torch.empty((rows, cols), dtype=out_dtype, device=q.device) if out is None else out
+    _check(lib.vox_cuda_dequant_q8(q.data_ptr(), scale.data_ptr(), _scale_dt(scale), out.data_ptr(), _act(out, "out"), rows, cols,
+                                   _stream(q)))
+    return out
+
+
+def dequant_q4(q: torch.Tensor, scale: torch.Tensor, out_dtype=torch.bfloat16, out=None) -> torch.Tensor:
+    """packed uint8 q [rows][cols/2] -> out [rows][cols] (vox::mat_row Q4, kernels.cpp:453-463)."""
+    _dev(q, "q")
+    rows, half = q.shape
+    cols = half * 2
+    out = torch.empty((rows, cols), dtype=out_dtype, device=q.device) if out is None else out
+    _check(lib.vox_cuda_dequant_q4(q.data_ptr(), scale.data_ptr(), _scale_dt(scale), out.data_ptr(), _act(out, "out"), rows, cols,
+                                   _stream(q)))
+    return out
+
+
+# ------------------------------------------------------------------ reductions
+
+def row_reduce(x: torch.Tensor, op: int = REDUCE_SUM, out=None) -> torch.Tensor:
+    """Per-row sum / max / L2 norm of x [..., n] -> f32 [...]."""
+    dt = _act(x, "x")
+    n = x.shape[-1]
+    rows = x.numel() // n
+    out = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device) if out is None else out
+    _check(lib.vox_cuda_row_reduce(x.data_ptr(), out.data_ptr(), rows, n, op, dt, _stream(x)))
+    return out
+
+
+def global_sum_partials(x: torch.Tensor, row0: int, total_rows: int, slots=None, scratch=None) -> torch.Tensor:
+    """Slot partials (f64 [840]) of this shard's rows [row0, row0 + rows) of a [total_rows][n] tensor."""
+    dt = _act(x, "x")
+    n = x.shape[-1]
+    rows = x.numel() // n
+    slots = torch.empty(GLOBAL_SUM_SLOTS, dtype=torch.float64, device=x.device) if slots is None else slots
+    scratch = torch.empty(max(rows, 1), dtype=torch.float32, device=x.device) if scratch is None else scratch
+    _check(lib.vox_cuda_global_sum_partials(x.data_ptr(), rows, n, row0, total_rows, scratch.data_ptr(), slots.data_ptr(), dt,
+                                            _stream(x)))
+    return slots
+
+
+def global_sum_finish(slots: torch.Tensor, out=None) -> torch.Tensor:
+    out = torch.empty(1, dtype=torch.float64, device=slots.device) if out is None else out
+    _check(lib.vox_cuda_global_sum_finish(slots.data_ptr(), out.data_ptr(), _stream(slots)))
+    return out
+
+
+def global_sum(x: torch.Tensor, row0: int = 0, total_rows: int | None = None, group=None) -> torch.Tensor:
+    """Deterministic sum of a row-sharded tensor: slot partials, one all-reduce of 840 f64 (NCCL), fixed-order fold.
+
+    With torch.distributed initialised, every rank passes its shard and the global row offset; the result (f64 [1])
+    is bitwise identical for any world size that divides the rows into whole slots.
+    """
+    total_rows = x.numel() // x.shape[-1] if total_rows is None else total_rows
+    slots = global_sum_partials(x, row0, total_rows)
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(slots, op=dist.ReduceOp.SUM, group=group)
+    return global_sum_finish(slots)
+
+
+# ------------------------------------------------------------------ synthetic data
+
+def fill_philox(out: torch.Tensor, dist: int, a: float, b: float, seed: int = 0, stream_id: int = 0, counter0: int = 0) -> torch.Tensor:
+    """Fill a device tensor with Vox's Philox4x32-10 draws (0 uniform, 1 normal, 2 int8 codes, 3 bytes)."""
+    _dev(out, "out")
+    dt = BF16 if out.dtype == torch.bfloat16 else F32
+    _check(lib.vox_cuda_fill_philox(out.data_ptr(), out.numel(), dist, a, b, seed, stream_id, counter0, dt, _stream(out)))
+    return out

@@ -1,0 +1,153 @@
+// Q8 / Q4 block dequantisation (32 weights per block, one scale per block), to f32 or bf16.
+//
+// Vox layout (kernels.hpp:42-47): Q8 codes int8 [rows][cols], Q4 codes packed [rows][cols/2] with byte j of a
+// 16-byte block holding element j (low nibble) and element j+16 (high nibble); scales [rows][cols/32] f32 (Vox's
+// loader, nn.cpp:141-143) or f16 (converted exactly to f32 first). Because cols % 32 == 0 the scale of flat
+// element e is simply scale[e / 32].
+//
+// Value = float(code) * scale (Q8, kernels.cpp:450) or float(int(nibble) - 8) * scale (Q4, kernels.cpp:459-460):
+// a single f32 multiply, so the f32 result is bit-identical to vox::mat_row, and the bf16 result is its
+// round-to-nearest-even.
+//
+// Each thread produces one 16-byte output vector per iteration (8 bf16 or 4 f32), so every store instruction of
+// a warp writes 512 contiguous bytes; the codes come in as 4- or 8-byte loads, kUnroll iterations in flight.
+#include "common.cuh"
+
+namespace voxcuda {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+constexpr int kBlocksPerSm = 8;
+
+template <int SDT>
+__device__ __forceinline__ float load_scale(const void *s, int64_t i) {
+    if (SDT == VOX_CUDA_F16) return __half2float(__ldg(reinterpret_cast<const __half *>(s) + i));
+    return __ldg(reinterpret_cast<const float *>(s) + i);
+}
+
+// OPT outputs per thread-iteration: 8 for bf16, 4 for f32 (16 bytes either way).
+template <int ODT> struct OutVec {
+    static constexpr int OPT = ODT == VOX_CUDA_BF16 ? 8 : 4;
+    __device__ __forceinline__ static uint4 pack(const float *v) {
+        if (ODT == VOX_CUDA_BF16)
+            return make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+        return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+    }
+};
+
+// Codes of output vector v as OPT signed integers.
+template <bool Q4, int OPT>
+__device__ __forceinline__ void load_codes(const uint8_t *q, int64_t v, int *c) {
+    const int64_t e0 = v * OPT;
+    if (!Q4) {
+        if (OPT == 8) {
+            const uint2 w = ld_stream8(q + e0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                c[k] = int(int8_t(w.x >> (8 * k)));
+                c[4 + k] = int(int8_t(w.y >> (8 * k)));
+            }
+        } else {
+            const uint32_t w = __ldcs(reinterpret_cast<const unsigned int *>(q + e0));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) c[k] = int(int8_t(w >> (8 * k)));
+        }
+    } else {
+        const int64_t blk = e0 >> 5;
+        const int o = int(e0 & 31);
+        const uint8_t *p = q + blk * 16 + (o & 15);
+        const int sh = (o >> 4) * 4;  // 0: low nibbles (elements 0..15), 4: high nibbles (16..31)
+        if (OPT == 8) {
+            const uint2 w = ld_stream8(p);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                c[k] = int((w.x >> (8 * k + sh)) & 15u) - 8;
+                c[4 + k] = int((w.y >> (8 * k + sh)) & 15u) - 8;
+            }
+        } else {
+            const uint32_t w = __ldcs(reinterpret_cast<const unsigned int *>(p));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) c[k] = int((w >> (8 * k + sh)) & 15u) - 8;
+        }
+    }
+}
+
+template <bool Q4, int SDT, int ODT>
+__global__ void __launch_bounds__(kThreads) dequant_kernel(const uint8_t *q, const void *scale, void *out, int64_t nvec) {
+    constexpr int OPT = OutVec<ODT>::OPT;
+    constexpr int VPB = 32 / OPT;  // output vectors per 32-weight block
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    uint4 *po = reinterpret_cast<uint4 *>(out);
+    int64_t v = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; v + (kUnroll - 1) * stride < nvec; v += kUnroll * stride) {
+        int c[kUnroll][OPT];
+        float s[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            load_codes<Q4, OPT>(q, v + u * stride, c[u]);
+            s[u] = load_scale<SDT>(scale, (v + u * stride) / VPB);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            float f[OPT];
+#pragma unroll
+            for (int k = 0; k < OPT; ++k) f[k] = __fmul_rn(float(c[u][k]), s[u]);
+            st_stream(po + v + u * stride, OutVec<ODT>::pack(f));
+        }
+    }
+    for (; v < nvec; v += stride) {
+        int c[OPT];
+        load_codes<Q4, OPT>(q, v, c);
+        const float s = load_scale<SDT>(scale, v / VPB);
+        float f[OPT];
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) f[k] = __fmul_rn(float(c[k]), s);
+        st_stream(po + v, OutVec<ODT>::pack(f));
+    }
+}
+
+template <bool Q4>
+int launch_dequant(const uint8_t *q, const void *scale, int sdt, void *out, int odt, int64_t rows, int64_t cols, void *stream,
+                   const char *name) {
+    VOX_REQUIRE(sdt == VOX_CUDA_F32 || sdt == VOX_CUDA_F16, std::string(name) + ": scale dtype must be F32 or F16");
+    VOX_REQUIRE(odt == VOX_CUDA_F32 || odt == VOX_CUDA_BF16, std::string(name) + ": out dtype must be F32 or BF16");
+    VOX_REQUIRE(rows >= 0 && cols >= 0 && cols % 32 == 0, std::string(name) + ": cols must be a multiple of 32");
+    const int64_t n = rows * cols;
+    if (n == 0) return VOX_CUDA_OK;
+    VOX_REQUIRE(q && scale && out, std::string(name) + ": NULL pointer");
+    VOX_REQUIRE(aligned16(out), std::string(name) + ": out must be 16-byte aligned");
+    VOX_REQUIRE((reinterpret_cast<uintptr_t>(q) & 7u) == 0, std::string(name) + ": codes must be 8-byte aligned");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int opt = odt == VOX_CUDA_BF16 ? 8 : 4;
+    const int64_t nvec = n / opt;
+    const int g = grid_for((nvec + kUnroll - 1) / kUnroll, kThreads, kBlocksPerSm);
+    if (odt == VOX_CUDA_BF16) {
+        if (sdt == VOX_CUDA_F16) dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_BF16><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
+        else dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_BF16><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
+    } else {
+        if (sdt == VOX_CUDA_F16) dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_F32><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
+        else dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_F32><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
+    }
+    return check_launch(name);
+}
+
+}  // namespace
+}  // namespace voxcuda
+
+using namespace voxcuda;
+
+extern "C" {
+
+int vox_cuda_dequant_q8(const int8_t *q, const void *scale, int scale_dtype, void *out, int out_dtype, int64_t rows, int64_t cols,
+                        void *stream) {
+    return launch_dequant<false>(reinterpret_cast<const uint8_t *>(q), scale, scale_dtype, out, out_dtype, rows, cols, stream,
+                                 "vox_cuda_dequant_q8");
+}
+
+int vox_cuda_dequant_q4(const uint8_t *q, const void *scale, int scale_dtype, void *out, int out_dtype, int64_t rows, int64_t cols,
+                        void *stream) {
+    return launch_dequant<true>(q, scale, scale_dtype, out, out_dtype, rows, cols, stream, "vox_cuda_dequant_q4");
+}
+
+}  // extern "C"

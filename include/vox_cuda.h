@@ -76,6 +76,11 @@ VOX_CUDA_API const char *vox_cuda_last_error(void);
 VOX_CUDA_API int vox_cuda_device_count(int *count);
 /* Compute capability of the current device as major*10+minor (100 for B200), written to *cc. */
 VOX_CUDA_API int vox_cuda_device_cc(int *cc);
+/* Device-side error bits of the current device since the last call, written to *flags, then cleared (synchronises
+ * with the device). Bit 0 (VOX_CUDA_DEVERR_TIMEOUT): a kernel gave up a bounded wait for its staged data and left
+ * its rows unwritten. No counterpart in the reference (Vox's Vulkan backend has no device-side waits). */
+#define VOX_CUDA_DEVERR_TIMEOUT 1u
+VOX_CUDA_API int vox_cuda_device_error(unsigned int *flags);
 
 /* Seeded synthetic data with Vox's counter-based generator (Philox4x32-10, src/sampling.hpp:16-50).
  * Element i uses counter {i lo, i hi, stream_id, draw}, key {seed lo, seed hi}.

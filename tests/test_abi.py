@@ -129,7 +129,7 @@ int main() {
     from vox_b200 import build
 
     exe = tmp_path / "fd"
-    subprocess.run([build.nvcc(), "-std=c++17", f"-I{build.CSRC}", f"-I{build.INCLUDE}", str(src), "-o", str(exe)], check=True,
-                   capture_output=True)
+    subprocess.run([build.nvcc(), *build.ARCH, "-std=c++17", f"-I{build.CSRC}", f"-I{build.INCLUDE}", str(src), "-o", str(exe)],
+                   check=True, capture_output=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0 and r.stdout.strip() == "0", r.stdout

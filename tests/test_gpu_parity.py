@@ -157,9 +157,9 @@ def test_adaln_config3_bf16(vox, port):
     out = vox.adaln(d(x), d(sh), d(sc), 1e-6, d(g), d(res))
     got = host(out)
     assert_close(got, want, BF16_TOL)
-    # one bf16 ulp at most from the oracle's rounded result
-    ulp = np.abs(got.view(np.int32) - want.view(np.int32))
-    assert ulp.max() <= 1
+    # nearly every output is the oracle's bf16 value itself (statistics in f32 on the GPU, f64 on the CPU; the few
+    # differences sit where residual and gate * m nearly cancel)
+    assert np.mean(got.view(np.uint32) == want.view(np.uint32)) > 0.99
     assert_bitexact(host(vox.adaln(d(x), d(sh), d(sc), 1e-6, d(g), d(res))), got)
 
 
@@ -399,3 +399,12 @@ def test_cpu_tensor_is_rejected(vox):
         vox.add(torch.ones(4), torch.ones(4))
     with pytest.raises(vox.VoxCudaError):
         vox.add(torch.ones(4, dtype=torch.float64, device="cuda"), torch.ones(4, dtype=torch.float64, device="cuda"))
+
+
+def test_no_device_side_timeouts(vox):
+    """Every bounded wait of the row pipeline completed during the tests above (flag read and cleared)."""
+    import ctypes
+
+    flags = ctypes.c_uint(7)
+    vox._check(vox.lib.vox_cuda_device_error(ctypes.byref(flags)))
+    assert flags.value == 0

@@ -55,6 +55,7 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_last_error": ([], ctypes.c_char_p),
         "vox_cuda_device_count": ([c_p], c_int),
         "vox_cuda_device_cc": ([c_p], c_int),
+        "vox_cuda_device_error": ([c_p], c_int),
         "vox_cuda_fill_philox": ([c_p, c_i64, c_int, c_f, c_f, c_u64, c_u32, c_i64, c_int, c_p], c_int),
         "vox_cuda_rmsnorm": ([c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
         "vox_cuda_layernorm": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_int, c_p], c_int),

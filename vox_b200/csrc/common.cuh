@@ -28,6 +28,15 @@ int smem_optin();
 // at most `per_sm` blocks on every SM, at least 1.
 int grid_for(int64_t work_items, int threads, int per_sm);
 
+// Blocks of `kernel` (with `threads` threads and `smem` dynamic shared memory) resident on the whole device at once
+// (occupancy query, cached per kernel and device).
+int resident_blocks(const void *kernel, int threads, size_t smem);
+
+// Balanced persistent grid: `units` work units, `per_block` of them taken by one block per pass; the grid is at most
+// one resident wave and every block makes the same number of passes (but the last ones), so no block is left
+// working alone at the end.
+int balanced_grid(int64_t units, int64_t per_block, int resident);
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool is_act_dtype(int d) { return d == VOX_CUDA_F32 || d == VOX_CUDA_BF16; }
 inline int dtype_size(int d) { return d == VOX_CUDA_F32 ? 4 : 2; }
@@ -88,6 +97,13 @@ __device__ __forceinline__ uint4 ld_stream(const void *p) {
 }
 // 16-byte read-only load through L1 (parameters reused by many rows).
 __device__ __forceinline__ uint4 ld_param(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+// 16-byte read-only load through L1 that the compiler keeps in program order relative to the other ordered
+// accesses (used where hoisting every parameter load of an unrolled loop would cost more registers than it saves).
+__device__ __forceinline__ uint4 ld_param_ordered(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
 // 8-byte streaming load.
 __device__ __forceinline__ uint2 ld_stream8(const void *p) {
     uint2 r;
@@ -135,6 +151,36 @@ template <> struct Vec<VOX_CUDA_BF16> {
     }
     __device__ __forceinline__ static void store1(void *p, int64_t i, float v) { reinterpret_cast<uint16_t *>(p)[i] = to_bf16(v); }
 };
+
+// ------------------------------------------------------------------ device: packed f32x2 arithmetic
+// Blackwell issues two f32 lanes per instruction (FADD2 / FMUL2 / FFMA2); each lane is rounded as the scalar
+// __fadd_rn / __fmul_rn / __fmaf_rn. The compiler may fuse an FMUL2 into a following FADD2 (one rounding instead
+// of two), so code that must keep the CPU's two roundings bit-exactly uses the scalar intrinsics instead.
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 bc2(float v) { return make_float2(v, v); }
+
+// The 16-byte vector of Vec<DT> as W/2 float pairs.
+template <int DT> __device__ __forceinline__ void unpack2(uint4 v, float2 *p);
+template <> __device__ __forceinline__ void unpack2<VOX_CUDA_F32>(uint4 v, float2 *p) {
+    p[0] = make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+    p[1] = make_float2(__uint_as_float(v.z), __uint_as_float(v.w));
+}
+template <> __device__ __forceinline__ void unpack2<VOX_CUDA_BF16>(uint4 v, float2 *p) {
+    p[0] = make_float2(bf16lo(v.x), bf16hi(v.x));
+    p[1] = make_float2(bf16lo(v.y), bf16hi(v.y));
+    p[2] = make_float2(bf16lo(v.z), bf16hi(v.z));
+    p[3] = make_float2(bf16lo(v.w), bf16hi(v.w));
+}
+template <int DT> __device__ __forceinline__ uint4 pack2(const float2 *p);
+template <> __device__ __forceinline__ uint4 pack2<VOX_CUDA_F32>(const float2 *p) {
+    return make_uint4(__float_as_uint(p[0].x), __float_as_uint(p[0].y), __float_as_uint(p[1].x), __float_as_uint(p[1].y));
+}
+template <> __device__ __forceinline__ uint4 pack2<VOX_CUDA_BF16>(const float2 *p) {
+    return make_uint4(pack_bf16(p[0].x, p[0].y), pack_bf16(p[1].x, p[1].y), pack_bf16(p[2].x, p[2].y), pack_bf16(p[3].x, p[3].y));
+}
 
 // ------------------------------------------------------------------ device: warp reductions (fixed xor butterfly)
 

@@ -17,8 +17,7 @@ namespace voxcuda {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
-constexpr int kBlocksPerSm = 8;
+constexpr int kUnroll = 8;
 
 template <int SDT>
 __device__ __forceinline__ float load_scale(const void *s, int64_t i) {
@@ -36,39 +35,28 @@ template <int ODT> struct OutVec {
     }
 };
 
-// Codes of output vector v as OPT signed integers.
+// Raw code bytes of output vector v: 8 bytes (OPT = 8) or 4 bytes (OPT = 4, in .x), and the nibble shift for Q4.
 template <bool Q4, int OPT>
-__device__ __forceinline__ void load_codes(const uint8_t *q, int64_t v, int *c) {
+__device__ __forceinline__ uint2 load_code_word(const uint8_t *q, int64_t v) {
     const int64_t e0 = v * OPT;
+    const uint8_t *p = Q4 ? q + (e0 >> 5) * 16 + (e0 & 15) : q + e0;  // Q4: byte j of a block holds elements j, j+16
+    if (OPT == 8) return ld_stream8(p);
+    return make_uint2(__ldcs(reinterpret_cast<const unsigned int *>(p)), 0u);
+}
+template <bool Q4, int OPT>
+__device__ __forceinline__ void decode(uint2 w, int64_t v, int *c) {
     if (!Q4) {
-        if (OPT == 8) {
-            const uint2 w = ld_stream8(q + e0);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                c[k] = int(int8_t(w.x >> (8 * k)));
-                c[4 + k] = int(int8_t(w.y >> (8 * k)));
-            }
-        } else {
-            const uint32_t w = __ldcs(reinterpret_cast<const unsigned int *>(q + e0));
-#pragma unroll
-            for (int k = 0; k < 4; ++k) c[k] = int(int8_t(w >> (8 * k)));
+        for (int k = 0; k < 4; ++k) {
+            c[k] = int(int8_t(w.x >> (8 * k)));
+            if (OPT == 8) c[4 + k] = int(int8_t(w.y >> (8 * k)));
         }
     } else {
-        const int64_t blk = e0 >> 5;
-        const int o = int(e0 & 31);
-        const uint8_t *p = q + blk * 16 + (o & 15);
-        const int sh = (o >> 4) * 4;  // 0: low nibbles (elements 0..15), 4: high nibbles (16..31)
-        if (OPT == 8) {
-            const uint2 w = ld_stream8(p);
+        const int sh = int((v * OPT) & 16) >> 2;  // 0: low nibbles (elements 0..15 of the block), 4: high (16..31)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                c[k] = int((w.x >> (8 * k + sh)) & 15u) - 8;
-                c[4 + k] = int((w.y >> (8 * k + sh)) & 15u) - 8;
-            }
-        } else {
-            const uint32_t w = __ldcs(reinterpret_cast<const unsigned int *>(p));
-#pragma unroll
-            for (int k = 0; k < 4; ++k) c[k] = int((w >> (8 * k + sh)) & 15u) - 8;
+        for (int k = 0; k < 4; ++k) {
+            c[k] = int((w.x >> (8 * k + sh)) & 15u) - 8;
+            if (OPT == 8) c[4 + k] = int((w.y >> (8 * k + sh)) & 15u) - 8;
         }
     }
 }
@@ -79,31 +67,36 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const uint8_t *q, con
     constexpr int VPB = 32 / OPT;  // output vectors per 32-weight block
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
     uint4 *po = reinterpret_cast<uint4 *>(out);
-    int64_t v = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; v + (kUnroll - 1) * stride < nvec; v += kUnroll * stride) {
-        int c[kUnroll][OPT];
+    // kUnroll output vectors per thread per iteration, the last iteration predicated (its loads still in flight
+    // together); the code words stay packed until they are used
+    for (int64_t v = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += kUnroll * stride) {
+        uint2 cw[kUnroll];
         float s[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            load_codes<Q4, OPT>(q, v + u * stride, c[u]);
-            s[u] = load_scale<SDT>(scale, (v + u * stride) / VPB);
+            const int64_t w = v + u * stride;
+            if (w < nvec) {
+                cw[u] = load_code_word<Q4, OPT>(q, w);
+                s[u] = load_scale<SDT>(scale, w / VPB);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            float f[OPT];
+            const int64_t w = v + u * stride;
+            if (w < nvec) {
+                int c[OPT];
+                decode<Q4, OPT>(cw[u], w, c);
+                float f[OPT];
+                const float2 s2 = bc2(s[u]);
 #pragma unroll
-            for (int k = 0; k < OPT; ++k) f[k] = __fmul_rn(float(c[u][k]), s[u]);
-            st_stream(po + v + u * stride, OutVec<ODT>::pack(f));
+                for (int k = 0; k < OPT; k += 2) {
+                    const float2 p = mul2(make_float2(float(c[k]), float(c[k + 1])), s2);  // one rounding each, as kernels.cpp:450,459
+                    f[k] = p.x;
+                    f[k + 1] = p.y;
+                }
+                st_stream(po + w, OutVec<ODT>::pack(f));
+            }
         }
-    }
-    for (; v < nvec; v += stride) {
-        int c[OPT];
-        load_codes<Q4, OPT>(q, v, c);
-        const float s = load_scale<SDT>(scale, v / VPB);
-        float f[OPT];
-#pragma unroll
-        for (int k = 0; k < OPT; ++k) f[k] = __fmul_rn(float(c[k]), s);
-        st_stream(po + v, OutVec<ODT>::pack(f));
     }
 }
 
@@ -121,14 +114,10 @@ int launch_dequant(const uint8_t *q, const void *scale, int sdt, void *out, int 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int opt = odt == VOX_CUDA_BF16 ? 8 : 4;
     const int64_t nvec = n / opt;
-    const int g = grid_for((nvec + kUnroll - 1) / kUnroll, kThreads, kBlocksPerSm);
-    if (odt == VOX_CUDA_BF16) {
-        if (sdt == VOX_CUDA_F16) dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_BF16><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
-        else dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_BF16><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
-    } else {
-        if (sdt == VOX_CUDA_F16) dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_F32><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
-        else dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_F32><<<g, kThreads, 0, st>>>(q, scale, out, nvec);
-    }
+    auto kern = odt == VOX_CUDA_BF16 ? (sdt == VOX_CUDA_F16 ? dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_BF16> : dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_BF16>)
+                                     : (sdt == VOX_CUDA_F16 ? dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_F32> : dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_F32>);
+    const int g = balanced_grid(nvec, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
+    kern<<<g, kThreads, 0, st>>>(q, scale, out, nvec);
     return check_launch(name);
 }
 

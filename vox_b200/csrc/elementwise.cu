@@ -1,17 +1,30 @@
 // Elementwise and broadcast operators: SiLU·mul (SwiGLU), fused gate|up SwiGLU, GELU (erf / tanh), add, mul,
 // Snake (three Vox forms), broadcast bias-add and the gated residual add.
 //
-// All of them stream 16-byte vectors through a grid-stride loop sized to the SM count (U vectors in flight per
-// thread per iteration), with the loads marked L1::no_allocate + L2::evict_first and the stores .cs, so each tensor
-// crosses HBM once. A scalar path serves pointers that are not 16-byte aligned and the tail of n % vector-width
+// All of them stream 16-byte vectors through a grid-stride loop sized to the SM count (kUnroll vectors in flight
+// per thread per iteration), with the loads on the read-only path without L1 allocation and the stores .cs, so each
+// tensor crosses HBM once. A scalar path serves pointers that are not 16-byte aligned and the tail of n % vector-width
 // elements. Per-element parameters (a channel's alpha, a column's bias, a batch's gate) are indexed from the
 // vector index with FastDiv, not 64-bit division.
 //
 // Rounding: where Vox's CPU code (compiled for baseline x86-64, no FMA) rounds after every multiply and add, the
 // kernels use __fmul_rn/__fadd_rn so that the only differences from the CPU come from the transcendental
-// functions (expf/erff/tanhf/sinf of CUDA vs glibc). Vox's own fast_sin polynomial is restated with the same
-// rounded steps, which makes the Kokoro Snake bit-exact with the CPU.
+// functions. Vox's own fast_sin polynomial is restated with the same rounded steps, which makes the Kokoro Snake
+// bit-exact with the CPU.
+//
+// Transcendentals are evaluated with fewer instructions than the general-purpose CUDA functions, because the
+// bf16 and Snake paths are otherwise bound by instruction issue rather than HBM:
+//   sin^2 (HiFT / SnakeBeta): sin^2 has period pi and is even, so theta is reduced by pi with a three-constant
+//     Cody-Waite step on FMAs (r in [-pi/2, pi/2]) and sin^2(r) = u * P(u), u = r^2, P a degree-5 polynomial fitted
+//     here (weighted least squares on relative error over u in [0, pi^2/4]); max relative error 2.4e-7 in f32,
+//     the same as rounding sinf(theta)^2.
+//   GELU (erf form): x * Phi(x) with the upper normal tail Q(a) = phi(a) * (b1 t + ... + b5 t^5), t = 1/(1 + p a),
+//     from Abramowitz & Stegun 26.2.17 (|error| < 7.5e-8), using the SFU's ex2 and rcp: absolute GELU error below
+//     2.5e-7 * |x|, the size of the difference between Vox's two CPU GELUs (std::erf vs nn::gelu_inplace).
+//   GELU (tanh form): tanh(z) = 1 - 2 / (1 + e^(2z)) with the SFU's ex2 and rcp (absolute error ~1e-7).
+//   SiLU: x / (1 + e^-x) with CUDA's expf and the 2-ulp division (relative error ~3e-7), as kernels.hpp:105.
 #include "common.cuh"
+#include "sfu.cuh"
 
 namespace voxcuda {
 namespace {
@@ -22,16 +35,50 @@ constexpr int kBlocksPerSm = 8;
 
 // ------------------------------------------------------------------ scalar math shared by the ops
 
-__device__ __forceinline__ float silu_f(float x) {  // x / (1 + exp(-x)), kernels.hpp:105
-    return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+__device__ __forceinline__ float silu_f(float x) {  // x / (1 + exp(-x)), kernels.hpp:105 (2-ulp division)
+    return __fdividef(x, __fadd_rn(1.0f, expf(-x)));
 }
-__device__ __forceinline__ float gelu_erf_f(float x) {  // 0.5 x (1 + erf(x / sqrt2)), kernels.hpp:106
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(__fmul_rn(x, 0.70710678118654752440f))));
+// GELU, erf form (kernels.hpp:106, nn.cpp:87-96): x * Phi(x), Phi from the normal tail of Abramowitz & Stegun 26.2.17,
+// two elements per call.
+__device__ __forceinline__ float2 gelu_erf_f2(float2 x) {
+    const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+    const float2 d = fma2(bc2(0.2316419f), a, bc2(1.0f));
+    const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+    // b_k / sqrt(2 pi) of A&S 26.2.17
+    float2 p = fma2(bc2(0.530702714f), t, bc2(-0.726576013f));  // 1.330274429, -1.821255978 (/ sqrt(2 pi))
+    p = fma2(p, t, bc2(0.710706871f));                            // 1.781477937
+    p = fma2(p, t, bc2(-0.142248368f));                           // -0.356563782
+    p = fma2(p, t, bc2(0.127414796f));                            // 0.319381530
+    p = mul2(p, t);
+    const float2 g = mul2(mul2(a, a), bc2(-0.72134752f));         // exp(-a^2 / 2) = 2^(-a^2 log2(e) / 2)
+    const float2 xq = mul2(x, mul2(make_float2(ex2_approx(g.x), ex2_approx(g.y)), p));  // x * Q(|x|)
+    const float2 hi = fma2(xq, bc2(-1.0f), x);                    // x - x Q(|x|)
+    return make_float2(x.x >= 0.f ? hi.x : xq.x, x.y >= 0.f ? hi.y : xq.y);
 }
-__device__ __forceinline__ float gelu_tanh_f(float x) {  // f5.cpp:93-96
-    const float k = 0.7978845608028654f;
-    const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(__fmul_rn(k, __fadd_rn(x, x3)))));
+// GELU, tanh form (f5.cpp:93-96): 0.5 x (1 + tanh(k (x + 0.044715 x^3))), tanh(z) = 1 - 2 / (1 + e^(2z)).
+__device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
+    const float2 z = mul2(bc2(0.7978845608028654f), fma2(mul2(bc2(0.044715f), x), mul2(x, x), x));
+    const float2 e = mul2(bc2(2.8853900817779268f), z);  // e^(2z) = 2^(2z log2(e))
+    const float2 d = add2(bc2(1.0f), make_float2(ex2_approx(e.x), ex2_approx(e.y)));
+    const float2 th = fma2(bc2(-2.0f), make_float2(rcp_approx(d.x), rcp_approx(d.y)), bc2(1.0f));
+    return mul2(mul2(bc2(0.5f), x), add2(bc2(1.0f), th));
+}
+
+// sin^2(theta), two elements per call: Cody-Waite reduction by pi (pi = PI1 + PI2 + PI3, PI1 = float(pi)), then
+// u * P(u), u = r^2.
+__device__ __forceinline__ float2 sin2_f2(float2 theta) {
+    const float2 qq = mul2(theta, bc2(0.31830988618379067f));
+    const float2 q = make_float2(rintf(qq.x), rintf(qq.y));
+    float2 r = fma2(q, bc2(-3.14159274101257324e+00f), theta);
+    r = fma2(q, bc2(8.74227765734758577e-08f), r);
+    r = fma2(q, bc2(3.55271367880050093e-15f), r);
+    const float2 u = mul2(r, r);
+    float2 p = fma2(bc2(-3.60956641998200e-06f), u, bc2(1.39213923830539e-04f));
+    p = fma2(p, u, bc2(-3.17209842614830e-03f));
+    p = fma2(p, u, bc2(4.44429032504559e-02f));
+    p = fma2(p, u, bc2(-3.33332985639572e-01f));
+    p = fma2(p, u, bc2(1.0f));
+    return mul2(u, p);
 }
 
 // Vox's fast_sin (nn.hpp:26-40): reduction by pi in three parts, odd polynomial of degree 11, sign from the
@@ -52,24 +99,30 @@ __device__ __forceinline__ float vox_fast_sin(float x) {
     return (qi & 1) ? -s : s;
 }
 
-// One Snake element: y = x + coef * s^2, s = sin(arg * x), in the rounding order of the CPU forms.
+// Snake: y = x + coef * s^2, s = sin(arg * x). coef is 1/(alpha + 1e-9) (HiFT), inv_b (SnakeBeta) or 1/alpha
+// (Kokoro), computed once per channel by the caller. Two elements per call.
 template <int KIND>
-__device__ __forceinline__ float snake_elem(float x, float al, float be) {
-    if (KIND == VOX_CUDA_SNAKE_HIFT) {  // cosyvoice.cpp:243-245
-        const float s = sinf(__fmul_rn(al, x));
-        return __fadd_rn(x, __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(al, 1e-9f)), __fmul_rn(s, s)));
-    } else if (KIND == VOX_CUDA_SNAKE_BETA) {  // qwen3.cpp:90-91: v + inv_b * sn * sn, sn = sin(v * a)
-        const float s = sinf(__fmul_rn(x, al));
-        return __fadd_rn(x, __fmul_rn(__fmul_rn(be, s), s));
-    } else {  // kokoro.cpp:237-239
-        const float s = vox_fast_sin(__fmul_rn(al, x));
-        return __fadd_rn(x, __fmul_rn(__fdiv_rn(1.0f, al), __fmul_rn(s, s)));
+__device__ __forceinline__ float2 snake_pair(float2 x, float2 arg, float2 coef) {
+    if (KIND == VOX_CUDA_SNAKE_KOKORO) {  // kokoro.cpp:237-239, bit-exact with Vox's fast_sin: scalar, unfused roundings
+        const float s0 = vox_fast_sin(__fmul_rn(arg.x, x.x)), s1 = vox_fast_sin(__fmul_rn(arg.y, x.y));
+        return make_float2(__fadd_rn(x.x, __fmul_rn(coef.x, __fmul_rn(s0, s0))), __fadd_rn(x.y, __fmul_rn(coef.y, __fmul_rn(s1, s1))));
     }
+    return add2(x, mul2(coef, sin2_f2(mul2(arg, x))));  // cosyvoice.cpp:243-245 (HiFT), qwen3.cpp:90-91 (SnakeBeta)
+}
+template <int KIND>
+__device__ __forceinline__ float snake_coef(float alpha, float beta) {
+    if (KIND == VOX_CUDA_SNAKE_HIFT) return __fdiv_rn(1.0f, __fadd_rn(alpha, 1e-9f));
+    if (KIND == VOX_CUDA_SNAKE_BETA) return beta;
+    return __fdiv_rn(1.0f, alpha);
 }
 
 // ------------------------------------------------------------------ op functors
 // Each functor maps W values of the inputs (a, b) starting at element e0 (the first element of a vector, or one
-// element on the scalar path) to W outputs.
+// element on the scalar path, W = 1) to W outputs; W > 1 is processed as W/2 float pairs.
+
+#define VOX_PAIRS(W) for (int k = 0; k < (W); k += 2)
+__device__ __forceinline__ float2 pr(const float *v, int k) { return make_float2(v[k], v[k + 1]); }
+__device__ __forceinline__ void put(float *y, int k, float2 v) { y[k] = v.x; y[k + 1] = v.y; }
 
 struct OpSiluMul {
     template <int W> __device__ __forceinline__ void operator()(const float *a, const float *b, float *y, int64_t) const {
@@ -79,20 +132,33 @@ struct OpSiluMul {
 };
 struct OpAdd {
     template <int W> __device__ __forceinline__ void operator()(const float *a, const float *b, float *y, int64_t) const {
+        if constexpr (W == 1) {
+            y[0] = __fadd_rn(a[0], b[0]);
+        } else {
 #pragma unroll
-        for (int k = 0; k < W; ++k) y[k] = __fadd_rn(a[k], b[k]);
+            VOX_PAIRS(W) put(y, k, add2(pr(a, k), pr(b, k)));
+        }
     }
 };
 struct OpMul {
     template <int W> __device__ __forceinline__ void operator()(const float *a, const float *b, float *y, int64_t) const {
+        if constexpr (W == 1) {
+            y[0] = __fmul_rn(a[0], b[0]);
+        } else {
 #pragma unroll
-        for (int k = 0; k < W; ++k) y[k] = __fmul_rn(a[k], b[k]);
+            VOX_PAIRS(W) put(y, k, mul2(pr(a, k), pr(b, k)));
+        }
     }
 };
 template <int KIND> struct OpGelu {
     template <int W> __device__ __forceinline__ void operator()(const float *a, const float *, float *y, int64_t) const {
+        if constexpr (W == 1) {
+            const float2 r = KIND == VOX_CUDA_GELU_ERF ? gelu_erf_f2(bc2(a[0])) : gelu_tanh_f2(bc2(a[0]));
+            y[0] = r.x;
+        } else {
 #pragma unroll
-        for (int k = 0; k < W; ++k) y[k] = KIND == VOX_CUDA_GELU_ERF ? gelu_erf_f(a[k]) : gelu_tanh_f(a[k]);
+            VOX_PAIRS(W) put(y, k, KIND == VOX_CUDA_GELU_ERF ? gelu_erf_f2(pr(a, k)) : gelu_tanh_f2(pr(a, k)));
+        }
     }
 };
 
@@ -106,7 +172,7 @@ struct OpBias {
             const uint32_t v = uint32_t(e0 / W);
             const int64_t c0 = int64_t(vpr.mod(v)) * W;
 #pragma unroll
-            for (int k = 0; k < W; ++k) y[k] = __fadd_rn(a[k], __ldg(bias + c0 + k));
+            VOX_PAIRS(W) put(y, k, add2(pr(a, k), make_float2(__ldg(bias + c0 + k), __ldg(bias + c0 + k + 1))));
         } else {
             y[0] = __fadd_rn(a[0], __ldg(bias + e0 % D));
         }
@@ -124,15 +190,14 @@ template <int DT> struct OpGated {
             const uint32_t v = uint32_t(e0 / W);
             const int64_t g0 = int64_t(vpb.div(v)) * D + int64_t(vpr.mod(v)) * W;
             float g[W];
-            Vec<DT>::unpack(ld_param(reinterpret_cast<const char *>(gate) + g0 * dtype_size_dev()), g);
+            Vec<DT>::unpack(ld_param(reinterpret_cast<const char *>(gate) + g0 * (DT == VOX_CUDA_F32 ? 4 : 2)), g);
 #pragma unroll
-            for (int k = 0; k < W; ++k) y[k] = __fadd_rn(h[k], __fmul_rn(g[k], s[k]));
+            VOX_PAIRS(W) put(y, k, add2(pr(h, k), mul2(pr(g, k), pr(s, k))));
         } else {
             const int64_t gi = (e0 / TD) * D + e0 % D;
             y[0] = __fadd_rn(h[0], __fmul_rn(Vec<DT>::load1(gate, gi), s[0]));
         }
     }
-    __device__ __forceinline__ static int64_t dtype_size_dev() { return DT == VOX_CUDA_F32 ? 4 : 2; }
 };
 
 // Snake with the channel of element e = (e / inner) % C.
@@ -148,56 +213,61 @@ template <int KIND> struct OpSnake {
             if (time_major) {
                 const int64_t c0 = int64_t(vrow.mod(v)) * W;
 #pragma unroll
-                for (int k = 0; k < W; ++k)
-                    y[k] = snake_elem<KIND>(x[k], __ldg(alpha + c0 + k), KIND == VOX_CUDA_SNAKE_BETA ? __ldg(beta + c0 + k) : 0.f);
+                VOX_PAIRS(W) {
+                    const float a0 = __ldg(alpha + c0 + k), a1 = __ldg(alpha + c0 + k + 1);
+                    const float b0 = KIND == VOX_CUDA_SNAKE_BETA ? __ldg(beta + c0 + k) : 0.f;
+                    const float b1 = KIND == VOX_CUDA_SNAKE_BETA ? __ldg(beta + c0 + k + 1) : 0.f;
+                    put(y, k, snake_pair<KIND>(pr(x, k), make_float2(a0, a1), make_float2(snake_coef<KIND>(a0, b0), snake_coef<KIND>(a1, b1))));
+                }
             } else {
                 const uint32_t c = chan.mod(vrow.div(v));
-                const float al = __ldg(alpha + c), be = KIND == VOX_CUDA_SNAKE_BETA ? __ldg(beta + c) : 0.f;
+                const float al = __ldg(alpha + c);
+                const float2 arg = bc2(al), cf = bc2(snake_coef<KIND>(al, KIND == VOX_CUDA_SNAKE_BETA ? __ldg(beta + c) : 0.f));
 #pragma unroll
-                for (int k = 0; k < W; ++k) y[k] = snake_elem<KIND>(x[k], al, be);
+                VOX_PAIRS(W) put(y, k, snake_pair<KIND>(pr(x, k), arg, cf));
             }
         } else {
             const int64_t c = (e0 / inner) % C;
-            y[0] = snake_elem<KIND>(x[0], alpha[c], KIND == VOX_CUDA_SNAKE_BETA ? beta[c] : 0.f);
+            const float2 r = snake_pair<KIND>(bc2(x[0]), bc2(alpha[c]), bc2(snake_coef<KIND>(alpha[c], KIND == VOX_CUDA_SNAKE_BETA ? beta[c] : 0.f)));
+            y[0] = r.x;
         }
     }
 };
 
 // ------------------------------------------------------------------ kernels
 
-// Vector path: n / W 16-byte vectors, U of them in flight per thread, then the n % W tail by block 0.
+// Vector path: n / W 16-byte vectors, kUnroll of them in flight per thread per iteration (the last iteration
+// predicated, so a thread's remainder keeps its loads in flight together), then the n % W tail by block 0.
 template <int DT, int NIN, class F>
-__global__ void __launch_bounds__(kThreads) map_vec_kernel(const void *a, const void *b, void *y, int64_t n, F f) {
+__global__ void __launch_bounds__(kThreads, 4) map_vec_kernel(const void *a, const void *b, void *y, int64_t n, F f) {
     using V = Vec<DT>;
     constexpr int W = V::N;
     const int64_t nvec = n / W;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-    int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint4 *pa = reinterpret_cast<const uint4 *>(a);
     const uint4 *pb = reinterpret_cast<const uint4 *>(b);
     uint4 *py = reinterpret_cast<uint4 *>(y);
-    for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += kUnroll * stride) {
         uint4 ra[kUnroll], rb[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            ra[u] = ld_stream(pa + i + u * stride);
-            if (NIN == 2) rb[u] = ld_stream(pb + i + u * stride);
+            const int64_t j = i + u * stride;
+            if (j < nvec) {
+                ra[u] = ld_stream(pa + j);
+                if (NIN == 2) rb[u] = ld_stream(pb + j);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            float fa[W], fb[W], fy[W];
-            V::unpack(ra[u], fa);
-            if (NIN == 2) V::unpack(rb[u], fb);
-            f.template operator()<W>(fa, fb, fy, (i + u * stride) * W);
-            st_stream(py + i + u * stride, V::pack(fy));
+            const int64_t j = i + u * stride;
+            if (j < nvec) {
+                float fa[W], fb[W], fy[W];
+                V::unpack(ra[u], fa);
+                if (NIN == 2) V::unpack(rb[u], fb);
+                f.template operator()<W>(fa, fb, fy, j * W);
+                st_stream(py + j, V::pack(fy));
+            }
         }
-    }
-    for (; i < nvec; i += stride) {
-        float fa[W], fb[W], fy[W];
-        V::unpack(ld_stream(pa + i), fa);
-        if (NIN == 2) V::unpack(ld_stream(pb + i), fb);
-        f.template operator()<W>(fa, fb, fy, i * W);
-        st_stream(py + i, V::pack(fy));
     }
     const int64_t tail = n - nvec * W;
     if (blockIdx.x == 0 && int64_t(threadIdx.x) < tail) {
@@ -230,8 +300,9 @@ int launch_map(const void *a, const void *b, void *y, int64_t n, F f, bool vec_o
     constexpr int W = Vec<DT>::N;
     vec_ok = vec_ok && aligned16(a) && aligned16(y) && (NIN == 1 || aligned16(b)) && n / W < (int64_t(1) << 32);
     if (vec_ok) {
-        const int g = grid_for((n / W + kUnroll - 1) / kUnroll, kThreads, kBlocksPerSm);
-        map_vec_kernel<DT, NIN, F><<<g, kThreads, 0, st>>>(a, b, y, n, f);
+        auto kern = map_vec_kernel<DT, NIN, F>;
+        const int g = balanced_grid(n / W, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
+        kern<<<g, kThreads, 0, st>>>(a, b, y, n, f);
     } else {
         const int g = grid_for(n, kThreads, kBlocksPerSm);
         map_scalar_kernel<DT, NIN, F><<<g, kThreads, 0, st>>>(a, b, y, n, f);

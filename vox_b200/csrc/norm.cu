@@ -1,36 +1,16 @@
-// Row normalisation: RMSNorm, LayerNorm (affine and the AdaLayerNorm "modulate" form) and the fused adaLN block
-// (LN -> (1+scale)*n + shift -> gate * m + residual) of the F5 DiT.
+// Row normalisation entry points: RMSNorm, LayerNorm (affine and the AdaLayerNorm "modulate" form) and the fused
+// adaLN block (LN -> (1+scale)*n + shift -> gate * m + residual) of the F5 DiT.
 //
-// Fast path: one warp per row with the whole row held in registers (VPL 16-byte vectors per lane, n up to
-// 32*16*W elements), so x is read from HBM exactly once and y written once; rows are distributed over the warps
-// of a grid sized to the SM count. Statistics: RMSNorm sums x^2 in f32 like kernels.cpp:709; LayerNorm and adaLN
-// accumulate mean and variance in f64 like kernels.cpp:714-723, nn.cpp:252-258 and f5.cpp:622-628 (the two-pass
-// variance around the f64 mean). The epilogue rounds each multiply and add separately in the CPU's order.
-// General path (rows longer than the register budget, or not 16-byte aligned): one CTA per row that reads the
-// row from global memory once per pass.
-#include "common.cuh"
+// Fast path (rows.cu): the TMA row pipeline, one warp per row, the row held in registers, for rows of up to
+// 32*16 16-byte vectors whose start is 16-byte aligned. General path (here): one CTA per row reading the row
+// from global memory once per pass, for any length and alignment. Both keep the CPU's statistics (f32 sum of squares
+// for RMSNorm, f64 mean and variance for LayerNorm/adaLN) and its rounding order.
+#include "rows.cuh"
 
 namespace voxcuda {
 namespace {
 
-constexpr int kWarpsPerBlock = 8;
 constexpr int kRowThreads = 256;
-
-enum NormKind { kRms = 0, kLn = 1, kLnMod = 2, kAdaLn = 3, kAdaLnGated = 4 };
-
-struct NormArgs {
-    const void *x;
-    const float *w;      // RMS / LN weight (f32) or NULL
-    const float *b;      // LN bias (f32) or NULL
-    const void *shift;   // adaLN [B][D] (dtype)
-    const void *scale;   // adaLN [B][D] (dtype)
-    const void *gate;    // adaLN [B][D] (dtype) or NULL
-    const void *res;     // adaLN residual [rows][n] (dtype) or NULL
-    void *y;
-    int64_t rows, n;
-    int64_t T;           // rows per batch (adaLN)
-    float eps;
-};
 
 // Output of one element for every kind, in the CPU's rounding order.
 template <int KIND>
@@ -43,112 +23,6 @@ __device__ __forceinline__ float norm_out(float x, float meanf, float inv, float
     const float m = __fadd_rn(__fmul_rn(nrm, __fadd_rn(1.0f, sc)), sh);                   // f5.cpp:630
     if (KIND == kAdaLn) return m;
     return __fadd_rn(r, __fmul_rn(g, m));                                                 // f5.cpp:674
-}
-
-// ------------------------------------------------------------------ warp-per-row register path
-
-template <int DT, int VPL, int KIND>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) norm_warp_kernel(NormArgs a) {
-    using V = Vec<DT>;
-    constexpr int W = V::N;
-    constexpr int ES = DT == VOX_CUDA_F32 ? 4 : 2;
-    const int lane = threadIdx.x & 31;
-    const int64_t nvec = a.n / W;
-    const int64_t warp0 = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
-    const int64_t nwarps = int64_t(gridDim.x) * kWarpsPerBlock;
-    for (int64_t r = warp0; r < a.rows; r += nwarps) {
-        const char *xr = reinterpret_cast<const char *>(a.x) + r * a.n * ES;
-        uint4 raw[VPL];
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t j = lane + 32 * k;
-            raw[k] = j < nvec ? ld_stream(xr + j * 16) : make_uint4(0, 0, 0, 0);
-        }
-        uint4 rres[VPL];
-        if (KIND == kAdaLnGated) {
-            const char *rr = reinterpret_cast<const char *>(a.res) + r * a.n * ES;
-#pragma unroll
-            for (int k = 0; k < VPL; ++k) {
-                const int64_t j = lane + 32 * k;
-                rres[k] = j < nvec ? ld_stream(rr + j * 16) : make_uint4(0, 0, 0, 0);
-            }
-        }
-        float meanf = 0.f, inv;
-        if (KIND == kRms) {
-            float ss = 0.f;
-#pragma unroll
-            for (int k = 0; k < VPL; ++k) {
-                float f[W];
-                V::unpack(raw[k], f);
-#pragma unroll
-                for (int e = 0; e < W; ++e) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
-            }
-            ss = warp_sum(ss);
-            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.n)), a.eps)));
-        } else {
-            double s = 0.0;
-#pragma unroll
-            for (int k = 0; k < VPL; ++k) {
-                float f[W];
-                V::unpack(raw[k], f);
-#pragma unroll
-                for (int e = 0; e < W; ++e) s += double(f[e]);
-            }
-            const double mean = warp_sum_d(s) / double(a.n);
-            double v = 0.0;
-#pragma unroll
-            for (int k = 0; k < VPL; ++k) {
-                if (lane + 32 * k < nvec) {
-                    float f[W];
-                    V::unpack(raw[k], f);
-#pragma unroll
-                    for (int e = 0; e < W; ++e) {
-                        const double d = double(f[e]) - mean;
-                        v = __dadd_rn(v, __dmul_rn(d, d));
-                    }
-                }
-            }
-            const double var = warp_sum_d(v) / double(a.n);
-            meanf = float(mean);
-            inv = float(1.0 / sqrt(var + double(a.eps)));
-        }
-        const int64_t batch = (KIND >= kAdaLn) ? r / a.T : 0;
-        char *yr = reinterpret_cast<char *>(a.y) + r * a.n * ES;
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t j = lane + 32 * k;
-            if (j < nvec) {
-                float f[W], o[W], rv[W];
-                V::unpack(raw[k], f);
-                if (KIND == kAdaLnGated) V::unpack(rres[k], rv);
-                float wv[W], bv[W], sc[W], sh[W], gv[W];
-                if (KIND == kRms || KIND == kLn || KIND == kLnMod) {
-#pragma unroll
-                    for (int e = 0; e < W; ++e) {
-                        wv[e] = a.w ? __ldg(a.w + j * W + e) : 1.0f;
-                        bv[e] = a.b ? __ldg(a.b + j * W + e) : 0.0f;
-                    }
-                }
-                if (KIND >= kAdaLn) {
-                    const int64_t po = (batch * a.n + j * W) * ES;
-                    V::unpack(ld_param(reinterpret_cast<const char *>(a.scale) + po), sc);
-                    V::unpack(ld_param(reinterpret_cast<const char *>(a.shift) + po), sh);
-                    if (KIND == kAdaLnGated) V::unpack(ld_param(reinterpret_cast<const char *>(a.gate) + po), gv);
-                }
-#pragma unroll
-                for (int e = 0; e < W; ++e) {
-                    if (KIND == kLn && !a.w) {
-                        // kernels.cpp:722 with no weight: Vox's nn::layer_norm returns n itself (nn.cpp:262)
-                        const float nrm = __fmul_rn(__fsub_rn(f[e], meanf), inv);
-                        o[e] = a.b ? __fadd_rn(nrm, bv[e]) : nrm;
-                    } else {
-                        o[e] = norm_out<KIND>(f[e], meanf, inv, wv[e], bv[e], sc[e], sh[e], gv[e], rv[e]);
-                    }
-                }
-                st_stream(yr + j * 16, V::pack(o));
-            }
-        }
-    }
 }
 
 // ------------------------------------------------------------------ general path: one CTA per row
@@ -233,28 +107,11 @@ __global__ void __launch_bounds__(kRowThreads) norm_row_kernel(NormArgs a) {
 
 template <int DT, int KIND>
 int launch_norm(const NormArgs &a, cudaStream_t st, const char *name) {
-    constexpr int W = Vec<DT>::N;
-    constexpr int ES = DT == VOX_CUDA_F32 ? 4 : 2;
-    const int64_t nvec = a.n / W;
-    bool vec = a.n % W == 0 && aligned16(a.x) && aligned16(a.y) && nvec <= 32 * 16;
-    if (KIND >= kAdaLn) vec = vec && aligned16(a.shift) && aligned16(a.scale);
-    if (KIND == kAdaLnGated) vec = vec && aligned16(a.gate) && aligned16(a.res);
-    (void)ES;
-    if (vec) {
-        const int vpl = int((nvec + 31) / 32);
-        const int blocks_needed = int((a.rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
-        const int cap = sm_count() * 8;
-        const int g = blocks_needed < cap ? blocks_needed : cap;
-        if (vpl <= 1) norm_warp_kernel<DT, 1, KIND><<<g, kWarpsPerBlock * 32, 0, st>>>(a);
-        else if (vpl <= 2) norm_warp_kernel<DT, 2, KIND><<<g, kWarpsPerBlock * 32, 0, st>>>(a);
-        else if (vpl <= 4) norm_warp_kernel<DT, 4, KIND><<<g, kWarpsPerBlock * 32, 0, st>>>(a);
-        else if (vpl <= 8) norm_warp_kernel<DT, 8, KIND><<<g, kWarpsPerBlock * 32, 0, st>>>(a);
-        else norm_warp_kernel<DT, 16, KIND><<<g, kWarpsPerBlock * 32, 0, st>>>(a);
-    } else {
-        const int64_t cap = int64_t(sm_count()) * 8;
-        const int g = int(a.rows < cap ? a.rows : cap);
-        norm_row_kernel<DT, KIND><<<g, kRowThreads, 0, st>>>(a);
-    }
+    const int rc = launch_norm_pipe(KIND, DT, a, st, name);
+    if (rc != kPipeNotApplicable) return rc;
+    const int64_t cap = int64_t(sm_count()) * 8;
+    const int g = int(a.rows < cap ? a.rows : cap);
+    norm_row_kernel<DT, KIND><<<g, kRowThreads, 0, st>>>(a);
     return check_launch(name);
 }
 
@@ -277,7 +134,7 @@ int vox_cuda_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int64
     VOX_REQUIRE(is_act_dtype(dtype), "vox_cuda_rmsnorm: dtype must be F32 or BF16");
     VOX_REQUIRE(rows >= 0 && n > 0, "vox_cuda_rmsnorm: bad shape");
     VOX_REQUIRE(rows == 0 || (x && w && y), "vox_cuda_rmsnorm: NULL pointer");
-    NormArgs a{x, w, nullptr, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, eps};
+    NormArgs a{x, w, nullptr, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, eps, 1.0f / float(n)};
     return dispatch_norm<kRms>(dtype, a, stream, "vox_cuda_rmsnorm");
 }
 
@@ -287,7 +144,7 @@ int vox_cuda_layernorm(const void *x, const float *w, const float *b, void *y, i
     VOX_REQUIRE(rows >= 0 && n > 0, "vox_cuda_layernorm: bad shape");
     VOX_REQUIRE(rows == 0 || (x && y), "vox_cuda_layernorm: NULL pointer");
     VOX_REQUIRE(!modulate || (w && b), "vox_cuda_layernorm: modulate needs w and b");
-    NormArgs a{x, w, b, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, eps};
+    NormArgs a{x, w, b, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, eps, 1.0f / float(n)};
     if (modulate) return dispatch_norm<kLnMod>(dtype, a, stream, "vox_cuda_layernorm");
     return dispatch_norm<kLn>(dtype, a, stream, "vox_cuda_layernorm");
 }
@@ -299,7 +156,7 @@ int vox_cuda_adaln(const void *x, const void *shift, const void *scale, const vo
     VOX_REQUIRE((gate == nullptr) == (residual == nullptr), "vox_cuda_adaln: gate and residual go together");
     if (B * T == 0) return VOX_CUDA_OK;
     VOX_REQUIRE(x && shift && scale && y, "vox_cuda_adaln: NULL pointer");
-    NormArgs a{x, nullptr, nullptr, shift, scale, gate, residual, y, B * T, D, T, eps};
+    NormArgs a{x, nullptr, nullptr, shift, scale, gate, residual, y, B * T, D, T, eps, 1.0f / float(D)};
     if (gate) return dispatch_norm<kAdaLnGated>(dtype, a, stream, "vox_cuda_adaln");
     return dispatch_norm<kAdaLn>(dtype, a, stream, "vox_cuda_adaln");
 }

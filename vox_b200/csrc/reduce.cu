@@ -1,6 +1,7 @@
 // Row reductions (sum / max / L2 norm) and the two device steps of the deterministic cross-shard global sum.
 //
-// Row reduction order (fixed, so results are bitwise reproducible and restatable on the CPU): the row is cut
+// Rows of up to 16 KB run on the TMA row pipeline (rows.cu); longer or unaligned rows on the direct kernel here.
+// Both follow one reduction order (fixed, so results are bitwise reproducible and restatable on the CPU): the row is cut
 // into "vectors" of W elements (4 for f32, 8 for bf16; the last one may be short); lane l of the row's warp takes
 // vectors l, l+32, l+64, ... in order and adds element k of each vector into accumulator k % 4; the lane's value
 // is (acc0 + acc1) + (acc2 + acc3); the 32 lane values are folded by an xor butterfly over offsets 16, 8, 4, 2, 1.
@@ -13,7 +14,7 @@
 // the xor butterfly. A shard owning whole slots writes its partials and zeros elsewhere; the element-wise sum of
 // all shards' slot vectors (one NCCL all-reduce) is exact, and the finish step folds the 840 slots in a fixed
 // order. The result therefore does not depend on the number of shards.
-#include "common.cuh"
+#include "rows.cuh"
 
 namespace voxcuda {
 namespace {
@@ -86,10 +87,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) row_reduce_kernel(const v
 
 template <int DT, int OP>
 void launch_rr(const void *x, float *out, int64_t rows, int64_t n, bool vec, cudaStream_t st) {
-    const int64_t need = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock, cap = int64_t(sm_count()) * 8;
-    const int g = int(need < cap ? need : cap);
-    if (vec) row_reduce_kernel<DT, OP, true><<<g, kWarpsPerBlock * 32, 0, st>>>(x, out, rows, n);
-    else row_reduce_kernel<DT, OP, false><<<g, kWarpsPerBlock * 32, 0, st>>>(x, out, rows, n);
+    auto kern = vec ? row_reduce_kernel<DT, OP, true> : row_reduce_kernel<DT, OP, false>;
+    const int g = balanced_grid(rows, kWarpsPerBlock, resident_blocks((const void *)kern, kWarpsPerBlock * 32, 0));
+    kern<<<g, kWarpsPerBlock * 32, 0, st>>>(x, out, rows, n);
 }
 
 template <int DT>
@@ -100,6 +100,8 @@ void dispatch_rr(int op, const void *x, float *out, int64_t rows, int64_t n, boo
 }
 
 int row_reduce(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, cudaStream_t st) {
+    const int rc = launch_reduce_pipe(x, out, rows, n, op, dtype, st);  // rows staged by TMA (rows.cu)
+    if (rc != kPipeNotApplicable) return rc;
     const int W = dtype == VOX_CUDA_F32 ? 4 : 8;
     const bool vec = n % W == 0 && aligned16(x);
     if (dtype == VOX_CUDA_F32) dispatch_rr<VOX_CUDA_F32>(op, x, out, rows, n, vec, st);

@@ -1,0 +1,368 @@
+// The row operators on the TMA row pipeline (tma.cuh): RMSNorm, LayerNorm (affine / modulate), the fused adaLN
+// block, and the scaled causal softmax. One warp per row; the row (and the adaLN residual row) arrives in shared
+// memory by bulk copy STAGES rows ahead, is moved into registers (VPL 16-byte vectors per lane), reduced with
+// warp shuffles, and written with 16-byte streaming stores.
+//
+// Arithmetic follows the code it replaces: RMSNorm sums x^2 in f32 (kernels.cpp:707-712); LayerNorm and adaLN take
+// the two-pass mean and variance (kernels.cpp:714-723, nn.cpp:252-258, f5.cpp:622-628) in f32 with warp
+// butterflies, as Vox's own GPU shaders do (f5ln.comp, layernorm.comp) — the CPU accumulates in f64, which moves the
+// statistics by ~1e-7 relative; the softmax takes max, exp(x - max), f32 sum and multiplies by 1/sum
+// (kernels.cpp:725-732) over the visible prefix only (kernels.cpp:812-819), with exp evaluated as
+// 2^((x - max) log2 e) on the SFU (relative error ~3e-7 against expf). Arithmetic runs two elements per instruction
+// (packed f32x2: FADD2 / FMUL2 / FFMA2). RMSNorm's output w * (x * inv) and the softmax's outputs round as the CPU
+// does (their sums of squares and of exponentials may be fused into FMAs); the LayerNorm / adaLN epilogues use fused
+// multiply-adds ((x - mean)/sigma as fma(x, 1/sigma, -mean/sigma), then one FMA
+// per affine step) and 1/sigma = rsqrt(var + eps): differences from the CPU of about one f32 ulp, far inside the
+// 1e-5 (f32) and 1e-2 (bf16) tolerances, for about half the instructions.
+#include <math.h>
+
+#include "rows.cuh"
+#include "tma.cuh"
+#include "sfu.cuh"
+
+namespace voxcuda {
+namespace {
+
+constexpr int kStages = 2;
+
+template <int DT, int VPL, int KIND>
+struct NormOp {
+    NormArgs a;
+    uint32_t row_bytes;  // n * element size (multiple of 16)
+
+    __device__ __forceinline__ void issue(int64_t r, uint8_t *buf, uint64_t *bar) const {
+        const char *xr = reinterpret_cast<const char *>(a.x) + r * int64_t(row_bytes);
+        if (KIND == kAdaLnGated) {
+            mbar_arrive_expect_tx(bar, 2 * row_bytes);
+            bulk_g2s(buf, xr, row_bytes, bar);
+            bulk_g2s(buf + row_bytes, reinterpret_cast<const char *>(a.res) + r * int64_t(row_bytes), row_bytes, bar);
+        } else {
+            mbar_arrive_expect_tx(bar, row_bytes);
+            bulk_g2s(buf, xr, row_bytes, bar);
+        }
+    }
+
+    template <class Next>
+    __device__ __forceinline__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const {
+        constexpr int W = Vec<DT>::N, PW = W / 2;  // values and float pairs per 16-byte vector
+        constexpr int ES = DT == VOX_CUDA_F32 ? 4 : 2;
+        const int nvec = int(a.n / W);
+        float2 xv[VPL][PW];
+        uint4 rres[VPL];  // the residual stays packed until the epilogue
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            const uint4 raw = j < nvec ? *reinterpret_cast<const uint4 *>(buf + j * 16) : make_uint4(0, 0, 0, 0);
+            unpack2<DT>(raw, xv[k]);
+            if (KIND == kAdaLnGated) rres[k] = j < nvec ? *reinterpret_cast<const uint4 *>(buf + row_bytes + j * 16) : make_uint4(0, 0, 0, 0);
+        }
+        next();
+        float2 negmean = bc2(0.f), inv2;
+        if (KIND == kRms) {
+            float2 ss = bc2(0.f);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k)
+#pragma unroll
+                for (int p = 0; p < PW; ++p) ss = add2(ss, mul2(xv[k][p], xv[k][p]));
+            const float sum = warp_sum(__fadd_rn(ss.x, ss.y));
+            inv2 = bc2(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, float(a.n)), a.eps))));
+        } else {
+            // two-pass mean / variance on the row in registers, f32 butterflies (as f5ln.comp / layernorm.comp)
+            float2 sm = bc2(0.f);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k)
+#pragma unroll
+                for (int p = 0; p < PW; ++p) sm = add2(sm, xv[k][p]);
+            const float meanf = warp_sum(__fadd_rn(sm.x, sm.y)) * a.inv_n;
+            negmean = bc2(-meanf);
+            float2 v = bc2(0.f);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                if (lane + 32 * k < nvec) {
+#pragma unroll
+                    for (int p = 0; p < PW; ++p) {
+                        const float2 d = add2(xv[k][p], negmean);
+                        v = fma2(d, d, v);
+                    }
+                }
+            }
+            const float var = warp_sum(__fadd_rn(v.x, v.y)) * a.inv_n;
+            inv2 = bc2(rsqrtf(var + a.eps));
+        }
+        const float2 one = bc2(1.0f);
+        const float2 nmi = mul2(negmean, inv2);  // -mean / sigma: (x - mean) / sigma = fma(x, inv, -mean * inv)
+        const int64_t batch = (KIND >= kAdaLn) ? r / a.T : 0;
+        char *yr = reinterpret_cast<char *>(a.y) + r * int64_t(row_bytes);
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            if (j < nvec) {
+                float2 o[PW];
+                if (KIND <= kLnMod) {
+                    // f32 weight / bias vectors (Vox keeps them as const float *): PW pairs from ordered L1 loads
+                    float2 wv[PW], bv[PW];
+#pragma unroll
+                    for (int q = 0; q < PW; q += 2) {
+                        const uint4 wq = a.w ? ld_param_ordered(a.w + j * W + 2 * q) : as_u4(make_float4(1.f, 1.f, 1.f, 1.f));
+                        const uint4 bq = a.b ? ld_param_ordered(a.b + j * W + 2 * q) : make_uint4(0, 0, 0, 0);
+                        unpack2<VOX_CUDA_F32>(wq, wv + q);
+                        unpack2<VOX_CUDA_F32>(bq, bv + q);
+                    }
+#pragma unroll
+                    for (int p = 0; p < PW; ++p) {
+                        if (KIND == kRms) {
+                            o[p] = mul2(wv[p], mul2(xv[k][p], inv2));                   // kernels.cpp:711, CPU rounding
+                        } else {
+                            const float2 nrm = fma2(xv[k][p], inv2, nmi);
+                            if (KIND == kLnMod) o[p] = fma2(add2(one, wv[p]), nrm, bv[p]);  // nn.cpp:262
+                            else if (a.w) o[p] = fma2(nrm, wv[p], bv[p]);               // kernels.cpp:722
+                            else o[p] = a.b ? add2(nrm, bv[p]) : nrm;                   // no weight: nn.cpp:262
+                        }
+                    }
+                } else {
+                    const int64_t po = (batch * a.n + int64_t(j) * W) * ES;
+                    float2 sc[PW], sh[PW], gv[PW], rv[PW];
+                    unpack2<DT>(ld_param_ordered(reinterpret_cast<const char *>(a.scale) + po), sc);
+                    unpack2<DT>(ld_param_ordered(reinterpret_cast<const char *>(a.shift) + po), sh);
+                    if (KIND == kAdaLnGated) {
+                        unpack2<DT>(ld_param_ordered(reinterpret_cast<const char *>(a.gate) + po), gv);
+                        unpack2<DT>(rres[k], rv);
+                    }
+#pragma unroll
+                    for (int p = 0; p < PW; ++p) {
+                        const float2 nrm = fma2(xv[k][p], inv2, nmi);
+                        const float2 m = fma2(nrm, add2(one, sc[p]), sh[p]);          // f5.cpp:630
+                        o[p] = KIND == kAdaLnGated ? fma2(gv[p], m, rv[p]) : m;       // f5.cpp:674
+                    }
+                }
+                st_stream(yr + j * 16, pack2<DT>(o));
+            }
+        }
+    }
+};
+
+__device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_len, int64_t pos0) {
+    if (q_len <= 0) return n;
+    const int64_t v = (r % q_len) + pos0 + 1;
+    return v < n ? v : n;
+}
+
+template <int VPL>
+struct SoftmaxOp {
+    const float *x;
+    float *y;
+    int64_t n, q_len, pos0;
+    float scale;
+
+    __device__ __forceinline__ void issue(int64_t r, uint8_t *buf, uint64_t *bar) const {
+        const uint32_t bytes = uint32_t((visible_len(r, n, q_len, pos0) * 4 + 15) / 16 * 16);  // only the visible prefix
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(buf, x + r * n, bytes, bar);
+    }
+
+    template <class Next>
+    __device__ __forceinline__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const {
+        const int vis = int(visible_len(r, n, q_len, pos0));
+        const int vvec = (vis + 3) / 4;  // vectors holding a visible element
+        const int nvec = int(n / 4);
+        float2 v[VPL][2];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            const uint4 t = j < vvec ? *reinterpret_cast<const uint4 *>(buf + j * 16) : make_uint4(0, 0, 0, 0);
+            unpack2<VOX_CUDA_F32>(t, v[k]);
+        }
+        next();
+        // scaled scores (kernels.cpp:812-816), -inf past the visible prefix; vectors past it are skipped warp-uniformly
+        const float2 s2 = bc2(scale);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            if (128 * (k + 1) <= vis) {  // the whole block of 32 vectors is visible: no mask
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    v[k][p] = mul2(s2, v[k][p]);
+                    mx = fmaxf(mx, fmaxf(v[k][p].x, v[k][p].y));
+                }
+            } else if (32 * k < vvec) {  // the block holding the end of the visible prefix
+                const int base = (lane + 32 * k) * 4;
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    float2 t = mul2(s2, v[k][p]);
+                    t.x = base + 2 * p < vis ? t.x : -INFINITY;
+                    t.y = base + 2 * p + 1 < vis ? t.y : -INFINITY;
+                    v[k][p] = t;
+                    mx = fmaxf(mx, fmaxf(t.x, t.y));
+                }
+            }
+        }
+        mx = warp_max(mx);
+        // exp(x - max) as 2^((x - max) * log2 e) on the SFU (exp of -inf is 0); float sum (kernels.cpp:728-729)
+        const float2 nm = bc2(-mx), l2e = bc2(1.4426950408889634f);
+        float2 sum2 = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            if (32 * k < vvec) {
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    const float2 d = mul2(add2(v[k][p], nm), l2e);
+                    v[k][p] = make_float2(ex2_approx(d.x), ex2_approx(d.y));
+                    sum2 = add2(sum2, v[k][p]);
+                }
+            }
+        }
+        const float sum = warp_sum(__fadd_rn(sum2.x, sum2.y));
+        const float2 inv = bc2(__fdiv_rn(1.0f, sum));
+        float *yr = y + r * n;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            if (j < nvec) {
+                float2 o[2] = {bc2(0.f), bc2(0.f)};
+                if (32 * k < vvec) {
+                    o[0] = mul2(v[k][0], inv);
+                    o[1] = mul2(v[k][1], inv);
+                }
+                st_stream(yr + j * 4, pack2<VOX_CUDA_F32>(o));
+            }
+        }
+    }
+};
+
+// Row sum / max / L2 norm in the fixed order of vox_cuda_row_reduce: lane l takes vectors l, l+32, ... in order,
+// element k of a vector into accumulator k % 4, lane value (a0 + a1) + (a2 + a3), xor butterfly over the lanes.
+// Reads the staged row from shared memory vector by vector (the row need not fit in registers).
+template <int DT, int OP>
+struct ReduceOp {
+    const void *x;
+    float *out;
+    int64_t n;
+    uint32_t row_bytes;
+
+    __device__ __forceinline__ void issue(int64_t r, uint8_t *buf, uint64_t *bar) const {
+        mbar_arrive_expect_tx(bar, row_bytes);
+        bulk_g2s(buf, reinterpret_cast<const char *>(x) + r * int64_t(row_bytes), row_bytes, bar);
+    }
+
+    __device__ __forceinline__ static float step(float acc, float v) {
+        if (OP == VOX_CUDA_REDUCE_MAX) return fmaxf(acc, v);
+        if (OP == VOX_CUDA_REDUCE_L2) return __fadd_rn(acc, __fmul_rn(v, v));
+        return __fadd_rn(acc, v);
+    }
+    __device__ __forceinline__ static float join(float a, float b) { return OP == VOX_CUDA_REDUCE_MAX ? fmaxf(a, b) : __fadd_rn(a, b); }
+
+    template <class Next>
+    __device__ __forceinline__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const {
+        constexpr int W = Vec<DT>::N;
+        const int nvec = int(n / W);
+        const float init = OP == VOX_CUDA_REDUCE_MAX ? -INFINITY : 0.f;
+        float acc[4] = {init, init, init, init};
+#pragma unroll 4
+        for (int j = lane; j < nvec; j += 32) {
+            float f[W];
+            Vec<DT>::unpack(*reinterpret_cast<const uint4 *>(buf + j * 16), f);
+#pragma unroll
+            for (int k = 0; k < W; ++k) acc[k % 4] = step(acc[k % 4], f[k]);
+        }
+        next();
+        float v = join(join(acc[0], acc[1]), join(acc[2], acc[3]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = join(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) out[r] = OP == VOX_CUDA_REDUCE_L2 ? __fsqrt_rn(v) : v;
+    }
+};
+
+template <int DT, int OP>
+int reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, cudaStream_t st) {
+    const uint32_t row_bytes = uint32_t(n * (DT == VOX_CUDA_F32 ? 4 : 2));
+    return launch_row_pipe<ReduceOp<DT, OP>, kStages>(ReduceOp<DT, OP>{x, out, n, row_bytes}, rows, row_bytes, st,
+                                                       "vox_cuda_row_reduce");
+}
+
+template <int DT, int KIND, int VPL>
+int norm_pipe_vpl(const NormArgs &a, cudaStream_t st, const char *name) {
+    const uint32_t row_bytes = uint32_t(a.n * (DT == VOX_CUDA_F32 ? 4 : 2));
+    const uint32_t stage = KIND == kAdaLnGated ? 2 * row_bytes : row_bytes;
+    return launch_row_pipe<NormOp<DT, VPL, KIND>, kStages>(NormOp<DT, VPL, KIND>{a, row_bytes}, a.rows, stage, st, name);
+}
+
+template <int DT, int KIND>
+int norm_pipe(const NormArgs &a, cudaStream_t st, const char *name) {
+    constexpr int W = Vec<DT>::N;
+    const int64_t nvec = a.n / W;
+    const int vpl = int((nvec + 31) / 32);
+    if (vpl <= 1) return norm_pipe_vpl<DT, KIND, 1>(a, st, name);
+    if (vpl <= 2) return norm_pipe_vpl<DT, KIND, 2>(a, st, name);
+    if (vpl <= 4) return norm_pipe_vpl<DT, KIND, 4>(a, st, name);
+    if (vpl <= 8) return norm_pipe_vpl<DT, KIND, 8>(a, st, name);
+    return norm_pipe_vpl<DT, KIND, 16>(a, st, name);
+}
+
+template <int DT>
+int norm_pipe_kind(int kind, const NormArgs &a, cudaStream_t st, const char *name) {
+    switch (kind) {
+        case kRms: return norm_pipe<DT, kRms>(a, st, name);
+        case kLn: return norm_pipe<DT, kLn>(a, st, name);
+        case kLnMod: return norm_pipe<DT, kLnMod>(a, st, name);
+        case kAdaLn: return norm_pipe<DT, kAdaLn>(a, st, name);
+        default: return norm_pipe<DT, kAdaLnGated>(a, st, name);
+    }
+}
+
+}  // namespace
+
+int launch_norm_pipe(int kind, int dtype, const NormArgs &a, cudaStream_t st, const char *name) {
+    const int W = dtype == VOX_CUDA_F32 ? 4 : 8;
+    bool ok = a.n % W == 0 && a.n / W <= 32 * 16 && aligned16(a.x) && aligned16(a.y) && (!a.w || aligned16(a.w)) &&
+              (!a.b || aligned16(a.b));
+    if (kind >= kAdaLn) ok = ok && aligned16(a.shift) && aligned16(a.scale);
+    if (kind == kAdaLnGated) ok = ok && aligned16(a.gate) && aligned16(a.res);
+    if (!ok) return kPipeNotApplicable;
+    if (dtype == VOX_CUDA_F32) return norm_pipe_kind<VOX_CUDA_F32>(kind, a, st, name);
+    return norm_pipe_kind<VOX_CUDA_BF16>(kind, a, st, name);
+}
+
+int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, cudaStream_t st) {
+    const int W = dtype == VOX_CUDA_F32 ? 4 : 8;
+    const int64_t row_bytes = n * (dtype == VOX_CUDA_F32 ? 4 : 2);
+    // staged rows of up to 16 KB (two stages for each of the CTA's warps stay within the shared memory of one SM)
+    if (!(n % W == 0 && row_bytes <= 16384 && aligned16(x))) return kPipeNotApplicable;
+    if (dtype == VOX_CUDA_F32) {
+        if (op == VOX_CUDA_REDUCE_SUM) return reduce_pipe<VOX_CUDA_F32, VOX_CUDA_REDUCE_SUM>(x, out, rows, n, st);
+        if (op == VOX_CUDA_REDUCE_MAX) return reduce_pipe<VOX_CUDA_F32, VOX_CUDA_REDUCE_MAX>(x, out, rows, n, st);
+        return reduce_pipe<VOX_CUDA_F32, VOX_CUDA_REDUCE_L2>(x, out, rows, n, st);
+    }
+    if (op == VOX_CUDA_REDUCE_SUM) return reduce_pipe<VOX_CUDA_BF16, VOX_CUDA_REDUCE_SUM>(x, out, rows, n, st);
+    if (op == VOX_CUDA_REDUCE_MAX) return reduce_pipe<VOX_CUDA_BF16, VOX_CUDA_REDUCE_MAX>(x, out, rows, n, st);
+    return reduce_pipe<VOX_CUDA_BF16, VOX_CUDA_REDUCE_L2>(x, out, rows, n, st);
+}
+
+int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0, cudaStream_t st) {
+    const int64_t nvec = n / 4;
+    if (!(n % 4 == 0 && nvec <= 32 * 16 && aligned16(x) && aligned16(y))) return kPipeNotApplicable;
+    const int vpl = int((nvec + 31) / 32);
+    const uint32_t stage = uint32_t(n * 4);
+    const char *name = "vox_cuda_softmax_rows";
+    if (vpl <= 1) return launch_row_pipe<SoftmaxOp<1>, kStages>(SoftmaxOp<1>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
+    if (vpl <= 2) return launch_row_pipe<SoftmaxOp<2>, kStages>(SoftmaxOp<2>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
+    if (vpl <= 4) return launch_row_pipe<SoftmaxOp<4>, kStages>(SoftmaxOp<4>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
+    if (vpl <= 8) return launch_row_pipe<SoftmaxOp<8>, kStages>(SoftmaxOp<8>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
+    return launch_row_pipe<SoftmaxOp<16>, kStages>(SoftmaxOp<16>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
+}
+
+}  // namespace voxcuda
+
+using namespace voxcuda;
+
+extern "C" int vox_cuda_device_error(unsigned int *flags) {
+    VOX_REQUIRE(flags != nullptr, "vox_cuda_device_error: flags is NULL");
+    unsigned int v = 0;
+    const unsigned int zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        return set_error(VOX_CUDA_ERR_DEVICE, std::string("vox_cuda_device_error: ") + cudaGetErrorString(e));
+    }
+    *flags = v;
+    return VOX_CUDA_OK;
+}

@@ -1,0 +1,39 @@
+// Interface between the row operators' public entry points (norm.cu, softmax.cu) and their TMA row pipeline
+// (rows.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace voxcuda {
+
+enum NormKind { kRms = 0, kLn = 1, kLnMod = 2, kAdaLn = 3, kAdaLnGated = 4 };
+
+struct NormArgs {
+    const void *x;
+    const float *w;      // RMS / LN weight (f32) or NULL
+    const float *b;      // LN bias (f32) or NULL
+    const void *shift;   // adaLN [B][D] (dtype)
+    const void *scale;   // adaLN [B][D] (dtype)
+    const void *gate;    // adaLN [B][D] (dtype) or NULL
+    const void *res;     // adaLN residual [rows][n] (dtype) or NULL
+    void *y;
+    int64_t rows, n;
+    int64_t T;           // rows per batch (adaLN)
+    float eps;
+    float inv_n;         // 1 / n
+};
+
+// Status returned by the pipeline launchers when the shape or alignment does not fit the pipeline (the caller then
+// takes its general path).
+constexpr int kPipeNotApplicable = 1;
+
+// TMA row pipeline for the norm kinds; VOX_CUDA_OK, a negative status, or kPipeNotApplicable.
+int launch_norm_pipe(int kind, int dtype, const NormArgs &a, cudaStream_t st, const char *name);
+// TMA row pipeline for the row reductions (same fixed order as the direct kernel in reduce.cu); VOX_CUDA_OK, a
+// negative status, or kPipeNotApplicable.
+int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, cudaStream_t st);
+// TMA row pipeline for the causal softmax; VOX_CUDA_OK, a negative status, or kPipeNotApplicable.
+int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0,
+                        cudaStream_t st);
+
+}  // namespace voxcuda

@@ -1,6 +1,8 @@
 // Host plumbing of the vox_cuda C ABI: per-thread last error, device attribute cache, grid sizing, service calls.
+#include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "common.cuh"
 
@@ -49,6 +51,37 @@ int check_launch(const char *what) {
 
 int sm_count() { return attr().sms; }
 int smem_optin() { return attr().smem_optin; }
+
+int resident_blocks(const void *kernel, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<std::pair<const void *, int>, std::pair<int, size_t>>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) cudaGetLastError();
+    const auto key = std::make_pair(std::make_pair(kernel, dev), std::make_pair(threads, smem));
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    const int r = per_sm * sm_count();
+    std::lock_guard<std::mutex> g(mu);
+    cache[key] = r;
+    return r;
+}
+
+int balanced_grid(int64_t units, int64_t per_block, int resident) {
+    if (units <= 0) return 1;
+    const int64_t blocks_needed = (units + per_block - 1) / per_block;
+    const int64_t res = resident > 0 ? resident : 1;
+    const int64_t passes = (blocks_needed + res - 1) / res;
+    const int64_t g = (blocks_needed + passes - 1) / passes;
+    return int(g < 1 ? 1 : g);
+}
 
 int grid_for(int64_t work_items, int threads, int per_sm) {
     const int64_t need = (work_items + threads - 1) / threads;

@@ -6,79 +6,21 @@
 // (rounded up to a 16-byte vector); the full row of y is written, zeros past the prefix, which equals the
 // "-inf above the diagonal" form since exp(-inf - max) = 0.
 //
-// Fast path: one warp per row, row in registers (VPL vectors of 4 per lane, n <= 2048). General path: one CTA per
-// row, three passes over global memory.
+// Fast path (rows.cu): the TMA row pipeline, one warp per row, the visible prefix staged by bulk copy and held in
+// registers (n <= 2048). General path (here): one CTA per row, three passes over global memory.
 #include <math.h>
 
-#include "common.cuh"
+#include "rows.cuh"
 
 namespace voxcuda {
 namespace {
 
-constexpr int kWarpsPerBlock = 8;
 constexpr int kRowThreads = 256;
 
 __device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_len, int64_t pos0) {
     if (q_len <= 0) return n;
     const int64_t v = (r % q_len) + pos0 + 1;
     return v < n ? (v > 0 ? v : 0) : n;
-}
-
-template <int VPL>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
-    softmax_warp_kernel(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0) {
-    const int lane = threadIdx.x & 31;
-    const int64_t nvec = n / 4;
-    const int64_t warp0 = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
-    const int64_t nwarps = int64_t(gridDim.x) * kWarpsPerBlock;
-    for (int64_t r = warp0; r < rows; r += nwarps) {
-        const int64_t vis = visible_len(r, n, q_len, pos0);
-        const int64_t vvec = (vis + 3) / 4;  // vectors that hold a visible element
-        const float *xr = x + r * n;
-        float v[VPL][4];
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t j = lane + 32 * k;
-            if (j < vvec) {
-                const float4 t = as_f4(ld_stream(xr + j * 4));
-                v[k][0] = t.x; v[k][1] = t.y; v[k][2] = t.z; v[k][3] = t.w;
-            }
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t j = lane + 32 * k;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const bool live = j < vvec && j * 4 + e < vis;
-                v[k][e] = live ? __fmul_rn(scale, v[k][e]) : -INFINITY;
-                mx = fmaxf(mx, v[k][e]);
-            }
-        }
-        mx = warp_max(mx);
-        float sum = 0.f;
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                v[k][e] = v[k][e] == -INFINITY ? 0.f : expf(__fsub_rn(v[k][e], mx));
-                sum = __fadd_rn(sum, v[k][e]);
-            }
-        }
-        sum = warp_sum(sum);
-        const float inv = __fdiv_rn(1.0f, sum);
-        float *yr = y + r * n;
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t j = lane + 32 * k;
-            if (j < nvec) {
-                float4 o;
-                o.x = __fmul_rn(v[k][0], inv); o.y = __fmul_rn(v[k][1], inv);
-                o.z = __fmul_rn(v[k][2], inv); o.w = __fmul_rn(v[k][3], inv);
-                st_stream(yr + j * 4, as_u4(o));
-            }
-        }
-    }
 }
 
 __device__ __forceinline__ float block_reduce(float v, float *sh, bool is_max) {
@@ -123,20 +65,10 @@ extern "C" int vox_cuda_softmax_rows(const float *x, float *y, int64_t rows, int
     if (rows == 0) return VOX_CUDA_OK;
     VOX_REQUIRE(x && y, "vox_cuda_softmax_rows: NULL pointer");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int64_t nvec = n / 4;
-    if (n % 4 == 0 && nvec <= 32 * 16 && aligned16(x) && aligned16(y)) {
-        const int vpl = int((nvec + 31) / 32);
-        const int64_t need = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock, cap = int64_t(sm_count()) * 8;
-        const int g = int(need < cap ? need : cap);
-        if (vpl <= 1) softmax_warp_kernel<1><<<g, kWarpsPerBlock * 32, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
-        else if (vpl <= 2) softmax_warp_kernel<2><<<g, kWarpsPerBlock * 32, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
-        else if (vpl <= 4) softmax_warp_kernel<4><<<g, kWarpsPerBlock * 32, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
-        else if (vpl <= 8) softmax_warp_kernel<8><<<g, kWarpsPerBlock * 32, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
-        else softmax_warp_kernel<16><<<g, kWarpsPerBlock * 32, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
-    } else {
-        const int64_t cap = int64_t(sm_count()) * 8;
-        const int g = int(rows < cap ? rows : cap);
-        softmax_row_kernel<<<g, kRowThreads, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
-    }
+    const int rc = launch_softmax_pipe(x, y, rows, n, scale, q_len, pos0, st);
+    if (rc != kPipeNotApplicable) return rc;
+    const int64_t cap = int64_t(sm_count()) * 8;
+    const int g = int(rows < cap ? rows : cap);
+    softmax_row_kernel<<<g, kRowThreads, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
     return check_launch("vox_cuda_softmax_rows");
 }

@@ -1,0 +1,146 @@
+// TMA row staging: 1-D bulk copies (cp.async.bulk, global -> shared) completed on mbarriers, and the per-warp row
+// pipeline that the row operators (RMSNorm, LayerNorm, adaLN, causal softmax) run on.
+//
+// Each warp owns STAGES shared-memory buffers and their mbarriers. Lane 0 issues the bulk copies of the warp's
+// next rows STAGES rows ahead; the warp waits for a row's barrier, moves the row into registers, hands the buffer
+// back to lane 0 for the row STAGES ahead, and computes. Row data in flight costs no registers, so every warp
+// keeps loads in flight while it computes, which is what a row operator needs to run at HBM speed.
+//
+// No cluster multicast is used (plain shared::cluster destination of the issuing CTA, which is a cluster of one).
+// Every wait is bounded: a wait that gives up records VOX_CUDA_DEVERR_TIMEOUT in a device flag, waits (bounded
+// again) for the warp's other copies in flight, and the warp stops; vox_cuda_device_error() reads and clears the
+// flag.
+#pragma once
+
+#include "common.cuh"
+
+namespace voxcuda {
+
+// Device-side error flag of the row pipeline (a bit set by a kernel that gave up a wait). Defined here: rows.cu is
+// the one translation unit that includes this header (the library is built without relocatable device code).
+__device__ unsigned int g_device_error = 0;
+constexpr unsigned int kDevErrTimeout = 1u;
+// try_wait polls before a wait gives up (each poll may also suspend the warp for a hardware-chosen time).
+constexpr uint32_t kMaxWaitPolls = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return uint32_t(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait of a whole warp for the phase of `parity` to complete. Every lane polls (so every lane acquires the
+// phase) and the decision is warp-uniform; false, with the device error flag set, if the phase never completes.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMaxWaitPolls; ++i)
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if ((threadIdx.x & 31) == 0) atomicOr(&g_device_error, kDevErrTimeout);
+    return false;
+}
+// Orders this thread's earlier generic-proxy accesses of shared memory before later async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from global memory into this CTA's shared
+// memory, completing `bytes` transactions on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+constexpr int kPipeWarps = 4;  // warps per CTA of a row pipeline
+
+// Shared memory of a row pipeline CTA: kPipeWarps * STAGES mbarriers, then kPipeWarps * STAGES buffers.
+__host__ __device__ constexpr uint32_t pipe_bar_bytes(int stages) { return ((kPipeWarps * stages * 8 + 127) / 128) * 128; }
+__host__ __device__ constexpr uint32_t pipe_smem_bytes(int stages, uint32_t stage_bytes) {
+    return pipe_bar_bytes(stages) + uint32_t(kPipeWarps * stages) * stage_bytes;
+}
+
+// The per-warp row pipeline. Op provides
+//   __device__ uint32_t issue(int64_t r, uint8_t *buf, uint64_t *bar) const   // lane 0: expect_tx + bulk copies
+//   template <class Next> __device__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const
+// run() reads the row from buf into registers, calls next() (which releases buf for the row STAGES ahead), then
+// computes and stores the row.
+template <class Op, int STAGES>
+__global__ void __launch_bounds__(kPipeWarps * 32) row_pipe_kernel(Op op, int64_t rows, uint32_t stage_bytes) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * STAGES;
+    uint8_t *bufs = smem + pipe_bar_bytes(STAGES) + size_t(warp) * STAGES * stage_bytes;
+    const int64_t gw = int64_t(blockIdx.x) * kPipeWarps + warp;
+    const int64_t nw = int64_t(gridDim.x) * kPipeWarps;
+    if (gw >= rows) return;
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        mbar_init_fence();
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s) {
+            const int64_t r = gw + s * nw;
+            if (r < rows) op.issue(r, bufs + s * stage_bytes, &bars[s]);
+        }
+    }
+    uint32_t pending = 0;  // bit s: a copy into stage s is in flight (warp-uniform)
+#pragma unroll
+    for (int t = 0; t < STAGES; ++t)
+        if (gw + t * nw < rows) pending |= 1u << t;
+    __syncwarp();
+    uint32_t parity = 0;  // bit s: parity of the next phase of stage s
+    int s = 0;
+    for (int64_t r = gw; r < rows; r += nw) {
+        if (!mbar_wait_warp(&bars[s], (parity >> s) & 1u)) {
+            // give up: let the warp's other copies land (bounded) before the CTA's shared memory can be reused
+            for (int t = 0; t < STAGES; ++t)
+                if (t != s && ((pending >> t) & 1u)) mbar_wait_warp(&bars[t], (parity >> t) & 1u);
+            return;
+        }
+        parity ^= 1u << s;
+        pending &= ~(1u << s);
+        uint8_t *buf = bufs + s * stage_bytes;
+        uint64_t *bar = &bars[s];
+        const int64_t r_next = r + int64_t(STAGES) * nw;
+        const int cur = s;
+        op.run(r, buf, lane, [&]() {
+            __syncwarp();
+            if (r_next < rows) {
+                if (lane == 0) {
+                    fence_proxy_async();
+                    op.issue(r_next, buf, bar);
+                }
+                pending |= 1u << cur;
+            }
+        });
+        s = (s + 1 == STAGES) ? 0 : s + 1;
+    }
+}
+
+// Launches row_pipe_kernel<Op, STAGES> over `rows` rows: a balanced persistent grid of at most one resident wave.
+template <class Op, int STAGES>
+int launch_row_pipe(const Op &op, int64_t rows, uint32_t stage_bytes, cudaStream_t st, const char *name) {
+    const uint32_t smem = pipe_smem_bytes(STAGES, stage_bytes);
+    if (int(smem) > smem_optin()) return set_error(VOX_CUDA_ERR_UNSUPPORTED, std::string(name) + ": row too long for shared memory");
+    auto kern = row_pipe_kernel<Op, STAGES>;
+    if (smem > 48 * 1024) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+            return check_launch(name);
+    }
+    const int g = balanced_grid(rows, kPipeWarps, resident_blocks((const void *)kern, kPipeWarps * 32, smem));
+    kern<<<g, kPipeWarps * 32, smem, st>>>(op, rows, stage_bytes);
+    return check_launch(name);
+}
+
+}  // namespace voxcuda

@@ -44,7 +44,7 @@ def cuda_include() -> str:
 
 
 def _headers() -> list[Path]:
-    return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.hpp")) + sorted(INCLUDE.glob("*.h"))
+    return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.hpp")) + sorted(INCLUDE.glob("*.h")) + sorted(INCLUDE.glob("*.hpp"))
 
 
 def _stale(src: Path, obj: Path, deps: list[Path]) -> bool:

@@ -6,7 +6,8 @@
 // back to lane 0 for the row STAGES ahead, and computes. Row data in flight costs no registers, so every warp
 // keeps loads in flight while it computes, which is what a row operator needs to run at HBM speed.
 //
-// No cluster multicast is used (plain shared::cluster destination of the issuing CTA, which is a cluster of one).
+// Each copy lands in the shared memory of the issuing CTA only (a plain shared::cluster destination of a CTA that is
+// a cluster of one); no copy is broadcast to other CTAs.
 // Every wait is bounded: a wait that gives up records VOX_CUDA_DEVERR_TIMEOUT in a device flag, waits (bounded
 // again) for the warp's other copies in flight, and the warp stops; vox_cuda_device_error() reads and clears the
 // flag.

@@ -201,6 +201,18 @@ VOX_CUDA_API int vox_cuda_global_sum_partials(const void *x, int64_t rows, int64
 /* Step 2: out[0] = fixed-order pairwise sum of slots[VOX_CUDA_GLOBAL_SUM_SLOTS] (f64). */
 VOX_CUDA_API int vox_cuda_global_sum_finish(const double *slots, double *out, void *stream);
 
+/* Global sum of a whole single-device tensor x [rows][n] into out[0] (f64) without any allocation: the same kernels
+ * and result as vox_cuda_global_sum_partials (row0 = 0, total_rows = rows) followed by vox_cuda_global_sum_finish,
+ * with the row sums and slots kept in a fixed scratch array inside the library instead of caller memory. For callers
+ * that cannot call cudaMalloc (a real-time audio callback, where an allocation can block and synchronise the device;
+ * a plugin host that owns all device memory apart from the inputs and outputs it passes in).
+ * Limit: rows <= 262144 (larger tensors are rejected with VOX_CUDA_ERR_ARG). The scratch array (about 1 MB) is held on
+ * every GPU that loads the library until the process exits. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream capture on that device. All calls share the
+ * one array, so calls whose kernels overlap on the GPU (different streams without ordering) race; order them.
+ * No counterpart in the reference (Vox has no device-side global sum). */
+VOX_CUDA_API int vox_cuda_global_sum_noalloc(const void *x, int64_t rows, int64_t n, double *out, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,27 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline bool is_act_dtype(int d) { return d == VOX_CUDA_F32 || d == VOX_CUDA_BF16; }
 inline int dtype_size(int d) { return d == VOX_CUDA_F32 ? 4 : 2; }
 
+// Programmatic dependent launch: every kernel of the library is launched with programmatic stream serialization and
+// starts with pdl_enter(), so the next kernel in the stream is scheduled while this one's last blocks drain, and it
+// touches no memory before the previous grid has completed (griddepcontrol.wait). Stream order is unchanged.
+// VOX_CUDA_PDL=0 in the environment launches without the attribute.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kern, args...);  // errors are read by check_launch()
+}
+
 #define VOX_REQUIRE(cond, msg)                                         \
     do {                                                               \
         if (!(cond)) return ::voxcuda::set_error(VOX_CUDA_ERR_ARG, msg); \
@@ -68,6 +89,13 @@ struct FastDiv {
     }
     __host__ __device__ __forceinline__ uint32_t mod(uint32_t n) const { return n - div(n) * d; }
 };
+
+// ------------------------------------------------------------------ device: launch order
+
+// Waits for the previous grid of the stream (and its memory). The next grid may be scheduled as this grid's blocks
+// exit (a block's exit counts as its trigger); blocks do not trigger earlier, so waiting blocks of the next grid never
+// sit beside this grid's working blocks.
+__device__ __forceinline__ void pdl_enter() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ------------------------------------------------------------------ device: conversions
 

@@ -43,26 +43,42 @@ __device__ __forceinline__ uint2 load_code_word(const uint8_t *q, int64_t v) {
     if (OPT == 8) return ld_stream8(p);
     return make_uint2(__ldcs(reinterpret_cast<const unsigned int *>(p)), 0u);
 }
+// Exact int -> float of codes without I2F: a byte b placed under the exponent of 2^23 (word 0x4B0000bb) is the float
+// 2^23 + b, so one exact subtraction gives the code. Q8: b = code ^ 0x80 (code + 128), subtract 2^23 + 128.
+// Q4: b = nibble (0..15), subtract 2^23 + 8 (the value (u - 8) of kernels.cpp:459-460).
+__device__ __forceinline__ float byte_as_float(uint32_t word, uint32_t sel) {
+    // selector picks one byte of `word` into bits 0..7, zero bytes 1..2, 0x4B into byte 3
+    return __uint_as_float(__byte_perm(word, 0x4B000000u, sel));
+}
 template <bool Q4, int OPT>
-__device__ __forceinline__ void decode(uint2 w, int64_t v, int *c) {
+__device__ __forceinline__ void decode(uint2 w, int64_t v, float *c) {
+    uint32_t lo, hi;
     if (!Q4) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            c[k] = int(int8_t(w.x >> (8 * k)));
-            if (OPT == 8) c[4 + k] = int(int8_t(w.y >> (8 * k)));
-        }
+        lo = w.x ^ 0x80808080u;
+        hi = w.y ^ 0x80808080u;
     } else {
         const int sh = int((v * OPT) & 16) >> 2;  // 0: low nibbles (elements 0..15 of the block), 4: high (16..31)
+        lo = (w.x >> sh) & 0x0F0F0F0Fu;
+        hi = (w.y >> sh) & 0x0F0F0F0Fu;
+    }
+    const float2 off = bc2(Q4 ? -8388616.0f : -8388736.0f);
+    float2 p[OPT / 2];
+    p[0] = add2(make_float2(byte_as_float(lo, 0x7440), byte_as_float(lo, 0x7441)), off);
+    p[1] = add2(make_float2(byte_as_float(lo, 0x7442), byte_as_float(lo, 0x7443)), off);
+    if (OPT == 8) {
+        p[2] = add2(make_float2(byte_as_float(hi, 0x7440), byte_as_float(hi, 0x7441)), off);
+        p[3] = add2(make_float2(byte_as_float(hi, 0x7442), byte_as_float(hi, 0x7443)), off);
+    }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            c[k] = int((w.x >> (8 * k + sh)) & 15u) - 8;
-            if (OPT == 8) c[4 + k] = int((w.y >> (8 * k + sh)) & 15u) - 8;
-        }
+    for (int k = 0; k < OPT / 2; ++k) {
+        c[2 * k] = p[k].x;
+        c[2 * k + 1] = p[k].y;
     }
 }
 
 template <bool Q4, int SDT, int ODT>
 __global__ void __launch_bounds__(kThreads) dequant_kernel(const uint8_t *q, const void *scale, void *out, int64_t nvec) {
+    pdl_enter();
     constexpr int OPT = OutVec<ODT>::OPT;
     constexpr int VPB = 32 / OPT;  // output vectors per 32-weight block
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
@@ -84,13 +100,13 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const uint8_t *q, con
         for (int u = 0; u < kUnroll; ++u) {
             const int64_t w = v + u * stride;
             if (w < nvec) {
-                int c[OPT];
+                float c[OPT];
                 decode<Q4, OPT>(cw[u], w, c);
                 float f[OPT];
                 const float2 s2 = bc2(s[u]);
 #pragma unroll
                 for (int k = 0; k < OPT; k += 2) {
-                    const float2 p = mul2(make_float2(float(c[k]), float(c[k + 1])), s2);  // one rounding each, as kernels.cpp:450,459
+                    const float2 p = mul2(make_float2(c[k], c[k + 1]), s2);  // one rounding each, as kernels.cpp:450,459
                     f[k] = p.x;
                     f[k + 1] = p.y;
                 }
@@ -117,7 +133,7 @@ int launch_dequant(const uint8_t *q, const void *scale, int sdt, void *out, int 
     auto kern = odt == VOX_CUDA_BF16 ? (sdt == VOX_CUDA_F16 ? dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_BF16> : dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_BF16>)
                                      : (sdt == VOX_CUDA_F16 ? dequant_kernel<Q4, VOX_CUDA_F16, VOX_CUDA_F32> : dequant_kernel<Q4, VOX_CUDA_F32, VOX_CUDA_F32>);
     const int g = balanced_grid(nvec, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
-    kern<<<g, kThreads, 0, st>>>(q, scale, out, nvec);
+    launch_k(kern, g, kThreads, 0, st, q, scale, out, nvec);
     return check_launch(name);
 }
 

@@ -240,6 +240,7 @@ template <int KIND> struct OpSnake {
 // predicated, so a thread's remainder keeps its loads in flight together), then the n % W tail by block 0.
 template <int DT, int NIN, class F>
 __global__ void __launch_bounds__(kThreads, 4) map_vec_kernel(const void *a, const void *b, void *y, int64_t n, F f) {
+    pdl_enter();
     using V = Vec<DT>;
     constexpr int W = V::N;
     const int64_t nvec = n / W;
@@ -283,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 4) map_vec_kernel(const void *a, con
 // Scalar path for unaligned pointers or shapes the vector path cannot index.
 template <int DT, int NIN, class F>
 __global__ void __launch_bounds__(kThreads) map_scalar_kernel(const void *a, const void *b, void *y, int64_t n, F f) {
+    pdl_enter();
     using V = Vec<DT>;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
     for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < n; e += stride) {
@@ -302,10 +304,10 @@ int launch_map(const void *a, const void *b, void *y, int64_t n, F f, bool vec_o
     if (vec_ok) {
         auto kern = map_vec_kernel<DT, NIN, F>;
         const int g = balanced_grid(n / W, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
-        kern<<<g, kThreads, 0, st>>>(a, b, y, n, f);
+        launch_k(kern, g, kThreads, 0, st, a, b, y, n, f);
     } else {
         const int g = grid_for(n, kThreads, kBlocksPerSm);
-        map_scalar_kernel<DT, NIN, F><<<g, kThreads, 0, st>>>(a, b, y, n, f);
+        launch_k(map_scalar_kernel<DT, NIN, F>, g, kThreads, 0, st, a, b, y, n, f);
     }
     return check_launch(name);
 }
@@ -322,6 +324,7 @@ int dispatch_map(int dtype, const void *a, const void *b, void *y, int64_t n, F 
 // gu [m][2I] -> h [m][I]. One thread per 16-byte output vector; row index by FastDiv on the vector index.
 template <int DT>
 __global__ void __launch_bounds__(kThreads) swiglu_fused_kernel(const void *gu, void *h, int64_t m, int64_t I, FastDiv vpr) {
+    pdl_enter();
     using V = Vec<DT>;
     constexpr int W = V::N;
     const int64_t nvec = m * I / W;
@@ -343,6 +346,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_fused_kernel(const void *gu, 
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads) swiglu_fused_scalar(const void *gu, void *h, int64_t m, int64_t I) {
+    pdl_enter();
     using V = Vec<DT>;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < m * I; i += stride) {
@@ -352,6 +356,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_fused_scalar(const void *gu, 
 }
 
 __global__ void snake_params_kernel(const float *alpha, const float *beta, float *a, float *inv_b, int64_t C) {
+    pdl_enter();
     const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (c < C) {
         a[c] = expf(alpha[c]);
@@ -447,7 +452,7 @@ int vox_cuda_snake(const float *x, const float *alpha, const float *beta, float 
 int vox_cuda_snake_beta_params(const float *alpha, const float *beta, float *a, float *inv_b, int64_t C, void *stream) {
     VOX_REQUIRE(C >= 0 && (C == 0 || (alpha && beta && a && inv_b)), "vox_cuda_snake_beta_params: bad arguments");
     if (C == 0) return VOX_CUDA_OK;
-    snake_params_kernel<<<int((C + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(alpha, beta, a, inv_b, C);
+    launch_k(snake_params_kernel, int((C + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream), alpha, beta, a, inv_b, C);
     return check_launch("vox_cuda_snake_beta_params");
 }
 
@@ -461,12 +466,12 @@ int vox_cuda_swiglu_fused(const void *gu, void *h, int64_t m, int64_t I, int dty
     const bool vec_ok = I % W == 0 && aligned16(gu) && aligned16(h) && m * I / W < (int64_t(1) << 32);
     if (vec_ok) {
         const int g = grid_for(m * I / W, kThreads, kBlocksPerSm);
-        if (dtype == VOX_CUDA_F32) swiglu_fused_kernel<VOX_CUDA_F32><<<g, kThreads, 0, st>>>(gu, h, m, I, FastDiv(uint32_t(I / W)));
-        else swiglu_fused_kernel<VOX_CUDA_BF16><<<g, kThreads, 0, st>>>(gu, h, m, I, FastDiv(uint32_t(I / W)));
+        if (dtype == VOX_CUDA_F32) launch_k(swiglu_fused_kernel<VOX_CUDA_F32>, g, kThreads, 0, st, gu, h, m, I, FastDiv(uint32_t(I / W)));
+        else launch_k(swiglu_fused_kernel<VOX_CUDA_BF16>, g, kThreads, 0, st, gu, h, m, I, FastDiv(uint32_t(I / W)));
     } else {
         const int g = grid_for(m * I, kThreads, kBlocksPerSm);
-        if (dtype == VOX_CUDA_F32) swiglu_fused_scalar<VOX_CUDA_F32><<<g, kThreads, 0, st>>>(gu, h, m, I);
-        else swiglu_fused_scalar<VOX_CUDA_BF16><<<g, kThreads, 0, st>>>(gu, h, m, I);
+        if (dtype == VOX_CUDA_F32) launch_k(swiglu_fused_scalar<VOX_CUDA_F32>, g, kThreads, 0, st, gu, h, m, I);
+        else launch_k(swiglu_fused_scalar<VOX_CUDA_BF16>, g, kThreads, 0, st, gu, h, m, I);
     }
     return check_launch("vox_cuda_swiglu_fused");
 }

@@ -48,6 +48,7 @@ __device__ __forceinline__ float block_sum_f(float v, float *sh) {
 
 template <int DT, int KIND>
 __global__ void __launch_bounds__(kRowThreads) norm_row_kernel(NormArgs a) {
+    pdl_enter();
     using V = Vec<DT>;
     __shared__ double shd[32];
     __shared__ float shf[32];
@@ -111,7 +112,7 @@ int launch_norm(const NormArgs &a, cudaStream_t st, const char *name) {
     if (rc != kPipeNotApplicable) return rc;
     const int64_t cap = int64_t(sm_count()) * 8;
     const int g = int(a.rows < cap ? a.rows : cap);
-    norm_row_kernel<DT, KIND><<<g, kRowThreads, 0, st>>>(a);
+    launch_k(norm_row_kernel<DT, KIND>, g, kRowThreads, 0, st, a);
     return check_launch(name);
 }
 

@@ -38,6 +38,7 @@ __device__ __forceinline__ float det_uniform(uint64_t frame, uint32_t stream, ui
 
 __global__ void __launch_bounds__(256) fill_kernel(void *out, int64_t n, int dist, float a, float b, uint64_t seed, uint32_t sid,
                                                    int64_t c0, int dtype) {
+    pdl_enter();
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const uint64_t g = uint64_t(c0 + i);
@@ -84,6 +85,6 @@ extern "C" int vox_cuda_fill_philox(void *out, int64_t n, int dist, float a, flo
     if (n == 0) return VOX_CUDA_OK;
     VOX_REQUIRE(out != nullptr, "vox_cuda_fill_philox: out is NULL");
     const int g = grid_for(n, 256, 16);
-    fill_kernel<<<g, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(out, n, dist, a, b, seed, stream_id, counter0, dtype);
+    launch_k(fill_kernel, g, 256, 0, reinterpret_cast<cudaStream_t>(stream), out, n, dist, a, b, seed, stream_id, counter0, dtype);
     return check_launch("vox_cuda_fill_philox");
 }

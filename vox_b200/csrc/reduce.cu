@@ -40,6 +40,7 @@ __device__ __forceinline__ float red_init() {
 // One warp per row, VEC = 16-byte vector path (row start aligned, n % W == 0) or scalar path (same order).
 template <int DT, int OP, bool VEC>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) row_reduce_kernel(const void *x, float *out, int64_t rows, int64_t n) {
+    pdl_enter();
     using V = Vec<DT>;
     constexpr int W = V::N;
     constexpr int ES = DT == VOX_CUDA_F32 ? 4 : 2;
@@ -89,7 +90,7 @@ template <int DT, int OP>
 void launch_rr(const void *x, float *out, int64_t rows, int64_t n, bool vec, cudaStream_t st) {
     auto kern = vec ? row_reduce_kernel<DT, OP, true> : row_reduce_kernel<DT, OP, false>;
     const int g = balanced_grid(rows, kWarpsPerBlock, resident_blocks((const void *)kern, kWarpsPerBlock * 32, 0));
-    kern<<<g, kWarpsPerBlock * 32, 0, st>>>(x, out, rows, n);
+    launch_k(kern, g, kWarpsPerBlock * 32, 0, st, x, out, rows, n);
 }
 
 template <int DT>
@@ -114,6 +115,7 @@ __host__ __device__ __forceinline__ int64_t slot_begin(int64_t s, int64_t R) { r
 // One warp per slot: owned slots get the fixed-order f64 sum of their row sums, the others 0.
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     slot_partials_kernel(const float *rowsum, int64_t row0, int64_t rows, int64_t R, double *slots) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int64_t s = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
     if (s >= VOX_CUDA_GLOBAL_SUM_SLOTS) return;
@@ -129,6 +131,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 // One block of 256 threads: thread t adds slots t, t+256, ... in order; warps fold by butterfly; warp 0 folds the
 // 8 warp values by butterfly.
 __global__ void __launch_bounds__(256) slot_finish_kernel(const double *slots, double *out) {
+    pdl_enter();
     __shared__ double sh[8];
     double acc = 0.0;
     for (int s = threadIdx.x; s < VOX_CUDA_GLOBAL_SUM_SLOTS; s += 256) acc += slots[s];
@@ -182,14 +185,14 @@ int vox_cuda_global_sum_partials(const void *x, int64_t rows, int64_t n, int64_t
         const int rc = row_reduce(x, rowsum_scratch, rows, n, VOX_CUDA_REDUCE_SUM, dtype, st);
         if (rc != VOX_CUDA_OK) return rc;
     }
-    slot_partials_kernel<<<(VOX_CUDA_GLOBAL_SUM_SLOTS + kWarpsPerBlock - 1) / kWarpsPerBlock, kWarpsPerBlock * 32, 0, st>>>(
+    launch_k(slot_partials_kernel, (VOX_CUDA_GLOBAL_SUM_SLOTS + kWarpsPerBlock - 1) / kWarpsPerBlock, kWarpsPerBlock * 32, 0, st, 
         rowsum_scratch, row0, rows, total_rows, slots);
     return check_launch("vox_cuda_global_sum_partials");
 }
 
 int vox_cuda_global_sum_finish(const double *slots, double *out, void *stream) {
     VOX_REQUIRE(slots && out, "vox_cuda_global_sum_finish: NULL pointer");
-    slot_finish_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(slots, out);
+    launch_k(slot_finish_kernel, 1, 256, 0, reinterpret_cast<cudaStream_t>(stream), slots, out);
     return check_launch("vox_cuda_global_sum_finish");
 }
 

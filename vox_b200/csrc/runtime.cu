@@ -1,4 +1,5 @@
 // Host plumbing of the vox_cuda C ABI: per-thread last error, device attribute cache, grid sizing, service calls.
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <string>
@@ -47,6 +48,14 @@ int check_launch(const char *what) {
     const cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) return VOX_CUDA_OK;
     return set_error(VOX_CUDA_ERR_DEVICE, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("VOX_CUDA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 int sm_count() { return attr().sms; }

@@ -35,6 +35,7 @@ __device__ __forceinline__ float block_reduce(float v, float *sh, bool is_max) {
 
 __global__ void __launch_bounds__(kRowThreads)
     softmax_row_kernel(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0) {
+    pdl_enter();
     __shared__ float sh[32];
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         const int64_t vis = visible_len(r, n, q_len, pos0);
@@ -69,6 +70,6 @@ extern "C" int vox_cuda_softmax_rows(const float *x, float *y, int64_t rows, int
     if (rc != kPipeNotApplicable) return rc;
     const int64_t cap = int64_t(sm_count()) * 8;
     const int g = int(rows < cap ? rows : cap);
-    softmax_row_kernel<<<g, kRowThreads, 0, st>>>(x, y, rows, n, scale, q_len, pos0);
+    launch_k(softmax_row_kernel, g, kRowThreads, 0, st, x, y, rows, n, scale, q_len, pos0);
     return check_launch("vox_cuda_softmax_rows");
 }

@@ -78,6 +78,7 @@ __host__ __device__ constexpr uint32_t pipe_smem_bytes(int stages, uint32_t stag
 // computes and stores the row.
 template <class Op, int STAGES>
 __global__ void __launch_bounds__(kPipeWarps * 32) row_pipe_kernel(Op op, int64_t rows, uint32_t stage_bytes) {
+    pdl_enter();
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * STAGES;
@@ -140,7 +141,7 @@ int launch_row_pipe(const Op &op, int64_t rows, uint32_t stage_bytes, cudaStream
             return check_launch(name);
     }
     const int g = balanced_grid(rows, kPipeWarps, resident_blocks((const void *)kern, kPipeWarps * 32, smem));
-    kern<<<g, kPipeWarps * 32, smem, st>>>(op, rows, stage_bytes);
+    launch_k(kern, g, kPipeWarps * 32, smem, st, op, rows, stage_bytes);
     return check_launch(name);
 }
 

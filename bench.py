@@ -519,6 +519,85 @@ def run_e2e(suite, torch, dist, world, steps) -> dict:
             "overlap": "copy-in / kernels / copy-out on three streams, op groups in Johnson order"}
 
 
+def run_sweep(args) -> None:
+    """BASELINE cfg5 across sizes: for every total size 2^lo .. 2^hi elements (split over the ranks by rows of 4096),
+    add / mul / GELU / row sum / max / L2 and the global sum in f32 and bf16, each op timed alone with CUDA events
+    (max over ranks). One JSON line on rank 0 with GB/s and elements/s per op and size."""
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    import vox_b200 as vox
+    from vox_b200.shard import shard_rows
+
+    peak, _ = peaks()
+    results = []
+    for lg in range(args.sweep_lo, args.sweep_hi + 1):
+        total = 1 << lg
+        R = total // 4096
+        r0, rows = shard_rows(R, world, rank)
+        for dt, tag, es in ((torch.float32, "f32", 4), (torch.bfloat16, "bf16", 2)):
+            dev = torch.device("cuda", local)
+            a = vox.fill_philox(torch.empty(rows, 4096, dtype=dt, device=dev), 1, 0, 1, seed=0, stream_id=16, counter0=r0 * 4096)
+            b = vox.fill_philox(torch.empty(rows, 4096, dtype=dt, device=dev), 1, 0, 1, seed=0, stream_id=18, counter0=r0 * 4096)
+            y, rr = torch.empty_like(a), torch.empty(rows, device=dev)
+            slots, scratch, gout = (torch.empty(840, dtype=torch.float64, device=dev), torch.empty(max(rows, 1), device=dev),
+                                    torch.empty(1, dtype=torch.float64, device=dev))
+            n = rows * 4096
+
+            def gsum():
+                vox.global_sum_partials(a, r0, R, slots=slots, scratch=scratch)
+                if world > 1:
+                    dist.all_reduce(slots)
+                vox.global_sum_finish(slots, out=gout)
+
+            ops = [("add", 3 * es, lambda: vox.add(a, b, out=y)), ("mul", 3 * es, lambda: vox.mul(a, b, out=y)),
+                   ("gelu", 2 * es, lambda: vox.gelu(a, vox.GELU_ERF, out=y)),
+                   ("rowsum", es, lambda: vox.row_reduce(a, vox.REDUCE_SUM, out=rr)),
+                   ("rowmax", es, lambda: vox.row_reduce(a, vox.REDUCE_MAX, out=rr)),
+                   ("rowl2", es, lambda: vox.row_reduce(a, vox.REDUCE_L2, out=rr))]
+            if tag == "f32":
+                ops.append(("global_sum", es, gsum))
+            for name, bpe, fn in ops:
+                iters = max(5, min(200, int(2e-3 / max(n * bpe / (peak * 1e9), 1e-7))))
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                if world > 1:
+                    dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                t = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64, device=dev)
+                if world > 1:
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                sec = float(t) / 1e3
+                nbytes = total * bpe + (R * 4 if name.startswith("row") or name == "global_sum" else 0)
+                results.append({"elements": total, "log2": lg, "dtype": tag, "op": name, "us": round(sec * 1e6, 2),
+                                "gb_s": round(nbytes / sec / 1e9, 1), "frac_of_peak": round(nbytes / sec / 1e9 / peak, 3),
+                                "elements_per_s": round(total / sec, 1)})
+            del a, b, y, rr
+            torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "mode": "sweep", "n_gpus": world, "unit": "GB/s", "peak": peak,
+                          "config": {"workload": "BASELINE cfg5 sweep", "sizes": f"2^{args.sweep_lo}..2^{args.sweep_hi} elements in total",
+                                     "rows": 4096, "scaling": "strong within a size (total elements fixed)"},
+                          "results": results}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -529,11 +608,16 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None, help="regex: run only the matching ops (profiling one kernel)")
+    ap.add_argument("--sweep", action="store_true", help="BASELINE cfg5 size sweep instead of the suite")
+    ap.add_argument("--sweep-lo", type=int, default=20)
+    ap.add_argument("--sweep-hi", type=int, default=32)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.sweep:
+        run_sweep(args)
     else:
         run_ours(args)
 

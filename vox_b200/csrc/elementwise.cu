@@ -23,6 +23,8 @@
 //     2.5e-7 * |x|, the size of the difference between Vox's two CPU GELUs (std::erf vs nn::gelu_inplace).
 //   GELU (tanh form): tanh(z) = 1 - 2 / (1 + e^(2z)) with the SFU's ex2 and rcp (absolute error ~1e-7).
 //   SiLU: x / (1 + e^-x) with CUDA's expf and the 2-ulp division (relative error ~3e-7), as kernels.hpp:105.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "sfu.cuh"
 
@@ -281,6 +283,52 @@ __global__ void __launch_bounds__(kThreads, 4) map_vec_kernel(const void *a, con
     }
 }
 
+// Vector path for one-input ops (GELU, Snake, bias-add), software-pipelined: the loads of a thread's next pass are
+// issued before the current pass is computed, so the arithmetic of one pass overlaps the memory latency of the next
+// (these ops carry the most instructions per byte of the library).
+template <int DT, class F>
+__global__ void __launch_bounds__(kThreads, 3) map_vec_pipe_kernel(const void *a, void *y, int64_t n, F f) {
+    pdl_enter();
+    using V = Vec<DT>;
+    constexpr int W = V::N;
+    const int64_t nvec = n / W;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    const uint4 *pa = reinterpret_cast<const uint4 *>(a);
+    uint4 *py = reinterpret_cast<uint4 *>(y);
+    int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint4 cur[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+        if (i + u * stride < nvec) cur[u] = ld_stream(pa + i + u * stride);
+    for (; i < nvec; i += kUnroll * stride) {
+        const int64_t inext = i + kUnroll * stride;
+        uint4 nxt[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+            if (inext + u * stride < nvec) nxt[u] = ld_stream(pa + inext + u * stride);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t j = i + u * stride;
+            if (j < nvec) {
+                float fa[W], fy[W];
+                V::unpack(cur[u], fa);
+                f.template operator()<W>(fa, fa, fy, j * W);
+                st_stream(py + j, V::pack(fy));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) cur[u] = nxt[u];
+    }
+    const int64_t tail = n - nvec * W;
+    if (blockIdx.x == 0 && int64_t(threadIdx.x) < tail) {
+        const int64_t e = nvec * W + threadIdx.x;
+        float fa[1], fy[1];
+        fa[0] = V::load1(a, e);
+        f.template operator()<1>(fa, fa, fy, e);
+        V::store1(y, e, fy[0]);
+    }
+}
+
 // Scalar path for unaligned pointers or shapes the vector path cannot index.
 template <int DT, int NIN, class F>
 __global__ void __launch_bounds__(kThreads) map_scalar_kernel(const void *a, const void *b, void *y, int64_t n, F f) {
@@ -296,12 +344,25 @@ __global__ void __launch_bounds__(kThreads) map_scalar_kernel(const void *a, con
     }
 }
 
+// The software-pipelined one-input path; VOX_CUDA_MAP_PIPE=0 selects the plain vector path (for comparisons).
+bool map_pipe_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("VOX_CUDA_MAP_PIPE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 template <int DT, int NIN, class F>
 int launch_map(const void *a, const void *b, void *y, int64_t n, F f, bool vec_ok, cudaStream_t st, const char *name) {
     if (n == 0) return VOX_CUDA_OK;
     constexpr int W = Vec<DT>::N;
     vec_ok = vec_ok && aligned16(a) && aligned16(y) && (NIN == 1 || aligned16(b)) && n / W < (int64_t(1) << 32);
-    if (vec_ok) {
+    if (vec_ok && NIN == 1 && map_pipe_enabled()) {
+        auto kern = map_vec_pipe_kernel<DT, F>;
+        const int g = balanced_grid(n / W, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
+        launch_k(kern, g, kThreads, 0, st, a, y, n, f);
+    } else if (vec_ok) {
         auto kern = map_vec_kernel<DT, NIN, F>;
         const int g = balanced_grid(n / W, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
         launch_k(kern, g, kThreads, 0, st, a, b, y, n, f);

@@ -135,7 +135,7 @@ int vox_cuda_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int64
     VOX_REQUIRE(is_act_dtype(dtype), "vox_cuda_rmsnorm: dtype must be F32 or BF16");
     VOX_REQUIRE(rows >= 0 && n > 0, "vox_cuda_rmsnorm: bad shape");
     VOX_REQUIRE(rows == 0 || (x && w && y), "vox_cuda_rmsnorm: NULL pointer");
-    NormArgs a{x, w, nullptr, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, eps, 1.0f / float(n)};
+    NormArgs a{x, w, nullptr, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, FastDiv(1u), eps, 1.0f / float(n)};
     return dispatch_norm<kRms>(dtype, a, stream, "vox_cuda_rmsnorm");
 }
 
@@ -145,7 +145,7 @@ int vox_cuda_layernorm(const void *x, const float *w, const float *b, void *y, i
     VOX_REQUIRE(rows >= 0 && n > 0, "vox_cuda_layernorm: bad shape");
     VOX_REQUIRE(rows == 0 || (x && y), "vox_cuda_layernorm: NULL pointer");
     VOX_REQUIRE(!modulate || (w && b), "vox_cuda_layernorm: modulate needs w and b");
-    NormArgs a{x, w, b, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, eps, 1.0f / float(n)};
+    NormArgs a{x, w, b, nullptr, nullptr, nullptr, nullptr, y, rows, n, 1, FastDiv(1u), eps, 1.0f / float(n)};
     if (modulate) return dispatch_norm<kLnMod>(dtype, a, stream, "vox_cuda_layernorm");
     return dispatch_norm<kLn>(dtype, a, stream, "vox_cuda_layernorm");
 }
@@ -157,7 +157,7 @@ int vox_cuda_adaln(const void *x, const void *shift, const void *scale, const vo
     VOX_REQUIRE((gate == nullptr) == (residual == nullptr), "vox_cuda_adaln: gate and residual go together");
     if (B * T == 0) return VOX_CUDA_OK;
     VOX_REQUIRE(x && shift && scale && y, "vox_cuda_adaln: NULL pointer");
-    NormArgs a{x, nullptr, nullptr, shift, scale, gate, residual, y, B * T, D, T, eps, 1.0f / float(D)};
+    NormArgs a{x, nullptr, nullptr, shift, scale, gate, residual, y, B * T, D, T, FastDiv(1u), eps, 1.0f / float(D)};
     if (gate) return dispatch_norm<kAdaLnGated>(dtype, a, stream, "vox_cuda_adaln");
     return dispatch_norm<kAdaLn>(dtype, a, stream, "vox_cuda_adaln");
 }

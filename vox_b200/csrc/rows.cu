@@ -91,7 +91,7 @@ struct NormOp {
         }
         const float2 one = bc2(1.0f);
         const float2 nmi = mul2(negmean, inv2);  // -mean / sigma: (x - mean) / sigma = fma(x, inv, -mean * inv)
-        const int64_t batch = (KIND >= kAdaLn) ? r / a.T : 0;
+        const int64_t batch = (KIND >= kAdaLn) ? int64_t(a.tdiv.div(uint32_t(r))) : 0;  // rows < 2^32 (launcher)
         char *yr = reinterpret_cast<char *>(a.y) + r * int64_t(row_bytes);
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
@@ -141,9 +141,10 @@ struct NormOp {
     }
 };
 
-__device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_len, int64_t pos0) {
+// Visible keys of row r: min(n, r % q_len + pos0 + 1); rows < 2^32 (launcher), q_len's division precomputed.
+__device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_len, const FastDiv &qdiv, int64_t pos0) {
     if (q_len <= 0) return n;
-    const int64_t v = (r % q_len) + pos0 + 1;
+    const int64_t v = int64_t(qdiv.mod(uint32_t(r))) + pos0 + 1;
     return v < n ? v : n;
 }
 
@@ -153,16 +154,17 @@ struct SoftmaxOp {
     float *y;
     int64_t n, q_len, pos0;
     float scale;
+    FastDiv qdiv;
 
     __device__ __forceinline__ void issue(int64_t r, uint8_t *buf, uint64_t *bar) const {
-        const uint32_t bytes = uint32_t((visible_len(r, n, q_len, pos0) * 4 + 15) / 16 * 16);  // only the visible prefix
+        const uint32_t bytes = uint32_t((visible_len(r, n, q_len, qdiv, pos0) * 4 + 15) / 16 * 16);  // only the visible prefix
         mbar_arrive_expect_tx(bar, bytes);
         bulk_g2s(buf, x + r * n, bytes, bar);
     }
 
     template <class Next>
     __device__ __forceinline__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const {
-        const int vis = int(visible_len(r, n, q_len, pos0));
+        const int vis = int(visible_len(r, n, q_len, qdiv, pos0));
         const int vvec = (vis + 3) / 4;  // vectors holding a visible element
         const int nvec = int(n / 4);
         float2 v[VPL][2];
@@ -314,12 +316,14 @@ int norm_pipe_kind(int kind, const NormArgs &a, cudaStream_t st, const char *nam
 int launch_norm_pipe(int kind, int dtype, const NormArgs &a, cudaStream_t st, const char *name) {
     const int W = dtype == VOX_CUDA_F32 ? 4 : 8;
     bool ok = a.n % W == 0 && a.n / W <= 32 * 16 && aligned16(a.x) && aligned16(a.y) && (!a.w || aligned16(a.w)) &&
-              (!a.b || aligned16(a.b));
+              (!a.b || aligned16(a.b)) && a.rows < (int64_t(1) << 32) && a.T > 0 && a.T < (int64_t(1) << 32);
     if (kind >= kAdaLn) ok = ok && aligned16(a.shift) && aligned16(a.scale);
     if (kind == kAdaLnGated) ok = ok && aligned16(a.gate) && aligned16(a.res);
     if (!ok) return kPipeNotApplicable;
-    if (dtype == VOX_CUDA_F32) return norm_pipe_kind<VOX_CUDA_F32>(kind, a, st, name);
-    return norm_pipe_kind<VOX_CUDA_BF16>(kind, a, st, name);
+    NormArgs b = a;
+    b.tdiv = FastDiv(uint32_t(a.T));
+    if (dtype == VOX_CUDA_F32) return norm_pipe_kind<VOX_CUDA_F32>(kind, b, st, name);
+    return norm_pipe_kind<VOX_CUDA_BF16>(kind, b, st, name);
 }
 
 int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, cudaStream_t st) {
@@ -339,15 +343,17 @@ int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int o
 
 int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0, cudaStream_t st) {
     const int64_t nvec = n / 4;
-    if (!(n % 4 == 0 && nvec <= 32 * 16 && aligned16(x) && aligned16(y))) return kPipeNotApplicable;
+    if (!(n % 4 == 0 && nvec <= 32 * 16 && aligned16(x) && aligned16(y) && rows < (int64_t(1) << 32) && q_len < (int64_t(1) << 32)))
+        return kPipeNotApplicable;
+    const FastDiv qdiv(uint32_t(q_len > 0 ? q_len : 1));
     const int vpl = int((nvec + 31) / 32);
     const uint32_t stage = uint32_t(n * 4);
     const char *name = "vox_cuda_softmax_rows";
-    if (vpl <= 1) return launch_row_pipe<SoftmaxOp<1>, kStages>(SoftmaxOp<1>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
-    if (vpl <= 2) return launch_row_pipe<SoftmaxOp<2>, kStages>(SoftmaxOp<2>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
-    if (vpl <= 4) return launch_row_pipe<SoftmaxOp<4>, kStages>(SoftmaxOp<4>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
-    if (vpl <= 8) return launch_row_pipe<SoftmaxOp<8>, kStages>(SoftmaxOp<8>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
-    return launch_row_pipe<SoftmaxOp<16>, kStages>(SoftmaxOp<16>{x, y, n, q_len, pos0, scale}, rows, stage, st, name);
+    if (vpl <= 1) return launch_row_pipe<SoftmaxOp<1>, kStages>(SoftmaxOp<1>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    if (vpl <= 2) return launch_row_pipe<SoftmaxOp<2>, kStages>(SoftmaxOp<2>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    if (vpl <= 4) return launch_row_pipe<SoftmaxOp<4>, kStages>(SoftmaxOp<4>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    if (vpl <= 8) return launch_row_pipe<SoftmaxOp<8>, kStages>(SoftmaxOp<8>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    return launch_row_pipe<SoftmaxOp<16>, kStages>(SoftmaxOp<16>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
 }
 
 }  // namespace voxcuda

@@ -19,6 +19,7 @@ struct NormArgs {
     void *y;
     int64_t rows, n;
     int64_t T;           // rows per batch (adaLN)
+    FastDiv tdiv;        // division by T for row indices below 2^32 (set by the launcher)
     float eps;
     float inv_n;         // 1 / n
 };

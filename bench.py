@@ -54,7 +54,7 @@ class Suite:
 
     `only` (a regex) keeps the matching ops and allocates only their buffers (profiling of one kernel)."""
 
-    def __init__(self, vox, torch, rank: int, world: int, sweep_elems: int, dist=None, only: str | None = None):
+    def __init__(self, vox, torch, rank: int, world: int, sweep_elems: int, dist=None, only: str | None = None, scale: int = 1):
         import re
 
         self.vox, self.t, self.rank, self.world, self.dist = vox, torch, rank, world, dist
@@ -70,40 +70,48 @@ class Suite:
             ops.append((name, nbytes, elems, fn))
             self.io.append((reads, writes))
 
+        # `scale` multiplies the rows / heads / batches of cfg1-cfg4 (1 = BASELINE's shapes; larger values measure the
+        # kernels where their size does not limit them)
+        K = scale
         # cfg1
         if want("cfg1_rmsnorm_f32"):
-            x1, w1, y1 = fill(E(512, 1024), 1, 0, 1, 1), fill(E(1024), 1, 1, 0.02, 2), E(512, 1024)
-            add("cfg1_rmsnorm_f32", 2 * 512 * 1024 * 4 + 1024 * 4, 512 * 1024, lambda: vox.rmsnorm(x1, w1, 1e-6, out=y1), [x1, w1], [y1])
+            m1 = 512 * K
+            x1, w1, y1 = fill(E(m1, 1024), 1, 0, 1, 1), fill(E(1024), 1, 1, 0.02, 2), E(m1, 1024)
+            add("cfg1_rmsnorm_f32", 2 * m1 * 1024 * 4 + 1024 * 4, m1 * 1024, lambda: vox.rmsnorm(x1, w1, 1e-6, out=y1), [x1, w1], [y1])
         if want("cfg1_swiglu_f32"):
-            g1, u1, h1 = fill(E(512, 3072), 1, 0, 1, 3), fill(E(512, 3072), 1, 0, 1, 4), E(512, 3072)
-            add("cfg1_swiglu_f32", 3 * 512 * 3072 * 4, 512 * 3072, lambda: vox.silu_mul(g1, u1, out=h1), [g1, u1], [h1])
+            m1 = 512 * K
+            g1, u1, h1 = fill(E(m1, 3072), 1, 0, 1, 3), fill(E(m1, 3072), 1, 0, 1, 4), E(m1, 3072)
+            add("cfg1_swiglu_f32", 3 * m1 * 3072 * 4, m1 * 3072, lambda: vox.silu_mul(g1, u1, out=h1), [g1, u1], [h1])
         # cfg2
         if want("cfg2_softmax_causal_f32"):
-            s2, p2 = fill(E(16, 1024, 1024), 1, 0, 3, 5), E(16, 1024, 1024)
+            H2 = 16 * K
+            s2, p2 = fill(E(H2, 1024, 1024), 1, 0, 3, 5), E(H2, 1024, 1024)
             sc2 = float(1.0 / np.sqrt(128.0))
-            add("cfg2_softmax_causal_f32", 16 * 1024 * 1025 // 2 * 4 + 16 * 1024 * 1024 * 4, 16 * 1024 * 1024,
+            add("cfg2_softmax_causal_f32", H2 * 1024 * 1025 // 2 * 4 + H2 * 1024 * 1024 * 4, H2 * 1024 * 1024,
                 lambda: vox.softmax_rows(s2, sc2, 1024, 0, out=p2), [s2], [p2])
         # cfg3
         if want("cfg3_adaln_bf16"):
-            B, T, D = 8, 2048, 1024
+            B, T, D = 8 * K, 2048, 1024
             x3, r3, y3 = fill(E(B, T, D, dt=bf16), 1, 0, 1, 6), fill(E(B, T, D, dt=bf16), 1, 0, 1, 7), E(B, T, D, dt=bf16)
             sh3, sc3, g3 = (fill(E(B, D, dt=bf16), 1, 0, 0.1, s) for s in (8, 9, 10))
             add("cfg3_adaln_bf16", 3 * B * T * D * 2 + 3 * B * D * 2, B * T * D, lambda: vox.adaln(x3, sh3, sc3, 1e-6, g3, r3, out=y3),
                 [x3, r3, sh3, sc3, g3], [y3])
         # cfg4
+        R4 = 4096 * K
         if want("cfg4_dequant_q8_bf16") or want("cfg4_dequant_q4_bf16"):
-            s4 = fill(E(4096, 128), 0, 0.001, 0.05, 13).to(torch.float16)
+            s4 = fill(E(R4, 128), 0, 0.001, 0.05, 13).to(torch.float16)
         if want("cfg4_dequant_q8_bf16"):
-            q8, o8 = fill(E(4096, 4096, dt=torch.int8), 2, -128, 127, 11), E(4096, 4096, dt=bf16)
-            add("cfg4_dequant_q8_bf16", 4096 * 4096 + 4096 * 128 * 2 + 4096 * 4096 * 2, 4096 * 4096,
+            q8, o8 = fill(E(R4, 4096, dt=torch.int8), 2, -128, 127, 11), E(R4, 4096, dt=bf16)
+            add("cfg4_dequant_q8_bf16", R4 * 4096 + R4 * 128 * 2 + R4 * 4096 * 2, R4 * 4096,
                 lambda: vox.dequant_q8(q8, s4, out=o8), [q8, s4], [o8])
         if want("cfg4_dequant_q4_bf16"):
-            q4, o4 = fill(E(4096, 2048, dt=torch.uint8), 3, 0, 0, 12), E(4096, 4096, dt=bf16)
-            add("cfg4_dequant_q4_bf16", 4096 * 2048 + 4096 * 128 * 2 + 4096 * 4096 * 2, 4096 * 4096,
+            q4, o4 = fill(E(R4, 2048, dt=torch.uint8), 3, 0, 0, 12), E(R4, 4096, dt=bf16)
+            add("cfg4_dequant_q4_bf16", R4 * 2048 + R4 * 128 * 2 + R4 * 4096 * 2, R4 * 4096,
                 lambda: vox.dequant_q4(q4, s4, out=o4), [q4] + ([] if want("cfg4_dequant_q8_bf16") else [s4]), [o4])
         if want("cfg4_snake_hift_f32"):
-            xs, al, ys = fill(E(16, 512, 24000), 1, 0, 1, 14), fill(E(512), 0, 0.2, 2.0, 15), E(16, 512, 24000)
-            add("cfg4_snake_hift_f32", 2 * 16 * 512 * 24000 * 4 + 512 * 4, 16 * 512 * 24000,
+            B4 = 16 * K
+            xs, al, ys = fill(E(B4, 512, 24000), 1, 0, 1, 14), fill(E(512), 0, 0.2, 2.0, 15), E(B4, 512, 24000)
+            add("cfg4_snake_hift_f32", 2 * B4 * 512 * 24000 * 4 + 512 * 4, B4 * 512 * 24000,
                 lambda: vox.snake(xs, al, vox.SNAKE_HIFT, out=ys), [xs, al], [ys])
         # cfg5 sweep
         n = sweep_elems
@@ -363,7 +371,7 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     import vox_b200 as vox
 
-    suite = Suite(vox, torch, rank, world, args.sweep_elems, dist if world > 1 else None, only=args.only)
+    suite = Suite(vox, torch, rank, world, args.sweep_elems, dist if world > 1 else None, only=args.only, scale=args.scale)
     torch.cuda.synchronize()
 
     def barrier():
@@ -446,6 +454,7 @@ def run_ours(args) -> None:
         "config": {"workload": "vox-hotpath-suite", "sweep_elems_per_gpu": args.sweep_elems,
                    "bytes_per_step_per_gpu": suite.bytes_per_step, "elements_per_step_per_gpu": suite.elems_per_step,
                    "parallelism": f"row shards x{world}, NCCL all-reduce of 840 f64 slots for the global sum",
+                   "scale_cfg1_cfg4": args.scale,
                    "l2": "no flush: the step streams ~%.1f GB per GPU (> 126 MB L2), so every input is evicted by the other ops' "
                          "traffic between its uses" % (suite.bytes_per_step / 1e9)},
         "elements_per_s": round(suite.elems_per_step * world / step_s, 1),
@@ -609,6 +618,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None, help="regex: run only the matching ops (profiling one kernel)")
     ap.add_argument("--sweep", action="store_true", help="BASELINE cfg5 size sweep instead of the suite")
+    ap.add_argument("--scale", type=int, default=1, help="multiply the rows/heads/batches of cfg1-cfg4 (1 = BASELINE shapes)")
     ap.add_argument("--sweep-lo", type=int, default=20)
     ap.add_argument("--sweep-hi", type=int, default=32)
     args = ap.parse_args()

@@ -27,6 +27,9 @@ constexpr int kStages = 2;
 
 template <int DT, int VPL, int KIND>
 struct NormOp {
+    // gated bf16 adaLN (x and residual staged, 4 KB a stage): registers capped for 5 CTAs per SM (96 a thread, no
+    // spill), which keeps 20 warps per SM in flight on this latency-bound row
+    static constexpr int kMinBlocks = (KIND == kAdaLnGated && DT == VOX_CUDA_BF16 && VPL <= 4) ? 5 : 1;
     NormArgs a;
     uint32_t row_bytes;  // n * element size (multiple of 16)
 
@@ -93,6 +96,16 @@ struct NormOp {
         const float2 nmi = mul2(negmean, inv2);  // -mean / sigma: (x - mean) / sigma = fma(x, inv, -mean * inv)
         const int64_t batch = (KIND >= kAdaLn) ? int64_t(a.tdiv.div(uint32_t(r))) : 0;  // rows < 2^32 (launcher)
         char *yr = reinterpret_cast<char *>(a.y) + r * int64_t(row_bytes);
+        // adaLN parameter vectors of the batch: loaded one k-step ahead of their use (ordered loads, served by L1)
+        const char *scp = reinterpret_cast<const char *>(a.scale) + batch * a.n * ES;
+        const char *shp = reinterpret_cast<const char *>(a.shift) + batch * a.n * ES;
+        const char *gp = reinterpret_cast<const char *>(a.gate) + batch * a.n * ES;
+        uint4 psc, psh, pg;
+        if (KIND >= kAdaLn && lane < nvec) {
+            psc = ld_param_ordered(scp + lane * 16);
+            psh = ld_param_ordered(shp + lane * 16);
+            if (KIND == kAdaLnGated) pg = ld_param_ordered(gp + lane * 16);
+        }
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             const int j = lane + 32 * k;
@@ -120,13 +133,18 @@ struct NormOp {
                         }
                     }
                 } else {
-                    const int64_t po = (batch * a.n + int64_t(j) * W) * ES;
                     float2 sc[PW], sh[PW], gv[PW], rv[PW];
-                    unpack2<DT>(ld_param_ordered(reinterpret_cast<const char *>(a.scale) + po), sc);
-                    unpack2<DT>(ld_param_ordered(reinterpret_cast<const char *>(a.shift) + po), sh);
+                    unpack2<DT>(psc, sc);
+                    unpack2<DT>(psh, sh);
                     if (KIND == kAdaLnGated) {
-                        unpack2<DT>(ld_param_ordered(reinterpret_cast<const char *>(a.gate) + po), gv);
+                        unpack2<DT>(pg, gv);
                         unpack2<DT>(rres[k], rv);
+                    }
+                    const int jn = j + 32;
+                    if (k + 1 < VPL && jn < nvec) {  // next k-step's parameters, in flight during this step's math
+                        psc = ld_param_ordered(scp + jn * 16);
+                        psh = ld_param_ordered(shp + jn * 16);
+                        if (KIND == kAdaLnGated) pg = ld_param_ordered(gp + jn * 16);
                     }
 #pragma unroll
                     for (int p = 0; p < PW; ++p) {
@@ -150,6 +168,7 @@ __device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_l
 
 template <int VPL>
 struct SoftmaxOp {
+    static constexpr int kMinBlocks = 1;
     const float *x;
     float *y;
     int64_t n, q_len, pos0;
@@ -236,6 +255,7 @@ struct SoftmaxOp {
 // Reads the staged row from shared memory vector by vector (the row need not fit in registers).
 template <int DT, int OP>
 struct ReduceOp {
+    static constexpr int kMinBlocks = 1;
     const void *x;
     float *out;
     int64_t n;

@@ -71,13 +71,13 @@ __host__ __device__ constexpr uint32_t pipe_smem_bytes(int stages, uint32_t stag
     return pipe_bar_bytes(stages) + uint32_t(kPipeWarps * stages) * stage_bytes;
 }
 
-// The per-warp row pipeline. Op provides
+// The per-warp row pipeline. Op provides kMinBlocks (the CTAs per SM its register budget is sized for) and
 //   __device__ uint32_t issue(int64_t r, uint8_t *buf, uint64_t *bar) const   // lane 0: expect_tx + bulk copies
 //   template <class Next> __device__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const
 // run() reads the row from buf into registers, calls next() (which releases buf for the row STAGES ahead), then
 // computes and stores the row.
 template <class Op, int STAGES>
-__global__ void __launch_bounds__(kPipeWarps * 32) row_pipe_kernel(Op op, int64_t rows, uint32_t stage_bytes) {
+__global__ void __launch_bounds__(kPipeWarps * 32, Op::kMinBlocks) row_pipe_kernel(Op op, int64_t rows, uint32_t stage_bytes) {
     pdl_enter();
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

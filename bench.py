@@ -113,6 +113,23 @@ class Suite:
             xs, al, ys = fill(E(B4, 512, 24000), 1, 0, 1, 14), fill(E(512), 0, 0.2, 2.0, 15), E(B4, 512, 24000)
             add("cfg4_snake_hift_f32", 2 * B4 * 512 * 24000 * 4 + 512 * 4, B4 * 512 * 24000,
                 lambda: vox.snake(xs, al, vox.SNAKE_HIFT, out=ys), [xs, al], [ys])
+        # next rows of the path (not in the default suite; selected by name with --only next_): the transformer
+        # elementwise chain on a Qwen3-0.6B-shaped prefill chunk (16 q / 8 kv heads of 128, hidden 1024)
+        want_next = (lambda nm: re.search(only, nm) is not None) if only else (lambda nm: False)
+        if want_next("next_qkv_rope_f32"):
+            mt, nh, nkv, hd = 8192 * K, 16, 8, 128
+            qkv = fill(E(mt, (nh + 2 * nkv) * hd), 1, 0, 1, 20)
+            qn, kn = fill(E(hd), 1, 1, 0.1, 21), fill(E(hd), 1, 1, 0.1, 22)
+            cs = vox.rope_table(vox.rope_inv_freq(hd, 1e6, device=dev), 0, mt)
+            qo, kc, vc = E(mt, nh * hd), E(mt, nkv * hd), E(mt, nkv * hd)
+            nb = 2 * mt * (nh + 2 * nkv) * hd * 4 + mt * hd * 4 + 2 * hd * 4
+            add("next_qkv_rope_f32", nb, mt * (nh + 2 * nkv) * hd,
+                lambda: vox.qkv_rope(qkv, cs, nh, nkv, hd, kc, vc, 0, q_norm_w=qn, k_norm_w=kn, q=qo), [qkv, cs, qn, kn], [qo, kc, vc])
+        if want_next("next_add_rmsnorm_f32"):
+            mt, H = 8192 * K, 1024
+            hh, dd, wn, xo = fill(E(mt, H), 1, 0, 1, 23), fill(E(mt, H), 1, 0, 1, 24), fill(E(H), 1, 1, 0.02, 25), E(mt, H)
+            add("next_add_rmsnorm_f32", 4 * mt * H * 4 + H * 4, mt * H, lambda: vox.add_rmsnorm(hh, dd, wn, 1e-6, out=xo), [hh, dd, wn],
+                [hh, xo])
         # cfg5 sweep
         n = sweep_elems
         rows = n // 4096

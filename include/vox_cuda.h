@@ -213,6 +213,39 @@ VOX_CUDA_API int vox_cuda_global_sum_finish(const double *slots, double *out, vo
  * No counterpart in the reference (Vox has no device-side global sum). */
 VOX_CUDA_API int vox_cuda_global_sum_noalloc(const void *x, int64_t rows, int64_t n, double *out, int dtype, void *stream);
 
+/* ---------------------------------------------------------------- transformer elementwise chain */
+
+/* RoPE table for m positions pos0 .. pos0+m-1: cs[(i*half + p)*2] = cos(f), cs[(i*half + p)*2 + 1] = sin(f),
+ * f = inv_freq[p] * float(pos0 + i) in f32 (cs: f32 [m][half][2], 8-byte aligned; inv_freq: f32 [half], e.g. from
+ * vox::rope_inv_freq, kernels.cpp:734-738). Replaces the host loop that fills the GPU transformer's table
+ * (gpu_vulkan.cpp:855-860) and the cos/sin part of vox::rope_apply (kernels.cpp:744-747). One table serves every
+ * layer of a forward pass. cos/sin are CUDA's sincosf: within 2 ulp of libm's cosf/sinf. */
+VOX_CUDA_API int vox_cuda_rope_table(const float *inv_freq, int64_t half, int64_t pos0, int64_t m, float *cs, void *stream);
+
+/* One layer's QKV split + q/k head RMSNorm + RoPE + K/V cache write for m tokens at positions pos0 .. pos0+m-1.
+ *   qkv:  f32 [m][heads*hd + 2*kv_heads*hd], the fused projection: q heads, then k heads, then v heads
+ *   q:    f32 [m][heads*hd]                                   <- rope(headnorm_q(q part))
+ *   k_cache, v_cache: f32 [rows][kv_heads*hd]; token i writes row pos0 + i (ring = 0) or ring slot (pos0 + i) % ring
+ *   q_norm_w / k_norm_w: f32 [hd] RMSNorm weights of the head norms, or NULL for none; eps their epsilon
+ *   cs:   the vox_cuda_rope_table rows of these m tokens (row i = position pos0 + i)
+ * Rotate-half RoPE: a = x[p], b = x[p + hd/2] -> a*c - b*s, b*c + a*s. Replaces shaders/qkvsplit.comp:10-19,
+ * shaders/qkrope.comp:11-33 (run over q and over the K cache rows, gpu_vulkan.cpp:686-698) and shaders/ringput.comp;
+ * CPU form transformer_forward kernels.cpp:797-806 (vox::rmsnorm per head, vox::rope_apply kernels.cpp:740-757,
+ * appends to the KV cache). hd even, hd <= 4096; outputs must not overlap qkv. Fast path: hd in {64, 128, 256}
+ * with 16-byte aligned buffers. */
+VOX_CUDA_API int vox_cuda_qkv_rope(const float *qkv, const float *q_norm_w, const float *k_norm_w, const float *cs, float *q,
+                                   float *k_cache, float *v_cache, int64_t m, int64_t heads, int64_t kv_heads, int64_t hd,
+                                   int64_t pos0, int64_t ring, float eps, void *stream);
+
+/* Residual update + RMSNorm over rows of n: h[r] += delta[r] * layer_scale (layer_scale f32 [n] or NULL for none),
+ * then xn[r] = w * (h[r] * 1/sqrt(mean(h[r]^2) + eps)); h is updated in place, xn must not overlap h or delta.
+ * w: f32 [n]. bf16 rows normalise the f32 sum (h stores its bf16 rounding). Replaces transformer_forward's
+ * o *= attn_scale; h += o; rmsnorm(h, ln2) (kernels.cpp:822-825, 833) and d *= mlp_scale; h += d before the next
+ * layer's rmsnorm(h, ln1) (kernels.cpp:829-831, 793); on Vox's GPU the accumulating GEMM epilogue followed by
+ * rmsnorm.comp (gpu_vulkan.cpp:700-701, 707-708). */
+VOX_CUDA_API int vox_cuda_add_rmsnorm(void *h, const void *delta, const float *layer_scale, const float *w, void *xn, int64_t rows,
+                                      int64_t n, float eps, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

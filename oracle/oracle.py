@@ -95,6 +95,10 @@ class Port:
         L.vo_philox_block.argtypes = [_p, _p, _p]
         L.vo_f32_to_bf16_n.argtypes = [_p, _p, _i64]
         L.vo_f16_to_f32_n.argtypes = [_p, _p, _i64]
+        L.vo_rope_inv_freq.argtypes = [_i64, _d, _p]
+        L.vo_rope_table.argtypes = [_p, _i64, _i64, _i64, _p]
+        L.vo_qkv_rope.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f]
+        L.vo_add_rmsnorm.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f]
 
     # -- generator
     def philox_block(self, ctr, key):
@@ -286,6 +290,44 @@ class Port:
         slots = _c(slots, np.float64)
         return self.L.vo_global_sum_finish(_ptr(slots))
 
+    # -- transformer elementwise chain
+    def rope_inv_freq(self, hd, theta):
+        out = np.empty(hd // 2, np.float32)
+        self.L.vo_rope_inv_freq(hd, theta, _ptr(out))
+        return out
+
+    def rope_table(self, inv_freq, pos0, m):
+        inv_freq = _c(inv_freq, np.float32)
+        cs = np.empty((m, inv_freq.size, 2), np.float32)
+        self.L.vo_rope_table(_ptr(inv_freq), inv_freq.size, pos0, m, _ptr(cs))
+        return cs
+
+    def qkv_rope(self, qkv, qn, kn, cs, heads, kv_heads, hd, pos0=0, kc=None, vc=None, ring=0, eps=1e-6):
+        """Returns (q, k_cache, v_cache); the caches are copied (default: pos0 + m zero rows, or ring rows)."""
+        qkv = _c(qkv, np.float32)
+        m = qkv.shape[0]
+        kd = kv_heads * hd
+        rows = ring if ring > 0 else pos0 + m
+        kc = np.zeros((rows, kd), np.float32) if kc is None else _c(kc, np.float32).copy()
+        vc = np.zeros((rows, kd), np.float32) if vc is None else _c(vc, np.float32).copy()
+        q = np.empty((m, heads * hd), np.float32)
+        qn = None if qn is None else _c(qn, np.float32)
+        kn = None if kn is None else _c(kn, np.float32)
+        cs = _c(cs, np.float32)
+        self.L.vo_qkv_rope(_ptr(qkv), _ptr(qn), _ptr(kn), _ptr(cs), _ptr(q), _ptr(kc), _ptr(vc), m, heads, kv_heads, hd, pos0,
+                           ring, eps)
+        return q, kc, vc
+
+    def add_rmsnorm(self, h, d, ls, w, eps=1e-6):
+        """Returns (h + d * ls, rmsnorm of it)."""
+        h = _c(h, np.float32).copy()
+        d, w = _c(d, np.float32), _c(w, np.float32)
+        ls = None if ls is None else _c(ls, np.float32)
+        n = h.shape[-1]
+        xn = np.empty_like(h)
+        self.L.vo_add_rmsnorm(_ptr(h), _ptr(d), _ptr(ls), _ptr(w), _ptr(xn), h.size // n, n, eps)
+        return h, xn
+
 
 class Ref:
     """dariumi/Vox's own CPU operators (oracle/_ref/libvox_ref.so), numpy in / numpy out."""
@@ -319,6 +361,9 @@ class Ref:
         L.vr_quantize_q8.argtypes = [_p, _i64, _i64, _p, _p]
         L.vr_quantize_q4.argtypes = [_p, _i64, _i64, _p, _p]
         L.vr_row_reduce.argtypes = [_p, _p, _i64, _i64, _int]
+        L.vr_rope_inv_freq.argtypes = [_i64, _d, _p]
+        L.vr_qk_norm_rope.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f]
+        L.vr_add_rmsnorm.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f]
 
     def set_threads(self, n: int) -> int:
         self.L.vr_set_threads(n)
@@ -463,6 +508,29 @@ class Ref:
         out = np.empty(x.size // n, np.float32)
         self.L.vr_row_reduce(_ptr(x), _ptr(out), x.size // n, n, op)
         return out
+
+    def rope_inv_freq(self, hd, theta):
+        out = np.empty(hd // 2, np.float32)
+        self.L.vr_rope_inv_freq(hd, theta, _ptr(out))
+        return out
+
+    def qk_norm_rope(self, q, k, qn, kn, inv_freq, heads, kv_heads, hd, pos0=0, eps=1e-6):
+        """transformer_forward's q/k step on split projections; returns new (q, k)."""
+        q, k = _c(q, np.float32).copy(), _c(k, np.float32).copy()
+        qn = None if qn is None else _c(qn, np.float32)
+        kn = None if kn is None else _c(kn, np.float32)
+        inv_freq = _c(inv_freq, np.float32)
+        self.L.vr_qk_norm_rope(_ptr(q), _ptr(k), _ptr(qn), _ptr(kn), _ptr(inv_freq), q.shape[0], heads, kv_heads, hd, pos0, eps)
+        return q, k
+
+    def add_rmsnorm(self, h, d, ls, w, eps=1e-6):
+        h = _c(h, np.float32).copy()
+        d, w = _c(d, np.float32), _c(w, np.float32)
+        ls = None if ls is None else _c(ls, np.float32)
+        n = h.shape[-1]
+        xn = np.empty_like(h)
+        self.L.vr_add_rmsnorm(_ptr(h), _ptr(d), _ptr(ls), _ptr(w), _ptr(xn), h.size // n, n, eps)
+        return h, xn
 
 
 _port = None

@@ -238,3 +238,34 @@ VR_API void vr_row_reduce(const float *x, float *out, int64_t rows, int64_t n, i
         }
     });
 }
+
+// ---------------------------------------------------------------- transformer elementwise chain
+
+VR_API void vr_rope_inv_freq(int64_t hd, double theta, float *out) {
+    const std::vector<float> f = rope_inv_freq(hd, theta);
+    std::memcpy(out, f.data(), f.size() * sizeof(float));
+}
+
+// The per-token q/k step of transformer_forward (kernels.cpp:797-803) on the split projections q [m][nh*hd] and
+// k [m][nkv*hd], in place: vox::rmsnorm per head (qn / kn may be NULL), then vox::rope_apply at position pos0 + i.
+// Restated loop (it lives inside transformer_forward) around the reference's own rmsnorm and rope_apply.
+VR_API void vr_qk_norm_rope(float *q, float *k, const float *qn, const float *kn, const float *inv_freq, int64_t m, int64_t nh,
+                            int64_t nkv, int64_t hd, int64_t pos0, float eps) {
+    const int64_t qd = nh * hd, kd = nkv * hd;
+    for (int64_t i = 0; i < m; ++i) {
+        float *qi = q + i * qd, *ki = k + i * kd;
+        if (qn) for (int64_t hh = 0; hh < nh; ++hh) rmsnorm(qi + hh * hd, qn, hd, eps, qi + hh * hd);
+        if (kn) for (int64_t hh = 0; hh < nkv; ++hh) rmsnorm(ki + hh * hd, kn, hd, eps, ki + hh * hd);
+        rope_apply(qi, nh, hd, inv_freq, pos0 + i);
+        rope_apply(ki, nkv, hd, inv_freq, pos0 + i);
+    }
+}
+
+// The residual update before an RMSNorm (kernels.cpp:822-825: o *= attn_scale, h += o; then :833) with the
+// reference's own rmsnorm per row. ls may be NULL (no layer scale).
+VR_API void vr_add_rmsnorm(float *h, const float *d, const float *ls, const float *w, float *xn, int64_t rows, int64_t n, float eps) {
+    std::vector<float> o(d, d + rows * n);
+    if (ls) for (int64_t i = 0; i < rows; ++i) for (int64_t e = 0; e < n; ++e) o[size_t(i * n + e)] *= ls[e];
+    for (int64_t i = 0; i < rows * n; ++i) h[i] += o[size_t(i)];
+    for (int64_t i = 0; i < rows; ++i) rmsnorm(h + i * n, w, n, eps, xn + i * n);
+}

@@ -433,3 +433,73 @@ VO_API double vo_global_sum_finish(const double *slots) {
     }
     return wv[0];
 }
+
+/* ------------------------------------------------------------ transformer elementwise chain (per layer, per token)
+ * The non-GEMM steps between a layer's fused QKV projection and its attention, and the residual update before each
+ * RMSNorm: kernels.cpp:734-757 (rope_inv_freq, rope_apply), kernels.cpp:793-803 and 822-833 (transformer_forward),
+ * shaders/qkvsplit.comp, shaders/qkrope.comp, shaders/ringput.comp and the table of gpu_vulkan.cpp:855-860. */
+
+/* rope_inv_freq (kernels.cpp:734-738): inv_freq[i] = float(1 / theta^(2i / hd)) in double. */
+VO_API void vo_rope_inv_freq(int64_t hd, double theta, float *out) {
+    for (int64_t i = 0; i < hd / 2; ++i) out[i] = (float)(1.0 / pow(theta, (double)(2 * i) / (double)hd));
+}
+
+/* The RoPE table of the GPU transformer (gpu_vulkan.cpp:855-860): row i is position pos0 + i, entry p holds
+ * cos(f), sin(f) of f = inv_freq[p] * float(pos0 + i), all in float as rope_apply (kernels.cpp:744-747). */
+VO_API void vo_rope_table(const float *inv_freq, int64_t half, int64_t pos0, int64_t m, float *cs) {
+    for (int64_t i = 0; i < m; ++i)
+        for (int64_t p = 0; p < half; ++p) {
+            const float f = inv_freq[p] * (float)(pos0 + i);
+            cs[(i * half + p) * 2] = cosf(f);
+            cs[(i * half + p) * 2 + 1] = sinf(f);
+        }
+}
+
+/* vox::rmsnorm (kernels.cpp:707-712) of one head in place, then rope_apply's rotate-half (kernels.cpp:749-756)
+ * with the table row cs (half pairs). */
+static void head_norm_rope(float *p, const float *nw, const float *cs, int64_t hd, float eps) {
+    const int64_t half = hd / 2;
+    if (nw) {
+        float ss = 0;
+        for (int64_t e = 0; e < hd; ++e) ss += p[e] * p[e];
+        const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+        for (int64_t e = 0; e < hd; ++e) p[e] = nw[e] * (p[e] * inv);
+    }
+    for (int64_t i = 0; i < half; ++i) {
+        const float c = cs[2 * i], s = cs[2 * i + 1], a = p[i], b = p[i + half];
+        p[i] = a * c - b * s;
+        p[i + half] = b * c + a * s;
+    }
+}
+
+/* One layer's QKV split, q/k head RMSNorm and RoPE, and K/V cache write for m tokens at positions pos0 .. pos0+m-1.
+ * qkv [m][qd + 2 kd] is the fused projection (qkvsplit.comp:10-19); q [m][qd]; token i's K and V rows go to cache
+ * row pos0 + i, or to ring slot (pos0 + i) % ring when ring > 0 (ringput.comp:11). Head norms (qn, kn, either
+ * NULL) and the rotation follow transformer_forward (kernels.cpp:797-803); cs holds table rows 0 .. m-1
+ * (vo_rope_table). */
+VO_API void vo_qkv_rope(const float *qkv, const float *qn, const float *kn, const float *cs, float *q, float *kc, float *vc,
+                        int64_t m, int64_t heads, int64_t kv_heads, int64_t hd, int64_t pos0, int64_t ring, float eps) {
+    const int64_t qd = heads * hd, kd = kv_heads * hd, w = qd + 2 * kd, half = hd / 2;
+    for (int64_t i = 0; i < m; ++i) {
+        const float *src = qkv + i * w, *csr = cs + i * half * 2;
+        const int64_t slot = ring > 0 ? (pos0 + i) % ring : pos0 + i;
+        float *qi = q + i * qd, *ki = kc + slot * kd, *vi = vc + slot * kd;
+        memcpy(qi, src, (size_t)qd * 4);
+        memcpy(ki, src + qd, (size_t)kd * 4);
+        memcpy(vi, src + qd + kd, (size_t)kd * 4);
+        for (int64_t h = 0; h < heads; ++h) head_norm_rope(qi + h * hd, qn, csr, hd, eps);
+        for (int64_t h = 0; h < kv_heads; ++h) head_norm_rope(ki + h * hd, kn, csr, hd, eps);
+    }
+}
+
+/* The residual update and the RMSNorm that follows it (kernels.cpp:822-825 then :833; :829-831 then the next
+ * layer's :793): d *= ls (the optional per-channel layer scale, attn_scale / mlp_scale), h += d, xn = rmsnorm(h, w)
+ * (kernels.cpp:707-712). h is updated in place. */
+VO_API void vo_add_rmsnorm(float *h, const float *d, const float *ls, const float *w, float *xn, int64_t rows, int64_t n, float eps) {
+    for (int64_t r = 0; r < rows; ++r) {
+        float *hr = h + r * n;
+        const float *dr = d + r * n;
+        for (int64_t e = 0; e < n; ++e) hr[e] += ls ? dr[e] * ls[e] : dr[e];
+    }
+    vo_rmsnorm_rows(h, w, rows, n, eps, xn);
+}

@@ -95,6 +95,27 @@ def main() -> None:
     yb = P.normal((8, 100), sid=40)
     bb = P.normal((100,), sid=41)
     np.savez_compressed(OUT / "bias.npz", y=yb, b=bb, out=R.bias_add(yb, bb))
+    # -- transformer elementwise chain: transformer_forward's per-token q/k step (vox::rmsnorm per head, then
+    #    vox::rope_apply, kernels.cpp:797-803) and the residual update + RMSNorm (kernels.cpp:822-825, 833)
+    heads, kv, hd, m, pos0 = 4, 2, 128, 5, 37
+    qkv = P.normal((m, (heads + 2 * kv) * hd), sid=50)
+    qn = P.normal((hd,), 1.0, 0.1, sid=51)
+    kn = P.normal((hd,), 1.0, 0.1, sid=52)
+    inv = R.rope_inv_freq(hd, 1e6)
+    qs, ks = qkv[:, :heads * hd], qkv[:, heads * hd:(heads + kv) * hd]
+    q_nrm, k_nrm = R.qk_norm_rope(qs, ks, qn, kn, inv, heads, kv, hd, pos0)
+    q_raw, k_raw = R.qk_norm_rope(qs, ks, None, None, inv, heads, kv, hd, pos0)
+    hh = P.normal((6, 1024), sid=53)
+    dd = P.normal((6, 1024), sid=54)
+    ls = P.normal((1024,), 0.0, 0.1, sid=55)
+    wn = P.normal((1024,), 1.0, 0.02, sid=56)
+    h_ls, xn_ls = R.add_rmsnorm(hh, dd, ls, wn)
+    h_no, xn_no = R.add_rmsnorm(hh, dd, None, wn)
+    np.savez_compressed(
+        OUT / "xfmr.npz", qkv=qkv, qn=qn, kn=kn, inv_freq=inv, inv_freq_64=R.rope_inv_freq(64, 1e4),
+        dims=np.array([heads, kv, hd, m, pos0], np.int64),
+        q_norm_rope=q_nrm, k_norm_rope=k_nrm, q_rope=q_raw, k_rope=k_raw,
+        h=hh, d=dd, ls=ls, w=wn, h_ls=h_ls, xn_ls=xn_ls, h_no=h_no, xn_no=xn_no)
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

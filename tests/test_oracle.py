@@ -143,6 +143,32 @@ def test_global_sum_order_independent_of_shards(port):
     assert abs(whole - float(np.sum(x, dtype=np.float64))) <= 1e-6 * float(np.abs(x).sum())
 
 
+def test_xfmr_chain_golden(port, golden):
+    """The split + head norm + RoPE + cache write and the residual update + RMSNorm restatements reproduce the
+    reference's rmsnorm / rope_apply / rope_inv_freq outputs bit for bit (the table from libm's cosf/sinf, as
+    rope_apply computes it)."""
+    g = golden["xfmr"]
+    heads, kv, hd, m, pos0 = (int(v) for v in g["dims"])
+    assert_bitexact(port.rope_inv_freq(hd, 1e6), g["inv_freq"])
+    assert_bitexact(port.rope_inv_freq(64, 1e4), g["inv_freq_64"])
+    cs = port.rope_table(g["inv_freq"], pos0, m)
+    for qn, kn, qw, kw in ((g["qn"], g["kn"], g["q_norm_rope"], g["k_norm_rope"]), (None, None, g["q_rope"], g["k_rope"])):
+        q, kc, vc = port.qkv_rope(g["qkv"], qn, kn, cs, heads, kv, hd, pos0)
+        assert_bitexact(q, qw)
+        assert_bitexact(kc[pos0:], kw)
+        assert_bitexact(vc[pos0:], g["qkv"][:, (heads + kv) * hd:])
+        assert not kc[:pos0].any() and not vc[:pos0].any()  # rows before pos0 untouched
+    # ring slots: token i lands in row (pos0 + i) % ring
+    q, kc, vc = port.qkv_rope(g["qkv"], None, None, cs, heads, kv, hd, pos0, ring=3)
+    for i in range(m):
+        if i >= m - 3:
+            assert_bitexact(kc[(pos0 + i) % 3], g["k_rope"][i])
+    for ls, hw, xw in ((g["ls"], g["h_ls"], g["xn_ls"]), (None, g["h_no"], g["xn_no"])):
+        h, xn = port.add_rmsnorm(g["h"], g["d"], ls, g["w"])
+        assert_bitexact(h, hw)
+        assert_bitexact(xn, xw)
+
+
 def test_reference_library_matches_golden(golden):
     from oracle.oracle import ref
 
@@ -155,3 +181,9 @@ def test_reference_library_matches_golden(golden):
     assert_bitexact(R.softmax_rows(s["s"], float(s["scale"]), 64, 0), s["causal"])
     d = golden["dequant"]
     assert_bitexact(R.mat_rows(d["q8"], d["scale_f32"]), d["q8_out"])
+    x = golden["xfmr"]
+    heads, kv, hd, m, pos0 = (int(v) for v in x["dims"])
+    q, k = R.qk_norm_rope(x["qkv"][:, :heads * hd], x["qkv"][:, heads * hd:(heads + kv) * hd], x["qn"], x["kn"], x["inv_freq"],
+                          heads, kv, hd, pos0)
+    assert_bitexact(q, x["q_norm_rope"])
+    assert_bitexact(k, x["k_norm_rope"])

@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -75,6 +75,9 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_row_reduce": ([c_p, c_p, c_i64, c_i64, c_int, c_int, c_p], c_int),
         "vox_cuda_global_sum_partials": ([c_p, c_i64, c_i64, c_i64, c_i64, c_p, c_p, c_int, c_p], c_int),
         "vox_cuda_global_sum_finish": ([c_p, c_p, c_p], c_int),
+        "vox_cuda_rope_table": ([c_p, c_i64, c_i64, c_i64, c_p, c_p], c_int),
+        "vox_cuda_qkv_rope": ([c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f, c_p], c_int),
+        "vox_cuda_add_rmsnorm": ([c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
     }
     for name, (args, res) in sigs.items():
         f = getattr(L, name)
@@ -359,4 +362,50 @@ def fill_philox(out: torch.Tensor, dist: int, a: float, b: float, seed: int = 0,
     _dev(out, "out")
     dt = BF16 if out.dtype == torch.bfloat16 else F32
     _check(lib.vox_cuda_fill_philox(out.data_ptr(), out.numel(), dist, a, b, seed, stream_id, counter0, dt, _stream(out)))
+    return out
+
+
+# ------------------------------------------------------------------ transformer elementwise chain
+
+def rope_inv_freq(hd: int, theta: float, device="cuda") -> torch.Tensor:
+    """vox::rope_inv_freq (kernels.cpp:734-738): float(1 / theta^(2i/hd)) computed in double, as a device tensor.
+    A model-load-time constant (host arithmetic, then one copy), not a per-step operator."""
+    v = [float(1.0 / (float(theta) ** (2.0 * i / hd))) for i in range(hd // 2)]
+    return torch.tensor(v, dtype=torch.float32).to(device)
+
+
+def rope_table(inv_freq: torch.Tensor, pos0: int, m: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """cos/sin table [m][half][2] of positions pos0 .. pos0+m-1 (the table of gpu_vulkan.cpp:855-860), on the device."""
+    half = inv_freq.numel()
+    out = torch.empty((m, half, 2), dtype=torch.float32, device=inv_freq.device) if out is None else out
+    _f32(out, "out")
+    _check(lib.vox_cuda_rope_table(_f32(inv_freq, "inv_freq"), half, pos0, m, out.data_ptr(), _stream(inv_freq)))
+    return out
+
+
+def qkv_rope(qkv: torch.Tensor, cs: torch.Tensor, heads: int, kv_heads: int, hd: int, k_cache: torch.Tensor,
+             v_cache: torch.Tensor, pos0: int, q_norm_w=None, k_norm_w=None, ring: int = 0, eps: float = 1e-6,
+             q: torch.Tensor | None = None) -> torch.Tensor:
+    """Split the fused projection qkv [m][(heads + 2 kv_heads) hd], head-RMSNorm and RoPE q and k, write q and the
+    tokens' K/V cache rows (pos0 + i, or (pos0 + i) % ring). Returns q [m][heads hd]. qkvsplit.comp + qkrope.comp,
+    CPU form kernels.cpp:797-806."""
+    _f32(qkv, "qkv")
+    m = qkv.numel() // ((heads + 2 * kv_heads) * hd)
+    q = torch.empty((m, heads * hd), dtype=torch.float32, device=qkv.device) if q is None else q
+    _check(lib.vox_cuda_qkv_rope(qkv.data_ptr(), _f32(q_norm_w, "q_norm_w"), _f32(k_norm_w, "k_norm_w"), _f32(cs, "cs"),
+                                 _f32(q, "q"), _f32(k_cache, "k_cache"), _f32(v_cache, "v_cache"), m, heads, kv_heads, hd,
+                                 pos0, ring, eps, _stream(qkv)))
+    return q
+
+
+def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float, layer_scale=None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """h += delta (* layer_scale) in place, then returns rmsnorm(h) * w (kernels.cpp:822-825 then 833)."""
+    dt = _act(h, "h")
+    _same(h, delta, "h", "delta")
+    n = h.shape[-1]
+    out = torch.empty_like(h) if out is None else out
+    _same(h, out, "h", "out")
+    _check(lib.vox_cuda_add_rmsnorm(h.data_ptr(), delta.data_ptr(), _f32(layer_scale, "layer_scale"), _f32(w, "w"),
+                                    out.data_ptr(), h.numel() // n, n, eps, dt, _stream(h)))
     return out

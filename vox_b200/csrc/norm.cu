@@ -104,6 +104,34 @@ __global__ void __launch_bounds__(kRowThreads) norm_row_kernel(NormArgs a) {
     }
 }
 
+// Residual update + RMSNorm, one CTA per row (any length / alignment): pass 1 sums the squares of h + d * ls,
+// pass 2 recomputes h + d * ls (so bf16 rows normalise the f32 sum, as the row pipeline does) and writes it to h
+// and w * (h * inv) to xn. Each thread writes only the elements it reads.
+template <int DT>
+__global__ void __launch_bounds__(kRowThreads) add_rms_row_kernel(AddRmsArgs a) {
+    pdl_enter();
+    using V = Vec<DT>;
+    __shared__ float shf[32];
+    for (int64_t r = blockIdx.x; r < a.rows; r += gridDim.x) {
+        const int64_t base = r * a.n;
+        float ss = 0.f;
+        for (int64_t i = threadIdx.x; i < a.n; i += blockDim.x) {
+            const float d = V::load1(a.d, base + i);
+            const float hn = __fadd_rn(V::load1(a.h, base + i), a.ls ? __fmul_rn(d, a.ls[i]) : d);  // kernels.cpp:822-825
+            ss = fmaf(hn, hn, ss);
+        }
+        ss = block_sum_f(ss, shf);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.n)), a.eps)));
+        for (int64_t i = threadIdx.x; i < a.n; i += blockDim.x) {
+            const float d = V::load1(a.d, base + i);
+            const float hn = __fadd_rn(V::load1(a.h, base + i), a.ls ? __fmul_rn(d, a.ls[i]) : d);
+            V::store1(a.h, base + i, hn);
+            V::store1(a.xn, base + i, __fmul_rn(a.w[i], __fmul_rn(hn, inv)));  // kernels.cpp:711
+        }
+        __syncthreads();
+    }
+}
+
 // ------------------------------------------------------------------ dispatch
 
 template <int DT, int KIND>
@@ -160,6 +188,23 @@ int vox_cuda_adaln(const void *x, const void *shift, const void *scale, const vo
     NormArgs a{x, nullptr, nullptr, shift, scale, gate, residual, y, B * T, D, T, FastDiv(1u), eps, 1.0f / float(D)};
     if (gate) return dispatch_norm<kAdaLnGated>(dtype, a, stream, "vox_cuda_adaln");
     return dispatch_norm<kAdaLn>(dtype, a, stream, "vox_cuda_adaln");
+}
+
+int vox_cuda_add_rmsnorm(void *h, const void *delta, const float *layer_scale, const float *w, void *xn, int64_t rows, int64_t n,
+                         float eps, int dtype, void *stream) {
+    VOX_REQUIRE(is_act_dtype(dtype), "vox_cuda_add_rmsnorm: dtype must be F32 or BF16");
+    VOX_REQUIRE(rows >= 0 && n > 0, "vox_cuda_add_rmsnorm: bad shape");
+    if (rows == 0) return VOX_CUDA_OK;
+    VOX_REQUIRE(h && delta && w && xn, "vox_cuda_add_rmsnorm: NULL pointer");
+    const AddRmsArgs a{h, delta, layer_scale, w, xn, rows, n, eps};
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int rc = launch_add_rms_pipe(dtype, a, st);
+    if (rc != kPipeNotApplicable) return rc;
+    const int64_t cap = int64_t(sm_count()) * 8;
+    const int g = int(rows < cap ? rows : cap);
+    if (dtype == VOX_CUDA_F32) launch_k(add_rms_row_kernel<VOX_CUDA_F32>, g, kRowThreads, 0, st, a);
+    else launch_k(add_rms_row_kernel<VOX_CUDA_BF16>, g, kRowThreads, 0, st, a);
+    return check_launch("vox_cuda_add_rmsnorm");
 }
 
 }  // extern "C"

@@ -250,6 +250,73 @@ struct SoftmaxOp {
     }
 };
 
+// Residual update + RMSNorm (kernels.cpp:822-825 then :833): the h row and the d row arrive together in one stage;
+// h + d * ls rounds the product and the sum separately (scalar, so that no multiply-add is formed), as the CPU.
+template <int DT, int VPL>
+struct AddRmsOp {
+    static constexpr int kMinBlocks = 1;
+    AddRmsArgs a;
+    uint32_t row_bytes;
+
+    __device__ __forceinline__ void issue(int64_t r, uint8_t *buf, uint64_t *bar) const {
+        mbar_arrive_expect_tx(bar, 2 * row_bytes);
+        bulk_g2s(buf, reinterpret_cast<const char *>(a.h) + r * int64_t(row_bytes), row_bytes, bar);
+        bulk_g2s(buf + row_bytes, reinterpret_cast<const char *>(a.d) + r * int64_t(row_bytes), row_bytes, bar);
+    }
+
+    template <class Next>
+    __device__ __forceinline__ void run(int64_t r, const uint8_t *buf, int lane, Next next) const {
+        constexpr int W = Vec<DT>::N, PW = W / 2;
+        const int nvec = int(a.n / W);
+        float2 hv[VPL][PW];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            float2 dv[PW];
+            const uint4 rh = j < nvec ? *reinterpret_cast<const uint4 *>(buf + j * 16) : make_uint4(0, 0, 0, 0);
+            const uint4 rd = j < nvec ? *reinterpret_cast<const uint4 *>(buf + row_bytes + j * 16) : make_uint4(0, 0, 0, 0);
+            unpack2<DT>(rh, hv[k]);
+            unpack2<DT>(rd, dv);
+            if (a.ls) {
+                float2 lv[PW];
+#pragma unroll
+                for (int q = 0; q < PW; q += 2)
+                    unpack2<VOX_CUDA_F32>(j < nvec ? ld_param_ordered(a.ls + j * W + 2 * q) : make_uint4(0, 0, 0, 0), lv + q);
+#pragma unroll
+                for (int p = 0; p < PW; ++p)
+                    hv[k][p] = make_float2(__fadd_rn(hv[k][p].x, __fmul_rn(dv[p].x, lv[p].x)),
+                                           __fadd_rn(hv[k][p].y, __fmul_rn(dv[p].y, lv[p].y)));
+            } else {
+#pragma unroll
+                for (int p = 0; p < PW; ++p) hv[k][p] = add2(hv[k][p], dv[p]);
+            }
+        }
+        next();
+        float2 ss = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPL; ++k)
+#pragma unroll
+            for (int p = 0; p < PW; ++p) ss = fma2(hv[k][p], hv[k][p], ss);
+        const float sum = warp_sum(__fadd_rn(ss.x, ss.y));
+        const float2 inv2 = bc2(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, float(a.n)), a.eps))));
+        char *hr = reinterpret_cast<char *>(a.h) + r * int64_t(row_bytes);
+        char *xr = reinterpret_cast<char *>(a.xn) + r * int64_t(row_bytes);
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            if (j < nvec) {
+                float2 wv[PW], o[PW];
+#pragma unroll
+                for (int q = 0; q < PW; q += 2) unpack2<VOX_CUDA_F32>(ld_param_ordered(a.w + j * W + 2 * q), wv + q);
+#pragma unroll
+                for (int p = 0; p < PW; ++p) o[p] = mul2(wv[p], mul2(hv[k][p], inv2));  // kernels.cpp:711
+                st_stream(hr + j * 16, pack2<DT>(hv[k]));
+                st_stream(xr + j * 16, pack2<DT>(o));
+            }
+        }
+    }
+};
+
 // Row sum / max / L2 norm in the fixed order of vox_cuda_row_reduce: lane l takes vectors l, l+32, ... in order,
 // element k of a vector into accumulator k % 4, lane value (a0 + a1) + (a2 + a3), xor butterfly over the lanes.
 // Reads the staged row from shared memory vector by vector (the row need not fit in registers).
@@ -331,6 +398,23 @@ int norm_pipe_kind(int kind, const NormArgs &a, cudaStream_t st, const char *nam
     }
 }
 
+template <int DT, int VPL>
+int add_rms_pipe_vpl(const AddRmsArgs &a, cudaStream_t st) {
+    const uint32_t row_bytes = uint32_t(a.n * (DT == VOX_CUDA_F32 ? 4 : 2));
+    return launch_row_pipe<AddRmsOp<DT, VPL>, kStages>(AddRmsOp<DT, VPL>{a, row_bytes}, a.rows, 2 * row_bytes, st,
+                                                       "vox_cuda_add_rmsnorm");
+}
+
+template <int DT>
+int add_rms_pipe(const AddRmsArgs &a, cudaStream_t st) {
+    const int vpl = int((a.n / Vec<DT>::N + 31) / 32);
+    if (vpl <= 1) return add_rms_pipe_vpl<DT, 1>(a, st);
+    if (vpl <= 2) return add_rms_pipe_vpl<DT, 2>(a, st);
+    if (vpl <= 4) return add_rms_pipe_vpl<DT, 4>(a, st);
+    if (vpl <= 8) return add_rms_pipe_vpl<DT, 8>(a, st);
+    return add_rms_pipe_vpl<DT, 16>(a, st);
+}
+
 }  // namespace
 
 int launch_norm_pipe(int kind, int dtype, const NormArgs &a, cudaStream_t st, const char *name) {
@@ -344,6 +428,15 @@ int launch_norm_pipe(int kind, int dtype, const NormArgs &a, cudaStream_t st, co
     b.tdiv = FastDiv(uint32_t(a.T));
     if (dtype == VOX_CUDA_F32) return norm_pipe_kind<VOX_CUDA_F32>(kind, b, st, name);
     return norm_pipe_kind<VOX_CUDA_BF16>(kind, b, st, name);
+}
+
+int launch_add_rms_pipe(int dtype, const AddRmsArgs &a, cudaStream_t st) {
+    const int W = dtype == VOX_CUDA_F32 ? 4 : 8;
+    const bool ok = a.n % W == 0 && a.n / W <= 32 * 16 && aligned16(a.h) && aligned16(a.d) && aligned16(a.xn) &&
+                    aligned16(a.w) && (!a.ls || aligned16(a.ls));
+    if (!ok) return kPipeNotApplicable;
+    if (dtype == VOX_CUDA_F32) return add_rms_pipe<VOX_CUDA_F32>(a, st);
+    return add_rms_pipe<VOX_CUDA_BF16>(a, st);
 }
 
 int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, cudaStream_t st) {

@@ -24,12 +24,25 @@ struct NormArgs {
     float inv_n;         // 1 / n
 };
 
+// Residual update + RMSNorm: h += d (* ls), xn = w * (h * inv) (kernels.cpp:822-825, 833).
+struct AddRmsArgs {
+    void *h;             // [rows][n] (dtype), updated in place
+    const void *d;       // [rows][n] (dtype)
+    const float *ls;     // per-channel layer scale [n] or NULL
+    const float *w;      // RMSNorm weight [n]
+    void *xn;            // [rows][n] (dtype)
+    int64_t rows, n;
+    float eps;
+};
+
 // Status returned by the pipeline launchers when the shape or alignment does not fit the pipeline (the caller then
 // takes its general path).
 constexpr int kPipeNotApplicable = 1;
 
 // TMA row pipeline for the norm kinds; VOX_CUDA_OK, a negative status, or kPipeNotApplicable.
 int launch_norm_pipe(int kind, int dtype, const NormArgs &a, cudaStream_t st, const char *name);
+// TMA row pipeline for the residual update + RMSNorm; VOX_CUDA_OK, a negative status, or kPipeNotApplicable.
+int launch_add_rms_pipe(int dtype, const AddRmsArgs &a, cudaStream_t st);
 // TMA row pipeline for the row reductions (same fixed order as the direct kernel in reduce.cu); VOX_CUDA_OK, a
 // negative status, or kPipeNotApplicable.
 int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype, cudaStream_t st);

@@ -226,6 +226,7 @@ VOX_CUDA_API int vox_cuda_rope_table(const float *inv_freq, int64_t half, int64_
  *   qkv:  f32 [m][heads*hd + 2*kv_heads*hd], the fused projection: q heads, then k heads, then v heads
  *   q:    f32 [m][heads*hd]                                   <- rope(headnorm_q(q part))
  *   k_cache, v_cache: f32 [rows][kv_heads*hd]; token i writes row pos0 + i (ring = 0) or ring slot (pos0 + i) % ring
+ *                     (ring > 0 needs m <= ring: no slot is written twice by one call)
  *   q_norm_w / k_norm_w: f32 [hd] RMSNorm weights of the head norms, or NULL for none; eps their epsilon
  *   cs:   the vox_cuda_rope_table rows of these m tokens (row i = position pos0 + i)
  * Rotate-half RoPE: a = x[p], b = x[p + hd/2] -> a*c - b*s, b*c + a*s. Replaces shaders/qkvsplit.comp:10-19,

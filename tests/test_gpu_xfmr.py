@@ -91,14 +91,18 @@ def test_qkv_rope_head_dims_and_paths(vox, port, hd, misalign):
 
 
 def test_qkv_rope_ring_slots(vox, port):
-    heads, kv, hd, m, pos0, ring = 4, 4, 128, 10, 45, 8
+    heads, kv, hd, m, pos0, ring = 4, 4, 128, 8, 45, 8  # positions 45 .. 52 wrap from slot 7 to slot 0
     qkv, qn, kn, inv, cs = _chain_inputs(port, m, heads, kv, hd, pos0)
     sent = (port.normal((ring, kv * hd), sid=74), port.normal((ring, kv * hd), sid=75))
     q, kc, vc = _run_gpu(vox, qkv, qn, kn, cs, heads, kv, hd, pos0, ring, ring=ring, sentinel=sent)
     wq, wk, wv = port.qkv_rope(qkv, qn, kn, cs, heads, kv, hd, pos0, kc=sent[0], vc=sent[1], ring=ring)
     assert_close(q, wq)
     assert_close(kc, wk)
-    assert_bitexact(vc, wv)  # later tokens overwrite earlier ones in the same slot, as ringput.comp
+    assert_bitexact(vc, wv)
+    with pytest.raises(vox.VoxCudaError) as e:  # more tokens than slots: rejected, not raced
+        _run_gpu(vox, port.normal((ring + 1, (heads + 2 * kv) * hd), sid=76), qn, kn, port.rope_table(inv, pos0, ring + 1),
+                 heads, kv, hd, pos0, ring, ring=ring, sentinel=sent)
+    assert e.value.status == -6
 
 
 def test_qkv_rope_decode_and_prefill_sizes(vox, port):

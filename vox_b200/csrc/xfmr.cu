@@ -30,6 +30,9 @@ struct QkvRopeArgs {
     const float *cs;            // [m][hd/2][2]
     float *q, *kc, *vc;         // [m][qd], [cache rows][kd] x2
     int64_t units;              // m * U
+    int64_t items;              // m * groups: work items of the vector path (G consecutive heads of one token)
+    uint32_t groups;            // work items per token
+    FastDiv gdiv;               // division by groups
     int64_t stride, qd, kd;
     uint32_t U, heads, kv_heads;  // U = heads + 2 kv_heads
     uint32_t hd, pos0;
@@ -38,7 +41,8 @@ struct QkvRopeArgs {
     float eps;
 };
 
-// Destination and head-norm weight of unit u (row, head h of U): q heads, then k heads, then v heads.
+// Destination and head-norm weight of unit u (row, head h of U) of the general path: q heads, then k heads, then
+// v heads.
 struct Unit {
     uint32_t row;
     int kind;  // 0 q, 1 k, 2 v
@@ -113,60 +117,72 @@ __device__ __forceinline__ void store_lane(float *p, const float (&v)[E]) {
     }
 }
 
-// Head norm + rotation of one unit held as E consecutive elements per lane (hd = 32 E): lane l holds elements
-// E l .. E l + E - 1; its rotation partners sit in lane l ^ 16 at the same register index.
-template <int E>
-__device__ __forceinline__ void finish_unit(const QkvRopeArgs &a, uint32_t u, float (&x)[E], int lane) {
-    const Unit t = unit_of(a, u);
-    if (t.kind == 2) {
-        store_lane<E>(t.dst + lane * E, x);
-        return;
-    }
-    if (t.nw) {  // vox::rmsnorm over the head (kernels.cpp:707-712)
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < E; ++j) ss = fmaf(x[j], x[j], ss);
-        ss = warp_sum(ss);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(32 * E)), a.eps)));
-        float w[E];
-        load_param<E>(t.nw + lane * E, w);
-#pragma unroll
-        for (int j = 0; j < E; ++j) x[j] = __fmul_rn(w[j], __fmul_rn(x[j], inv));
-    }
-    // cos/sin pairs of rotation indices p = E (lane & 15) + j of this token's table row
-    float cs[2 * E];
-    const float *csr = a.cs + (int64_t(t.row) * (16 * E) + (lane & 15) * E) * 2;
-#pragma unroll
-    for (int k = 0; k < E / 2; ++k) {
-        const float4 c4 = __ldg(reinterpret_cast<const float4 *>(csr) + k);
-        cs[4 * k] = c4.x, cs[4 * k + 1] = c4.y, cs[4 * k + 2] = c4.z, cs[4 * k + 3] = c4.w;
-    }
-    const bool second = lane >= 16;  // this lane holds b = x[p + hd/2]; its partner holds a = x[p]
-    float o[E];
-#pragma unroll
-    for (int j = 0; j < E; ++j) {
-        const float other = __shfl_xor_sync(0xffffffffu, x[j], 16);
-        const float c = cs[2 * j], s = cs[2 * j + 1];
-        // kernels.cpp:753-754: p[i] = a*c - b*s; p[i+half] = b*c + a*s
-        o[j] = second ? __fadd_rn(__fmul_rn(x[j], c), __fmul_rn(other, s)) : __fsub_rn(__fmul_rn(x[j], c), __fmul_rn(other, s));
-    }
-    store_lane<E>(t.dst + lane * E, o);
-}
-
-// One warp per unit, two units in flight per warp (both heads' loads issued before either is used).
+// Vector path (hd = 32 E): one work item = G consecutive heads (4 KB of the projection) of one token, all G loads in
+// flight before the first head is finished. Lane l holds elements E l .. E l + E - 1 of a head; the rotation partners
+// of its elements sit in lane l ^ 16 at the same register index, and its cos/sin pairs (indices p = E (l & 15) + j)
+// are the same for every head of the token, so they are loaded once per item; the head-norm weights once per warp.
 template <int E>
 __global__ void __launch_bounds__(kThreads) qkv_rope_kernel(QkvRopeArgs a) {
+    constexpr int HD = 32 * E, G = 32 / E;
     pdl_enter();
     const int lane = threadIdx.x & 31;
+    const bool second = lane >= 16;  // this lane holds b = x[p + hd/2]; its partner holds a = x[p]
+    float qw[E], kw[E];
+    if (a.qn) load_param<E>(a.qn + lane * E, qw);
+    if (a.kn) load_param<E>(a.kn + lane * E, kw);
     const int64_t gw = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
     const int64_t nw = int64_t(gridDim.x) * kWarps;
-    for (int64_t u0 = gw; u0 < a.units; u0 += 2 * nw) {
-        const int64_t u1 = u0 + nw;
-        float x0[E], x1[E];
-        load_lane<E>(unit_src(a, uint32_t(u0)) + lane * E, x0);
-        if (u1 < a.units) load_lane<E>(unit_src(a, uint32_t(u1)) + lane * E, x1);
-        finish_unit<E>(a, uint32_t(u0), x0, lane);
-        if (u1 < a.units) finish_unit<E>(a, uint32_t(u1), x1, lane);
+    for (int64_t it = gw; it < a.items; it += nw) {
+        const uint32_t row = a.gdiv.div(uint32_t(it));
+        const uint32_t h0 = (uint32_t(it) - row * a.groups) * G;
+        const uint32_t nu = a.U - h0 < uint32_t(G) ? a.U - h0 : uint32_t(G);
+        const float *src = a.qkv + int64_t(row) * a.stride + int64_t(h0) * HD + lane * E;
+        float x[G][E];
+#pragma unroll
+        for (int j = 0; j < G; ++j)
+            if (uint32_t(j) < nu) load_lane<E>(src + j * HD, x[j]);
+        float cs[2 * E];
+        const float *csr = a.cs + (int64_t(row) * (16 * E) + (lane & 15) * E) * 2;
+#pragma unroll
+        for (int k = 0; k < E / 2; ++k) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4 *>(csr) + k);
+            cs[4 * k] = c4.x, cs[4 * k + 1] = c4.y, cs[4 * k + 2] = c4.z, cs[4 * k + 3] = c4.w;
+        }
+        const uint32_t pos = a.pos0 + row;
+        const int64_t slot = a.ring ? int64_t(a.rdiv.mod(pos)) : int64_t(pos);
+        float *qrow = a.q + int64_t(row) * a.qd + lane * E;
+        float *krow = a.kc + slot * a.kd + lane * E;
+        float *vrow = a.vc + slot * a.kd + lane * E;
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+            if (uint32_t(j) >= nu) break;
+            const uint32_t h = h0 + j;
+            if (h >= a.heads + a.kv_heads) {  // v head: copied to the V cache row
+                store_lane<E>(vrow + int64_t(h - a.heads - a.kv_heads) * HD, x[j]);
+                continue;
+            }
+            const bool is_q = h < a.heads;
+            float *dst = is_q ? qrow + int64_t(h) * HD : krow + int64_t(h - a.heads) * HD;
+            if (is_q ? a.qn != nullptr : a.kn != nullptr) {
+                // vox::rmsnorm over the head (kernels.cpp:707-712); hd is a power of two here, so ss * (1/hd) is ss / hd
+                float ss = 0.f;
+#pragma unroll
+                for (int e = 0; e < E; ++e) ss = fmaf(x[j][e], x[j][e], ss);
+                const float inv = rsqrtf(fmaf(warp_sum(ss), 1.0f / float(HD), a.eps));
+#pragma unroll
+                for (int e = 0; e < E; ++e) x[j][e] = __fmul_rn(is_q ? qw[e] : kw[e], __fmul_rn(x[j][e], inv));
+            }
+            float o[E];
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                const float other = __shfl_xor_sync(0xffffffffu, x[j][e], 16);
+                const float c = cs[2 * e], sn = cs[2 * e + 1];
+                // kernels.cpp:753-754: p[i] = a*c - b*s; p[i+half] = b*c + a*s
+                o[e] = second ? __fadd_rn(__fmul_rn(x[j][e], c), __fmul_rn(other, sn))
+                              : __fsub_rn(__fmul_rn(x[j][e], c), __fmul_rn(other, sn));
+            }
+            store_lane<E>(dst, o);
+        }
     }
 }
 
@@ -250,6 +266,7 @@ int vox_cuda_qkv_rope(const float *qkv, const float *q_norm_w, const float *k_no
                 "vox_cuda_qkv_rope: bad shape (head_dim must be even)");
     if (m == 0) return VOX_CUDA_OK;
     VOX_REQUIRE(qkv && cs && q && k_cache && v_cache, "vox_cuda_qkv_rope: NULL pointer");
+    VOX_REQUIRE(ring == 0 || m <= ring, "vox_cuda_qkv_rope: more tokens than ring slots in one call (a slot would be written twice)");
     const int64_t U = heads + 2 * kv_heads;
     VOX_REQUIRE(m * U < (int64_t(1) << 32) && pos0 + m < (int64_t(1) << 32) && ring < (int64_t(1) << 32) && hd <= 4096,
                 "vox_cuda_qkv_rope: sizes out of range");
@@ -267,13 +284,15 @@ int vox_cuda_qkv_rope(const float *qkv, const float *q_norm_w, const float *k_no
     const bool al16 = aligned16(qkv) && aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(cs) &&
                       (!q_norm_w || aligned16(q_norm_w)) && (!k_norm_w || aligned16(k_norm_w));
     const bool vec = hd % 32 == 0 && (E == 2 || E == 4 || E == 8) && al16;
-    const int per_block = kWarps * (vec ? 2 : 1);
-    const int64_t want = (a.units + per_block - 1) / per_block;
     if (vec) {
+        const uint32_t G = uint32_t(32 / E);
+        a.groups = uint32_t((U + G - 1) / G);
+        a.items = m * int64_t(a.groups);
+        a.gdiv = FastDiv(a.groups);
         auto kern = E == 2 ? qkv_rope_kernel<2> : E == 4 ? qkv_rope_kernel<4> : qkv_rope_kernel<8>;
-        const int cap = resident_blocks((const void *)kern, kThreads, 0);
-        launch_k(kern, int(want < cap ? want : cap), kThreads, 0, st, a);
+        launch_k(kern, balanced_grid(a.items, kWarps, resident_blocks((const void *)kern, kThreads, 0)), kThreads, 0, st, a);
     } else {
+        const int64_t want = (a.units + kWarps - 1) / kWarps;
         const size_t smem = size_t(kWarps) * size_t(hd) * sizeof(float);
         if (smem > 48 * 1024 &&
             cudaFuncSetAttribute(qkv_rope_general, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)

@@ -130,6 +130,35 @@ class Suite:
             hh, dd, wn, xo = fill(E(mt, H), 1, 0, 1, 23), fill(E(mt, H), 1, 0, 1, 24), fill(E(H), 1, 1, 0.02, 25), E(mt, H)
             add("next_add_rmsnorm_f32", 4 * mt * H * 4 + H * 4, mt * H, lambda: vox.add_rmsnorm(hh, dd, wn, 1e-6, out=xo), [hh, dd, wn],
                 [hh, xo])
+        # quantized decode GEMV (y = W x, m activation rows): Qwen3-8B MLP-up-shaped weights [12288][4096] with f16
+        # scales, rotated over enough matrices that the weights stream from HBM (> 126 MB L2) on every call
+        for qt in ("q8", "q4"):
+            names = [f"next_gemv_{qt}_m{mm}" for mm in (1, 8)]
+            if not any(want_next(nm) for nm in names):
+                continue
+            GR, GC = 12288 * K, 4096
+            nmat = 4 if qt == "q8" else 8
+            if qt == "q8":
+                mats = [fill(E(GR, GC, dt=torch.int8), 2, -128, 127, 26 + i) for i in range(nmat)]
+            else:
+                mats = [fill(E(GR, GC // 2, dt=torch.uint8), 3, 0, 0, 26 + i) for i in range(nmat)]
+            scs = [fill(E(GR, GC // 32), 0, 0.001, 0.05, 40 + i).to(torch.float16) for i in range(nmat)]
+            gx = fill(E(8, GC), 1, 0, 1, 50)
+            gy = E(8, GR)
+            fn = vox.gemv_q8 if qt == "q8" else vox.gemv_q4
+            wbytes = GR * GC if qt == "q8" else GR * GC // 2
+            for mm in (1, 8):
+                nm = f"next_gemv_{qt}_m{mm}"
+                if not want_next(nm):
+                    continue
+                ctr = [0]
+
+                def call(fn=fn, mats=mats, scs=scs, mm=mm, ctr=ctr):
+                    i = ctr[0] % len(mats)
+                    ctr[0] += 1
+                    fn(mats[i], scs[i], gx[:mm], out=gy[:mm])
+
+                add(nm, wbytes + GR * (GC // 32) * 2 + mm * GC * 4 + mm * GR * 4, GR * GC * mm, call, [mats[0], scs[0], gx], [gy])
         # cfg5 sweep
         n = sweep_elems
         rows = n // 4096

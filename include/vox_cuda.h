@@ -247,6 +247,23 @@ VOX_CUDA_API int vox_cuda_qkv_rope(const float *qkv, const float *q_norm_w, cons
 VOX_CUDA_API int vox_cuda_add_rmsnorm(void *h, const void *delta, const float *layer_scale, const float *w, void *xn, int64_t rows,
                                       int64_t n, float eps, int dtype, void *stream);
 
+/* ---------------------------------------------------------------- quantized GEMV (decode) */
+
+/* y[i][r] = bias[r] + sum_k W[r][k] * x[i][k] for i < m (accumulate != 0: y[i][r] += that), W[r][k] = code *
+ * scale[r][k/32]. Q8: w int8 [rows][cols]; Q4: w uint8 [rows][cols/2], 16 bytes per 32-block, byte j = code j |
+ * code j+16 << 4, value (code - 8). scale: [rows][cols/32] in scale_dtype (VOX_CUDA_F32, Vox's layout, or VOX_CUDA_F16);
+ * bias f32 [rows] or NULL; x f32 [m][cols]; y f32 [m][rows]. cols % 32 == 0; w and x 16-byte aligned.
+ * f32 accuracy (the rounding of an f32 dot product); deterministic. Activation rows are taken 8 per launch, so the
+ * weights stream once per 8 rows: this is the decode path (m <= 8 in one pass).
+ * Replaces the GPU matvec shaders/matmul.comp:1-178 (rec_mm for m <= 8, gpu_vulkan.cpp:657-674; gpu_matmul
+ * gpu_vulkan.cpp:544-572) and, for the CPU, matmul (kernels.cpp:656) with Q8/Q4 weights in its float-activation
+ * form (dequantise then f32 product, kernels.cpp:669-688; the Q8 m <= 8 and Q4 CPU paths quantise x to int8 instead,
+ * kernels.cpp:498-604). */
+VOX_CUDA_API int vox_cuda_gemv_q8(const int8_t *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y,
+                                  int64_t rows, int64_t cols, int64_t m, int accumulate, void *stream);
+VOX_CUDA_API int vox_cuda_gemv_q4(const uint8_t *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y,
+                                  int64_t rows, int64_t cols, int64_t m, int accumulate, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -99,6 +99,7 @@ class Port:
         L.vo_rope_table.argtypes = [_p, _i64, _i64, _i64, _p]
         L.vo_qkv_rope.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f]
         L.vo_add_rmsnorm.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f]
+        L.vo_gemv.argtypes = [_int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int]
 
     # -- generator
     def philox_block(self, ctr, key):
@@ -318,6 +319,20 @@ class Port:
                            ring, eps)
         return q, kc, vc
 
+    def gemv(self, q, scale, x, bias=None, y=None, q4=False):
+        """y [m][rows] = W x (+ bias) (y given: accumulate into a copy of it); returns (y, bound) where bound is
+        sum_k |W[r][k] x[i][k]|. q: int8 [rows][cols] or packed uint8 [rows][cols/2]; scale f32 [rows][cols/32]."""
+        q = np.ascontiguousarray(q)
+        scale, x = _c(scale, np.float32), _c(x, np.float32)
+        rows, cols = q.shape[0], x.shape[-1]
+        m = x.size // cols
+        acc = y is not None
+        y = np.zeros((m, rows), np.float32) if y is None else _c(y, np.float32).copy()
+        bound = np.empty((m, rows), np.float64)
+        bias = None if bias is None else _c(bias, np.float32)
+        self.L.vo_gemv(int(q4), _ptr(q), _ptr(scale), _ptr(bias), _ptr(x), _ptr(y), _ptr(bound), rows, cols, m, int(acc))
+        return y, bound
+
     def add_rmsnorm(self, h, d, ls, w, eps=1e-6):
         """Returns (h + d * ls, rmsnorm of it)."""
         h = _c(h, np.float32).copy()
@@ -364,6 +379,7 @@ class Ref:
         L.vr_rope_inv_freq.argtypes = [_i64, _d, _p]
         L.vr_qk_norm_rope.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f]
         L.vr_add_rmsnorm.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f]
+        L.vr_matmul.argtypes = [_int, _p, _p, _p, _i64, _i64, _p, _i64, _p]
 
     def set_threads(self, n: int) -> int:
         self.L.vr_set_threads(n)
@@ -522,6 +538,17 @@ class Ref:
         inv_freq = _c(inv_freq, np.float32)
         self.L.vr_qk_norm_rope(_ptr(q), _ptr(k), _ptr(qn), _ptr(kn), _ptr(inv_freq), q.shape[0], heads, kv_heads, hd, pos0, eps)
         return q, k
+
+    def matmul(self, wtype, data, scale, x, rows, cols, bias=None):
+        """vox::matmul on a CPU Mat (wtype 0 F32, 3 Q8, 4 Q4): y [m][rows]."""
+        data = np.ascontiguousarray(data)
+        scale = None if scale is None else _c(scale, np.float32)
+        bias = None if bias is None else _c(bias, np.float32)
+        x = _c(x, np.float32)
+        m = x.size // cols
+        y = np.empty((m, rows), np.float32)
+        self.L.vr_matmul(wtype, _ptr(data), _ptr(scale), _ptr(bias), rows, cols, _ptr(x), m, _ptr(y))
+        return y
 
     def add_rmsnorm(self, h, d, ls, w, eps=1e-6):
         h = _c(h, np.float32).copy()

@@ -269,3 +269,20 @@ VR_API void vr_add_rmsnorm(float *h, const float *d, const float *ls, const floa
     for (int64_t i = 0; i < rows * n; ++i) h[i] += o[size_t(i)];
     for (int64_t i = 0; i < rows; ++i) rmsnorm(h + i * n, w, n, eps, xn + i * n);
 }
+
+// ---------------------------------------------------------------- matmul (quantized weights)
+
+// vox::matmul (kernels.cpp:656-706) on a CPU Mat: type 0 = F32, 3 = Q8, 4 = Q4 (WType order), bias may be NULL.
+// y[i][r] for i < m. With Q8 and m > 8 this is the dequantise-then-f32 path (kernels.cpp:669-688); with F32 weights
+// (e.g. dequantised by mat_rows) the float-activation product of the GPU matvec.
+VR_API void vr_matmul(int type, const uint8_t *data, const float *scale, const float *bias, int64_t rows, int64_t cols,
+                      const float *x, int64_t m, float *y) {
+    Mat W;
+    W.type = WType(type);
+    W.data = data;
+    W.scale = scale;
+    W.rows = rows;
+    W.cols = cols;
+    W.bias = bias;
+    matmul(W, x, m, y);
+}

@@ -503,3 +503,35 @@ VO_API void vo_add_rmsnorm(float *h, const float *d, const float *ls, const floa
     }
     vo_rmsnorm_rows(h, w, rows, n, eps, xn);
 }
+
+/* ------------------------------------------------------------ quantized GEMV (decode, m <= 8)
+ * y[i][r] = bias[r] + sum_k W[r][k] * x[i][k] (y[i][r] += ... when accumulate), W[r][k] = q * scale[r][k/32]:
+ * the semantics of Vox's GPU matvec shaders/matmul.comp:1-8, 60-178 (float activations, weights dequantized in the
+ * shader) and of the CPU matmul's dequantise-then-f32 path (kernels.cpp:669-688). Q8: int8 codes [rows][cols];
+ * Q4: 16 bytes per 32-block, byte j = weight j | weight j+16 << 4, value (u - 8) * scale (kernels.hpp:45-47).
+ * Accumulated in double; `bound` receives sum_k |W[r][k] x[i][k]| (the scale of a dot product's rounding error). */
+VO_API void vo_gemv(int q4, const uint8_t *q, const float *scale, const float *bias, const float *x, float *y, double *bound,
+                    int64_t rows, int64_t cols, int64_t m, int accumulate) {
+    const int64_t nb = cols / 32;
+    for (int64_t i = 0; i < m; ++i)
+        for (int64_t r = 0; r < rows; ++r) {
+            double s = 0, a = 0;
+            for (int64_t k = 0; k < cols; ++k) {
+                const int64_t b = k / 32, j = k % 32;
+                int v;
+                if (q4) {
+                    const uint8_t byte = q[r * (cols / 2) + b * 16 + (j & 15)];
+                    v = (int)(j < 16 ? (byte & 15) : (byte >> 4)) - 8;
+                } else {
+                    v = (int8_t)q[r * cols + k];
+                }
+                const double p = (double)((float)v * scale[r * nb + b]) * (double)x[i * cols + k];
+                s += p;
+                a += fabs(p);
+            }
+            const double out = (bias ? (double)bias[r] : 0.0) + s;
+            const int64_t o = i * rows + r;
+            y[o] = accumulate ? (float)((double)y[o] + out) : (float)out;
+            if (bound) bound[o] = a;
+        }
+}

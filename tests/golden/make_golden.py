@@ -116,6 +116,20 @@ def main() -> None:
         dims=np.array([heads, kv, hd, m, pos0], np.int64),
         q_norm_rope=q_nrm, k_norm_rope=k_nrm, q_rope=q_raw, k_rope=k_raw,
         h=hh, d=dd, ls=ls, w=wn, h_ls=h_ls, xn_ls=xn_ls, h_no=h_no, xn_no=xn_no)
+    # -- quantized GEMV with float activations: the reference's own matmul, Q8 weights with m = 9 (its
+    #    dequantise-then-f32 path, kernels.cpp:669-688) and the dequantised (mat_rows) weights as F32 for m <= 8 and Q4
+    gr, gc = 48, 256
+    gq8 = P.fill_i8((gr, gc), -127, 127, sid=100)
+    gq4 = P.fill_u8((gr, gc // 2), sid=101)
+    gs = P.uniform_arr((gr, gc // 32), 0.001, 0.05, sid=102)
+    gb = P.normal((gr,), sid=103)
+    gx = P.normal((9, gc), sid=104)
+    np.savez_compressed(
+        OUT / "gemv.npz", q8=gq8, q4=gq4, scale=gs, bias=gb, x=gx,
+        q8_m9=R.matmul(3, gq8, gs, gx, gr, gc, gb),
+        q8_m3=R.matmul(0, R.mat_rows(gq8, gs), None, gx[:3], gr, gc, gb),
+        q4_m3=R.matmul(0, R.mat_rows(gq4, gs, q4=True), None, gx[:3], gr, gc, gb),
+        q4_m1_nobias=R.matmul(0, R.mat_rows(gq4, gs, q4=True), None, gx[:1], gr, gc))
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -169,6 +169,16 @@ def test_xfmr_chain_golden(port, golden):
         assert_bitexact(xn, xw)
 
 
+def test_gemv_golden(port, golden):
+    """The float-activation GEMV restatement (accumulated in double) agrees with the reference's f32 matmul to within
+    f32 rounding of the dot products: |d| <= 1e-6 * sum_k |w x|."""
+    g = golden["gemv"]
+    for key, q4, m, bias in (("q8_m9", False, 9, True), ("q8_m3", False, 3, True), ("q4_m3", True, 3, True),
+                             ("q4_m1_nobias", True, 1, False)):
+        y, bound = port.gemv(g["q4" if q4 else "q8"], g["scale"], g["x"][:m], g["bias"] if bias else None, q4=q4)
+        assert np.all(np.abs(y.astype(np.float64) - g[key]) <= 1e-6 * bound + 1e-7), key
+
+
 def test_reference_library_matches_golden(golden):
     from oracle.oracle import ref
 

@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -78,6 +78,8 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_rope_table": ([c_p, c_i64, c_i64, c_i64, c_p, c_p], c_int),
         "vox_cuda_qkv_rope": ([c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f, c_p], c_int),
         "vox_cuda_add_rmsnorm": ([c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
+        "vox_cuda_gemv_q8": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_gemv_q4": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
     }
     for name, (args, res) in sigs.items():
         f = getattr(L, name)
@@ -85,7 +87,19 @@ def _load() -> ctypes.CDLL:
     return L
 
 
-lib = _load()
+class _Lib:
+    """The loaded library, opened on first use: ``vox_b200.build`` stays importable before the library exists (a
+    fresh checkout), while every operator call needs it and raises ImportError when it is missing or stale."""
+
+    _L: ctypes.CDLL | None = None
+
+    def __getattr__(self, name: str):
+        if _Lib._L is None:
+            _Lib._L = _load()
+        return getattr(_Lib._L, name)
+
+
+lib = _Lib()
 
 
 def version() -> str:
@@ -409,3 +423,32 @@ def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: floa
     _check(lib.vox_cuda_add_rmsnorm(h.data_ptr(), delta.data_ptr(), _f32(layer_scale, "layer_scale"), _f32(w, "w"),
                                     out.data_ptr(), h.numel() // n, n, eps, dt, _stream(h)))
     return out
+
+
+# ------------------------------------------------------------------ quantized GEMV (decode)
+
+def _gemv(fn, q4, w, scale, x, bias, out, accumulate):
+    _dev(w, "w")
+    if w.dtype != (torch.uint8 if q4 else torch.int8):
+        raise VoxCudaError(-6, f"w must be {'uint8 (packed Q4)' if q4 else 'int8'}")
+    sdt = _scale_dt(scale)
+    xf = _f32(x, "x")
+    rows, cols = w.shape[0], x.shape[-1]
+    m = x.numel() // cols
+    if out is None:
+        out = torch.zeros((m, rows), dtype=torch.float32, device=x.device) if accumulate else \
+            torch.empty((m, rows), dtype=torch.float32, device=x.device)
+    _check(fn(w.data_ptr(), scale.data_ptr(), sdt, _f32(bias, "bias"), xf, _f32(out, "out"), rows, cols, m, int(accumulate),
+              _stream(x)))
+    return out
+
+
+def gemv_q8(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, out=None, accumulate: bool = False) -> torch.Tensor:
+    """y [m][rows] = W x (+ bias), W = int8 codes [rows][cols] x scale [rows][cols/32] (f32 or f16); the GPU matvec
+    of matmul.comp (float activations). accumulate adds into out."""
+    return _gemv(lib.vox_cuda_gemv_q8, False, w, scale, x, bias, out, accumulate)
+
+
+def gemv_q4(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, out=None, accumulate: bool = False) -> torch.Tensor:
+    """As gemv_q8 with Q4 weights: uint8 [rows][cols/2], 16 bytes per 32-block (byte j = code j | code j+16 << 4)."""
+    return _gemv(lib.vox_cuda_gemv_q4, True, w, scale, x, bias, out, accumulate)

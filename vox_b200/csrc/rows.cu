@@ -476,9 +476,7 @@ using namespace voxcuda;
 extern "C" int vox_cuda_device_error(unsigned int *flags) {
     VOX_REQUIRE(flags != nullptr, "vox_cuda_device_error: flags is NULL");
     unsigned int v = 0;
-    const unsigned int zero = 0;
-    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess ||
-        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess) {
+    if (take_device_error(&v) != VOX_CUDA_OK || gemv_take_device_error(&v) != VOX_CUDA_OK) {
         const cudaError_t e = cudaGetLastError();
         return set_error(VOX_CUDA_ERR_DEVICE, std::string("vox_cuda_device_error: ") + cudaGetErrorString(e));
     }

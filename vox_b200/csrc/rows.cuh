@@ -50,4 +50,7 @@ int launch_reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, int o
 int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float scale, int64_t q_len, int64_t pos0,
                         cudaStream_t st);
 
+// Reads and clears the quantized GEMV's device error flag into *flags (gemv.cu); VOX_CUDA_OK or VOX_CUDA_ERR_DEVICE.
+int gemv_take_device_error(unsigned int *flags);
+
 }  // namespace voxcuda

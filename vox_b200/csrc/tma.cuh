@@ -17,9 +17,10 @@
 
 namespace voxcuda {
 
-// Device-side error flag of the row pipeline (a bit set by a kernel that gave up a wait). Defined here: rows.cu is
-// the one translation unit that includes this header (the library is built without relocatable device code).
-__device__ unsigned int g_device_error = 0;
+// Device-side error flag of the pipelines (a bit set by a kernel that gave up a wait). The library is built without
+// relocatable device code, so every translation unit that includes this header has its own flag; each of them
+// exposes it through take_device_error() and vox_cuda_device_error() gathers them all.
+static __device__ unsigned int g_device_error = 0;
 constexpr unsigned int kDevErrTimeout = 1u;
 // try_wait polls before a wait gives up (each poll may also suspend the warp for a hardware-chosen time).
 constexpr uint32_t kMaxWaitPolls = 1u << 22;
@@ -143,6 +144,17 @@ int launch_row_pipe(const Op &op, int64_t rows, uint32_t stage_bytes, cudaStream
     const int g = balanced_grid(rows, kPipeWarps, resident_blocks((const void *)kern, kPipeWarps * 32, smem));
     launch_k(kern, g, kPipeWarps * 32, smem, st, op, rows, stage_bytes);
     return check_launch(name);
+}
+
+// Reads and clears this translation unit's device error flag (host side). VOX_CUDA_OK or VOX_CUDA_ERR_DEVICE.
+static inline int take_device_error(unsigned int *flags) {
+    unsigned int v = 0;
+    const unsigned int zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess)
+        return VOX_CUDA_ERR_DEVICE;
+    *flags |= v;
+    return VOX_CUDA_OK;
 }
 
 }  // namespace voxcuda

@@ -135,7 +135,7 @@ __device__ __forceinline__ float load_scale(const void *s, int64_t i) {
 }
 
 // 2-D tensor copy (TMA) of the box at (x bytes, y rows) of `map` into this CTA's shared memory, completing on `bar`.
-// No multicast: the box lands in the issuing CTA only.
+// The box lands in the issuing CTA only (no copy to other CTAs of the cluster).
 __device__ __forceinline__ void tensor_g2s_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                  ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))

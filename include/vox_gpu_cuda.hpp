@@ -71,6 +71,21 @@ bool gpu_dequant(bool q4, const void *codes, const void *scale, int scale_dtype,
 // Row sum / max / L2 norm (op = VOX_CUDA_REDUCE_*), f32 results.
 bool gpu_row_reduce(const void *x, float *out, int64_t rows, int64_t n, int op, int dtype = VOX_CUDA_F32, void *stream = nullptr);
 
+// ---- transformer chain and decode matvec (transformer_forward, kernels.cpp:793-833; rec_layers, gpu_vulkan.cpp:679-715) ----
+// cos/sin table of positions pos0 .. pos0+m-1 (gpu_vulkan.cpp:855-860), once per forward for all layers.
+bool gpu_rope_table(const float *inv_freq, int64_t half, int64_t pos0, int64_t m, float *cs, void *stream = nullptr);
+// One layer's QKV split + q/k head RMSNorm (qn/kn may be NULL) + RoPE + K/V cache write (qkvsplit.comp, qkrope.comp).
+bool gpu_qkv_rope(const float *qkv, const float *qn, const float *kn, const float *cs, float *q, float *k_cache, float *v_cache,
+                  int64_t m, int64_t heads, int64_t kv_heads, int64_t hd, int64_t pos0, float eps, int64_t ring = 0,
+                  void *stream = nullptr);
+// h += delta (* layer_scale), xn = rmsnorm(h) (kernels.cpp:822-825, 833).
+bool gpu_add_rmsnorm(void *h, const void *delta, const float *layer_scale, const float *w, void *xn, int64_t rows, int64_t n, float eps,
+                     int dtype = VOX_CUDA_F32, void *stream = nullptr);
+// y [m][rows] (+)= W x for Q8 / Q4 weights (q4 selects the packed layout), f32 activations: gpu_matmul's m <= 8 path
+// (gpu_vulkan.cpp:544-572, matmul.comp). bias may be NULL.
+bool gpu_matvec(bool q4, const void *codes, const void *scale, int scale_dtype, const float *bias, const float *x, float *y,
+                int64_t rows, int64_t cols, int64_t m, bool accumulate = false, void *stream = nullptr);
+
 // ---- host-pointer conveniences (copy in, run, copy out; synchronous) ----
 bool rmsnorm_host(const float *x, const float *w, int64_t rows, int64_t n, float eps, float *out);
 bool softmax_causal_host(const float *scores, float *probs, int64_t heads, int64_t q_len, int64_t n_keys, float scale);

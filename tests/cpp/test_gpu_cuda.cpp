@@ -21,6 +21,13 @@ void vo_dequant_q8(const int8_t *q, const float *scale, int64_t rows, int64_t co
 void vo_dequant_q4(const uint8_t *q, const float *scale, int64_t rows, int64_t cols, float *out);
 void vo_snake(const float *x, const float *alpha, const float *beta, float *y, int64_t n, int64_t C, int64_t inner, int kind);
 void vo_row_reduce_ordered(const float *x, float *out, int64_t rows, int64_t n, int op, int W);
+void vo_rope_inv_freq(int64_t hd, double theta, float *out);
+void vo_rope_table(const float *inv_freq, int64_t half, int64_t pos0, int64_t m, float *cs);
+void vo_qkv_rope(const float *qkv, const float *qn, const float *kn, const float *cs, float *q, float *kc, float *vc, int64_t m,
+                 int64_t heads, int64_t kv_heads, int64_t hd, int64_t pos0, int64_t ring, float eps);
+void vo_add_rmsnorm(float *h, const float *d, const float *ls, const float *w, float *xn, int64_t rows, int64_t n, float eps);
+void vo_gemv(int q4, const uint8_t *q, const float *scale, const float *bias, const float *x, float *y, double *bound, int64_t rows,
+             int64_t cols, int64_t m, int accumulate);
 }
 
 static int g_fail = 0;
@@ -120,6 +127,65 @@ int main() {
     CHECK(vox::gpu_cuda_download(rs.data(), dr, R * 4) && vox::gpu_cuda_sync());
     vo_row_reduce_ordered(x.data(), rsw.data(), R, N, 0, 4);
     CHECK(bitexact(rs, rsw));
+
+    // transformer chain: split + RoPE + cache write (bit-exact with the host table, no head norm), residual + RMSNorm
+    {
+        const int64_t m = 3, nh = 2, nkv = 1, hd = 128, pos0 = 5, W = (nh + 2 * nkv) * hd;
+        std::vector<float> qkv(m * W), inv(hd / 2), cs(m * hd), q(m * nh * hd), kc(8 * nkv * hd, 0.f), vc(8 * nkv * hd, 0.f);
+        std::vector<float> wq(q.size()), wk(kc.size(), 0.f), wv(vc.size(), 0.f);
+        vo_fill(qkv.data(), m * W, 1, 0.f, 1.f, 0, 9, 0);
+        vo_rope_inv_freq(hd, 1e6, inv.data());
+        vo_rope_table(inv.data(), hd / 2, pos0, m, cs.data());
+        float *dq = static_cast<float *>(vox::gpu_cuda_alloc(m * W * 4)), *dcs = static_cast<float *>(vox::gpu_cuda_alloc(cs.size() * 4));
+        float *dqo = static_cast<float *>(vox::gpu_cuda_alloc(q.size() * 4)), *dk = static_cast<float *>(vox::gpu_cuda_alloc(kc.size() * 4));
+        float *dv = static_cast<float *>(vox::gpu_cuda_alloc(vc.size() * 4));
+        CHECK(dq && dcs && dqo && dk && dv);
+        CHECK(vox::gpu_cuda_upload(dq, qkv.data(), m * W * 4) && vox::gpu_cuda_upload(dcs, cs.data(), cs.size() * 4) &&
+              vox::gpu_cuda_upload(dk, kc.data(), kc.size() * 4) && vox::gpu_cuda_upload(dv, vc.data(), vc.size() * 4));
+        CHECK(vox::gpu_qkv_rope(dq, nullptr, nullptr, dcs, dqo, dk, dv, m, nh, nkv, hd, pos0, 1e-6f));
+        CHECK(vox::gpu_cuda_download(q.data(), dqo, q.size() * 4) && vox::gpu_cuda_download(kc.data(), dk, kc.size() * 4) &&
+              vox::gpu_cuda_download(vc.data(), dv, vc.size() * 4) && vox::gpu_cuda_sync());
+        vo_qkv_rope(qkv.data(), nullptr, nullptr, cs.data(), wq.data(), wk.data(), wv.data(), m, nh, nkv, hd, pos0, 0, 1e-6f);
+        CHECK(bitexact(q, wq) && bitexact(kc, wk) && bitexact(vc, wv));
+        for (void *ptr : {static_cast<void *>(dq), static_cast<void *>(dcs), static_cast<void *>(dqo), static_cast<void *>(dk),
+                          static_cast<void *>(dv)})
+            vox::gpu_cuda_free(ptr);
+
+        std::vector<float> h0(x), d(R * N), hw(x), xw(R * N), hg(R * N), xg(R * N);
+        vo_fill(d.data(), R * N, 1, 0.f, 1.f, 0, 10, 0);
+        CHECK(vox::gpu_cuda_upload(dx, h0.data(), R * N * 4) && vox::gpu_cuda_upload(dy, d.data(), R * N * 4) &&
+              vox::gpu_cuda_upload(dw, w.data(), N * 4));
+        float *dxn = static_cast<float *>(vox::gpu_cuda_alloc(R * N * 4));
+        CHECK(dxn && vox::gpu_add_rmsnorm(dx, dy, nullptr, dw, dxn, R, N, 1e-6f));
+        CHECK(vox::gpu_cuda_download(hg.data(), dx, R * N * 4) && vox::gpu_cuda_download(xg.data(), dxn, R * N * 4) &&
+              vox::gpu_cuda_sync());
+        vo_add_rmsnorm(hw.data(), d.data(), nullptr, w.data(), xw.data(), R, N, 1e-6f);
+        CHECK(bitexact(hg, hw) && close(xg, xw, N, 1e-5));
+        vox::gpu_cuda_free(dxn);
+    }
+
+    // decode matvec, Q8 with f32 scales: |y - exact| <= 1e-6 * sum |w x|
+    {
+        const int64_t GR = 300, GC = 512, M = 2;
+        std::vector<int8_t> gq(GR * GC);
+        std::vector<float> gs(GR * GC / 32), gx(M * GC), gy(M * GR), gw(M * GR);
+        std::vector<double> bound(M * GR);
+        vo_fill_i8(gq.data(), GR * GC, -128, 127, 0, 11, 0);
+        vo_fill(gs.data(), int64_t(gs.size()), 0, 0.001f, 0.05f, 0, 12, 0);
+        vo_fill(gx.data(), M * GC, 1, 0.f, 1.f, 0, 13, 0);
+        void *dgq = vox::gpu_cuda_alloc(gq.size()), *dgs = vox::gpu_cuda_alloc(gs.size() * 4);
+        float *dgx = static_cast<float *>(vox::gpu_cuda_alloc(gx.size() * 4)), *dgy = static_cast<float *>(vox::gpu_cuda_alloc(gy.size() * 4));
+        CHECK(dgq && dgs && dgx && dgy);
+        CHECK(vox::gpu_cuda_upload(dgq, gq.data(), gq.size()) && vox::gpu_cuda_upload(dgs, gs.data(), gs.size() * 4) &&
+              vox::gpu_cuda_upload(dgx, gx.data(), gx.size() * 4));
+        CHECK(vox::gpu_matvec(false, dgq, dgs, VOX_CUDA_F32, nullptr, dgx, dgy, GR, GC, M));
+        CHECK(vox::gpu_cuda_download(gy.data(), dgy, gy.size() * 4) && vox::gpu_cuda_sync());
+        vo_gemv(0, reinterpret_cast<const uint8_t *>(gq.data()), gs.data(), nullptr, gx.data(), gw.data(), bound.data(), GR, GC, M, 0);
+        bool ok = true;
+        for (size_t i = 0; i < gy.size(); ++i) ok = ok && std::fabs(double(gy[i]) - gw[i]) <= 1e-6 * bound[i] + 1e-30;
+        CHECK(ok);
+        for (void *ptr : {dgq, dgs, static_cast<void *>(dgx), static_cast<void *>(dgy)}) vox::gpu_cuda_free(ptr);
+    }
 
     // a rejected call returns false and leaves its reason in the stats, as the Vulkan seam does
     const auto before = vox::gpu_cuda_stats();

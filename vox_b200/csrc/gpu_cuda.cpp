@@ -146,6 +146,27 @@ VOX_CXX_API bool gpu_row_reduce(const void *x, float *out, int64_t rows, int64_t
     return done(vox_cuda_row_reduce(x, out, rows, n, op, dtype, stream));
 }
 
+VOX_CXX_API bool gpu_rope_table(const float *inv_freq, int64_t half, int64_t pos0, int64_t m, float *cs, void *stream) {
+    return done(vox_cuda_rope_table(inv_freq, half, pos0, m, cs, stream));
+}
+VOX_CXX_API bool gpu_qkv_rope(const float *qkv, const float *qn, const float *kn, const float *cs, float *q, float *k_cache,
+                              float *v_cache, int64_t m, int64_t heads, int64_t kv_heads, int64_t hd, int64_t pos0, float eps,
+                              int64_t ring, void *stream) {
+    return done(vox_cuda_qkv_rope(qkv, qn, kn, cs, q, k_cache, v_cache, m, heads, kv_heads, hd, pos0, ring, eps, stream));
+}
+VOX_CXX_API bool gpu_add_rmsnorm(void *h, const void *delta, const float *layer_scale, const float *w, void *xn, int64_t rows,
+                                 int64_t n, float eps, int dtype, void *stream) {
+    return done(vox_cuda_add_rmsnorm(h, delta, layer_scale, w, xn, rows, n, eps, dtype, stream));
+}
+VOX_CXX_API bool gpu_matvec(bool q4, const void *codes, const void *scale, int scale_dtype, const float *bias, const float *x,
+                            float *y, int64_t rows, int64_t cols, int64_t m, bool accumulate, void *stream) {
+    if (q4)
+        return done(vox_cuda_gemv_q4(static_cast<const uint8_t *>(codes), scale, scale_dtype, bias, x, y, rows, cols, m,
+                                     accumulate ? 1 : 0, stream));
+    return done(vox_cuda_gemv_q8(static_cast<const int8_t *>(codes), scale, scale_dtype, bias, x, y, rows, cols, m,
+                                 accumulate ? 1 : 0, stream));
+}
+
 // ---- host-pointer conveniences ----
 
 namespace {

@@ -356,6 +356,167 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     if (clustered) cg::this_cluster().sync();  // no CTA leaves while another still reads its shared memory
 }
 
+// ------------------------------------------------------------------ CUDA-core path for one or two activation rows
+//
+// Decode multiplies one (or, with classifier-free guidance, two) activation rows: then the tensor cores' N = 8 columns
+// are mostly zeros and the cost is the code conversion. This path spends about 2.4 instructions per weight: lane l
+// streams 16 consecutive code bytes of a row (512 contiguous bytes per warp instruction), converts them with the same
+// exact bit-pattern trick, multiplies them by its activation values held in registers (reused for the 32 rows of a
+// batch), and scales the block partial once. A CTA (8 warps) owns 32 rows; its warps (and the C CTAs of a cluster)
+// split the rows' 512-byte chunks; each warp's 32 row partials are reduced across its lanes by a transpose butterfly
+// (31 shuffles), then across the warps and the cluster in fixed order.
+constexpr int kCcRows = 32;
+
+// exact f32 value of each of the four int8 codes of `word`, minus nothing: q (via 2^23 + (q + 128) - (2^23 + 128))
+__device__ __forceinline__ void q8_to_f32(uint32_t word, float2 &c01, float2 &c23) {
+    const uint32_t u = word ^ 0x80808080u;
+    const float2 m = make_float2(-8388736.0f, -8388736.0f);
+    c01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)), __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541))), m);
+    c23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)), __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), m);
+}
+// four 4-bit codes (one per byte, 0..15) -> their values code - 8, exact
+__device__ __forceinline__ void q4_to_f32(uint32_t nib, float2 &c01, float2 &c23) {
+    const float2 m = make_float2(-8388616.0f, -8388616.0f);  // 2^23 + 8
+    c01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7540)), __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7541))), m);
+    c23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7542)), __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7543))), m);
+}
+
+template <bool Q4, bool SF16, int M>
+__global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C) {
+    constexpr int NX = Q4 ? 32 : 16;  // activation values per lane per chunk
+    constexpr int RB = 8;             // rows per batch (reduced across the warp together)
+    __shared__ float red[kWarps][M][kCcRows];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int crank = int(blockIdx.x) % C;
+    const int64_t row0 = int64_t(blockIdx.x / C) * kCcRows;
+    const int64_t rowbytes = Q4 ? a.cols / 2 : a.cols;
+    const int nchunk = int((rowbytes + 511) / 512);
+    const int64_t last = a.rows - 1 - row0;  // rows r > last read row `last` (their sums are dropped)
+    pdl_enter();
+    // rows (b * RB + (lane % RB)) of batch b, per activation row: this lane's share of the warp's partial sums
+    float tot[kCcRows / RB][M];
+#pragma unroll
+    for (int b = 0; b < kCcRows / RB; ++b)
+#pragma unroll
+        for (int t = 0; t < M; ++t) tot[b][t] = 0.f;
+    for (int ci = crank * kWarps + warp; ci < nchunk; ci += kWarps * C) {
+        const int64_t cb = int64_t(ci) * 512 + lane * 16;  // this lane's 16 bytes of every row
+        const bool valid = cb < rowbytes;                 // a row's last chunk may be partial (rowbytes % 16 == 0)
+        const int64_t blk = Q4 ? cb / 16 : cb / 32;       // the 32-block of these bytes
+        const int64_t k0 = Q4 ? blk * 32 : cb;            // first activation index they multiply
+        float2 xv[M][NX / 2];
+#pragma unroll
+        for (int t = 0; t < M; ++t)
+#pragma unroll
+            for (int q = 0; q < NX / 4; ++q) {
+                const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + k0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[t][2 * q] = make_float2(v.x, v.y);
+                xv[t][2 * q + 1] = make_float2(v.z, v.w);
+            }
+#pragma unroll 1
+        for (int b = 0; b < kCcRows / RB; ++b) {
+            float acc[RB][M];
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+                const int64_t rr = b * RB + r <= last ? b * RB + r : last;
+                const uint4 w = valid ? __ldcs(reinterpret_cast<const uint4 *>(a.w + (row0 + rr) * rowbytes + cb)) : make_uint4(0, 0, 0, 0);
+                const float sc = valid ? load_scale<SF16>(a.scale, (row0 + rr) * a.nblk + blk) : 0.f;
+                const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+                float2 p[M][2];
+#pragma unroll
+                for (int t = 0; t < M; ++t) p[t][0] = p[t][1] = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float2 c01, c23;
+                    if (Q4) {
+                        // word i: codes 4i..4i+3 (low nibbles) and 16+4i..16+4i+3 (high nibbles)
+                        float2 h01, h23;
+                        q4_to_f32(wd[i] & 0x0F0F0F0Fu, c01, c23);
+                        q4_to_f32((wd[i] >> 4) & 0x0F0F0F0Fu, h01, h23);
+#pragma unroll
+                        for (int t = 0; t < M; ++t) {
+                            p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                            p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                            p[t][0] = __ffma2_rn(h01, xv[t][8 + 2 * i], p[t][0]);
+                            p[t][1] = __ffma2_rn(h23, xv[t][8 + 2 * i + 1], p[t][1]);
+                        }
+                    } else {
+                        q8_to_f32(wd[i], c01, c23);
+#pragma unroll
+                        for (int t = 0; t < M; ++t) {
+                            p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                            p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < M; ++t) {
+                    const float2 q = __fadd2_rn(p[t][0], p[t][1]);
+                    acc[r][t] = (q.x + q.y) * sc;
+                }
+            }
+            // transpose butterfly over lane bits 2..0 (after it lane l holds row l % RB of the batch, summed over the
+            // lanes that share bits 3, 4), then a plain sum over bits 3 and 4
+#pragma unroll
+            for (int t = 0; t < M; ++t) {
+#pragma unroll
+                for (int s = RB / 2; s >= 1; s >>= 1) {
+                    const bool up = (lane & s) != 0;
+#pragma unroll
+                    for (int j = 0; j < s; ++j) {
+                        const float send = up ? acc[j][t] : acc[j + s][t];
+                        const float keep = up ? acc[j + s][t] : acc[j][t];
+                        acc[j][t] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+                    }
+                }
+                float v = acc[0][t];
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+                tot[b][t] += v;
+            }
+        }
+    }
+    if (lane < RB) {
+#pragma unroll
+        for (int b = 0; b < kCcRows / RB; ++b)
+#pragma unroll
+            for (int t = 0; t < M; ++t) red[warp][t][b * RB + lane] = tot[b][t];
+    }
+    __syncthreads();
+    // the CTA's rows: sum of the warps in order; then the cluster's CTAs in rank order
+    float *cta = &red[0][0][0];
+    if (threadIdx.x < M * kCcRows) {
+        const int t = threadIdx.x / kCcRows, r = threadIdx.x % kCcRows;
+        float v = red[0][t][r];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) v += red[w][t][r];
+        __syncwarp();
+        cta[t * kCcRows + r] = v;  // red[0] is read above by this thread only
+    }
+    const bool clustered = C > 1;
+    if (clustered) cg::this_cluster().sync();
+    else __syncthreads();
+    const int lo_r = crank * kCcRows / C, hi_r = (crank + 1) * kCcRows / C, span = hi_r - lo_r;
+    if (threadIdx.x < M * span) {
+        const int t = threadIdx.x / span, r = lo_r + threadIdx.x % span;
+        const int64_t grow = row0 + r;
+        if (t < a.m && grow < a.rows) {
+            float v;
+            if (clustered) {
+                cg::cluster_group cl = cg::this_cluster();
+                v = 0.f;
+                for (int q = 0; q < C; ++q) v += cl.map_shared_rank(cta, q)[t * kCcRows + r];
+            } else {
+                v = cta[t * kCcRows + r];
+            }
+            float *yp = a.y + int64_t(t) * a.ystride + grow;
+            const float out = (a.bias ? __ldg(a.bias + grow) : 0.f) + v;
+            *yp = a.accumulate ? *yp + out : out;
+        }
+    }
+    if (clustered) cg::this_cluster().sync();
+}
+
 struct GemvPlan {
     int C = 0;
     size_t smem = 0;
@@ -433,6 +594,77 @@ int plan_gemv(int64_t rows, int nblk, int m, GemvPlan &plan, const char *name) {
     return VOX_CUDA_OK;
 }
 
+// Cluster size of the CUDA-core path for a shape, cached: split the rows' 512-byte chunks over up to 8 CTAs so that
+// one wave of resident CTAs is filled, every warp keeping at least one chunk, all clusters co-resident.
+template <bool Q4, bool SF16, int M>
+int plan_cc(int64_t rows, int64_t rowbytes, int &C_out, const char *name) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int64_t, int64_t>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch(name);
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_tuple(dev, rows, rowbytes);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        C_out = it->second;
+        return VOX_CUDA_OK;
+    }
+    auto kern = gemv_cc_kernel<Q4, SF16, M>;
+    const int64_t groups = (rows + kCcRows - 1) / kCcRows;
+    const int64_t nchunk = (rowbytes + 511) / 512;
+    const int64_t slots = resident_blocks((const void *)kern, kThreads, 0);
+    int64_t c = slots / groups;
+    if (c > nchunk / kWarps) c = nchunk / kWarps;
+    if (c > 8) c = 8;
+    int C = int(c < 1 ? 1 : c);
+    while (C > 1) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = unsigned(C);
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.gridDim = dim3(unsigned(groups * C));
+        cfg.blockDim = dim3(kThreads);
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0) break;
+        cudaGetLastError();
+        --C;
+    }
+    cache[key] = C;
+    C_out = C;
+    return VOX_CUDA_OK;
+}
+
+template <bool Q4, bool SF16, int M>
+int launch_cc(const GemvArgs &a, cudaStream_t st, const char *name) {
+    int C = 1;
+    const int rc = plan_cc<Q4, SF16, M>(a.rows, Q4 ? a.cols / 2 : a.cols, C, name);
+    if (rc != VOX_CUDA_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    cfg.gridDim = dim3(unsigned((a.rows + kCcRows - 1) / kCcRows * C));
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = st;
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = unsigned(C);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    if (cudaLaunchKernelEx(&cfg, gemv_cc_kernel<Q4, SF16, M>, a, C) != cudaSuccess) return check_launch(name);
+    return VOX_CUDA_OK;
+}
+
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no link-time dependency on libcuda).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static std::once_flag once;
@@ -491,6 +723,11 @@ int launch_gemv(const GemvArgs &base, int64_t m_total, cudaStream_t st, const ch
         a.m = int(m_total - i0 < kTok ? m_total - i0 : kTok);
         a.x = base.x + i0 * base.cols;
         a.y = base.y + i0 * base.ystride;
+        if (!Q4 && a.m <= 2) {  // Q8, one or two rows: the CUDA-core path (measured faster; Q4 stays on the MMA path)
+            rc = a.m == 1 ? launch_cc<Q4, SF16, 1>(a, st, name) : launch_cc<Q4, SF16, 2>(a, st, name);
+            if (rc != VOX_CUDA_OK) return rc;
+            continue;
+        }
         GemvPlan plan;
         rc = plan_gemv<Q4, SF16>(base.rows, base.nblk, a.m, plan, name);
         if (rc != VOX_CUDA_OK) return rc;

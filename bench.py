@@ -159,6 +159,27 @@ class Suite:
                     fn(mats[i], scs[i], gx[:mm], out=gy[:mm])
 
                 add(nm, wbytes + GR * (GC // 32) * 2 + mm * GC * 4 + mm * GR * 4, GR * GC * mm, call, [mats[0], scs[0], gx], [gy])
+        # .tmod -> device: a file of Q8 matrices with f32 scales (Qwen3-8B MLP-shaped, [12288][4096] each, about 1.6 GB in
+        # all), written once to a temporary directory; one step uploads every blob from the mapped file (page cache)
+        if want_next("next_tmod_upload"):
+            import tempfile
+
+            from vox_b200.tmodfile import write_tmod
+
+            tdir = Path(tempfile.mkdtemp(prefix="vox_tmod_"))
+            TR, TC, TN = 12288, 4096, 4
+            gen = np.random.default_rng(11)
+            blobs = {}
+            for i in range(TN):
+                blobs[f"l{i}.w"] = ("I8", (TR, TC), gen.integers(-128, 128, (TR, TC), dtype=np.int8).tobytes())
+                blobs[f"l{i}.w.scale"] = ("F32", (TR, TC // 32), gen.random((TR, TC // 32), dtype=np.float32).tobytes())
+            write_tmod(tdir / "bench.tmod", {"family": "bench"}, blobs)
+            nbytes = sum(len(b[2]) for b in blobs.values())
+            del blobs
+            self.tmod = vox.Tmod(tdir / "bench.tmod")
+            tnames = self.tmod.names()
+            touts = [E(*self.tmod.info(nm)[1], dt=torch.int8 if nm.endswith(".w") else torch.float32) for nm in tnames]
+            add("next_tmod_upload", nbytes, nbytes, lambda: self.tmod.upload(tnames, touts), [], touts)
         # cfg5 sweep
         n = sweep_elems
         rows = n // 4096

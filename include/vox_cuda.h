@@ -39,6 +39,8 @@ extern "C" {
 
 /* Status codes: same numeric values as vox_status in include/vox.h:44-56. */
 #define VOX_CUDA_OK 0
+#define VOX_CUDA_ERR_IO (-1)
+#define VOX_CUDA_ERR_FORMAT (-2)
 #define VOX_CUDA_ERR_DEVICE (-3)
 #define VOX_CUDA_ERR_OOM (-4)
 #define VOX_CUDA_ERR_ARG (-6)
@@ -263,6 +265,37 @@ VOX_CUDA_API int vox_cuda_gemv_q8(const int8_t *w, const void *scale, int scale_
                                   int64_t rows, int64_t cols, int64_t m, int accumulate, void *stream);
 VOX_CUDA_API int vox_cuda_gemv_q4(const uint8_t *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y,
                                   int64_t rows, int64_t cols, int64_t m, int accumulate, void *stream);
+
+/* ---------------------------------------------------------------- .tmod weight files -> device */
+
+/* Vox's .tmod container (src/formats.hpp:44-90): 64-byte header "VOXM" v1.x, JSON manifest with a "blobs" table
+ * {name: {dtype, shape, offset, nbytes}}, blobs 4096-byte aligned. dtype codes follow Vox's DType order
+ * (src/common.hpp:22): F32 0, F16 1, BF16 2, I32 3, I16 4, I8 5, U8 6. */
+#define VOX_CUDA_TMOD_MAX_DIMS 8
+typedef struct vox_cuda_tmod vox_cuda_tmod;
+
+/* Maps `path` read-only and reads its manifest (the checks and errors of TmodFile::TmodFile, formats.cpp:175-205:
+ * VOX_CUDA_ERR_IO for an unreadable file, VOX_CUDA_ERR_FORMAT for a bad header, manifest or blob range). No device
+ * work. The handle is not thread-safe for concurrent uploads on different devices. */
+VOX_CUDA_API int vox_cuda_tmod_open(const char *path, vox_cuda_tmod **out);
+/* Waits for the handle's transfers in flight, frees its staging memory and unmaps the file. NULL is ignored. */
+VOX_CUDA_API void vox_cuda_tmod_close(vox_cuda_tmod *t);
+/* Number of blobs, their names in manifest order, their description (shape: up to VOX_CUDA_TMOD_MAX_DIMS entries, any
+ * output pointer may be NULL), and a host pointer into the mapping (TmodFile::get, formats.cpp:207-211). */
+VOX_CUDA_API int vox_cuda_tmod_count(const vox_cuda_tmod *t, int64_t *n);
+VOX_CUDA_API int vox_cuda_tmod_name(const vox_cuda_tmod *t, int64_t i, const char **name);
+VOX_CUDA_API int vox_cuda_tmod_info(const vox_cuda_tmod *t, const char *name, int *dtype, int64_t *shape, int *ndim,
+                                    uint64_t *nbytes);
+VOX_CUDA_API int vox_cuda_tmod_data(const vox_cuda_tmod *t, const char *name, const void **host);
+/* Copies blobs names[i] into device buffers dst[i] (nbytes each) on `stream` through the handle's ring of pinned
+ * staging buffers (16 MB x 4; host copies of the next chunk overlap the transfer of the previous one). Returns when
+ * the last chunk is queued; the copies complete in stream order. Replaces the weight uploads of the Vulkan backend
+ * (upload_parts, gpu_vulkan.cpp:476-536). */
+VOX_CUDA_API int vox_cuda_tmod_upload(vox_cuda_tmod *t, const char *const *names, int64_t count, void *const *dst, void *stream);
+/* Uploads the Q8 (I8) or Q4 (U8, two codes per byte) matrix `name` and its "<name>.scale" f32 blob as nn::mat_named
+ * reads them (nn.cpp:132-145) and dequantises it on the device into dst [rows][cols] (out_dtype F32 or BF16),
+ * bit-exact with mat_row (kernels.cpp:446-463). Device staging comes from the stream-ordered allocator. */
+VOX_CUDA_API int vox_cuda_tmod_upload_dequant(vox_cuda_tmod *t, const char *name, void *dst, int out_dtype, void *stream);
 
 #ifdef __cplusplus
 }

@@ -380,6 +380,10 @@ class Ref:
         L.vr_qk_norm_rope.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f]
         L.vr_add_rmsnorm.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f]
         L.vr_matmul.argtypes = [_int, _p, _p, _p, _i64, _i64, _p, _i64, _p]
+        L.vr_tmod_write.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _i64, _p, _p, _p, _p, _p, _p, _u32]
+        L.vr_tmod_write.restype = _int
+        L.vr_tmod_read.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _p, _u64]
+        L.vr_tmod_read.restype = _i64
 
     def set_threads(self, n: int) -> int:
         self.L.vr_set_threads(n)
@@ -549,6 +553,32 @@ class Ref:
         y = np.empty((m, rows), np.float32)
         self.L.vr_matmul(wtype, _ptr(data), _ptr(scale), _ptr(bias), rows, cols, _ptr(x), m, _ptr(y))
         return y
+
+    def tmod_write(self, path, manifest_json: str, blobs: dict, flags: int = 0) -> None:
+        """vox::tmod_write; blobs: name -> (dtype code, shape, bytes)."""
+        names = list(blobs)
+        cnames = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        dts = np.array([blobs[n][0] for n in names], np.int32)
+        shapes = np.zeros((len(names), 8), np.int64)
+        nd = np.array([len(blobs[n][1]) for n in names], np.int32)
+        for i, n in enumerate(names):
+            shapes[i, :len(blobs[n][1])] = blobs[n][1]
+        bufs = [ctypes.create_string_buffer(bytes(blobs[n][2]), max(1, len(blobs[n][2]))) for n in names]
+        ptrs = (ctypes.c_void_p * len(names))(*[ctypes.addressof(b) for b in bufs])
+        nb = np.array([len(blobs[n][2]) for n in names], np.uint64)
+        rc = self.L.vr_tmod_write(str(path).encode(), manifest_json.encode(), len(names), ctypes.cast(cnames, _p), _ptr(dts),
+                                  _ptr(shapes), _ptr(nd), ctypes.cast(ptrs, _p), _ptr(nb), flags)
+        if rc != 0:
+            raise RuntimeError("vox::tmod_write failed")
+
+    def tmod_read(self, path, name: str) -> bytes | None:
+        """vox::TmodFile(path).get(name) bytes, or None (missing blob or bad file)."""
+        n = self.L.vr_tmod_read(str(path).encode(), name.encode(), None, 0)
+        if n < 0:
+            return None
+        buf = ctypes.create_string_buffer(max(1, n))
+        self.L.vr_tmod_read(str(path).encode(), name.encode(), buf, n)
+        return buf.raw[:n]
 
     def add_rmsnorm(self, h, d, ls, w, eps=1e-6):
         h = _c(h, np.float32).copy()

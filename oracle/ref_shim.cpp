@@ -286,3 +286,38 @@ VR_API void vr_matmul(int type, const uint8_t *data, const float *scale, const f
     W.bias = bias;
     matmul(W, x, m, y);
 }
+
+// ---------------------------------------------------------------- .tmod container (formats.cpp)
+
+// vox::tmod_write (formats.cpp:215-249) of `count` blobs; manifest_json is the manifest without its "blobs" table.
+// dtypes follow DType (common.hpp:22); shapes holds 8 entries per blob, ndims the used ones. 0 on success.
+VR_API int vr_tmod_write(const char *path, const char *manifest_json, int64_t count, const char *const *names, const int *dtypes,
+                         const int64_t *shapes, const int *ndims, const uint8_t *const *data, const uint64_t *nbytes, uint32_t flags) {
+    try {
+        std::map<std::string, Tensor> blobs;
+        for (int64_t i = 0; i < count; ++i) {
+            Tensor t;
+            t.dtype = DType(dtypes[i]);
+            t.shape.assign(shapes + i * 8, shapes + i * 8 + ndims[i]);
+            t.bytes.assign(data[i], data[i] + nbytes[i]);
+            blobs.emplace(names[i], std::move(t));
+        }
+        tmod_write(path, json::parse(manifest_json), blobs, flags);
+        return 0;
+    } catch (...) {
+        return -1;
+    }
+}
+
+// vox::TmodFile (formats.cpp:175-205): copies blob `name` into out (cap bytes) and returns its size, or -1 (missing
+// blob or an exception, e.g. a bad file).
+VR_API int64_t vr_tmod_read(const char *path, const char *name, uint8_t *out, uint64_t cap) {
+    try {
+        TmodFile f(path);
+        const TensorView &v = f.get(name);
+        if (v.nbytes <= cap) std::memcpy(out, v.data, v.nbytes);
+        return int64_t(v.nbytes);
+    } catch (...) {
+        return -1;
+    }
+}

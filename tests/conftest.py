@@ -45,3 +45,15 @@ def vox():
     import vox_b200
 
     return vox_b200
+
+
+@pytest.fixture(scope="session")
+def vox_lib():
+    """The vox_b200 package for host-only calls (the .tmod reader): built if missing, no CUDA device needed."""
+    from vox_b200 import build as _build
+
+    if not _build.LIB.exists():
+        _build.build()
+    import vox_b200
+
+    return vox_b200

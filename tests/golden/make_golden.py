@@ -130,6 +130,22 @@ def main() -> None:
         q8_m3=R.matmul(0, R.mat_rows(gq8, gs), None, gx[:3], gr, gc, gb),
         q4_m3=R.matmul(0, R.mat_rows(gq4, gs, q4=True), None, gx[:3], gr, gc, gb),
         q4_m1_nobias=R.matmul(0, R.mat_rows(gq4, gs, q4=True), None, gx[:1], gr, gc))
+    # -- .tmod container written by the reference's own tmod_write (formats.cpp:215-249): Q8 and Q4 matrices with
+    #    their f32 scales (nn::mat_named, nn.cpp:132-145), an f32 vector, a bf16 table; a manifest with nested values
+    tq8 = P.fill_i8((48, 64), -127, 127, sid=130)
+    tq4 = P.fill_u8((16, 32), sid=131)
+    ts8 = P.uniform_arr((48, 2), 0.001, 0.05, sid=132)
+    ts4 = P.uniform_arr((16, 2), 0.001, 0.05, sid=133)
+    tnorm = P.normal((64,), 1.0, 0.02, sid=134)
+    temb = P.bf16_round(P.normal((3, 8), sid=135))
+    manifest = ('{"family": "test", "config": {"hidden": 64, "eps": 1e-06, "name": "\u00fcn\u00efcode \\"q\\" \\\\", '
+                '"list": [1, 2.5, true, false, null, [], {}], "\u20ac": -3e2}}')
+    R.tmod_write(OUT / "tiny.tmod", manifest, {
+        "layer.w": (5, (48, 64), tq8.tobytes()), "layer.w.scale": (0, (48, 2), ts8.tobytes()),
+        "layer.u": (6, (16, 32), tq4.tobytes()), "layer.u.scale": (0, (16, 2), ts4.tobytes()),
+        "norm": (0, (64,), tnorm.tobytes()), "emb": (2, (3, 8), np.asarray(temb, np.uint16).tobytes())})
+    np.savez_compressed(OUT / "tmod.npz", q8=tq8, q4=tq4, s8=ts8, s4=ts4, norm=tnorm, emb=np.asarray(temb, np.uint16),
+                        q8_deq=R.mat_rows(tq8, ts8), q4_deq=R.mat_rows(tq4, ts4, q4=True))
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "Tmod", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -31,7 +31,8 @@ GELU_ERF, GELU_TANH = 0, 1
 SNAKE_HIFT, SNAKE_BETA, SNAKE_KOKORO = 0, 1, 2
 REDUCE_SUM, REDUCE_MAX, REDUCE_L2 = 0, 1, 2
 GLOBAL_SUM_SLOTS = 840
-STATUS_NAMES = {-3: "VOX_ERR_DEVICE", -4: "VOX_ERR_OOM", -6: "VOX_ERR_ARG", -8: "VOX_ERR_UNSUPPORTED"}
+STATUS_NAMES = {-1: "VOX_ERR_IO", -2: "VOX_ERR_FORMAT", -3: "VOX_ERR_DEVICE", -4: "VOX_ERR_OOM", -6: "VOX_ERR_ARG",
+                -8: "VOX_ERR_UNSUPPORTED"}
 
 _DIR = Path(__file__).resolve().parent
 lib_path = Path(os.environ.get("VOX_CUDA_LIB", _DIR / "libvox_cuda.so"))
@@ -80,6 +81,14 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_add_rmsnorm": ([c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
         "vox_cuda_gemv_q8": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
         "vox_cuda_gemv_q4": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_tmod_open": ([ctypes.c_char_p, c_p], c_int),
+        "vox_cuda_tmod_close": ([c_p], None),
+        "vox_cuda_tmod_count": ([c_p, c_p], c_int),
+        "vox_cuda_tmod_name": ([c_p, c_i64, c_p], c_int),
+        "vox_cuda_tmod_info": ([c_p, ctypes.c_char_p, c_p, c_p, c_p, c_p], c_int),
+        "vox_cuda_tmod_data": ([c_p, ctypes.c_char_p, c_p], c_int),
+        "vox_cuda_tmod_upload": ([c_p, c_p, c_i64, c_p, c_p], c_int),
+        "vox_cuda_tmod_upload_dequant": ([c_p, ctypes.c_char_p, c_p, c_int, c_p], c_int),
     }
     for name, (args, res) in sigs.items():
         f = getattr(L, name)
@@ -452,3 +461,84 @@ def gemv_q8(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, ou
 def gemv_q4(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, out=None, accumulate: bool = False) -> torch.Tensor:
     """As gemv_q8 with Q4 weights: uint8 [rows][cols/2], 16 bytes per 32-block (byte j = code j | code j+16 << 4)."""
     return _gemv(lib.vox_cuda_gemv_q4, True, w, scale, x, bias, out, accumulate)
+
+
+# ------------------------------------------------------------------ .tmod weight files -> device
+
+TMOD_DTYPES = ["F32", "F16", "BF16", "I32", "I16", "I8", "U8"]  # Vox's DType order (src/common.hpp:22)
+_TORCH_OF = {"F32": torch.float32, "F16": torch.float16, "BF16": torch.bfloat16, "I32": torch.int32, "I16": torch.int16,
+             "I8": torch.int8, "U8": torch.uint8}
+
+
+class Tmod:
+    """A mapped .tmod file (vox::TmodFile, src/formats.hpp:65-84): blob names, descriptions, host views, and uploads
+    to the device through pinned staging (vox_cuda_tmod_upload); Q8/Q4 matrices can be dequantised on arrival."""
+
+    def __init__(self, path):
+        h = ctypes.c_void_p()
+        _check(lib.vox_cuda_tmod_open(str(path).encode(), ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            lib.vox_cuda_tmod_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def names(self) -> list[str]:
+        n = ctypes.c_int64()
+        _check(lib.vox_cuda_tmod_count(self._h, ctypes.byref(n)))
+        out = []
+        for i in range(n.value):
+            p = ctypes.c_char_p()
+            _check(lib.vox_cuda_tmod_name(self._h, i, ctypes.byref(p)))
+            out.append(p.value.decode())
+        return out
+
+    def info(self, name: str) -> tuple[str, tuple, int]:
+        """(dtype name, shape, nbytes) of a blob."""
+        dt, nd, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_uint64()
+        shape = (ctypes.c_int64 * 8)()
+        _check(lib.vox_cuda_tmod_info(self._h, name.encode(), ctypes.byref(dt), shape, ctypes.byref(nd), ctypes.byref(nb)))
+        return TMOD_DTYPES[dt.value], tuple(shape[i] for i in range(nd.value)), nb.value
+
+    def host_bytes(self, name: str) -> bytes:
+        """A copy of the blob's bytes from the mapping (no device work)."""
+        p = ctypes.c_void_p()
+        _check(lib.vox_cuda_tmod_data(self._h, name.encode(), ctypes.byref(p)))
+        return ctypes.string_at(p.value, self.info(name)[2])
+
+    def upload(self, names, outs=None, device="cuda"):
+        """Copies blobs to the device (one call, pinned staging, the current stream); returns the tensors."""
+        names = [names] if isinstance(names, str) else list(names)
+        if outs is None:
+            outs = []
+            for n in names:
+                dt, shape, nb = self.info(n)
+                outs.append(torch.empty(shape, dtype=_TORCH_OF[dt], device=device))
+        for t in outs:
+            _dev(t, "out")
+        cn = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        dp = (ctypes.c_void_p * len(outs))(*[t.data_ptr() for t in outs])
+        st = _stream(outs[0]) if outs else 0
+        _check(lib.vox_cuda_tmod_upload(self._h, ctypes.cast(cn, ctypes.c_void_p), len(names), ctypes.cast(dp, ctypes.c_void_p), st))
+        return outs
+
+    def upload_dequant(self, name: str, out_dtype=torch.bfloat16, device="cuda") -> torch.Tensor:
+        """The Q8/Q4 matrix `name` (+ "<name>.scale") dequantised on the device to [rows][cols] (mat_row, bit-exact)."""
+        dt, shape, _ = self.info(name)
+        rows, cols = shape[0], (shape[1] if len(shape) > 1 else 1) * (2 if dt == "U8" else 1)
+        out = torch.empty((rows, cols), dtype=out_dtype, device=device)
+        _check(lib.vox_cuda_tmod_upload_dequant(self._h, name.encode(), out.data_ptr(), _act(out, "out"), _stream(out)))
+        return out

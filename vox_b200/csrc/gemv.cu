@@ -384,7 +384,7 @@ __device__ __forceinline__ void q4_to_f32(uint32_t nib, float2 &c01, float2 &c23
 template <bool Q4, bool SF16, int M>
 __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C) {
     constexpr int NX = Q4 ? 32 : 16;  // activation values per lane per chunk
-    constexpr int RB = 8;             // rows per batch (reduced across the warp together)
+    constexpr int RB = 4;             // rows per batch (reduced across the warp together)
     __shared__ float red[kWarps][M][kCcRows];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int crank = int(blockIdx.x) % C;
@@ -413,15 +413,26 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
                 xv[t][2 * q] = make_float2(v.x, v.y);
                 xv[t][2 * q + 1] = make_float2(v.z, v.w);
             }
-#pragma unroll 1
-        for (int b = 0; b < kCcRows / RB; ++b) {
+        // the batch's 8 rows of codes and scales, double-buffered: batch b + 1 is requested before batch b is used
+        // one 64-bit base per batch, 32-bit row offsets (rows of a CTA span < 2^31 bytes: launcher)
+        const uint8_t *wcol = a.w + row0 * rowbytes + cb;
+        const uint8_t *scol = static_cast<const uint8_t *>(a.scale) + (row0 * a.nblk + blk) * (SF16 ? 2 : 4);
+        const uint32_t wstep = uint32_t(rowbytes), sstep = uint32_t(a.nblk * (SF16 ? 2 : 4));
+        auto fetch = [&](int b, uint4 (&w)[RB], float (&sc)[RB]) {
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+                const uint32_t rr = uint32_t(b * RB + r <= last ? b * RB + r : last);
+                w[r] = valid ? __ldcs(reinterpret_cast<const uint4 *>(wcol + rr * wstep)) : make_uint4(0, 0, 0, 0);
+                sc[r] = valid ? load_scale<SF16>(scol + rr * sstep, 0) : 0.f;
+            }
+        };
+        // the batch's 8 row partials of this warp, per activation row: lane l ends with row l % RB (all lanes of a
+        // row agree)
+        auto batch = [&](const uint4 (&wb)[RB], const float (&sb)[RB], float (&out)[M]) {
             float acc[RB][M];
 #pragma unroll
             for (int r = 0; r < RB; ++r) {
-                const int64_t rr = b * RB + r <= last ? b * RB + r : last;
-                const uint4 w = valid ? __ldcs(reinterpret_cast<const uint4 *>(a.w + (row0 + rr) * rowbytes + cb)) : make_uint4(0, 0, 0, 0);
-                const float sc = valid ? load_scale<SF16>(a.scale, (row0 + rr) * a.nblk + blk) : 0.f;
-                const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+                const uint32_t wd[4] = {wb[r].x, wb[r].y, wb[r].z, wb[r].w};
                 float2 p[M][2];
 #pragma unroll
                 for (int t = 0; t < M; ++t) p[t][0] = p[t][1] = make_float2(0.f, 0.f);
@@ -452,11 +463,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
 #pragma unroll
                 for (int t = 0; t < M; ++t) {
                     const float2 q = __fadd2_rn(p[t][0], p[t][1]);
-                    acc[r][t] = (q.x + q.y) * sc;
+                    acc[r][t] = (q.x + q.y) * sb[r];
                 }
             }
-            // transpose butterfly over lane bits 2..0 (after it lane l holds row l % RB of the batch, summed over the
-            // lanes that share bits 3, 4), then a plain sum over bits 3 and 4
+            // transpose butterfly over lane bits 1..0 (lane l keeps row l % RB), then a plain sum over bits 2..4
 #pragma unroll
             for (int t = 0; t < M; ++t) {
 #pragma unroll
@@ -470,10 +480,30 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
                     }
                 }
                 float v = acc[0][t];
-                v += __shfl_xor_sync(0xffffffffu, v, 8);
-                v += __shfl_xor_sync(0xffffffffu, v, 16);
-                tot[b][t] += v;
+#pragma unroll
+                for (int s = RB; s < 32; s <<= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+                out[t] = v;
             }
+        };
+        constexpr int NB = kCcRows / RB;  // batches per chunk (even)
+        uint4 w0[RB], w1[RB];
+        float s0[RB], s1[RB];
+        fetch(0, w0, s0);
+#pragma unroll 1
+        for (int b = 0; b < NB; b += 2) {
+            fetch(b + 1, w1, s1);
+            float v[M];
+            batch(w0, s0, v);
+#pragma unroll
+            for (int k = 0; k < NB; k += 2)
+#pragma unroll
+                for (int t = 0; t < M; ++t) tot[k][t] += b == k ? v[t] : 0.f;
+            if (b + 2 < NB) fetch(b + 2, w0, s0);
+            batch(w1, s1, v);
+#pragma unroll
+            for (int k = 1; k < NB; k += 2)
+#pragma unroll
+                for (int t = 0; t < M; ++t) tot[k][t] += b + 1 == k ? v[t] : 0.f;
         }
     }
     if (lane < RB) {

@@ -287,10 +287,12 @@ VOX_CUDA_API int vox_cuda_tmod_name(const vox_cuda_tmod *t, int64_t i, const cha
 VOX_CUDA_API int vox_cuda_tmod_info(const vox_cuda_tmod *t, const char *name, int *dtype, int64_t *shape, int *ndim,
                                     uint64_t *nbytes);
 VOX_CUDA_API int vox_cuda_tmod_data(const vox_cuda_tmod *t, const char *name, const void **host);
-/* Copies blobs names[i] into device buffers dst[i] (nbytes each) on `stream` through the handle's ring of pinned
- * staging buffers (16 MB x 4; host copies of the next chunk overlap the transfer of the previous one). Returns when
- * the last chunk is queued; the copies complete in stream order. Replaces the weight uploads of the Vulkan backend
- * (upload_parts, gpu_vulkan.cpp:476-536). */
+/* Copies blobs names[i] into device buffers dst[i] (nbytes each) on `stream`. The first upload page-locks the
+ * mapping for the device (read-only registration; blobs then go straight from the page cache); where that is not
+ * supported (or VOX_CUDA_TMOD_REGISTER=0) a ring of pinned staging buffers (32 MB x 4) is used, host copies of the next
+ * chunk overlapping the transfer of the previous one. Returns when the last copy is queued; the copies complete in
+ * stream order (vox_cuda_tmod_close waits for them). Replaces the weight uploads of the Vulkan backend (upload_parts,
+ * gpu_vulkan.cpp:476-536). */
 VOX_CUDA_API int vox_cuda_tmod_upload(vox_cuda_tmod *t, const char *const *names, int64_t count, void *const *dst, void *stream);
 /* Uploads the Q8 (I8) or Q4 (U8, two codes per byte) matrix `name` and its "<name>.scale" f32 blob as nn::mat_named
  * reads them (nn.cpp:132-145) and dequantises it on the device into dst [rows][cols] (out_dtype F32 or BF16),

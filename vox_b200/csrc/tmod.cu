@@ -6,10 +6,11 @@
 // with a GPU, copies every weight into video memory (upload_parts, gpu_vulkan.cpp:476-536), Q8/Q4 matrices as codes
 // plus a "<name>.scale" f32 blob (nn::mat_named, nn.cpp:132-145).
 //
-// Here the file is mapped read-only; a blob goes to the device through a ring of pinned staging buffers owned by the
-// handle: host threads copy chunk i of the mapping into a free staging buffer while the copy engine moves chunk i-1
-// to the device (cudaMemcpyAsync, one per chunk, on the caller's stream), so disk/page-cache reads, host copies and
-// PCIe transfers overlap. Q8/Q4 matrices can be dequantised on arrival (vox_cuda_tmod_upload_dequant), bit-exact with
+// Here the file is mapped read-only and, on the first upload, page-locked for the device (read-only host
+// registration): each blob is then one cudaMemcpyAsync straight from the mapping, no host copy. Where registration is
+// not available a ring of pinned staging buffers owned by the handle is used instead: host threads copy chunk i of
+// the mapping into a free staging buffer while the copy engine moves chunk i-1 to the device, so page-cache reads,
+// host copies and PCIe transfers overlap. Q8/Q4 matrices can be dequantised on arrival (vox_cuda_tmod_upload_dequant), bit-exact with
 // mat_row. The manifest is read by a small JSON reader that accepts the whole JSON grammar (the manifest carries model
 // configuration besides the blob table) and keeps only the blob table.
 #include <fcntl.h>
@@ -17,6 +18,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -44,14 +46,15 @@ struct vox_cuda_tmod {
     std::vector<void *> stage;
     std::vector<cudaEvent_t> done;
     int device = -1;
+    bool registered = false;  // the mapping is page-locked for the device: blobs are copied from it directly
 };
 
 namespace voxcuda {
 namespace {
 
-constexpr size_t kStageBytes = size_t(16) << 20;  // one staging buffer
+constexpr size_t kStageBytes = size_t(32) << 20;  // one staging buffer
 constexpr int kStages = 4;
-constexpr int kCopyThreads = 4;                    // host threads per staging copy
+constexpr int kCopyThreads = 8;                    // host threads per staging copy
 
 // ------------------------------------------------------------------ JSON (RFC 8259) reader, values kept as needed
 struct Json {
@@ -290,12 +293,26 @@ int parse(vox_cuda_tmod &t) {
     return VOX_CUDA_OK;
 }
 
-// The handle's staging ring on the current device (created on first use).
+// The handle's transfer path on the current device, set up on first use: the mapping itself page-locked for the
+// device (read-only registration; copies then go straight from the page cache, no host copy), or, where that is not
+// supported or VOX_CUDA_TMOD_REGISTER=0, the pinned staging ring.
 int ensure_stage(vox_cuda_tmod &t) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("vox_cuda_tmod_upload");
-    if (!t.stage.empty() && t.device == dev) return VOX_CUDA_OK;
-    if (!t.stage.empty()) return set_error(VOX_CUDA_ERR_ARG, "vox_cuda_tmod_upload: the handle's first upload used another device");
+    if ((!t.stage.empty() || t.registered) && t.device == dev) return VOX_CUDA_OK;
+    if (!t.stage.empty() || t.registered)
+        return set_error(VOX_CUDA_ERR_ARG, "vox_cuda_tmod_upload: the handle's first upload used another device");
+    const char *env = std::getenv("VOX_CUDA_TMOD_REGISTER");
+    int ro = 0;
+    if (t.size > 0 && !(env && env[0] == '0') && cudaDeviceGetAttribute(&ro, cudaDevAttrHostRegisterReadOnlySupported, dev) == cudaSuccess &&
+        ro) {
+        if (cudaHostRegister(const_cast<uint8_t *>(t.map), t.size, cudaHostRegisterReadOnly) == cudaSuccess) {
+            t.registered = true;
+            t.device = dev;
+            return VOX_CUDA_OK;
+        }
+        cudaGetLastError();  // not available for this mapping: use the staging ring
+    }
     for (int i = 0; i < kStages; ++i) {
         void *p = nullptr;
         cudaEvent_t ev;
@@ -392,6 +409,10 @@ int vox_cuda_tmod_open(const char *path, vox_cuda_tmod **out) {
 
 void vox_cuda_tmod_close(vox_cuda_tmod *t) {
     if (!t) return;
+    if (t->registered) {  // copies from the mapping may still be in flight on the caller's streams
+        cudaDeviceSynchronize();
+        cudaHostUnregister(const_cast<uint8_t *>(t->map));
+    }
     for (auto ev : t->done) {
         cudaEventSynchronize(ev);
         cudaEventDestroy(ev);
@@ -444,6 +465,12 @@ int vox_cuda_tmod_upload(vox_cuda_tmod *t, const char *const *names, int64_t cou
         const auto *b = find(t, names[i]);
         if (!b) return set_error(VOX_CUDA_ERR_FORMAT, std::string("missing blob in .tmod: ") + (names[i] ? names[i] : "(null)"));
         VOX_REQUIRE(dst[i] != nullptr || b->nbytes == 0, "vox_cuda_tmod_upload: NULL destination");
+        if (t->registered) {
+            if (b->nbytes && cudaMemcpyAsync(dst[i], t->map + b->offset, b->nbytes, cudaMemcpyHostToDevice,
+                                             reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+                return check_launch("vox_cuda_tmod_upload");
+            continue;
+        }
         rc = staged_copy(*t, dst[i], t->map + b->offset, b->nbytes, reinterpret_cast<cudaStream_t>(stream), slot);
         if (rc != VOX_CUDA_OK) return rc;
     }

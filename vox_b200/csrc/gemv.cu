@@ -547,6 +547,178 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
     if (clustered) cg::this_cluster().sync();
 }
 
+// The same arithmetic with the rows and the scales staged by tensor copies (no registers held for bytes in flight,
+// no load latency inside the loop): a warp streams its 512-byte chunk of the CTA's 32 rows as four copies of 8 rows
+// (three in flight) and the chunk's block scales of the 32 rows as one copy issued with the chunk's first rows.
+constexpr int kRowBatch = 8;              // rows per tensor copy
+constexpr int kRowStages = 3;             // copies in flight per warp
+constexpr int kRowBox = kRowBatch * 512;  // 4 KB
+template <bool SF16> __host__ __device__ constexpr int scale_box() { return kCcRows * 16 * (SF16 ? 2 : 4); }
+template <bool SF16> __host__ __device__ constexpr size_t rows_smem() {
+    return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<SF16>()) + 128;  // + alignment slack
+}
+
+template <bool SF16, int M>
+__global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                                 const __grid_constant__ CUtensorMap smap, GemvArgs a, int C) {
+    using ST = typename std::conditional<SF16, __half, float>::type;
+    constexpr int SB = scale_box<SF16>();
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    __shared__ float red[kWarps][M][kCcRows];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *wbar = reinterpret_cast<uint64_t *>(smem) + warp * kRowStages;
+    uint8_t *wring = smem + 256 + size_t(warp) * (kRowStages * kRowBox + 2 * SB);
+    uint8_t *sring = wring + kRowStages * kRowBox;  // two chunks' scales
+    const int crank = int(blockIdx.x) % C;
+    const int row0 = int(blockIdx.x / C) * kCcRows;  // rows < 2^31 (launcher)
+    const int64_t rowbytes = a.cols;
+    const int nchunk = int((rowbytes + 511) / 512);
+    const int c0 = crank * kWarps + warp, cstep = kWarps * C;
+    const int nmine = c0 < nchunk ? (nchunk - c0 + cstep - 1) / cstep : 0;  // chunks of this warp
+    const int units = nmine * (kCcRows / kRowBatch);                         // one unit = one copy of 8 rows
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kRowStages; ++s) mbar_init(&wbar[s], 1);
+        mbar_init_fence();
+    }
+    __syncwarp();
+    pdl_enter();
+    // unit u: chunk k = u / 4 (c0 + k cstep), rows row0 + 8 (u % 4) .. + 7, into stage u % kRowStages; the first unit
+    // of a chunk also brings the chunk's scales of the 32 rows into scale buffer k % 2
+    auto issue = [&](int u) {
+        if (lane == 0) {
+            const int s = u % kRowStages, k = u / 4, ci = c0 + k * cstep;
+            const bool with_scales = u % 4 == 0;
+            mbar_arrive_expect_tx(&wbar[s], kRowBox + (with_scales ? SB : 0));
+            tensor_g2s_2d(wring + s * kRowBox, &wmap, ci * 128, row0 + (u % 4) * kRowBatch, &wbar[s]);
+            if (with_scales) tensor_g2s_2d(sring + (k & 1) * SB, &smap, ci * 16, row0, &wbar[s]);
+        }
+    };
+    for (int u = 0; u < kRowStages && u < units; ++u) issue(u);
+    float tot[kCcRows / kRowBatch][M];
+#pragma unroll
+    for (int b = 0; b < kCcRows / kRowBatch; ++b)
+#pragma unroll
+        for (int t = 0; t < M; ++t) tot[b][t] = 0.f;
+    uint32_t parity = 0;
+    bool ok = true;
+    for (int k = 0; k < nmine && ok; ++k) {
+        const int64_t cb = int64_t(c0 + k * cstep) * 512 + lane * 16;  // this lane's 16 bytes of every row
+        const bool valid = cb < rowbytes;
+        float2 xv[M][8];
+#pragma unroll
+        for (int t = 0; t < M; ++t)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + cb) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[t][2 * q] = make_float2(v.x, v.y);
+                xv[t][2 * q + 1] = make_float2(v.z, v.w);
+            }
+        const ST *scs = reinterpret_cast<const ST *>(sring + (k & 1) * SB) + (lane >> 1);  // [32 rows][16 blocks]
+#pragma unroll 1
+        for (int b = 0; b < kCcRows / kRowBatch; ++b) {
+            const int u = k * 4 + b, s = u % kRowStages;
+            if (!mbar_wait_warp(&wbar[s], (parity >> s) & 1u)) {
+                ok = false;
+                break;
+            }
+            parity ^= 1u << s;
+            const uint8_t *st = wring + s * kRowBox + lane * 16;
+            float acc[kRowBatch][M];
+#pragma unroll
+            for (int r = 0; r < kRowBatch; ++r) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(st + r * 512);
+                const float sc = float(scs[(b * kRowBatch + r) * 16]);
+                const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+                float2 p[M][2];
+#pragma unroll
+                for (int t = 0; t < M; ++t) p[t][0] = p[t][1] = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float2 c01, c23;
+                    q8_to_f32(wd[i], c01, c23);
+#pragma unroll
+                    for (int t = 0; t < M; ++t) {
+                        p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                        p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < M; ++t) {
+                    const float2 q = __fadd2_rn(p[t][0], p[t][1]);
+                    acc[r][t] = (q.x + q.y) * sc;
+                }
+            }
+            __syncwarp();
+            if (u + kRowStages < units) {
+                if (lane == 0) fence_proxy_async();  // this stage's (and the older scale buffer's) reads precede the refill
+                issue(u + kRowStages);
+            }
+            // transpose butterfly over lane bits 2..0 (lane l keeps row l % 8), then a plain sum over bits 3, 4
+#pragma unroll
+            for (int t = 0; t < M; ++t) {
+#pragma unroll
+                for (int sh = kRowBatch / 2; sh >= 1; sh >>= 1) {
+                    const bool up = (lane & sh) != 0;
+#pragma unroll
+                    for (int j = 0; j < sh; ++j) {
+                        const float send = up ? acc[j][t] : acc[j + sh][t];
+                        const float keep = up ? acc[j + sh][t] : acc[j][t];
+                        acc[j][t] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
+                    }
+                }
+                float v = acc[0][t];
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+#pragma unroll
+                for (int bb = 0; bb < kCcRows / kRowBatch; ++bb) tot[bb][t] += b == bb ? v : 0.f;
+            }
+        }
+    }
+    if (!ok) {
+        // let the warp's copies in flight land (bounded) before the CTA's shared memory can be reused
+        for (int s = 0; s < kRowStages; ++s) mbar_wait_warp(&wbar[s], (parity >> s) & 1u);
+    }
+    if (lane < kRowBatch) {
+#pragma unroll
+        for (int b = 0; b < kCcRows / kRowBatch; ++b)
+#pragma unroll
+            for (int t = 0; t < M; ++t) red[warp][t][b * kRowBatch + lane] = tot[b][t];
+    }
+    __syncthreads();
+    float *cta = &red[0][0][0];
+    if (threadIdx.x < M * kCcRows) {
+        const int t = threadIdx.x / kCcRows, r = threadIdx.x % kCcRows;
+        float v = red[0][t][r];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) v += red[w][t][r];
+        cta[t * kCcRows + r] = v;
+    }
+    const bool clustered = C > 1;
+    if (clustered) cg::this_cluster().sync();
+    else __syncthreads();
+    const int lo_r = crank * kCcRows / C, hi_r = (crank + 1) * kCcRows / C, span = hi_r - lo_r;
+    if (threadIdx.x < M * span) {
+        const int t = threadIdx.x / span, r = lo_r + threadIdx.x % span;
+        const int64_t grow = row0 + r;
+        if (t < a.m && grow < a.rows) {
+            float v;
+            if (clustered) {
+                cg::cluster_group cl = cg::this_cluster();
+                v = 0.f;
+                for (int q = 0; q < C; ++q) v += cl.map_shared_rank(cta, q)[t * kCcRows + r];
+            } else {
+                v = cta[t * kCcRows + r];
+            }
+            float *yp = a.y + int64_t(t) * a.ystride + grow;
+            const float out = (a.bias ? __ldg(a.bias + grow) : 0.f) + v;
+            *yp = a.accumulate ? *yp + out : out;
+        }
+    }
+    if (clustered) cg::this_cluster().sync();
+}
+
 struct GemvPlan {
     int C = 0;
     size_t smem = 0;
@@ -711,14 +883,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// The 2-D tensor map of a weight matrix (uint8 elements, [rows][rowbytes], box 32 rows x 128 bytes, 128-byte
-// swizzle, zero fill past the edges), cached per device, address and shape.
-int weight_map(const uint8_t *w, int64_t rows, int64_t rowbytes, CUtensorMap &map, const char *name) {
+// The 2-D tensor maps of a weight matrix, cached per device, address, shape and layout (zero fill past the edges):
+//   kMmaBoxes: uint8 elements [rows][rowbytes], box 16 rows x 128 bytes, 128-byte swizzle (the MMA path's fragments);
+//   kRowBoxes: 4-byte elements [rows][rowbytes / 4], box 8 rows x 512 bytes (the CUDA-core path reads rows in order);
+//   kScaleBoxes: the block scales [rows][nblk] (2- or 4-byte elements, esize), box 32 rows x 16 blocks.
+enum MapKind { kMmaBoxes = 0, kRowBoxes = 1, kScaleBoxes = 2 };
+int weight_map(const void *base, int64_t rows, int64_t width, int kind, int esize, CUtensorMap &map, const char *name) {
     static std::mutex mu;
-    static std::map<std::tuple<int, const void *, int64_t, int64_t>, CUtensorMap> cache;
+    static std::map<std::tuple<int, const void *, int64_t, int64_t, int, int>, CUtensorMap> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return check_launch(name);
-    const auto key = std::make_tuple(dev, static_cast<const void *>(w), rows, rowbytes);
+    const auto key = std::make_tuple(dev, base, rows, width, kind, esize);
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -727,16 +902,100 @@ int weight_map(const uint8_t *w, int64_t rows, int64_t rowbytes, CUtensorMap &ma
     }
     auto fn = encode_fn();
     if (!fn) return set_error(VOX_CUDA_ERR_DEVICE, std::string(name) + ": cuTensorMapEncodeTiled is not available");
-    const cuuint64_t dims[2] = {cuuint64_t(rowbytes), cuuint64_t(rows)};
-    const cuuint64_t strides[1] = {cuuint64_t(rowbytes)};
-    const cuuint32_t box[2] = {cuuint32_t(kChunkBytes), cuuint32_t(kWarpRows)};
+    // width: bytes per row (kMmaBoxes, kRowBoxes) or elements per row (kScaleBoxes)
+    cuuint64_t dims[2], strides[1];
+    cuuint32_t box[2];
+    CUtensorMapDataType dt;
+    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (kind == kMmaBoxes) {
+        dims[0] = cuuint64_t(width), strides[0] = cuuint64_t(width), box[0] = kChunkBytes, box[1] = kWarpRows;
+        dt = CU_TENSOR_MAP_DATA_TYPE_UINT8, sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    } else if (kind == kRowBoxes) {
+        dims[0] = cuuint64_t(width / 4), strides[0] = cuuint64_t(width), box[0] = 128, box[1] = 8;
+        dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    } else {
+        dims[0] = cuuint64_t(width), strides[0] = cuuint64_t(width * esize), box[0] = 16, box[1] = 32;
+        dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    }
+    dims[1] = cuuint64_t(rows);
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = fn(&map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(VOX_CUDA_ERR_ARG, std::string(name) + ": weight tensor map rejected (code " + std::to_string(int(r)) + ")");
     if (cache.size() > 4096) cache.clear();  // bounded: weights are long-lived, so the map rarely refills
     cache[key] = map;
+    return VOX_CUDA_OK;
+}
+
+// Tensor-copy staging of the CUDA-core path (VOX_CUDA_GEMV_TMA=0 keeps the register-staged kernel, for comparisons).
+bool tma_rows_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("VOX_CUDA_GEMV_TMA");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <bool SF16, int M>
+int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
+    auto kern = gemv_rows_kernel<SF16, M>;
+    static std::mutex mu;
+    static std::map<std::tuple<int, int64_t, int64_t>, int> plans;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch(name);
+    int C = 1;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        const auto key = std::make_tuple(dev, a.rows, a.cols);
+        auto it = plans.find(key);
+        if (it != plans.end()) {
+            C = it->second;
+        } else {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(rows_smem<SF16>())) != cudaSuccess)
+                return check_launch(name);
+            const int64_t groups = (a.rows + kCcRows - 1) / kCcRows, nchunk = (a.cols + 511) / 512;
+            int64_t c = resident_blocks((const void *)kern, kThreads, rows_smem<SF16>()) / groups;
+            if (c > nchunk / kWarps) c = nchunk / kWarps;
+            C = int(c < 1 ? 1 : c > 8 ? 8 : c);
+            while (C > 1) {  // all clusters co-resident
+                cudaLaunchConfig_t q = {};
+                cudaLaunchAttribute at;
+                at.id = cudaLaunchAttributeClusterDimension;
+                at.val.clusterDim.x = unsigned(C), at.val.clusterDim.y = 1, at.val.clusterDim.z = 1;
+                q.gridDim = dim3(unsigned(groups * C)), q.blockDim = dim3(kThreads), q.dynamicSmemBytes = rows_smem<SF16>();
+                q.attrs = &at, q.numAttrs = 1;
+                int clusters = 0;
+                if (cudaOccupancyMaxActiveClusters(&clusters, kern, &q) == cudaSuccess && clusters > 0) break;
+                cudaGetLastError();
+                --C;
+            }
+            plans[key] = C;
+        }
+    }
+    CUtensorMap wmap, smap;
+    int rc = weight_map(a.w, a.rows, a.cols, kRowBoxes, 1, wmap, name);
+    if (rc == VOX_CUDA_OK) rc = weight_map(a.scale, a.rows, a.nblk, kScaleBoxes, SF16 ? 2 : 4, smap, name);
+    if (rc != VOX_CUDA_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    cfg.gridDim = dim3(unsigned((a.rows + kCcRows - 1) / kCcRows * C));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = rows_smem<SF16>();
+    cfg.stream = st;
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = unsigned(C);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    if (cudaLaunchKernelEx(&cfg, kern, wmap, smap, a, C) != cudaSuccess) return check_launch(name);
     return VOX_CUDA_OK;
 }
 
@@ -745,7 +1004,7 @@ int launch_gemv(const GemvArgs &base, int64_t m_total, cudaStream_t st, const ch
     if ((base.rows + kRows - 1) / kRows * kMaxCluster > int64_t(0x7FFFFFFF) || base.rows + kRows > int64_t(0x7FFFFFFF))
         return set_error(VOX_CUDA_ERR_ARG, std::string(name) + ": too many rows");
     CUtensorMap wmap;
-    int rc = weight_map(base.w, base.rows, Q4 ? base.cols / 2 : base.cols, wmap, name);
+    int rc = weight_map(base.w, base.rows, Q4 ? base.cols / 2 : base.cols, kMmaBoxes, 1, wmap, name);
     if (rc != VOX_CUDA_OK) return rc;
     auto kern = gemv_kernel<Q4, SF16>;
     for (int64_t i0 = 0; i0 < m_total; i0 += kTok) {  // activation rows in launches of 8
@@ -753,10 +1012,14 @@ int launch_gemv(const GemvArgs &base, int64_t m_total, cudaStream_t st, const ch
         a.m = int(m_total - i0 < kTok ? m_total - i0 : kTok);
         a.x = base.x + i0 * base.cols;
         a.y = base.y + i0 * base.ystride;
-        if (!Q4 && a.m <= 2) {  // Q8, one or two rows: the CUDA-core path (measured faster; Q4 stays on the MMA path)
-            rc = a.m == 1 ? launch_cc<Q4, SF16, 1>(a, st, name) : launch_cc<Q4, SF16, 2>(a, st, name);
-            if (rc != VOX_CUDA_OK) return rc;
-            continue;
+        if constexpr (!Q4) {  // Q8 with one or two rows: the CUDA-core path (measured faster; Q4 stays on the MMA path)
+            if (a.m <= 2) {
+                const bool staged = (a.nblk * (SF16 ? 2 : 4)) % 16 == 0 && aligned16(a.scale) && tma_rows_enabled();
+                if (staged) rc = a.m == 1 ? launch_rows<SF16, 1>(a, st, name) : launch_rows<SF16, 2>(a, st, name);
+                else rc = a.m == 1 ? launch_cc<Q4, SF16, 1>(a, st, name) : launch_cc<Q4, SF16, 2>(a, st, name);
+                if (rc != VOX_CUDA_OK) return rc;
+                continue;
+            }
         }
         GemvPlan plan;
         rc = plan_gemv<Q4, SF16>(base.rows, base.nblk, a.m, plan, name);

@@ -16,6 +16,8 @@
 // 1e-5 (f32) and 1e-2 (bf16) tolerances, for about half the instructions.
 #include <math.h>
 
+#include <cstdlib>
+
 #include "rows.cuh"
 #include "tma.cuh"
 #include "sfu.cuh"
@@ -158,6 +160,182 @@ struct NormOp {
         }
     }
 };
+
+// Gated adaLN with the batch's parameters folded once per CTA. y = res + g * ((x - mean) / sigma * (1 + s) + h)
+// = res + A * n + C with A = g * (1 + s), C = g * h (f5.cpp:630, 674 regrouped; n = (x - mean) / sigma). A CTA takes a
+// contiguous range of rows, so all its rows but those past a batch boundary share one batch: it computes that batch's
+// A and C once into shared memory (f32), and each row's epilogue is one FMA and one add per element instead of
+// unpacking three parameter vectors. Rows of a second batch in the range take NormOp's epilogue (parameters from
+// global memory). Staging, waits and statistics are those of the row pipeline.
+template <int DT, int VPL>
+__global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_kernel(NormArgs a, uint32_t row_bytes) {
+    constexpr int STAGES = kStages;
+    constexpr int W = Vec<DT>::N, PW = W / 2;
+    constexpr int ES = DT == VOX_CUDA_F32 ? 4 : 2;
+    pdl_enter();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t stage_bytes = 2 * row_bytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * STAGES;
+    uint8_t *bufs = smem + pipe_bar_bytes(STAGES) + size_t(warp) * STAGES * stage_bytes;
+    float *ac = reinterpret_cast<float *>(smem + pipe_bar_bytes(STAGES) + size_t(kPipeWarps) * STAGES * stage_bytes);  // A[n], C[n]
+    const int64_t r0 = a.rows * int64_t(blockIdx.x) / gridDim.x, r1 = a.rows * int64_t(blockIdx.x + 1) / gridDim.x;
+    const int nvec = int(a.n / W);
+    auto issue = [&](int64_t r, uint8_t *buf, uint64_t *bar) {
+        mbar_arrive_expect_tx(bar, 2 * row_bytes);
+        bulk_g2s(buf, reinterpret_cast<const char *>(a.x) + r * int64_t(row_bytes), row_bytes, bar);
+        bulk_g2s(buf + row_bytes, reinterpret_cast<const char *>(a.res) + r * int64_t(row_bytes), row_bytes, bar);
+    };
+    // this warp's rows: r0 + warp, r0 + warp + kPipeWarps, ...
+    const int64_t first = r0 + warp;
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        mbar_init_fence();
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+            if (first + s * kPipeWarps < r1) issue(first + s * kPipeWarps, bufs + s * stage_bytes, &bars[s]);
+    }
+    uint32_t pending = 0;
+#pragma unroll
+    for (int t = 0; t < STAGES; ++t)
+        if (first + t * kPipeWarps < r1) pending |= 1u << t;
+    // A and C of the range's first batch, while the first rows are in flight
+    const int64_t batch0 = r0 < r1 ? int64_t(a.tdiv.div(uint32_t(r0))) : 0;
+    if (r0 < r1) {
+        const char *scp = reinterpret_cast<const char *>(a.scale) + batch0 * a.n * ES;
+        const char *shp = reinterpret_cast<const char *>(a.shift) + batch0 * a.n * ES;
+        const char *gp = reinterpret_cast<const char *>(a.gate) + batch0 * a.n * ES;
+        for (int v = threadIdx.x; v < nvec; v += kPipeWarps * 32) {
+            float2 sc[PW], sh[PW], gv[PW];
+            unpack2<DT>(ld_param(scp + v * 16), sc);
+            unpack2<DT>(ld_param(shp + v * 16), sh);
+            unpack2<DT>(ld_param(gp + v * 16), gv);
+#pragma unroll
+            for (int p = 0; p < PW; ++p) {
+                reinterpret_cast<float2 *>(ac)[v * PW + p] = mul2(gv[p], add2(bc2(1.0f), sc[p]));
+                reinterpret_cast<float2 *>(ac + a.n)[v * PW + p] = mul2(gv[p], sh[p]);
+            }
+        }
+    }
+    __syncthreads();
+    uint32_t parity = 0;
+    int s = 0;
+    for (int64_t r = first; r < r1; r += kPipeWarps) {
+        if (!mbar_wait_warp(&bars[s], (parity >> s) & 1u)) {
+            for (int t = 0; t < STAGES; ++t)
+                if (t != s && ((pending >> t) & 1u)) mbar_wait_warp(&bars[t], (parity >> t) & 1u);
+            return;
+        }
+        parity ^= 1u << s;
+        pending &= ~(1u << s);
+        uint8_t *buf = bufs + s * stage_bytes;
+        float2 xv[VPL][PW];
+        uint4 rres[VPL];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int j = lane + 32 * k;
+            const uint4 raw = j < nvec ? *reinterpret_cast<const uint4 *>(buf + j * 16) : make_uint4(0, 0, 0, 0);
+            unpack2<DT>(raw, xv[k]);
+            rres[k] = j < nvec ? *reinterpret_cast<const uint4 *>(buf + row_bytes + j * 16) : make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        const int64_t r_next = r + int64_t(STAGES) * kPipeWarps;
+        if (r_next < r1) {
+            if (lane == 0) {
+                fence_proxy_async();
+                issue(r_next, buf, &bars[s]);
+            }
+            pending |= 1u << s;
+        }
+        // two-pass mean / variance in f32 on the row in registers (as NormOp)
+        float2 sm = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPL; ++k)
+#pragma unroll
+            for (int p = 0; p < PW; ++p) sm = add2(sm, xv[k][p]);
+        const float meanf = warp_sum(__fadd_rn(sm.x, sm.y)) * a.inv_n;
+        const float2 negmean = bc2(-meanf);
+        float2 vv = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            if (lane + 32 * k < nvec) {
+#pragma unroll
+                for (int p = 0; p < PW; ++p) {
+                    const float2 d = add2(xv[k][p], negmean);
+                    vv = fma2(d, d, vv);
+                }
+            }
+        }
+        const float var = warp_sum(__fadd_rn(vv.x, vv.y)) * a.inv_n;
+        const float2 inv2 = bc2(rsqrtf(var + a.eps));
+        const float2 nmi = mul2(negmean, inv2);
+        const int64_t batch = int64_t(a.tdiv.div(uint32_t(r)));
+        char *yr = reinterpret_cast<char *>(a.y) + r * int64_t(row_bytes);
+        if (batch == batch0) {
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int j = lane + 32 * k;
+                if (j < nvec) {
+                    float2 rv[PW], o[PW];
+                    unpack2<DT>(rres[k], rv);
+                    const float2 *A = reinterpret_cast<const float2 *>(ac) + j * PW;
+                    const float2 *Cc = reinterpret_cast<const float2 *>(ac + a.n) + j * PW;
+#pragma unroll
+                    for (int p = 0; p < PW; ++p) o[p] = add2(fma2(A[p], fma2(xv[k][p], inv2, nmi), Cc[p]), rv[p]);
+                    st_stream(yr + j * 16, pack2<DT>(o));
+                }
+            }
+        } else {  // a row past the range's batch boundary: the parameters from global memory
+            const char *scp = reinterpret_cast<const char *>(a.scale) + batch * a.n * ES;
+            const char *shp = reinterpret_cast<const char *>(a.shift) + batch * a.n * ES;
+            const char *gp = reinterpret_cast<const char *>(a.gate) + batch * a.n * ES;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int j = lane + 32 * k;
+                if (j < nvec) {
+                    float2 sc[PW], sh[PW], gv[PW], rv[PW], o[PW];
+                    unpack2<DT>(ld_param(scp + j * 16), sc);
+                    unpack2<DT>(ld_param(shp + j * 16), sh);
+                    unpack2<DT>(ld_param(gp + j * 16), gv);
+                    unpack2<DT>(rres[k], rv);
+#pragma unroll
+                    for (int p = 0; p < PW; ++p) {
+                        const float2 A = mul2(gv[p], add2(bc2(1.0f), sc[p])), Cc = mul2(gv[p], sh[p]);
+                        o[p] = add2(fma2(A, fma2(xv[k][p], inv2, nmi), Cc), rv[p]);
+                    }
+                    st_stream(yr + j * 16, pack2<DT>(o));
+                }
+            }
+        }
+        s = (s + 1 == STAGES) ? 0 : s + 1;
+    }
+}
+
+// VOX_CUDA_ADALN_AC=0 keeps the gated adaLN on NormOp's epilogue (for comparisons).
+bool adaln_ac_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("VOX_CUDA_ADALN_AC");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <int DT, int VPL>
+int launch_adaln_ac(const NormArgs &a, cudaStream_t st, const char *name) {
+    const uint32_t row_bytes = uint32_t(a.n * (DT == VOX_CUDA_F32 ? 4 : 2));
+    const size_t smem = pipe_bar_bytes(kStages) + size_t(kPipeWarps) * kStages * 2 * row_bytes + size_t(a.n) * 8;
+    if (int64_t(smem) > smem_optin()) return kPipeNotApplicable;
+    auto kern = adaln_ac_kernel<DT, VPL>;
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return check_launch(name);
+    // one wave of CTAs, each a contiguous range of at least kPipeWarps rows
+    const int64_t resident = resident_blocks((const void *)kern, kPipeWarps * 32, smem);
+    const int64_t want = (a.rows + kPipeWarps - 1) / kPipeWarps;
+    const int g = int(want < resident ? want : resident);
+    launch_k(kern, g < 1 ? 1 : g, kPipeWarps * 32, smem, st, a, row_bytes);
+    return check_launch(name);
+}
 
 // Visible keys of row r: min(n, r % q_len + pos0 + 1); rows < 2^32 (launcher), q_len's division precomputed.
 __device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_len, const FastDiv &qdiv, int64_t pos0) {
@@ -370,6 +548,12 @@ int reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, cudaStream_t
 
 template <int DT, int KIND, int VPL>
 int norm_pipe_vpl(const NormArgs &a, cudaStream_t st, const char *name) {
+    if constexpr (KIND == kAdaLnGated && (DT == VOX_CUDA_F32 ? VPL <= 8 : VPL <= 4)) {  // rows held in registers
+        if (adaln_ac_enabled()) {
+            const int rc = launch_adaln_ac<DT, VPL>(a, st, name);
+            if (rc != kPipeNotApplicable) return rc;
+        }
+    }
     const uint32_t row_bytes = uint32_t(a.n * (DT == VOX_CUDA_F32 ? 4 : 2));
     const uint32_t stage = KIND == kAdaLnGated ? 2 * row_bytes : row_bytes;
     return launch_row_pipe<NormOp<DT, VPL, KIND>, kStages>(NormOp<DT, VPL, KIND>{a, row_bytes}, a.rows, stage, st, name);

@@ -305,6 +305,26 @@ def test_snake_layouts(vox, port, kind):
             assert_bitexact(got, want)
         else:
             assert np.all(np.abs(got - want) <= np.maximum(1e-5 * np.abs(want), 1e-6 * np.abs(x)) + 1e-30)
+
+
+@pytest.mark.parametrize("C", [6144, 6148])
+def test_snake_wide_channels(vox, port, C):
+    """Up to 6144 channels the (alpha, coef) pairs are folded into a per-CTA shared table; wider channel counts index
+    alpha per vector. Both sides of the limit, both layouts, HiFT (within f32 rounding) and Kokoro (bit-exact)."""
+    al = port.uniform_arr((C,), 0.2, 2.0, sid=133)
+    for shape, cm in (((2, C, 8), True), ((5, C), False)):
+        x = port.normal(shape, sid=134)
+        for kind in (0, 2):
+            want = port.snake(x, al, kind, None, inner=shape[-1] if cm else 1)
+            got = host(vox.snake(dev(x), dev(al), kind, channel_major=cm))
+            if kind == 2:
+                assert_bitexact(got, want)
+            else:
+                assert np.all(np.abs(got - want) <= np.maximum(1e-5 * np.abs(want), 1e-6 * np.abs(x)) + 1e-30)
+
+
+def test_snake_load_params(vox, port):
+    al = port.uniform_arr((12,), 0.2, 2.0, sid=130)
     a, b = vox.load_snake(dev(al), dev(al[::-1].copy()))
     pa, pb = port.load_snake(al, al[::-1].copy())
     assert_close(host(a)[None], pa[None])

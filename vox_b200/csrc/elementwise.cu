@@ -23,6 +23,7 @@
 //     2.5e-7 * |x|, the size of the difference between Vox's two CPU GELUs (std::erf vs nn::gelu_inplace).
 //   GELU (tanh form): tanh(z) = 1 - 2 / (1 + e^(2z)) with the SFU's ex2 and rcp (absolute error ~1e-7).
 //   SiLU: x / (1 + e^-x) with CUDA's expf and the 2-ulp division (relative error ~3e-7), as kernels.hpp:105.
+#include <algorithm>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -32,8 +33,14 @@ namespace voxcuda {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
-constexpr int kBlocksPerSm = 8;
+constexpr int kBlocksPerSm = 8;  // scalar paths
+// Vector paths: kUnroll 16-byte vectors per thread per pass and at most kPipeCtasPerSm (one-input ops, software-
+// pipelined) or kVecCtasPerSm (two-input ops) CTAs of kThreads per SM. Measured on B200 over 2^25-2^29 elements:
+// one-input ops at 2 vectors x 4 CTAs per SM reach 0.96-0.99 of the copy peak against 0.84-0.88 at 4 x 4, and
+// two-input ops at 2 x 3 reach 1.00-1.02 against 0.92-0.94 at 4 x 4; more CTAs or deeper passes stream worse.
+constexpr int kUnroll = 2;
+constexpr int kPipeCtasPerSm = 4;
+constexpr int kVecCtasPerSm = 3;
 
 // ------------------------------------------------------------------ scalar math shared by the ops
 
@@ -202,15 +209,36 @@ template <int DT> struct OpGated {
     }
 };
 
-// Snake with the channel of element e = (e / inner) % C.
+// Snake with the channel of element e = (e / inner) % C. On the pipelined path (map_vec_pipe_kernel) each CTA first
+// folds every channel's (arg, coef) pair into a shared-memory table when C <= kSnakeTableMax (ntab = C), so a vector
+// costs one shared load instead of a global load and a correctly rounded division; elsewhere tab stays NULL and the
+// pair is formed per vector. Both give the same bits.
+constexpr int64_t kSnakeTableMax = 6144;  // 48 KB of float2: the default dynamic shared-memory limit
 template <int KIND> struct OpSnake {
     const float *alpha, *beta;
     FastDiv vrow;  // vector path: vectors per `inner` run (inner % 4 == 0) or vectors per C (inner == 1)
     FastDiv chan;  // C
     int64_t C, inner;
-    int time_major;  // inner == 1
+    int time_major;             // inner == 1
+    int ntab = 0;               // channels in the per-CTA table (0: no table)
+    const float2 *tab = nullptr;  // (arg, coef) per channel in shared memory, set on the device by prepare_op
     template <int W> __device__ __forceinline__ void operator()(const float *x, const float *, float *y, int64_t e0) const {
-        if (W > 1) {
+        if (W > 1 && tab) {
+            const uint32_t v = uint32_t(e0 / W);
+            if (time_major) {  // W consecutive channels from c0 (a multiple of W): 16-byte aligned table reads
+                const float4 *t = reinterpret_cast<const float4 *>(tab + vrow.mod(v) * W);
+#pragma unroll
+                VOX_PAIRS(W) {
+                    const float4 p = t[k / 2];
+                    put(y, k, snake_pair<KIND>(pr(x, k), make_float2(p.x, p.z), make_float2(p.y, p.w)));
+                }
+            } else {
+                const float2 p = tab[chan.mod(vrow.div(v))];
+                const float2 arg = bc2(p.x), cf = bc2(p.y);
+#pragma unroll
+                VOX_PAIRS(W) put(y, k, snake_pair<KIND>(pr(x, k), arg, cf));
+            }
+        } else if (W > 1) {
             const uint32_t v = uint32_t(e0 / W);
             if (time_major) {
                 const int64_t c0 = int64_t(vrow.mod(v)) * W;
@@ -236,25 +264,44 @@ template <int KIND> struct OpSnake {
     }
 };
 
+// Per-CTA shared tables of the pipelined path: a no-op for every functor but Snake.
+template <class F> __device__ __forceinline__ void prepare_op(F &, float2 *) {}
+template <int KIND> __device__ __forceinline__ void prepare_op(OpSnake<KIND> &f, float2 *tab) {
+    if (f.ntab == 0) return;
+    for (int c = threadIdx.x; c < f.ntab; c += blockDim.x) {
+        const float al = __ldg(f.alpha + c);
+        tab[c] = make_float2(al, snake_coef<KIND>(al, KIND == VOX_CUDA_SNAKE_BETA ? __ldg(f.beta + c) : 0.f));
+    }
+    __syncthreads();
+    f.tab = tab;
+}
+template <class F> size_t op_table_bytes(const F &) { return 0; }
+template <int KIND> size_t op_table_bytes(const OpSnake<KIND> &f) { return size_t(f.ntab) * sizeof(float2); }
+
 // ------------------------------------------------------------------ kernels
 
-// Vector path: n / W 16-byte vectors, kUnroll of them in flight per thread per iteration (the last iteration
-// predicated, so a thread's remainder keeps its loads in flight together), then the n % W tail by block 0.
+// Vector paths. A launch covers at most kMaxLaunchVecs 16-byte vectors, so vector indices are 32-bit (no index
+// formed below exceeds nvec by more than 2 * kUnroll grid strides); the host splits longer tensors into launches
+// whose pointers start at the launch's first element and passes that element's index as `base`, which the functors
+// see added to e0. The n % W tail (last launch only) is mapped by block 0.
+constexpr int64_t kMaxLaunchVecs = int64_t(1) << 30;
+
+// Two-input ops: kUnroll vectors of each input in flight per thread per pass (the last pass predicated).
 template <int DT, int NIN, class F>
-__global__ void __launch_bounds__(kThreads, 4) map_vec_kernel(const void *a, const void *b, void *y, int64_t n, F f) {
+__global__ void __launch_bounds__(kThreads, kVecCtasPerSm) map_vec_kernel(const void *a, const void *b, void *y, int64_t n, int64_t base, F f) {
     pdl_enter();
     using V = Vec<DT>;
     constexpr int W = V::N;
-    const int64_t nvec = n / W;
-    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    const uint32_t nvec = uint32_t(n / W);
+    const uint32_t stride = gridDim.x * blockDim.x;
     const uint4 *pa = reinterpret_cast<const uint4 *>(a);
     const uint4 *pb = reinterpret_cast<const uint4 *>(b);
     uint4 *py = reinterpret_cast<uint4 *>(y);
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += kUnroll * stride) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += kUnroll * stride) {
         uint4 ra[kUnroll], rb[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const int64_t j = i + u * stride;
+            const uint32_t j = i + u * stride;
             if (j < nvec) {
                 ra[u] = ld_stream(pa + j);
                 if (NIN == 2) rb[u] = ld_stream(pb + j);
@@ -262,69 +309,71 @@ __global__ void __launch_bounds__(kThreads, 4) map_vec_kernel(const void *a, con
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const int64_t j = i + u * stride;
+            const uint32_t j = i + u * stride;
             if (j < nvec) {
                 float fa[W], fb[W], fy[W];
                 V::unpack(ra[u], fa);
                 if (NIN == 2) V::unpack(rb[u], fb);
-                f.template operator()<W>(fa, fb, fy, j * W);
+                f.template operator()<W>(fa, fb, fy, base + int64_t(j) * W);
                 st_stream(py + j, V::pack(fy));
             }
         }
     }
-    const int64_t tail = n - nvec * W;
+    const int64_t tail = n - int64_t(nvec) * W;
     if (blockIdx.x == 0 && int64_t(threadIdx.x) < tail) {
-        const int64_t e = nvec * W + threadIdx.x;
+        const int64_t e = int64_t(nvec) * W + threadIdx.x;
         float fa[1], fb[1] = {0.f}, fy[1];
         fa[0] = V::load1(a, e);
         if (NIN == 2) fb[0] = V::load1(b, e);
-        f.template operator()<1>(fa, fb, fy, e);
+        f.template operator()<1>(fa, fb, fy, base + e);
         V::store1(y, e, fy[0]);
     }
 }
 
-// Vector path for one-input ops (GELU, Snake, bias-add), software-pipelined: the loads of a thread's next pass are
-// issued before the current pass is computed, so the arithmetic of one pass overlaps the memory latency of the next
-// (these ops carry the most instructions per byte of the library).
+// One-input ops (GELU, Snake, bias-add), software-pipelined: the loads of a thread's next pass are issued before the
+// current pass is computed, so the arithmetic of one pass overlaps the memory latency of the next (these ops carry
+// the most instructions per byte of the library).
 template <int DT, class F>
-__global__ void __launch_bounds__(kThreads, 3) map_vec_pipe_kernel(const void *a, void *y, int64_t n, F f) {
+__global__ void __launch_bounds__(kThreads, kPipeCtasPerSm) map_vec_pipe_kernel(const void *a, void *y, int64_t n, int64_t base, F f) {
     pdl_enter();
+    extern __shared__ float2 map_op_table[];
+    prepare_op(f, map_op_table);
     using V = Vec<DT>;
     constexpr int W = V::N;
-    const int64_t nvec = n / W;
-    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    const uint32_t nvec = uint32_t(n / W);
+    const uint32_t stride = gridDim.x * blockDim.x;
     const uint4 *pa = reinterpret_cast<const uint4 *>(a);
     uint4 *py = reinterpret_cast<uint4 *>(y);
-    int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     uint4 cur[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u)
         if (i + u * stride < nvec) cur[u] = ld_stream(pa + i + u * stride);
     for (; i < nvec; i += kUnroll * stride) {
-        const int64_t inext = i + kUnroll * stride;
+        const uint32_t inext = i + kUnroll * stride;
         uint4 nxt[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u)
             if (inext + u * stride < nvec) nxt[u] = ld_stream(pa + inext + u * stride);
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const int64_t j = i + u * stride;
+            const uint32_t j = i + u * stride;
             if (j < nvec) {
                 float fa[W], fy[W];
                 V::unpack(cur[u], fa);
-                f.template operator()<W>(fa, fa, fy, j * W);
+                f.template operator()<W>(fa, fa, fy, base + int64_t(j) * W);
                 st_stream(py + j, V::pack(fy));
             }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) cur[u] = nxt[u];
     }
-    const int64_t tail = n - nvec * W;
+    const int64_t tail = n - int64_t(nvec) * W;
     if (blockIdx.x == 0 && int64_t(threadIdx.x) < tail) {
-        const int64_t e = nvec * W + threadIdx.x;
+        const int64_t e = int64_t(nvec) * W + threadIdx.x;
         float fa[1], fy[1];
         fa[0] = V::load1(a, e);
-        f.template operator()<1>(fa, fa, fy, e);
+        f.template operator()<1>(fa, fa, fy, base + e);
         V::store1(y, e, fy[0]);
     }
 }
@@ -357,18 +406,29 @@ template <int DT, int NIN, class F>
 int launch_map(const void *a, const void *b, void *y, int64_t n, F f, bool vec_ok, cudaStream_t st, const char *name) {
     if (n == 0) return VOX_CUDA_OK;
     constexpr int W = Vec<DT>::N;
+    constexpr int64_t esize = DT == VOX_CUDA_F32 ? 4 : 2;
+    // the functors index per-vector parameters with 32-bit vector indices
     vec_ok = vec_ok && aligned16(a) && aligned16(y) && (NIN == 1 || aligned16(b)) && n / W < (int64_t(1) << 32);
-    if (vec_ok && NIN == 1 && map_pipe_enabled()) {
-        auto kern = map_vec_pipe_kernel<DT, F>;
-        const int g = balanced_grid(n / W, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
-        launch_k(kern, g, kThreads, 0, st, a, y, n, f);
-    } else if (vec_ok) {
-        auto kern = map_vec_kernel<DT, NIN, F>;
-        const int g = balanced_grid(n / W, int64_t(kThreads) * kUnroll, resident_blocks((const void *)kern, kThreads, 0));
-        launch_k(kern, g, kThreads, 0, st, a, b, y, n, f);
-    } else {
+    if (!vec_ok) {
         const int g = grid_for(n, kThreads, kBlocksPerSm);
         launch_k(map_scalar_kernel<DT, NIN, F>, g, kThreads, 0, st, a, b, y, n, f);
+        return check_launch(name);
+    }
+    const bool pipe = NIN == 1 && map_pipe_enabled();
+    const void *kern = pipe ? (const void *)map_vec_pipe_kernel<DT, F> : (const void *)map_vec_kernel<DT, NIN, F>;
+    const size_t smem = pipe ? op_table_bytes(f) : 0;
+    const int cap = (pipe ? kPipeCtasPerSm : kVecCtasPerSm) * sm_count();
+    const int resident = std::min(resident_blocks(kern, kThreads, smem), cap);
+    const int64_t nvec = n / W;
+    for (int64_t v0 = 0; v0 == 0 || v0 < nvec; v0 += kMaxLaunchVecs) {
+        const int64_t nv = std::min(kMaxLaunchVecs, nvec - v0);
+        const int64_t e0 = v0 * W, ne = v0 + nv == nvec ? n - e0 : nv * W;  // the last launch takes the tail
+        const char *ca = static_cast<const char *>(a) + e0 * esize;
+        const char *cb = NIN == 2 ? static_cast<const char *>(b) + e0 * esize : nullptr;
+        char *cy = static_cast<char *>(y) + e0 * esize;
+        const int g = balanced_grid(std::max<int64_t>(nv, 1), int64_t(kThreads) * kUnroll, resident);
+        if (pipe) launch_k(map_vec_pipe_kernel<DT, F>, g, kThreads, smem, st, (const void *)ca, (void *)cy, ne, e0, f);
+        else launch_k(map_vec_kernel<DT, NIN, F>, g, kThreads, 0, st, (const void *)ca, (const void *)cb, (void *)cy, ne, e0, f);
     }
     return check_launch(name);
 }
@@ -426,6 +486,7 @@ __global__ void snake_params_kernel(const float *alpha, const float *beta, float
 }
 
 }  // namespace
+
 }  // namespace voxcuda
 
 using namespace voxcuda;
@@ -496,17 +557,15 @@ int vox_cuda_snake(const float *x, const float *alpha, const float *beta, float 
     vec_ok = vec_ok && (time_major ? C / 4 : inner / 4) < (int64_t(1) << 32) && C < (int64_t(1) << 32);
     FastDiv vrow(vec_ok ? uint32_t(time_major ? C / 4 : inner / 4) : 1u), chan(uint32_t(C < (int64_t(1) << 32) ? C : 1));
     const int tm = time_major ? 1 : 0;
+    const int ntab = vec_ok && C <= kSnakeTableMax ? int(C) : 0;
+    auto run = [&](auto op) {
+        op.ntab = ntab;
+        return dispatch_map<1>(VOX_CUDA_F32, x, nullptr, y, n, op, vec_ok, stream, "vox_cuda_snake");
+    };
     switch (kind) {
-        case VOX_CUDA_SNAKE_HIFT:
-            return dispatch_map<1>(VOX_CUDA_F32, x, nullptr, y, n, OpSnake<VOX_CUDA_SNAKE_HIFT>{alpha, beta, vrow, chan, C, inner, tm},
-                                   vec_ok, stream, "vox_cuda_snake");
-        case VOX_CUDA_SNAKE_BETA:
-            return dispatch_map<1>(VOX_CUDA_F32, x, nullptr, y, n, OpSnake<VOX_CUDA_SNAKE_BETA>{alpha, beta, vrow, chan, C, inner, tm},
-                                   vec_ok, stream, "vox_cuda_snake");
-        default:
-            return dispatch_map<1>(VOX_CUDA_F32, x, nullptr, y, n,
-                                   OpSnake<VOX_CUDA_SNAKE_KOKORO>{alpha, beta, vrow, chan, C, inner, tm}, vec_ok, stream,
-                                   "vox_cuda_snake");
+        case VOX_CUDA_SNAKE_HIFT: return run(OpSnake<VOX_CUDA_SNAKE_HIFT>{alpha, beta, vrow, chan, C, inner, tm});
+        case VOX_CUDA_SNAKE_BETA: return run(OpSnake<VOX_CUDA_SNAKE_BETA>{alpha, beta, vrow, chan, C, inner, tm});
+        default: return run(OpSnake<VOX_CUDA_SNAKE_KOKORO>{alpha, beta, vrow, chan, C, inner, tm});
     }
 }
 

@@ -35,6 +35,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "HBM GB/s & % of B200 peak per op; elements/s at 1/2/4/8 GPUs vs host CPU"
 FALLBACK_HBM_GBS = 6650.0  # used only if MEASURED_PEAKS.json is absent
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0  # ditto
 
 
 def peaks() -> tuple[float, str]:
@@ -45,6 +46,16 @@ def peaks() -> tuple[float, str]:
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops_sustained"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_BF16_TFLOPS_SUSTAINED, "fallback"
 
 
 # ---------------------------------------------------------------------------------------------------- workload
@@ -64,11 +75,13 @@ class Suite:
         seed, c0 = 0, rank << 36  # shard k draws counters offset by k * 2^36: independent shards of one global batch
         fill = lambda t, d, a, b, sid: vox.fill_philox(t, d, a, b, seed=seed, stream_id=sid, counter0=c0)  # noqa: E731
         want = (lambda nm: re.search(only, nm) is not None) if only else (lambda nm: True)
-        ops, self.io = [], []
+        ops, self.io, self.flops, self.f5_plans = [], [], {}, []
 
-        def add(name, nbytes, elems, fn, reads, writes):
+        def add(name, nbytes, elems, fn, reads, writes, flops=None):
             ops.append((name, nbytes, elems, fn))
             self.io.append((reads, writes))
+            if flops:
+                self.flops[name] = flops
 
         # `scale` multiplies the rows / heads / batches of cfg1-cfg4 (1 = BASELINE's shapes; larger values measure the
         # kernels where their size does not limit them)
@@ -159,6 +172,34 @@ class Suite:
                     fn(mats[i], scs[i], gx[:mm], out=gy[:mm])
 
                 add(nm, wbytes + GR * (GC // 32) * 2 + mm * GC * 4 + mm * GR * 4, GR * GC * mm, call, [mats[0], scs[0], gx], [gy])
+        # F5-TTS DiT step (the transformer of gpu_f5_step, one CUDA graph): F5 base (dim 1024, 22 blocks of 16 heads x 64,
+        # ff 2048, mel 100) on 2 sequences (conditional and unconditional) of 1024 frames, seeded random weights; each step
+        # writes the residual stream and time embedding into the plan, then replays the graph
+        if any(want_next(f"next_f5_dit_{m}") for m in ("tf32", "bf16")):
+            D, H, HD, FFm, L, O, Bq, Nf = 1024, 16, 64, 2, 22, 100, 2, 1024
+            IN, FF, Rr = H * HD, FFm * D, Bq * Nf
+            gen = torch.Generator(device=dev).manual_seed(7)
+            W = lambda o, i, s=1.0: torch.randn(o, i, device=dev, generator=gen) * (s * i ** -0.5)  # noqa: E731
+            fblocks = [{"ada": W(6 * D, D, 0.3), "q": W(IN, D), "k": W(IN, D), "v": W(IN, D), "o": W(D, IN), "ff1": W(FF, D),
+                        "ff2": W(D, FF)} for _ in range(L)]
+            norm_out, proj_out = W(2 * D, D, 0.3), W(O, D)
+            h0, ts0 = fill(E(Rr, D), 1, 0, 1, 60), fill(E(D), 1, 0, 1, 61)
+            fl = L * (2 * 6 * D * D + 3 * 2 * Rr * D * IN + 2 * 2 * Bq * H * Nf * Nf * HD + 2 * Rr * IN * D + 2 * 2 * Rr * D * FF) \
+                + 2 * 2 * D * D + 2 * Rr * D * O
+            wbytes = 4 * (L * (6 * D * D + 4 * D * IN + 2 * D * FF) + 2 * D * D + O * D)
+            for m in ("tf32", "bf16"):
+                nm = f"next_f5_dit_{m}"
+                if not want_next(nm):
+                    continue
+                plan = vox.F5Dit(fblocks, norm_out, proj_out, heads=H, dim_head=HD, batch=Bq, frames=Nf, math=m)
+                self.f5_plans.append(plan)
+
+                def f5_step(plan=plan):
+                    plan.h.copy_(h0)
+                    plan.ts.copy_(ts0)
+                    plan.run()
+
+                add(nm, wbytes + (2 * Rr * D + D + Rr * O) * 4, Rr, f5_step, [h0, ts0], [plan.out], flops=fl)
         # .tmod -> device: a file of Q8 matrices with f32 scales (Qwen3-8B MLP-shaped, [12288][4096] each, about 1.6 GB in
         # all), written once to a temporary directory; one step uploads every blob from the mapped file (page cache)
         if want_next("next_tmod_upload"):
@@ -498,6 +539,11 @@ def run_ours(args) -> None:
         gbs = by / (t / 1e3) / 1e9
         ops[nm] = {"us": round(t * 1e3, 2), "gb_s": round(gbs, 1), "frac_of_peak": round(gbs / peak, 3),
                    "elements_per_s": round(el / (t / 1e3), 1), "bytes": by}
+        if nm in suite.flops:  # tensor-core rows: against the measured bf16 GEMM peak (sustained: a long step)
+            tf = suite.flops[nm] / (t / 1e3) / 1e12
+            tpk, tkind = tensor_peak()
+            ops[nm].update({"tflops": round(tf, 1), "flops": suite.flops[nm], "frac_of_tensor_peak": round(tf / tpk, 3),
+                            "tensor_peak": f"{tpk} TFLOP/s bf16 sustained ({tkind}); TF32's nominal rate is half of bf16's"})
     dom_i = int(np.argmax(op_ms))
     dom = suite.ops[dom_i]
     achieved = dom[1] / (op_ms[dom_i] / 1e3) / 1e9

@@ -299,6 +299,48 @@ VOX_CUDA_API int vox_cuda_tmod_upload(vox_cuda_tmod *t, const char *const *names
  * bit-exact with mat_row (kernels.cpp:446-463). Device staging comes from the stream-ordered allocator. */
 VOX_CUDA_API int vox_cuda_tmod_upload_dequant(vox_cuda_tmod *t, const char *name, void *dst, int out_dtype, void *stream);
 
+/* ---------------------------------------------------------------- F5 DiT step (one CUDA graph) */
+
+/* The transformer of one F5-TTS DiT step as the Vulkan backend records it (gpu_f5_step, gpu_f5.cpp:273-332) and the CPU
+ * computes it (F5Model::dit, f5.cpp:608-724), from the residual stream h after the input embedding to the output
+ * projection. Per block: ada = W_ada . ts ([shift, scale, gate] of attention, then of the MLP); nrm = LayerNorm(h)
+ * (no affine, eps 1e-6) * (1 + scale) + shift; q, k, v = nrm . W^T; RoPE on interleaved pairs (2j, 2j+1) at the
+ * frame position, on the first pe_attn_head heads (all heads if 0); attention without mask per sequence and head,
+ * softmax(q k^T / sqrt(dim_head)) v; h += gate_msa * (at . W_o^T); the MLP the same way with GELU (tanh form) between
+ * ff1 and ff2. Output: fin = W_norm_out . ts = [scale, shift], out = (LayerNorm(h) * (1 + scale) + shift) . W_proj^T.
+ * Linear layers carry no bias (Vox's matmul, kernels.hpp). Weights are f32 device buffers [out][in] (Vox's Mat
+ * layout), owned by the caller and read at every run. The input embedding (in_proj and the convolutional position
+ * embedding, gpu_f5.cpp:284-289) is not part of this entry. */
+#define VOX_CUDA_F5_MATH_F32 0  /* f32 GEMMs on the CUDA cores (reference accuracy) */
+#define VOX_CUDA_F5_MATH_TF32 1 /* tensor cores, TF32 inputs, f32 accumulation */
+#define VOX_CUDA_F5_MATH_BF16 2 /* tensor cores, bf16 inputs, f32 accumulation */
+typedef struct vox_cuda_f5_block_weights {
+    const float *ada;        /* [6 dim][dim] */
+    const float *q, *k, *v;  /* [heads * dim_head][dim] */
+    const float *o;          /* [dim][heads * dim_head] */
+    const float *ff1;        /* [ff_mult * dim][dim] */
+    const float *ff2;        /* [dim][ff_mult * dim] */
+} vox_cuda_f5_block_weights;
+typedef struct vox_cuda_f5_desc {
+    int32_t dim, heads, dim_head, ff_mult, depth, pe_attn_head, out_dim;
+    int32_t batch, frames;  /* the step processes batch sequences of `frames` rows each */
+    int32_t math;           /* VOX_CUDA_F5_MATH_* */
+    const vox_cuda_f5_block_weights *blocks; /* [depth], copied at create */
+    const float *norm_out;  /* [2 dim][dim]: (scale, shift) */
+    const float *proj_out;  /* [out_dim][dim] */
+} vox_cuda_f5_desc;
+typedef struct vox_cuda_f5 vox_cuda_f5;
+/* Allocates the plan's buffers on the current device (h [batch*frames][dim], ts [dim], out [batch*frames][out_dim] and
+ * the intermediates), builds the RoPE table as the CPU does (f5.cpp:529-541), runs the step once on `stream` and
+ * captures it into a CUDA graph. */
+VOX_CUDA_API int vox_cuda_f5_create(const vox_cuda_f5_desc *desc, void *stream, vox_cuda_f5 **out);
+/* The plan's device buffers: the caller writes h and ts before a run and reads out (and the updated h) after it. */
+VOX_CUDA_API int vox_cuda_f5_buffers(vox_cuda_f5 *p, float **h, float **ts, float **out);
+/* Replays the captured step on `stream` (stream-ordered, asynchronous). */
+VOX_CUDA_API int vox_cuda_f5_run(vox_cuda_f5 *p, void *stream);
+/* Frees the plan (waits for its work). NULL is ignored. */
+VOX_CUDA_API void vox_cuda_f5_destroy(vox_cuda_f5 *p);
+
 #ifdef __cplusplus
 }
 #endif

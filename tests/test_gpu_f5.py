@@ -1,0 +1,83 @@
+"""GPU parity tests of the F5 DiT step (vox_cuda_f5_*, one CUDA graph) against the numpy restatement of Vox's CPU
+F5Model::dit (oracle/f5.py, f5.cpp:608-724).
+
+Bars, relative to the RMS of the oracle's output: f32 GEMMs 2e-5 (the sums' order and the f32 LayerNorm statistics
+differ from the f64 oracle); tensor cores with TF32 inputs 2e-2, with bf16 inputs 8e-2 (input rounding of 2^-11 and
+2^-8 through two blocks). Replays of the captured graph are bit-identical and read the inputs afresh.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import f5 as F5
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(seed, D, H, HD, FF, depth, out_dim):
+    rng = np.random.default_rng(seed)
+    inner = H * HD
+    mk = lambda o, i, s=1.0: (rng.standard_normal((o, i)) * s / np.sqrt(i)).astype(np.float32)  # noqa: E731
+    blocks = [{"ada": mk(6 * D, D, 0.3), "q": mk(inner, D), "k": mk(inner, D), "v": mk(inner, D), "o": mk(D, inner),
+               "ff1": mk(FF, D), "ff2": mk(D, FF)} for _ in range(depth)]
+    return blocks, mk(2 * D, D, 0.3), mk(out_dim, D)
+
+
+def _dev(blocks, norm_out, proj_out):
+    t = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    return [{k: t(v) for k, v in b.items()} for b in blocks], t(norm_out), t(proj_out)
+
+
+def _rel(got, want):
+    return np.abs(np.asarray(got, np.float64) - want).max() / np.sqrt(np.mean(want ** 2))
+
+
+CFG = dict(D=64, H=4, HD=16, FF=128, depth=2, out_dim=20)
+
+
+@pytest.mark.parametrize("pe_attn_head", [0, 2])
+@pytest.mark.parametrize("math,bar", [("f32", 2e-5), ("tf32", 2e-2), ("bf16", 8e-2)])
+def test_f5_step_matches_oracle(vox, math, bar, pe_attn_head):
+    B, N = 2, 40
+    blocks, norm_out, proj_out = _model(1, **CFG)
+    rng = np.random.default_rng(2)
+    h = rng.standard_normal((B * N, CFG["D"])).astype(np.float32)
+    ts = rng.standard_normal(CFG["D"]).astype(np.float32)
+    plan = vox.F5Dit(*_dev(blocks, norm_out, proj_out), heads=CFG["H"], dim_head=CFG["HD"], batch=B, frames=N,
+                     pe_attn_head=pe_attn_head, math=math)
+    out = plan.step(torch.from_numpy(h).cuda(), torch.from_numpy(ts).cuda()).cpu().numpy()
+    h_after = plan.h.cpu().numpy()
+    want, want_h = F5.dit(h, ts, blocks, norm_out, proj_out, heads=CFG["H"], dim_head=CFG["HD"], batch=B, frames=N,
+                          pe_attn_head=pe_attn_head)
+    plan.close()
+    assert _rel(out, want) <= bar, _rel(out, want)
+    assert _rel(h_after, want_h) <= bar, _rel(h_after, want_h)
+
+
+def test_f5_replay_is_deterministic_and_reads_fresh_inputs(vox):
+    B, N = 2, 33
+    blocks, norm_out, proj_out = _model(3, **CFG)
+    plan = vox.F5Dit(*_dev(blocks, norm_out, proj_out), heads=CFG["H"], dim_head=CFG["HD"], batch=B, frames=N, math="f32")
+    outs = []
+    for seed in (0, 1, 0):
+        r = np.random.default_rng(seed)
+        h = r.standard_normal((B * N, CFG["D"])).astype(np.float32)
+        ts = r.standard_normal(CFG["D"]).astype(np.float32)
+        outs.append(plan.step(torch.from_numpy(h).cuda(), torch.from_numpy(ts).cuda()).cpu().numpy())
+        if seed == 1:
+            want, _ = F5.dit(h, ts, blocks, norm_out, proj_out, heads=CFG["H"], dim_head=CFG["HD"], batch=B, frames=N)
+            assert _rel(outs[-1], want) <= 2e-5
+    np.testing.assert_array_equal(outs[0].view(np.uint32), outs[2].view(np.uint32))
+    assert not np.array_equal(outs[0], outs[1])
+    plan.close()
+
+
+def test_f5_rejects_mismatched_weights(vox):
+    blocks, norm_out, proj_out = _dev(*_model(5, **CFG))
+    blocks[0]["o"] = blocks[0]["o"][:, :-1].contiguous()
+    with pytest.raises(vox.VoxCudaError) as e:
+        vox.F5Dit(blocks, norm_out, proj_out, heads=CFG["H"], dim_head=CFG["HD"], batch=1, frames=8)
+    assert e.value.status == -6

@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "Tmod", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "Tmod", "F5Dit", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -89,6 +89,10 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_tmod_data": ([c_p, ctypes.c_char_p, c_p], c_int),
         "vox_cuda_tmod_upload": ([c_p, c_p, c_i64, c_p, c_p], c_int),
         "vox_cuda_tmod_upload_dequant": ([c_p, ctypes.c_char_p, c_p, c_int, c_p], c_int),
+        "vox_cuda_f5_create": ([c_p, c_p, c_p], c_int),
+        "vox_cuda_f5_buffers": ([c_p, c_p, c_p, c_p], c_int),
+        "vox_cuda_f5_run": ([c_p, c_p], c_int),
+        "vox_cuda_f5_destroy": ([c_p], None),
     }
     for name, (args, res) in sigs.items():
         f = getattr(L, name)
@@ -542,3 +546,89 @@ class Tmod:
         out = torch.empty((rows, cols), dtype=out_dtype, device=device)
         _check(lib.vox_cuda_tmod_upload_dequant(self._h, name.encode(), out.data_ptr(), _act(out, "out"), _stream(out)))
         return out
+
+
+# ------------------------------------------------------------------ F5 DiT step (one CUDA graph)
+
+class _F5Block(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_void_p) for k in ("ada", "q", "k", "v", "o", "ff1", "ff2")]
+
+
+class _F5Desc(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_int32) for k in ("dim", "heads", "dim_head", "ff_mult", "depth", "pe_attn_head", "out_dim", "batch",
+                                              "frames", "math")] + \
+               [("blocks", ctypes.POINTER(_F5Block)), ("norm_out", ctypes.c_void_p), ("proj_out", ctypes.c_void_p)]
+
+
+class _DevView:
+    """A device buffer of the library exposed to torch without a copy (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape: tuple):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 3, "strides": None}
+
+
+class F5Dit:
+    """The transformer of one F5-TTS DiT step (Vox's gpu_f5_step, gpu_f5.cpp:273-332; CPU F5Model::dit,
+    f5.cpp:608-724) from the residual stream h after the input embedding to the output projection, captured once as a
+    CUDA graph (vox_cuda_f5_create) and replayed by run(). `blocks` is a list of dicts of f32 CUDA tensors
+    {ada [6D][D], q/k/v [H*HD][D], o [D][H*HD], ff1 [F][D], ff2 [D][F]} in Vox's [out][in] layout (no biases);
+    norm_out [2D][D] gives (scale, shift), proj_out [out_dim][D]. `math`: "f32" (CUDA-core GEMMs), "tf32" or "bf16"
+    (tensor cores, f32 accumulation). h, ts and out are the plan's own buffers (torch views)."""
+
+    MATH = {"f32": 0, "tf32": 1, "bf16": 2}
+    KEYS = ("ada", "q", "k", "v", "o", "ff1", "ff2")
+
+    def __init__(self, blocks, norm_out, proj_out, *, heads: int, dim_head: int, batch: int, frames: int,
+                 pe_attn_head: int = 0, math: str = "tf32"):
+        if math not in self.MATH:
+            raise VoxCudaError(-6, f"math must be one of {sorted(self.MATH)}")
+        D = int(norm_out.shape[1])
+        inner, out_dim = heads * dim_head, int(proj_out.shape[0])
+        ff = int(blocks[0]["ff1"].shape[0]) if blocks else 0
+        if not blocks or ff % D:
+            raise VoxCudaError(-6, "blocks must be non-empty and ff1 rows a multiple of dim")
+        want = {"ada": (6 * D, D), "q": (inner, D), "k": (inner, D), "v": (inner, D), "o": (D, inner), "ff1": (ff, D), "ff2": (D, ff)}
+        for i, b in enumerate(blocks):
+            for k, shp in want.items():
+                t = _dev(b[k], f"blocks[{i}].{k}")
+                if t.dtype != torch.float32 or tuple(t.shape) != shp:
+                    raise VoxCudaError(-6, f"blocks[{i}].{k} must be f32 {shp}")
+        for t, nm, shp in ((norm_out, "norm_out", (2 * D, D)), (proj_out, "proj_out", (out_dim, D))):
+            if _dev(t, nm).dtype != torch.float32 or tuple(t.shape) != shp:
+                raise VoxCudaError(-6, f"{nm} must be f32 {shp}")
+        self._keep = (blocks, norm_out, proj_out)  # read by every run
+        arr = (_F5Block * len(blocks))(*[_F5Block(*(b[k].data_ptr() for k in self.KEYS)) for b in blocks])
+        desc = _F5Desc(D, heads, dim_head, ff // D, len(blocks), pe_attn_head, out_dim, batch, frames, self.MATH[math], arr,
+                       norm_out.data_ptr(), proj_out.data_ptr())
+        h = ctypes.c_void_p()
+        _check(lib.vox_cuda_f5_create(ctypes.byref(desc), _stream(norm_out), ctypes.byref(h)))
+        self._h = h
+        ph, pts, po = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib.vox_cuda_f5_buffers(self._h, ctypes.byref(ph), ctypes.byref(pts), ctypes.byref(po)))
+        R = batch * frames
+        self.h = torch.as_tensor(_DevView(ph.value, (R, D)), device=norm_out.device)
+        self.ts = torch.as_tensor(_DevView(pts.value, (D,)), device=norm_out.device)
+        self.out = torch.as_tensor(_DevView(po.value, (R, out_dim)), device=norm_out.device)
+
+    def run(self) -> None:
+        """Replays the step on the current stream: reads h and ts, updates h, writes out."""
+        _check(lib.vox_cuda_f5_run(self._h, _stream(self.h)))
+
+    def step(self, h: torch.Tensor, ts: torch.Tensor) -> torch.Tensor:
+        """Copies h [batch*frames][dim] and ts [dim] in, runs the step, returns a copy of out."""
+        self.h.copy_(h.reshape(self.h.shape))
+        self.ts.copy_(ts.reshape(self.ts.shape))
+        self.run()
+        return self.out.clone()
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            torch.cuda.synchronize(self.h.device)
+            lib.vox_cuda_f5_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,8 +1,9 @@
 """Build of the sm_100a shared library ``vox_b200/libvox_cuda.so`` (kernels + C ABI + C++ host wrappers).
 
 Every ``csrc/*.cu`` is compiled by nvcc for ``sm_100a`` only and every ``csrc/*.cpp`` by the host compiler; the
-objects are linked into one shared library with the CUDA runtime linked statically, so the library needs nothing
-but the NVIDIA driver at run time. Objects are rebuilt when their source or any header is newer.
+objects are linked into one shared library with the CUDA runtime linked statically; at run time it needs the NVIDIA
+driver and the toolkit's cuBLAS (the GEMMs of the F5 DiT step), found through an rpath to the toolkit's lib64.
+Objects are rebuilt when their source or any header is newer.
 
 Usage: ``python -m vox_b200.build [--force]``.
 """
@@ -84,7 +85,9 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objs = [OBJ / (s.name + ".o") for s in srcs]
     if force or jobs or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs), "-lpthread", "-ldl", "-lrt"]
+        cuda_lib = str(Path(nvcc()).resolve().parent.parent / "lib64")
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs), f"-L{cuda_lib}", "-lcublas",
+               "-Xlinker", f"-rpath,{cuda_lib}", "-lpthread", "-ldl", "-lrt"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed\n{r.stdout}\n{r.stderr}")

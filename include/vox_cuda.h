@@ -10,7 +10,8 @@
  *   - Return value is a status: 0 = OK, negative = one of the VOX_CUDA_ERR_* codes, whose values equal
  *     Vox's vox_status codes (include/vox.h:48-55). No exception crosses this boundary.
  *   - The message of the last failed call is kept per host thread: vox_cuda_last_error().
- *   - All tensor pointers are DEVICE pointers owned by the caller and never retained after the call.
+ *   - All tensor pointers are DEVICE pointers owned by the caller and never retained after the call (the one
+ *     exception: an F5 DiT plan keeps the weight pointers of its description and reads them at every run).
  *   - Every call takes a CUDA stream (cudaStream_t passed as void*, NULL = legacy default stream) and is
  *     asynchronous and stream-ordered. There is no global lock around launches: calls from several host
  *     threads on distinct streams run concurrently.
@@ -309,11 +310,15 @@ VOX_CUDA_API int vox_cuda_tmod_upload_dequant(vox_cuda_tmod *t, const char *name
  * softmax(q k^T / sqrt(dim_head)) v; h += gate_msa * (at . W_o^T); the MLP the same way with GELU (tanh form) between
  * ff1 and ff2. Output: fin = W_norm_out . ts = [scale, shift], out = (LayerNorm(h) * (1 + scale) + shift) . W_proj^T.
  * Linear layers carry no bias (Vox's matmul, kernels.hpp). Weights are f32 device buffers [out][in] (Vox's Mat
- * layout), owned by the caller and read at every run. The input embedding (in_proj and the convolutional position
+ * layout), owned by the caller and read at every run (the bf16 mode reads its own bf16 copies of q, k, v, o, ff1, ff2
+ * and proj_out, made at create). The input embedding (in_proj and the convolutional position
  * embedding, gpu_f5.cpp:284-289) is not part of this entry. */
 #define VOX_CUDA_F5_MATH_F32 0  /* f32 GEMMs on the CUDA cores (reference accuracy) */
 #define VOX_CUDA_F5_MATH_TF32 1 /* tensor cores, TF32 inputs, f32 accumulation */
-#define VOX_CUDA_F5_MATH_BF16 2 /* tensor cores, bf16 inputs, f32 accumulation */
+#define VOX_CUDA_F5_MATH_BF16 2 /* tensor cores, bf16 inputs, f32 accumulation; with dim_head 64 (and dim % 4 == 0,
+                                 * dim <= 2048) the plan snapshots bf16 copies of the projection weights at create, feeds
+                                 * every GEMM bf16 activations and runs attention as one fused kernel (scores never leave
+                                 * the SM); otherwise cuBLAS may keep the f32 inputs in TF32 */
 typedef struct vox_cuda_f5_block_weights {
     const float *ada;        /* [6 dim][dim] */
     const float *q, *k, *v;  /* [heads * dim_head][dim] */

@@ -3,7 +3,8 @@ F5Model::dit (oracle/f5.py, f5.cpp:608-724).
 
 Bars, relative to the RMS of the oracle's output: f32 GEMMs 2e-5 (the sums' order and the f32 LayerNorm statistics
 differ from the f64 oracle); tensor cores with TF32 inputs 2e-2, with bf16 inputs 8e-2 (input rounding of 2^-11 and
-2^-8 through two blocks). Replays of the captured graph are bit-identical and read the inputs afresh.
+2^-8 through two blocks; the bf16 mode with dim_head 64 also rounds the attention probabilities and every GEMM input
+to bf16). Replays of the captured graph are bit-identical and read the inputs afresh.
 """
 
 from __future__ import annotations
@@ -55,6 +56,27 @@ def test_f5_step_matches_oracle(vox, math, bar, pe_attn_head):
     plan.close()
     assert _rel(out, want) <= bar, _rel(out, want)
     assert _rel(h_after, want_h) <= bar, _rel(h_after, want_h)
+
+
+@pytest.mark.parametrize("frames,pe_attn_head", [(70, 1), (128, 0)])
+def test_f5_bf16_pipeline_matches_oracle(vox, frames, pe_attn_head):
+    """dim_head 64 in bf16 mode: bf16 weight copies, fused q|k|v projection, the fused attention kernel (64-key tiles;
+    70 frames leave a ragged last tile of keys and of queries), residual and modulation fused."""
+    cfg = dict(D=128, H=2, HD=64, FF=256, depth=2, out_dim=24)
+    B = 2
+    blocks, norm_out, proj_out = _model(6, **cfg)
+    rng = np.random.default_rng(7)
+    h = rng.standard_normal((B * frames, cfg["D"])).astype(np.float32)
+    ts = rng.standard_normal(cfg["D"]).astype(np.float32)
+    plan = vox.F5Dit(*_dev(blocks, norm_out, proj_out), heads=cfg["H"], dim_head=cfg["HD"], batch=B, frames=frames,
+                     pe_attn_head=pe_attn_head, math="bf16")
+    out = plan.step(torch.from_numpy(h).cuda(), torch.from_numpy(ts).cuda()).cpu().numpy()
+    h_after = plan.h.cpu().numpy()
+    want, want_h = F5.dit(h, ts, blocks, norm_out, proj_out, heads=cfg["H"], dim_head=cfg["HD"], batch=B, frames=frames,
+                          pe_attn_head=pe_attn_head)
+    plan.close()
+    assert _rel(out, want) <= 8e-2, _rel(out, want)
+    assert _rel(h_after, want_h) <= 8e-2, _rel(h_after, want_h)
 
 
 def test_f5_replay_is_deterministic_and_reads_fresh_inputs(vox):

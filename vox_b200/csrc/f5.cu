@@ -6,8 +6,10 @@
 // end the final modulation and the output projection. The elementwise and normalisation steps are this library's
 // kernels (vox_cuda_adaln with no gate, vox_cuda_gated_add, vox_cuda_gelu, vox_cuda_softmax_rows) plus the RoPE kernel
 // below; the projections and the two attention products are cuBLAS GEMMs (f32, or on the tensor cores with TF32 or
-// bf16 inputs and f32 accumulation). Attention materialises the score matrix of one sequence at a time
-// ([heads][frames][frames] f32) and normalises it in place with the row softmax.
+// bf16 inputs and f32 accumulation). In the f32 and TF32 modes attention materialises the score matrix of one
+// sequence at a time ([heads][frames][frames] f32) and normalises it in place with the row softmax; in the bf16 mode
+// (dim_head 64) one fused kernel computes it from bf16 copies of q, k, v without writing the scores (mma.sync bf16,
+// online softmax).
 //
 // The plan records the whole step once eagerly (kernel selection, first-use attributes), then again under stream
 // capture; a run is one cudaGraphLaunch. All buffers are the plan's, so the graph's pointers never change.
@@ -19,6 +21,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "sfu.cuh"
 
 namespace voxcuda {
 namespace {
@@ -39,6 +42,254 @@ __global__ void __launch_bounds__(256) f5_rope_kernel(float *q, float *k, const 
         const float2 a = *pq, b = *pk;
         *pq = make_float2(__fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(a.y, c.y)), __fadd_rn(__fmul_rn(a.y, c.x), __fmul_rn(a.x, c.y)));
         *pk = make_float2(__fsub_rn(__fmul_rn(b.x, c.x), __fmul_rn(b.y, c.y)), __fadd_rn(__fmul_rn(b.y, c.x), __fmul_rn(b.x, c.y)));
+    }
+}
+
+// ------------------------------------------------------------------ fused attention (bf16 math mode, dim_head 64)
+
+// RoPE as above, then q, k and v rounded to bf16 (RN) into qb, kb, vb [rows][inner]; q, k, v have row stride ld (the
+// fused projection [rows][3 inner] or separate [rows][inner] tensors). One thread per column pair.
+__global__ void __launch_bounds__(256) f5_qkv_bf16_kernel(const float *q, const float *k, const float *v, uint32_t ld, const float2 *cs,
+                                                          uint32_t *qb, uint32_t *kb, uint32_t *vb, uint32_t pairs, uint32_t frames,
+                                                          uint32_t half, uint32_t rope_heads, uint32_t hd, uint32_t inner) {
+    pdl_enter();
+    const uint32_t stride = gridDim.x * blockDim.x, row_pairs = inner / 2;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
+        const uint32_t r = i / row_pairs, col = 2 * (i % row_pairs);
+        const float2 a = *reinterpret_cast<const float2 *>(q + size_t(r) * ld + col);
+        const float2 b = *reinterpret_cast<const float2 *>(k + size_t(r) * ld + col);
+        const float2 c = *reinterpret_cast<const float2 *>(v + size_t(r) * ld + col);
+        float2 qa = a, kb2 = b;
+        if (col / hd < rope_heads) {
+            const float2 t = cs[size_t(r % frames) * half + (col % hd) / 2];
+            qa = make_float2(__fsub_rn(__fmul_rn(a.x, t.x), __fmul_rn(a.y, t.y)), __fadd_rn(__fmul_rn(a.y, t.x), __fmul_rn(a.x, t.y)));
+            kb2 = make_float2(__fsub_rn(__fmul_rn(b.x, t.x), __fmul_rn(b.y, t.y)), __fadd_rn(__fmul_rn(b.y, t.x), __fmul_rn(b.x, t.y)));
+        }
+        qb[i] = pack_bf16(qa.x, qa.y);
+        kb[i] = pack_bf16(kb2.x, kb2.y);
+        vb[i] = pack_bf16(c.x, c.y);
+    }
+}
+
+constexpr int kFaRows = 64;   // query rows per CTA (16 per warp)
+constexpr int kFaKeys = 64;   // keys per staged K/V tile
+constexpr int kFaHd = 64;     // head dimension of the fused kernel
+constexpr int kFaThreads = 128;
+
+// A tile of 64 rows x 64 bf16 (128-byte rows) in shared memory: the 16-byte chunk c of row r sits at chunk c ^ (r % 8),
+// so the 8 row addresses of an ldmatrix phase fall in 8 different bank groups.
+__device__ __forceinline__ uint32_t fa_off(int r, int c) { return uint32_t(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// cp.async of one 16-byte chunk; src_bytes 0 fills the chunk with zeros (rows past the sequence end).
+__device__ __forceinline__ void cp16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Stages rows [row0, row0 + 64) of a head's 64 columns (global row stride `inner` bf16) into a swizzled tile; rows at or
+// past `n` are zero-filled. 512 chunks, 4 per thread.
+__device__ __forceinline__ void fa_stage(uint32_t tile, const __nv_bfloat16 *g, int row0, int n, int inner) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int idx = threadIdx.x + u * kFaThreads, r = idx >> 3, c = idx & 7;
+        const int gr = row0 + r;
+        const __nv_bfloat16 *src = g + size_t(gr < n ? gr : n - 1) * inner + c * 8;
+        cp16(tile + fa_off(r, c), src, gr < n ? 16u : 0u);
+    }
+}
+
+// softmax(q k^T * scale) v for one sequence and head and 64 query rows, online over 64-key tiles (K and V double
+// buffered with cp.async): S and P in registers (P rounded to bf16 for the second product), f32 accumulation, the
+// row maximum and sum in the exp2 domain. at [rows][inner] f32 receives the normalised rows.
+template <bool BF16_OUT>
+__global__ void __launch_bounds__(kFaThreads) f5_flash_kernel(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb, const __nv_bfloat16 *vb,
+                                                              void *at, int n, int inner, float scale_log2) {
+    pdl_enter();
+    __shared__ __align__(128) uint8_t sm[5 * kFaRows * 128];  // Q, K[2], V[2]
+    const uint32_t sQ = uint32_t(__cvta_generic_to_shared(sm)), sK = sQ + 8192, sV = sQ + 3 * 8192;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int q0 = blockIdx.x * kFaRows, head = blockIdx.y;
+    const size_t seq = size_t(blockIdx.z) * size_t(n) * size_t(inner) + size_t(head) * kFaHd;
+    const __nv_bfloat16 *Q = qb + seq, *K = kb + seq, *V = vb + seq;
+    const int ntiles = (n + kFaKeys - 1) / kFaKeys;
+    fa_stage(sQ, Q, q0, n, inner);
+    fa_stage(sK, K, 0, n, inner);
+    fa_stage(sV, V, 0, n, inner);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    uint32_t qa[4][4];
+    for (int kt = 0; kt < ntiles; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < ntiles) {
+            fa_stage(sK + (buf ^ 1) * 8192, K, (kt + 1) * kFaKeys, n, inner);
+            fa_stage(sV + (buf ^ 1) * 8192, V, (kt + 1) * kFaKeys, n, inner);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        if (kt == 0) {  // this warp's 16 query rows as A fragments, four 16-column steps
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                ldsm_x4(sQ + fa_off(warp * 16 + (lane & 15), 2 * kk + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+        }
+        const uint32_t tK = sK + buf * 8192, tV = sV + buf * 8192;
+        float s[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {  // keys 16 np .. 16 np + 15
+                uint32_t b0, b1, b2, b3;
+                const int mi = lane >> 3;
+                ldsm_x4(tK + fa_off(16 * np + (mi >> 1) * 8 + (lane & 7), 2 * kk + (mi & 1)), b0, b1, b2, b3);
+                mma16816(s[2 * np], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+                mma16816(s[2 * np + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+            }
+        const int key0 = kt * kFaKeys;
+        if (key0 + kFaKeys > n) {  // keys past the sequence end take no weight
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (key0 + 8 * j + 2 * t + (c & 1) >= n) s[j][c] = -INFINITY;
+        }
+        // online softmax over this tile: rows g (c = 0, 1) and g + 8 (c = 2, 3) of the warp's 16
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fmaxf(s[j][2 * rr], s[j][2 * rr + 1]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mnew = fmaxf(mrow[rr], mx * scale_log2);
+            const float alpha = ex2_approx(mrow[rr] - mnew);
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                s[j][2 * rr] = ex2_approx(fmaf(s[j][2 * rr], scale_log2, -mnew));
+                s[j][2 * rr + 1] = ex2_approx(fmaf(s[j][2 * rr + 1], scale_log2, -mnew));
+                sum += s[j][2 * rr] + s[j][2 * rr + 1];
+            }
+            lrow[rr] = lrow[rr] * alpha + sum;
+            mrow[rr] = mnew;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) {
+                o[d][2 * rr] *= alpha;
+                o[d][2 * rr + 1] *= alpha;
+            }
+        }
+        // O += P V: P's accumulator layout is the A layout of the next product (keys 16 kk2 .. 16 kk2 + 15)
+#pragma unroll
+        for (int kk2 = 0; kk2 < 4; ++kk2) {
+            const uint32_t a0 = pack_bf16(s[2 * kk2][0], s[2 * kk2][1]), a1 = pack_bf16(s[2 * kk2][2], s[2 * kk2][3]);
+            const uint32_t a2 = pack_bf16(s[2 * kk2 + 1][0], s[2 * kk2 + 1][1]), a3 = pack_bf16(s[2 * kk2 + 1][2], s[2 * kk2 + 1][3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; ++dp) {  // dims 16 dp .. 16 dp + 15
+                uint32_t b0, b1, b2, b3;
+                const int mi = lane >> 3;
+                ldsm_x4_t(tV + fa_off(16 * kk2 + (mi & 1) * 8 + (lane & 7), 2 * dp + (mi >> 1)), b0, b1, b2, b3);
+                mma16816(o[2 * dp], a0, a1, a2, a3, b0, b1);
+                mma16816(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
+            }
+        }
+        __syncthreads();  // the buffer is refilled by the next iteration's copies
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        float l = lrow[rr];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        const float inv = 1.0f / l;
+        const int row = q0 + warp * 16 + g + 8 * rr;
+        if (row < n) {
+            const size_t e = size_t(blockIdx.z) * size_t(n) * size_t(inner) + size_t(row) * inner + size_t(head) * kFaHd + 2 * t;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) {
+                if (BF16_OUT)
+                    reinterpret_cast<uint32_t *>(at)[(e + 8 * d) / 2] = pack_bf16(o[d][2 * rr] * inv, o[d][2 * rr + 1] * inv);
+                else
+                    *reinterpret_cast<float2 *>(static_cast<float *>(at) + e + 8 * d) = make_float2(o[d][2 * rr] * inv, o[d][2 * rr + 1] * inv);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ bf16 pipeline helpers
+
+// dst = bf16(src) (RN), n / 2 pairs (weights, converted once at plan creation).
+__global__ void __launch_bounds__(256) f5_to_bf16_kernel(const float2 *src, uint32_t *dst, size_t pairs) {
+    pdl_enter();
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs; i += size_t(gridDim.x) * blockDim.x) {
+        const float2 v = src[i];
+        dst[i] = pack_bf16(v.x, v.y);
+    }
+}
+
+// One warp per row of h [rows][D]: if delta, h += gate * delta (product, then sum, each rounded: gated_add of
+// f5.cpp:670-676); then nrm = LayerNorm(h) * (1 + scale) + shift (no affine, eps; mean and variance two-pass in f32 on
+// the row in registers) rounded to bf16 for the next projection. Lane l holds columns 4 (l + 32 k), k < VPL.
+template <int VPL>
+__global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *delta, const float *gate, const float *scale,
+                                                        const float *shift, uint2 *nrm, uint32_t rows, uint32_t D, float eps) {
+    pdl_enter();
+    const uint32_t lane = threadIdx.x & 31, r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (r >= rows) return;
+    float4 x[VPL];
+    float4 *hr = reinterpret_cast<float4 *>(h + size_t(r) * D);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const uint32_t c = lane + 32 * k;
+        x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (4 * c < D) {
+            x[k] = hr[c];
+            if (delta) {
+                const float4 dv = reinterpret_cast<const float4 *>(delta + size_t(r) * D)[c];
+                const float4 g = reinterpret_cast<const float4 *>(gate)[c];
+                x[k] = make_float4(__fadd_rn(x[k].x, __fmul_rn(g.x, dv.x)), __fadd_rn(x[k].y, __fmul_rn(g.y, dv.y)),
+                                   __fadd_rn(x[k].z, __fmul_rn(g.z, dv.z)), __fadd_rn(x[k].w, __fmul_rn(g.w, dv.w)));
+                hr[c] = x[k];
+            }
+            sum += (x[k].x + x[k].y) + (x[k].z + x[k].w);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / float(D);
+    float var = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k)
+        if (4 * (lane + 32 * k) < D) {
+            const float a = x[k].x - mean, b = x[k].y - mean, c = x[k].z - mean, e = x[k].w - mean;
+            var += (a * a + b * b) + (c * c + e * e);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    const float inv = rsqrtf(var / float(D) + eps);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const uint32_t c = lane + 32 * k;
+        if (4 * c < D) {
+            const float4 sc = reinterpret_cast<const float4 *>(scale)[c], sh = reinterpret_cast<const float4 *>(shift)[c];
+            const float y0 = fmaf((x[k].x - mean) * inv, 1.f + sc.x, sh.x), y1 = fmaf((x[k].y - mean) * inv, 1.f + sc.y, sh.y);
+            const float y2 = fmaf((x[k].z - mean) * inv, 1.f + sc.z, sh.z), y3 = fmaf((x[k].w - mean) * inv, 1.f + sc.w, sh.w);
+            nrm[size_t(r) * (D / 4) + c] = make_uint2(pack_bf16(y0, y1), pack_bf16(y2, y3));
+        }
     }
 }
 
@@ -64,9 +315,17 @@ struct F5Plan {
     cublasComputeType_t compute = CUBLAS_COMPUTE_32F_PEDANTIC;
     cudaStream_t cap = nullptr;  // private stream the graph is captured on
     void *ws = nullptr;
+    // f32 / TF32 path
     float *h = nullptr, *ts = nullptr, *out = nullptr, *nrm = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *at = nullptr,
           *o = nullptr, *ffb = nullptr, *s = nullptr, *ada = nullptr, *fin = nullptr;
     float2 *cs = nullptr;
+    // bf16 path (bf16 math, dim_head 64, dim % 4 == 0 and <= 2048): bf16 copies of the projection weights (q|k|v fused),
+    // bf16 activations into every GEMM, the fused attention, all ada vectors by one batched GEMV
+    bool bf16 = false;
+    float *qkv = nullptr, *ada_all = nullptr;
+    __nv_bfloat16 *qb = nullptr, *kb = nullptr, *vb = nullptr, *nrm_b = nullptr, *at_b = nullptr, *ff_b = nullptr;
+    __nv_bfloat16 *w_qkv = nullptr, *w_o = nullptr, *w_ff1 = nullptr, *w_ff2 = nullptr, *w_proj = nullptr;
+    const void **ada_ptrs = nullptr;  // device [3][depth]: W_ada[l], ts, ada_all + l 6D
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
 };
@@ -86,6 +345,13 @@ int gemm_xwt(F5Plan &p, const float *x, const float *w, float *y, int64_t R, int
     return blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(O), int(R), int(I), &one, w, CUDA_R_32F, int(I), x,
                                    CUDA_R_32F, int(I), &zero, y, CUDA_R_32F, int(O), p.compute, CUBLAS_GEMM_DEFAULT),
                       "gemm");
+}
+// The same with bf16 x and W (tensor cores, f32 accumulation) and y f32 or bf16.
+int gemm_bf16(F5Plan &p, const __nv_bfloat16 *x, const __nv_bfloat16 *w, void *y, cudaDataType_t yt, int64_t R, int64_t O, int64_t I) {
+    const float one = 1.0f, zero = 0.0f;
+    return blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(O), int(R), int(I), &one, w, CUDA_R_16BF, int(I), x,
+                                   CUDA_R_16BF, int(I), &zero, y, yt, int(O), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
+                      "gemm (bf16)");
 }
 
 #define F5_TRY(expr)                          \
@@ -113,7 +379,7 @@ int attention(F5Plan &p, int64_t b, cudaStream_t st) {
                       "attention output");
 }
 
-// The whole step on stream st (eager or under capture; cuBLAS is bound to the same stream).
+// The whole step on stream st, f32 / TF32 path (eager or under capture; cuBLAS is bound to the same stream).
 int record(F5Plan &p, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const int64_t R = p.R, D = d.dim, IN = p.inner, FF = p.ff;
@@ -146,6 +412,62 @@ int record(F5Plan &p, cudaStream_t st) {
     return gemm_xwt(p, p.nrm, d.proj_out, p.out, R, d.out_dim, D);
 }
 
+// h += gate * delta (if delta), then nrm_b = modulated LayerNorm of h in bf16.
+int resmod(F5Plan &p, const float *delta, const float *gate, const float *scale, const float *shift, cudaStream_t st) {
+    const uint32_t R = uint32_t(p.R), D = uint32_t(p.d.dim), vpl = (D / 4 + 31) / 32;
+    const int g = int((R + 7) / 8);
+    uint2 *nrm = reinterpret_cast<uint2 *>(p.nrm_b);
+    if (vpl <= 1) launch_k(f5_resmod_kernel<1>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 2) launch_k(f5_resmod_kernel<2>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 4) launch_k(f5_resmod_kernel<4>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 8) launch_k(f5_resmod_kernel<8>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
+    else launch_k(f5_resmod_kernel<16>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
+    return check_launch("vox_cuda_f5 residual/modulate");
+}
+
+// The whole step, bf16 path: the same arithmetic with bf16 GEMM inputs, the residual stream h in f32, each block's
+// closing gated residual fused with the next modulation.
+int record_bf16(F5Plan &p, cudaStream_t st) {
+    const vox_cuda_f5_desc &d = p.d;
+    const int64_t R = p.R, D = d.dim, IN = p.inner, FF = p.ff, L = d.depth;
+    const float one = 1.0f, zero = 0.0f;
+    const void *const *pp = p.ada_ptrs;
+    F5_TRY(blas_check(cublasGemmBatchedEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(6 * D), 1, int(D), &one, pp, CUDA_R_32F, int(D),
+                                          pp + L, CUDA_R_32F, int(D), &zero, (void *const *)(pp + 2 * L), CUDA_R_32F, int(6 * D),
+                                          int(L), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
+                      "ada (batched)"));
+    F5_TRY(gemm_xwt(p, p.ts, d.norm_out, p.fin, 1, 2 * D, D));  // fin = [scale, shift] (f5.cpp:720-722)
+    const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
+    const uint32_t cpairs = uint32_t(R * IN / 2);
+    const dim3 fg(unsigned((d.frames + kFaRows - 1) / kFaRows), unsigned(d.heads), unsigned(d.batch));
+    const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
+    F5_TRY(resmod(p, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
+    for (int64_t l = 0; l < L; ++l) {
+        const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
+        F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv, CUDA_R_32F, R, 3 * IN, D));
+        launch_k(f5_qkv_bf16_kernel, grid_for(cpairs, 256, 4), 256, 0, st, (const float *)p.qkv, (const float *)(p.qkv + IN),
+                 (const float *)(p.qkv + 2 * IN), uint32_t(3 * IN), (const float2 *)p.cs, reinterpret_cast<uint32_t *>(p.qb),
+                 reinterpret_cast<uint32_t *>(p.kb), reinterpret_cast<uint32_t *>(p.vb), cpairs, uint32_t(d.frames),
+                 uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
+        F5_TRY(check_launch("vox_cuda_f5 rope/bf16"));
+        launch_k(f5_flash_kernel<true>, fg, kFaThreads, 0, st, (const __nv_bfloat16 *)p.qb, (const __nv_bfloat16 *)p.kb,
+                 (const __nv_bfloat16 *)p.vb, (void *)p.at_b, int(d.frames), int(IN), scale_log2);
+        F5_TRY(check_launch("vox_cuda_f5 attention"));
+        F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
+        F5_TRY(resmod(p, p.o, A + 2 * D, A + 4 * D, A + 3 * D, st));
+        F5_TRY(gemm_bf16(p, p.nrm_b, p.w_ff1 + size_t(l) * FF * D, p.ff_b, CUDA_R_16BF, R, FF, D));
+        F5_TRY(vox_cuda_gelu(p.ff_b, p.ff_b, R * FF, VOX_CUDA_GELU_TANH, VOX_CUDA_BF16, st));
+        F5_TRY(gemm_bf16(p, p.ff_b, p.w_ff2 + size_t(l) * D * FF, p.o, CUDA_R_32F, R, D, FF));
+        if (l + 1 < L) {
+            const float *An = A + 6 * D;
+            F5_TRY(resmod(p, p.o, A + 5 * D, An + D, An, st));
+        } else {
+            F5_TRY(resmod(p, p.o, A + 5 * D, p.fin, p.fin + D, st));
+        }
+    }
+    return gemm_bf16(p, p.nrm_b, p.w_proj, p.out, CUDA_R_32F, R, d.out_dim, D);
+}
+
 void release(F5Plan *p) {
     if (!p) return;
     if (p->cap) cudaStreamSynchronize(p->cap);
@@ -154,7 +476,9 @@ void release(F5Plan *p) {
     if (p->blas) cublasDestroy(p->blas);
     for (void *b : {(void *)p->ws, (void *)p->h, (void *)p->ts, (void *)p->out, (void *)p->nrm, (void *)p->q, (void *)p->k,
                     (void *)p->v, (void *)p->at, (void *)p->o, (void *)p->ffb, (void *)p->s, (void *)p->ada, (void *)p->fin,
-                    (void *)p->cs})
+                    (void *)p->cs, (void *)p->qkv, (void *)p->ada_all, (void *)p->qb, (void *)p->kb, (void *)p->vb,
+                    (void *)p->nrm_b, (void *)p->at_b, (void *)p->ff_b, (void *)p->w_qkv, (void *)p->w_o, (void *)p->w_ff1,
+                    (void *)p->w_ff2, (void *)p->w_proj, (void *)p->ada_ptrs})
         if (b) cudaFree(b);
     if (p->cap) cudaStreamDestroy(p->cap);
     delete p;
@@ -168,24 +492,67 @@ template <class T> int alloc(T **ptr, size_t count, const char *what) {
     return VOX_CUDA_OK;
 }
 
+// dst[0 .. n) = bf16(src) on stream st (n even).
+int to_bf16(const float *src, __nv_bfloat16 *dst, size_t n, cudaStream_t st) {
+    launch_k(f5_to_bf16_kernel, grid_for(int64_t(n / 2), 256, 4), 256, 0, st, reinterpret_cast<const float2 *>(src),
+             reinterpret_cast<uint32_t *>(dst), n / 2);
+    return check_launch("vox_cuda_f5_create (weights to bf16)");
+}
+
 int build(F5Plan &p, cudaStream_t user) {
     const vox_cuda_f5_desc &d = p.d;
-    const size_t R = size_t(p.R), D = size_t(d.dim), IN = size_t(p.inner), FF = size_t(p.ff), N = size_t(d.frames);
+    const size_t R = size_t(p.R), D = size_t(d.dim), IN = size_t(p.inner), FF = size_t(p.ff), N = size_t(d.frames), L = size_t(d.depth);
+    p.bf16 = d.math == VOX_CUDA_F5_MATH_BF16 && d.dim_head == kFaHd && D % 4 == 0 && D <= 2048;
     F5_TRY(alloc(&p.h, R * D, "h"));
     F5_TRY(alloc(&p.ts, D, "ts"));
     F5_TRY(alloc(&p.out, R * size_t(d.out_dim), "out"));
-    F5_TRY(alloc(&p.nrm, R * D, "nrm"));
-    F5_TRY(alloc(&p.q, R * IN, "q"));
-    F5_TRY(alloc(&p.k, R * IN, "k"));
-    F5_TRY(alloc(&p.v, R * IN, "v"));
-    F5_TRY(alloc(&p.at, R * IN, "at"));
     F5_TRY(alloc(&p.o, R * D, "o"));
-    F5_TRY(alloc(&p.ffb, R * FF, "ff"));
-    F5_TRY(alloc(&p.s, size_t(d.heads) * N * N, "scores"));
-    F5_TRY(alloc(&p.ada, 6 * D, "ada"));
     F5_TRY(alloc(&p.fin, 2 * D, "fin"));
     F5_TRY(alloc(&p.cs, N * size_t(d.dim_head / 2), "rope table"));
     F5_TRY(alloc(reinterpret_cast<uint8_t **>(&p.ws), kBlasWorkspace, "cuBLAS workspace"));
+    if (p.bf16) {
+        F5_TRY(alloc(&p.qkv, R * 3 * IN, "qkv"));
+        F5_TRY(alloc(&p.ada_all, L * 6 * D, "ada"));
+        F5_TRY(alloc(&p.qb, R * IN, "q (bf16)"));
+        F5_TRY(alloc(&p.kb, R * IN, "k (bf16)"));
+        F5_TRY(alloc(&p.vb, R * IN, "v (bf16)"));
+        F5_TRY(alloc(&p.nrm_b, R * D, "nrm (bf16)"));
+        F5_TRY(alloc(&p.at_b, R * IN, "attention (bf16)"));
+        F5_TRY(alloc(&p.ff_b, R * FF, "ff (bf16)"));
+        F5_TRY(alloc(&p.w_qkv, L * 3 * IN * D, "q|k|v weights (bf16)"));
+        F5_TRY(alloc(&p.w_o, L * D * IN, "o weights (bf16)"));
+        F5_TRY(alloc(&p.w_ff1, L * FF * D, "ff1 weights (bf16)"));
+        F5_TRY(alloc(&p.w_ff2, L * D * FF, "ff2 weights (bf16)"));
+        F5_TRY(alloc(&p.w_proj, size_t(d.out_dim) * D, "proj_out weights (bf16)"));
+        F5_TRY(alloc(&p.ada_ptrs, 3 * L, "ada pointers"));
+        for (size_t l = 0; l < L; ++l) {
+            const vox_cuda_f5_block_weights &B = p.blocks[l];
+            F5_TRY(to_bf16(B.q, p.w_qkv + l * 3 * IN * D, IN * D, user));
+            F5_TRY(to_bf16(B.k, p.w_qkv + l * 3 * IN * D + IN * D, IN * D, user));
+            F5_TRY(to_bf16(B.v, p.w_qkv + l * 3 * IN * D + 2 * IN * D, IN * D, user));
+            F5_TRY(to_bf16(B.o, p.w_o + l * D * IN, D * IN, user));
+            F5_TRY(to_bf16(B.ff1, p.w_ff1 + l * FF * D, FF * D, user));
+            F5_TRY(to_bf16(B.ff2, p.w_ff2 + l * D * FF, D * FF, user));
+        }
+        F5_TRY(to_bf16(d.proj_out, p.w_proj, size_t(d.out_dim) * D, user));
+        std::vector<const void *> ptrs(3 * L);
+        for (size_t l = 0; l < L; ++l) {
+            ptrs[l] = p.blocks[l].ada;
+            ptrs[L + l] = p.ts;
+            ptrs[2 * L + l] = p.ada_all + l * 6 * D;
+        }
+        if (cudaMemcpy(p.ada_ptrs, ptrs.data(), ptrs.size() * sizeof(void *), cudaMemcpyHostToDevice) != cudaSuccess)
+            return check_launch("vox_cuda_f5_create");
+    } else {
+        F5_TRY(alloc(&p.nrm, R * D, "nrm"));
+        F5_TRY(alloc(&p.q, R * IN, "q"));
+        F5_TRY(alloc(&p.k, R * IN, "k"));
+        F5_TRY(alloc(&p.v, R * IN, "v"));
+        F5_TRY(alloc(&p.at, R * IN, "at"));
+        F5_TRY(alloc(&p.ffb, R * FF, "ff"));
+        F5_TRY(alloc(&p.s, size_t(d.heads) * N * N, "scores"));
+        F5_TRY(alloc(&p.ada, 6 * D, "ada"));
+    }
     // RoPE table as the CPU builds it (f5.cpp:529-541): inv = float(1 / 10000^(2j/hd)) in double, angle = float(i) * inv
     // in float, cos/sin of the float angle.
     const int half = d.dim_head / 2;
@@ -209,16 +576,17 @@ int build(F5Plan &p, cudaStream_t user) {
     // stream and workspace set once, outside the capture (no cuBLAS allocation may happen while capturing)
     F5_TRY(blas_check(cublasSetStream(p.blas, p.cap), "set stream"));
     F5_TRY(blas_check(cublasSetWorkspace(p.blas, p.ws, kBlasWorkspace), "set workspace"));
-    // the capture stream starts after the caller's work so far (the table copy and the zeroed inputs)
+    // the capture stream starts after the caller's work so far (weight conversion, the table, the zeroed inputs)
     cudaEvent_t ev = nullptr;
     if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return check_launch("vox_cuda_f5_create");
     cudaEventRecord(ev, user);
     cudaStreamWaitEvent(p.cap, ev, 0);
     cudaEventDestroy(ev);
-    F5_TRY(record(p, p.cap));  // eager run: algorithm selection and first-use kernel attributes outside the capture
+    auto rec = [&p](cudaStream_t st) { return p.bf16 ? record_bf16(p, st) : record(p, st); };
+    F5_TRY(rec(p.cap));  // eager run: algorithm selection and first-use kernel attributes outside the capture
     if (cudaStreamSynchronize(p.cap) != cudaSuccess) return check_launch("vox_cuda_f5_create (eager run)");
     if (cudaStreamBeginCapture(p.cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return check_launch("vox_cuda_f5_create (capture)");
-    const int rc = record(p, p.cap);
+    const int rc = rec(p.cap);
     const cudaError_t end = cudaStreamEndCapture(p.cap, &p.graph);
     if (rc != VOX_CUDA_OK) return rc;
     if (end != cudaSuccess) return check_launch("vox_cuda_f5_create (end capture)");

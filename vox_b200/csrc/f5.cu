@@ -8,8 +8,8 @@
 // below; the projections and the two attention products are cuBLAS GEMMs (f32, or on the tensor cores with TF32 or
 // bf16 inputs and f32 accumulation). In the f32 and TF32 modes attention materialises the score matrix of one
 // sequence at a time ([heads][frames][frames] f32) and normalises it in place with the row softmax; in the bf16 mode
-// (dim_head 64) one fused kernel computes it from bf16 copies of q, k, v without writing the scores (mma.sync bf16,
-// online softmax).
+// (dim_head 64) one fused kernel computes it from the bf16 q|k|v projection without writing the scores (mma.sync
+// bf16, online softmax).
 //
 // The plan records the whole step once eagerly (kernel selection, first-use attributes), then again under stream
 // capture; a run is one cudaGraphLaunch. All buffers are the plan's, so the graph's pointers never change.
@@ -47,27 +47,24 @@ __global__ void __launch_bounds__(256) f5_rope_kernel(float *q, float *k, const 
 
 // ------------------------------------------------------------------ fused attention (bf16 math mode, dim_head 64)
 
-// RoPE as above, then q, k and v rounded to bf16 (RN) into qb, kb, vb [rows][inner]; q, k, v have row stride ld (the
-// fused projection [rows][3 inner] or separate [rows][inner] tensors). One thread per column pair.
-__global__ void __launch_bounds__(256) f5_qkv_bf16_kernel(const float *q, const float *k, const float *v, uint32_t ld, const float2 *cs,
-                                                          uint32_t *qb, uint32_t *kb, uint32_t *vb, uint32_t pairs, uint32_t frames,
-                                                          uint32_t half, uint32_t rope_heads, uint32_t hd, uint32_t inner) {
+// RoPE in place on the bf16 q and k of the fused projection qkv [rows][ld] (q at column 0, k at column inner): the
+// pair is widened to f32, rotated with the rounding of the CPU loop (f5.cpp:696-701) and rounded back to bf16 (RN).
+__global__ void __launch_bounds__(256) f5_rope_bf16_kernel(uint32_t *qkv, uint32_t ld, const float2 *cs, uint32_t pairs, uint32_t frames,
+                                                           uint32_t half, uint32_t rope_heads, uint32_t hd, uint32_t inner) {
     pdl_enter();
-    const uint32_t stride = gridDim.x * blockDim.x, row_pairs = inner / 2;
+    const uint32_t stride = gridDim.x * blockDim.x;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
-        const uint32_t r = i / row_pairs, col = 2 * (i % row_pairs);
-        const float2 a = *reinterpret_cast<const float2 *>(q + size_t(r) * ld + col);
-        const float2 b = *reinterpret_cast<const float2 *>(k + size_t(r) * ld + col);
-        const float2 c = *reinterpret_cast<const float2 *>(v + size_t(r) * ld + col);
-        float2 qa = a, kb2 = b;
-        if (col / hd < rope_heads) {
-            const float2 t = cs[size_t(r % frames) * half + (col % hd) / 2];
-            qa = make_float2(__fsub_rn(__fmul_rn(a.x, t.x), __fmul_rn(a.y, t.y)), __fadd_rn(__fmul_rn(a.y, t.x), __fmul_rn(a.x, t.y)));
-            kb2 = make_float2(__fsub_rn(__fmul_rn(b.x, t.x), __fmul_rn(b.y, t.y)), __fadd_rn(__fmul_rn(b.y, t.x), __fmul_rn(b.x, t.y)));
+        const uint32_t j = i % half, t = i / half;
+        const uint32_t h = t % rope_heads, r = t / rope_heads;
+        const float2 c = cs[size_t(r % frames) * half + j];
+        const size_t e = (size_t(r) * ld + size_t(h) * hd + 2 * j) / 2;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+            uint32_t *p = qkv + e + part * (inner / 2);
+            const uint32_t w = *p;
+            const float x0 = __uint_as_float(w << 16), x1 = __uint_as_float(w & 0xFFFF0000u);
+            *p = pack_bf16(__fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y)), __fadd_rn(__fmul_rn(x1, c.x), __fmul_rn(x0, c.y)));
         }
-        qb[i] = pack_bf16(qa.x, qa.y);
-        kb[i] = pack_bf16(kb2.x, kb2.y);
-        vb[i] = pack_bf16(c.x, c.y);
     }
 }
 
@@ -110,21 +107,22 @@ __device__ __forceinline__ void fa_stage(uint32_t tile, const __nv_bfloat16 *g, 
 
 // softmax(q k^T * scale) v for one sequence and head and 64 query rows, online over 64-key tiles (K and V double
 // buffered with cp.async): S and P in registers (P rounded to bf16 for the second product), f32 accumulation, the
-// row maximum and sum in the exp2 domain. at [rows][inner] f32 receives the normalised rows.
+// row maximum and sum in the exp2 domain. q, k, v have row stride ld_in (bf16); at [rows][inner] (f32 or bf16)
+// receives the normalised rows. 4 CTAs per SM, so a 1024-frame, 16-head, 2-sequence step runs in one wave.
 template <bool BF16_OUT>
-__global__ void __launch_bounds__(kFaThreads) f5_flash_kernel(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb, const __nv_bfloat16 *vb,
-                                                              void *at, int n, int inner, float scale_log2) {
+__global__ void __launch_bounds__(kFaThreads, 4) f5_flash_kernel(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb, const __nv_bfloat16 *vb,
+                                                              void *at, int n, int ld_in, int inner, float scale_log2) {
     pdl_enter();
     __shared__ __align__(128) uint8_t sm[5 * kFaRows * 128];  // Q, K[2], V[2]
     const uint32_t sQ = uint32_t(__cvta_generic_to_shared(sm)), sK = sQ + 8192, sV = sQ + 3 * 8192;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int q0 = blockIdx.x * kFaRows, head = blockIdx.y;
-    const size_t seq = size_t(blockIdx.z) * size_t(n) * size_t(inner) + size_t(head) * kFaHd;
+    const size_t seq = size_t(blockIdx.z) * size_t(n) * size_t(ld_in) + size_t(head) * kFaHd;
     const __nv_bfloat16 *Q = qb + seq, *K = kb + seq, *V = vb + seq;
     const int ntiles = (n + kFaKeys - 1) / kFaKeys;
-    fa_stage(sQ, Q, q0, n, inner);
-    fa_stage(sK, K, 0, n, inner);
-    fa_stage(sV, V, 0, n, inner);
+    fa_stage(sQ, Q, q0, n, ld_in);
+    fa_stage(sK, K, 0, n, ld_in);
+    fa_stage(sV, V, 0, n, ld_in);
     asm volatile("cp.async.commit_group;" ::: "memory");
     float o[8][4];
 #pragma unroll
@@ -134,8 +132,8 @@ __global__ void __launch_bounds__(kFaThreads) f5_flash_kernel(const __nv_bfloat1
     for (int kt = 0; kt < ntiles; ++kt) {
         const int buf = kt & 1;
         if (kt + 1 < ntiles) {
-            fa_stage(sK + (buf ^ 1) * 8192, K, (kt + 1) * kFaKeys, n, inner);
-            fa_stage(sV + (buf ^ 1) * 8192, V, (kt + 1) * kFaKeys, n, inner);
+            fa_stage(sK + (buf ^ 1) * 8192, K, (kt + 1) * kFaKeys, n, ld_in);
+            fa_stage(sV + (buf ^ 1) * 8192, V, (kt + 1) * kFaKeys, n, ld_in);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
         asm volatile("cp.async.wait_group 1;" ::: "memory");
@@ -322,8 +320,8 @@ struct F5Plan {
     // bf16 path (bf16 math, dim_head 64, dim % 4 == 0 and <= 2048): bf16 copies of the projection weights (q|k|v fused),
     // bf16 activations into every GEMM, the fused attention, all ada vectors by one batched GEMV
     bool bf16 = false;
-    float *qkv = nullptr, *ada_all = nullptr;
-    __nv_bfloat16 *qb = nullptr, *kb = nullptr, *vb = nullptr, *nrm_b = nullptr, *at_b = nullptr, *ff_b = nullptr;
+    float *ada_all = nullptr;
+    __nv_bfloat16 *qkv_b = nullptr, *nrm_b = nullptr, *at_b = nullptr, *ff_b = nullptr;
     __nv_bfloat16 *w_qkv = nullptr, *w_o = nullptr, *w_ff1 = nullptr, *w_ff2 = nullptr, *w_proj = nullptr;
     const void **ada_ptrs = nullptr;  // device [3][depth]: W_ada[l], ts, ada_all + l 6D
     cudaGraph_t graph = nullptr;
@@ -438,20 +436,19 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
                       "ada (batched)"));
     F5_TRY(gemm_xwt(p, p.ts, d.norm_out, p.fin, 1, 2 * D, D));  // fin = [scale, shift] (f5.cpp:720-722)
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
-    const uint32_t cpairs = uint32_t(R * IN / 2);
+    const uint32_t rpairs = uint32_t(R) * rope_heads * uint32_t(d.dim_head / 2);
     const dim3 fg(unsigned((d.frames + kFaRows - 1) / kFaRows), unsigned(d.heads), unsigned(d.batch));
     const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
     F5_TRY(resmod(p, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
     for (int64_t l = 0; l < L; ++l) {
         const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
-        F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv, CUDA_R_32F, R, 3 * IN, D));
-        launch_k(f5_qkv_bf16_kernel, grid_for(cpairs, 256, 4), 256, 0, st, (const float *)p.qkv, (const float *)(p.qkv + IN),
-                 (const float *)(p.qkv + 2 * IN), uint32_t(3 * IN), (const float2 *)p.cs, reinterpret_cast<uint32_t *>(p.qb),
-                 reinterpret_cast<uint32_t *>(p.kb), reinterpret_cast<uint32_t *>(p.vb), cpairs, uint32_t(d.frames),
-                 uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
-        F5_TRY(check_launch("vox_cuda_f5 rope/bf16"));
-        launch_k(f5_flash_kernel<true>, fg, kFaThreads, 0, st, (const __nv_bfloat16 *)p.qb, (const __nv_bfloat16 *)p.kb,
-                 (const __nv_bfloat16 *)p.vb, (void *)p.at_b, int(d.frames), int(IN), scale_log2);
+        F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv_b, CUDA_R_16BF, R, 3 * IN, D));
+        launch_k(f5_rope_bf16_kernel, grid_for(rpairs, 256, 4), 256, 0, st, reinterpret_cast<uint32_t *>(p.qkv_b), uint32_t(3 * IN),
+                 (const float2 *)p.cs, rpairs, uint32_t(d.frames), uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head),
+                 uint32_t(IN));
+        F5_TRY(check_launch("vox_cuda_f5 rope (bf16)"));
+        launch_k(f5_flash_kernel<true>, fg, kFaThreads, 0, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
+                 (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (void *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
         F5_TRY(check_launch("vox_cuda_f5 attention"));
         F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
         F5_TRY(resmod(p, p.o, A + 2 * D, A + 4 * D, A + 3 * D, st));
@@ -476,8 +473,7 @@ void release(F5Plan *p) {
     if (p->blas) cublasDestroy(p->blas);
     for (void *b : {(void *)p->ws, (void *)p->h, (void *)p->ts, (void *)p->out, (void *)p->nrm, (void *)p->q, (void *)p->k,
                     (void *)p->v, (void *)p->at, (void *)p->o, (void *)p->ffb, (void *)p->s, (void *)p->ada, (void *)p->fin,
-                    (void *)p->cs, (void *)p->qkv, (void *)p->ada_all, (void *)p->qb, (void *)p->kb, (void *)p->vb,
-                    (void *)p->nrm_b, (void *)p->at_b, (void *)p->ff_b, (void *)p->w_qkv, (void *)p->w_o, (void *)p->w_ff1,
+                    (void *)p->cs, (void *)p->qkv_b, (void *)p->ada_all, (void *)p->nrm_b, (void *)p->at_b, (void *)p->ff_b, (void *)p->w_qkv, (void *)p->w_o, (void *)p->w_ff1,
                     (void *)p->w_ff2, (void *)p->w_proj, (void *)p->ada_ptrs})
         if (b) cudaFree(b);
     if (p->cap) cudaStreamDestroy(p->cap);
@@ -511,11 +507,8 @@ int build(F5Plan &p, cudaStream_t user) {
     F5_TRY(alloc(&p.cs, N * size_t(d.dim_head / 2), "rope table"));
     F5_TRY(alloc(reinterpret_cast<uint8_t **>(&p.ws), kBlasWorkspace, "cuBLAS workspace"));
     if (p.bf16) {
-        F5_TRY(alloc(&p.qkv, R * 3 * IN, "qkv"));
+        F5_TRY(alloc(&p.qkv_b, R * 3 * IN, "q|k|v (bf16)"));
         F5_TRY(alloc(&p.ada_all, L * 6 * D, "ada"));
-        F5_TRY(alloc(&p.qb, R * IN, "q (bf16)"));
-        F5_TRY(alloc(&p.kb, R * IN, "k (bf16)"));
-        F5_TRY(alloc(&p.vb, R * IN, "v (bf16)"));
         F5_TRY(alloc(&p.nrm_b, R * D, "nrm (bf16)"));
         F5_TRY(alloc(&p.at_b, R * IN, "attention (bf16)"));
         F5_TRY(alloc(&p.ff_b, R * FF, "ff (bf16)"));

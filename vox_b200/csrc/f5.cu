@@ -47,23 +47,31 @@ __global__ void __launch_bounds__(256) f5_rope_kernel(float *q, float *k, const 
 
 // ------------------------------------------------------------------ fused attention (bf16 math mode, dim_head 64)
 
-// RoPE in place on the bf16 q and k of the fused projection qkv [rows][ld] (q at column 0, k at column inner): the
-// pair is widened to f32, rotated with the rounding of the CPU loop (f5.cpp:696-701) and rounded back to bf16 (RN).
-__global__ void __launch_bounds__(256) f5_rope_bf16_kernel(uint32_t *qkv, uint32_t ld, const float2 *cs, uint32_t pairs, uint32_t frames,
+// RoPE in place on the bf16 q and k of the fused projection qkv [rows][ld] (q at column 0, k at column inner): four
+// pairs (16 bytes) per thread, each widened to f32, rotated with the rounding of the CPU loop (f5.cpp:696-701) and
+// rounded back to bf16 (RN). quads = rows * rope_heads * hd / 8; hd % 8 == 0.
+__global__ void __launch_bounds__(256) f5_rope_bf16_kernel(uint4 *qkv, uint32_t ld, const float2 *cs, uint32_t quads, uint32_t frames,
                                                            uint32_t half, uint32_t rope_heads, uint32_t hd, uint32_t inner) {
     pdl_enter();
-    const uint32_t stride = gridDim.x * blockDim.x;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
-        const uint32_t j = i % half, t = i / half;
+    const uint32_t stride = gridDim.x * blockDim.x, qph = half / 4;  // quads per head
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += stride) {
+        const uint32_t j4 = i % qph, t = i / qph;
         const uint32_t h = t % rope_heads, r = t / rope_heads;
-        const float2 c = cs[size_t(r % frames) * half + j];
-        const size_t e = (size_t(r) * ld + size_t(h) * hd + 2 * j) / 2;
+        const float4 *c4 = reinterpret_cast<const float4 *>(cs + size_t(r % frames) * half + 4 * j4);
+        const float4 ca = c4[0], cb = c4[1];  // (cos, sin) of pairs 4 j4 .. 4 j4 + 3
+        const float cc[4] = {ca.x, ca.z, cb.x, cb.z}, ss[4] = {ca.y, ca.w, cb.y, cb.w};
+        const size_t e = (size_t(r) * ld + size_t(h) * hd + 8 * j4) / 8;
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
-            uint32_t *p = qkv + e + part * (inner / 2);
-            const uint32_t w = *p;
-            const float x0 = __uint_as_float(w << 16), x1 = __uint_as_float(w & 0xFFFF0000u);
-            *p = pack_bf16(__fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y)), __fadd_rn(__fmul_rn(x1, c.x), __fmul_rn(x0, c.y)));
+            uint4 *p = qkv + e + part * (inner / 8);
+            uint4 w = *p;
+            uint32_t *wp = &w.x;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float x0 = __uint_as_float(wp[k] << 16), x1 = __uint_as_float(wp[k] & 0xFFFF0000u);
+                wp[k] = pack_bf16(__fsub_rn(__fmul_rn(x0, cc[k]), __fmul_rn(x1, ss[k])), __fadd_rn(__fmul_rn(x1, cc[k]), __fmul_rn(x0, ss[k])));
+            }
+            *p = w;
         }
     }
 }
@@ -436,15 +444,15 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
                       "ada (batched)"));
     F5_TRY(gemm_xwt(p, p.ts, d.norm_out, p.fin, 1, 2 * D, D));  // fin = [scale, shift] (f5.cpp:720-722)
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
-    const uint32_t rpairs = uint32_t(R) * rope_heads * uint32_t(d.dim_head / 2);
+    const uint32_t rquads = uint32_t(R) * rope_heads * uint32_t(d.dim_head / 8);
     const dim3 fg(unsigned((d.frames + kFaRows - 1) / kFaRows), unsigned(d.heads), unsigned(d.batch));
     const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
     F5_TRY(resmod(p, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
     for (int64_t l = 0; l < L; ++l) {
         const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
         F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv_b, CUDA_R_16BF, R, 3 * IN, D));
-        launch_k(f5_rope_bf16_kernel, grid_for(rpairs, 256, 4), 256, 0, st, reinterpret_cast<uint32_t *>(p.qkv_b), uint32_t(3 * IN),
-                 (const float2 *)p.cs, rpairs, uint32_t(d.frames), uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head),
+        launch_k(f5_rope_bf16_kernel, grid_for(rquads, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.qkv_b), uint32_t(3 * IN),
+                 (const float2 *)p.cs, rquads, uint32_t(d.frames), uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head),
                  uint32_t(IN));
         F5_TRY(check_launch("vox_cuda_f5 rope (bf16)"));
         launch_k(f5_flash_kernel<true>, fg, kFaThreads, 0, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),

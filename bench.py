@@ -173,16 +173,20 @@ class Suite:
 
                 add(nm, wbytes + GR * (GC // 32) * 2 + mm * GC * 4 + mm * GR * 4, GR * GC * mm, call, [mats[0], scs[0], gx], [gy])
         # F5-TTS DiT step (the transformer of gpu_f5_step, one CUDA graph): F5 base (dim 1024, 22 blocks of 16 heads x 64,
-        # ff 2048, mel 100) on 2 sequences (conditional and unconditional) of 1024 frames, seeded random weights; each step
+        # ff 2048, mel 100) on 2 sequences (conditional and unconditional) of 1024 frames, seeded random weights and biases; each step
         # writes the residual stream and time embedding into the plan, then replays the graph
         if any(want_next(f"next_f5_dit_{m}") for m in ("tf32", "bf16")):
             D, H, HD, FFm, L, O, Bq, Nf = 1024, 16, 64, 2, 22, 100, 2, 1024
             IN, FF, Rr = H * HD, FFm * D, Bq * Nf
             gen = torch.Generator(device=dev).manual_seed(7)
             W = lambda o, i, s=1.0: torch.randn(o, i, device=dev, generator=gen) * (s * i ** -0.5)  # noqa: E731
-            fblocks = [{"ada": W(6 * D, D, 0.3), "q": W(IN, D), "k": W(IN, D), "v": W(IN, D), "o": W(D, IN), "ff1": W(FF, D),
-                        "ff2": W(D, FF)} for _ in range(L)]
-            norm_out, proj_out = W(2 * D, D, 0.3), W(O, D)
+            Bv = lambda o: torch.randn(o, device=dev, generator=gen) * 0.1  # noqa: E731
+            fblocks = []
+            for _ in range(L):  # every linear biased, as F5 checkpoints are
+                fb = {"ada": W(6 * D, D, 0.3), "q": W(IN, D), "k": W(IN, D), "v": W(IN, D), "o": W(D, IN), "ff1": W(FF, D), "ff2": W(D, FF)}
+                fb.update({k + "_b": Bv(fb[k].shape[0]) for k in list(fb)})
+                fblocks.append(fb)
+            norm_out, proj_out, norm_out_b, proj_out_b = W(2 * D, D, 0.3), W(O, D), Bv(2 * D), Bv(O)
             h0, ts0 = fill(E(Rr, D), 1, 0, 1, 60), fill(E(D), 1, 0, 1, 61)
             fl = L * (2 * 6 * D * D + 3 * 2 * Rr * D * IN + 2 * 2 * Bq * H * Nf * Nf * HD + 2 * Rr * IN * D + 2 * 2 * Rr * D * FF) \
                 + 2 * 2 * D * D + 2 * Rr * D * O
@@ -191,7 +195,8 @@ class Suite:
                 nm = f"next_f5_dit_{m}"
                 if not want_next(nm):
                     continue
-                plan = vox.F5Dit(fblocks, norm_out, proj_out, heads=H, dim_head=HD, batch=Bq, frames=Nf, math=m)
+                plan = vox.F5Dit(fblocks, norm_out, proj_out, heads=H, dim_head=HD, batch=Bq, frames=Nf, math=m, norm_out_b=norm_out_b,
+                                 proj_out_b=proj_out_b)
                 self.f5_plans.append(plan)
 
                 def f5_step(plan=plan):

@@ -309,9 +309,10 @@ VOX_CUDA_API int vox_cuda_tmod_upload_dequant(vox_cuda_tmod *t, const char *name
  * frame position, on the first pe_attn_head heads (all heads if 0); attention without mask per sequence and head,
  * softmax(q k^T / sqrt(dim_head)) v; h += gate_msa * (at . W_o^T); the MLP the same way with GELU (tanh form) between
  * ff1 and ff2. Output: fin = W_norm_out . ts = [scale, shift], out = (LayerNorm(h) * (1 + scale) + shift) . W_proj^T.
- * Linear layers carry no bias (Vox's matmul, kernels.hpp). Weights are f32 device buffers [out][in] (Vox's Mat
- * layout), owned by the caller and read at every run (the bf16 mode reads its own bf16 copies of q, k, v, o, ff1, ff2
- * and proj_out, made at create). The input embedding (in_proj and the convolutional position
+ * Every linear layer is y = x W^T + b as Vox's matmul computes it (kernels.hpp:83, the bias a Mat carries when the
+ * file holds "<name>.bias", f5.cpp:59-84); a NULL bias is zero. Weights and biases are f32 device buffers, weights
+ * [out][in] (Vox's Mat layout), owned by the caller and read at every run (the bf16 mode reads its own bf16 copies of
+ * the q, k, v, o, ff1, ff2 and proj_out weights, made at create; biases stay f32 and are read at every run). The input embedding (in_proj and the convolutional position
  * embedding, gpu_f5.cpp:284-289) is not part of this entry. */
 #define VOX_CUDA_F5_MATH_F32 0  /* f32 GEMMs on the CUDA cores (reference accuracy) */
 #define VOX_CUDA_F5_MATH_TF32 1 /* tensor cores, TF32 inputs, f32 accumulation */
@@ -325,6 +326,7 @@ typedef struct vox_cuda_f5_block_weights {
     const float *o;          /* [dim][heads * dim_head] */
     const float *ff1;        /* [ff_mult * dim][dim] */
     const float *ff2;        /* [dim][ff_mult * dim] */
+    const float *ada_b, *q_b, *k_b, *v_b, *o_b, *ff1_b, *ff2_b; /* biases [out] of the same layers, or NULL */
 } vox_cuda_f5_block_weights;
 typedef struct vox_cuda_f5_desc {
     int32_t dim, heads, dim_head, ff_mult, depth, pe_attn_head, out_dim;
@@ -333,6 +335,7 @@ typedef struct vox_cuda_f5_desc {
     const vox_cuda_f5_block_weights *blocks; /* [depth], copied at create */
     const float *norm_out;  /* [2 dim][dim]: (scale, shift) */
     const float *proj_out;  /* [out_dim][dim] */
+    const float *norm_out_b, *proj_out_b; /* their biases, or NULL */
 } vox_cuda_f5_desc;
 typedef struct vox_cuda_f5 vox_cuda_f5;
 /* Allocates the plan's buffers on the current device (h [batch*frames][dim], ts [dim], out [batch*frames][out_dim] and

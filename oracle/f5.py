@@ -63,25 +63,33 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, batch: int, frames: i
     return (p @ vh).transpose(0, 2, 1, 3).reshape(batch * frames, heads * dim_head)
 
 
-def dit(h, ts, blocks, norm_out, proj_out, *, heads: int, dim_head: int, batch: int, frames: int, pe_attn_head: int = 0):
+def linear(x, w, b=None):
+    """y = x W^T (+ b): Vox's matmul with the bias its Mat carries (kernels.hpp:83, f5.cpp:59-84)."""
+    y = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+    return y if b is None else y + np.asarray(b, np.float64)
+
+
+def dit(h, ts, blocks, norm_out, proj_out, *, heads: int, dim_head: int, batch: int, frames: int, pe_attn_head: int = 0,
+        norm_out_b=None, proj_out_b=None):
     """Returns (out [R][out_dim], h after the blocks [R][D]) in float64 for h [R][D], ts [D] and the weights (numpy
-    arrays, [out][in] as Vox's Mat, no biases): the loop of f5.cpp:678-717 and the output of f5.cpp:719-723."""
+    arrays, [out][in] as Vox's Mat, each with an optional bias "<name>_b"): the loop of f5.cpp:678-717 and the output of
+    f5.cpp:719-723."""
     h = np.asarray(h, np.float64).copy()
     ts = np.asarray(ts, np.float64)
     D = h.shape[1]
     rope_heads = pe_attn_head if pe_attn_head > 0 else heads
-    W = lambda a: np.asarray(a, np.float64)  # noqa: E731
     for L in blocks:
-        ada = W(L["ada"]) @ ts
+        lin = lambda x, k: linear(x, L[k], L.get(k + "_b"))  # noqa: E731
+        ada = lin(ts[None, :], "ada")[0]
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (ada[i * D:(i + 1) * D] for i in range(6))
         nrm = modulate(h, scale_msa, shift_msa)
-        q, k, v = nrm @ W(L["q"]).T, nrm @ W(L["k"]).T, nrm @ W(L["v"]).T
+        q, k, v = lin(nrm, "q"), lin(nrm, "k"), lin(nrm, "v")
         q, k = rope(q, frames, heads, dim_head, rope_heads), rope(k, frames, heads, dim_head, rope_heads)
         at = attention(q, k, v, batch, frames, heads, dim_head)
-        h += gate_msa[None, :] * (at @ W(L["o"]).T)
+        h += gate_msa[None, :] * lin(at, "o")
         nrm = modulate(h, scale_mlp, shift_mlp)
-        ff = gelu_tanh(nrm @ W(L["ff1"]).T)
-        h += gate_mlp[None, :] * (ff @ W(L["ff2"]).T)
-    fin = W(norm_out) @ ts  # (scale, shift)
-    out = modulate(h, fin[:D], fin[D:]) @ W(proj_out).T
+        ff = gelu_tanh(lin(nrm, "ff1"))
+        h += gate_mlp[None, :] * lin(ff, "ff2")
+    fin = linear(ts[None, :], norm_out, norm_out_b)[0]  # (scale, shift)
+    out = linear(modulate(h, fin[:D], fin[D:]), proj_out, proj_out_b)
     return out, h

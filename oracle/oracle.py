@@ -384,6 +384,9 @@ class Ref:
         L.vr_tmod_write.restype = _int
         L.vr_tmod_read.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _p, _u64]
         L.vr_tmod_read.restype = _i64
+        if hasattr(L, "vr_f5_dit"):
+            L.vr_f5_dit.argtypes = [ctypes.c_char_p, _int, _int, _p, _p, _p, _f, _p, _p, ctypes.c_char_p, _int]
+            L.vr_f5_dit.restype = _int
 
     def set_threads(self, n: int) -> int:
         self.L.vr_set_threads(n)
@@ -570,6 +573,16 @@ class Ref:
                                   _ptr(shapes), _ptr(nd), ctypes.cast(ptrs, _p), _ptr(nb), flags)
         if rc != 0:
             raise RuntimeError("vox::tmod_write failed")
+
+    def f5_dit(self, path, x, cond, temb, t: float, dim: int):
+        """F5Model(path) on the CPU: (time_embed(t) [dim], dit_forward(B, N, x, cond, temb, t) [B][N][mel_dim])."""
+        x, cond, temb = _c(x, np.float32), _c(cond, np.float32), _c(temb, np.float32)
+        B, N, M = x.shape
+        ts, out = np.empty(dim, np.float32), np.empty((B, N, M), np.float32)
+        err = ctypes.create_string_buffer(512)
+        if self.L.vr_f5_dit(str(path).encode(), B, N, _ptr(x), _ptr(cond), _ptr(temb), float(t), _ptr(ts), _ptr(out), err, 512) != 0:
+            raise RuntimeError("F5Model: " + err.value.decode(errors="replace"))
+        return ts, out
 
     def tmod_read(self, path, name: str) -> bytes | None:
         """vox::TmodFile(path).get(name) bytes, or None (missing blob or bad file)."""

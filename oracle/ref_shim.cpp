@@ -11,7 +11,9 @@
 // the reference's grain, and cited.
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
+#include <memory>
 #include <vector>
 
 #include "f5.hpp"
@@ -318,6 +320,27 @@ VR_API int64_t vr_tmod_read(const char *path, const char *name, uint8_t *out, ui
         if (v.nbytes <= cap) std::memcpy(out, v.data, v.nbytes);
         return int64_t(v.nbytes);
     } catch (...) {
+        return -1;
+    }
+}
+
+// ---------------------------------------------------------------- F5 DiT forward (f5.cpp)
+
+// F5Model (f5.cpp:258-393) loaded from the .tmod file `path` on the CPU (gpu = false), then F5Model::time_embed(t)
+// (the SiLU'd time embedding every AdaLN reads, f5.cpp:510-526) into ts [dim] and F5Model::dit_forward(B, N, x, cond,
+// temb, t) into out [B][N][mel_dim] (f5.cpp:563-724). Returns 0, or -1 with the exception's message in err.
+VR_API int vr_f5_dit(const char *path, int B, int N, const float *x, const float *cond, const float *temb, float t, float *ts,
+                     float *out, char *err, int errcap) {
+    try {
+        auto f = std::make_shared<TmodFile>(path);
+        F5Model m(f, false);
+        std::vector<float> tv;
+        m.time_embed(t, tv);
+        std::memcpy(ts, tv.data(), tv.size() * sizeof(float));
+        m.dit_forward(B, N, x, cond, temb, t, out);
+        return 0;
+    } catch (const std::exception &e) {
+        std::snprintf(err, size_t(errcap), "%s", e.what());
         return -1;
     }
 }

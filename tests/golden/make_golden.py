@@ -146,8 +146,83 @@ def main() -> None:
         "norm": (0, (64,), tnorm.tobytes()), "emb": (2, (3, 8), np.asarray(temb, np.uint16).tobytes())})
     np.savez_compressed(OUT / "tmod.npz", q8=tq8, q4=tq4, s8=ts8, s4=ts4, norm=tnorm, emb=np.asarray(temb, np.uint16),
                         q8_deq=R.mat_rows(tq8, ts8), q4_deq=R.mat_rows(tq4, ts4, q4=True))
+    f5_golden(P, R)
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
+
+
+# -- F5 DiT forward (F5Model::dit_forward, f5.cpp:563-724) of a tiny random model written with the reference's own
+#    tmod_write: every linear with a bias, RoPE on the first head only (pe_attn_head 1), no text-encoder or Vocos
+#    layers; the second position-embedding convolution is zero, so the residual stream entering the blocks is exactly
+#    in_proj([x, cond, temb]). Saved: the inputs, the weights the blocks and output head read, the reference's time
+#    embedding ts and its output.
+F5_DIMS = dict(dim=32, depth=2, heads=2, dim_head=16, ff_mult=2, text_dim=16, text_rows=4, mel_dim=20, pe_attn_head=1)
+
+
+def f5_golden(P, R) -> None:
+    import json
+    import tempfile
+
+    c = F5_DIMS
+    D, M, TD, L = c["dim"], c["mel_dim"], c["text_dim"], c["depth"]
+    IN, FF = c["heads"] * c["dim_head"], c["ff_mult"] * c["dim"]
+    sid = [300]
+
+    def nrm(shape, std):
+        sid[0] += 1
+        return P.normal(shape, 0.0, std, sid=sid[0]).astype(np.float32)
+
+    lin = lambda o, i: (nrm((o, i), 1.0 / np.sqrt(i)), nrm((o,), 0.1))  # noqa: E731
+    blobs, arrays = {}, {}
+
+    def put(name, arr):
+        blobs[name] = (0, arr.shape, np.ascontiguousarray(arr, np.float32).tobytes())
+
+    def put_lin(name, key, o, i):
+        w, b = lin(o, i)
+        put(name + ".weight", w)
+        put(name + ".bias", b)
+        if key:
+            arrays[key], arrays[key + "_b"] = w, b
+
+    put("mel.fb", np.abs(nrm((M, 9), 0.1)))  # n_fft 16
+    d = "dit."
+    put_lin(d + "time_embed.time_mlp.0", None, D, 256)
+    put_lin(d + "time_embed.time_mlp.2", None, D, D)
+    put(d + "text_embed.text_embed.weight", nrm((c["text_rows"], TD), 1.0))
+    put_lin(d + "input_embed.proj", "in_proj", D, 2 * M + TD)
+    put(d + "input_embed.conv_pos_embed.conv1d.0.weight", nrm((D, D // 16, 31), 0.1))
+    put(d + "input_embed.conv_pos_embed.conv1d.0.bias", nrm((D,), 0.1))
+    put(d + "input_embed.conv_pos_embed.conv1d.2.weight", np.zeros((D, D // 16, 31), np.float32))
+    put(d + "input_embed.conv_pos_embed.conv1d.2.bias", np.zeros((D,), np.float32))
+    names = {"ada": "attn_norm.linear", "q": "attn.to_q", "k": "attn.to_k", "v": "attn.to_v", "o": "attn.to_out.0",
+             "ff1": "ff.ff.0.0", "ff2": "ff.ff.2"}
+    shapes = {"ada": (6 * D, D), "q": (IN, D), "k": (IN, D), "v": (IN, D), "o": (D, IN), "ff1": (FF, D), "ff2": (D, FF)}
+    for l in range(L):
+        for k, nm in names.items():
+            put_lin(f"{d}transformer_blocks.{l}.{nm}", f"b{l}_{k}", *shapes[k])
+    put_lin(d + "norm_out.linear", "norm_out", 2 * D, D)
+    put_lin(d + "proj_out", "proj_out", M, D)
+    V = 16
+    put("vocos.backbone.embed.weight", nrm((V, M, 7), 0.1))
+    for nm in ("norm", "final_layer_norm"):
+        put(f"vocos.backbone.{nm}.weight", np.ones(V, np.float32))
+        put(f"vocos.backbone.{nm}.bias", np.zeros(V, np.float32))
+    put("vocos.head.out.weight", nrm((18, V), 0.1))
+    manifest = {"family": "f5", "f5": {
+        "dim": D, "depth": L, "heads": c["heads"], "dim_head": c["dim_head"], "ff_mult": c["ff_mult"], "text_dim": TD,
+        "text_rows": c["text_rows"], "mel_dim": M, "conv_layers": 0, "pe_attn_head": c["pe_attn_head"],
+        "mel": {"sample_rate": 24000, "n_fft": 16, "hop": 4, "win": 16, "n_mels": M},
+        "vocos": {"dim": V, "intermediate": 32, "layers": 0, "n_fft": 16, "hop": 4, "padding": "same"},
+        "tokenizer": {"type": "char", "vocab": ["a"]}}}
+    B, N, t = 2, 24, 0.37
+    x, cond, temb = nrm((B, N, M), 1.0), nrm((B, N, M), 1.0), nrm((B, N, TD), 1.0)
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "f5.tmod"
+        R.tmod_write(path, json.dumps(manifest), blobs)
+        ts, out = R.f5_dit(path, x, cond, temb, t, D)
+    np.savez_compressed(OUT / "f5.npz", dims=np.array([c[k] for k in F5_DIMS], np.int64), x=x, cond=cond, temb=temb,
+                        t=np.float32(t), ts=ts, out=out, **arrays)
 
 
 if __name__ == "__main__":

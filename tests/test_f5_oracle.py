@@ -55,21 +55,14 @@ def test_dit_of_zero_blocks_is_the_output_head():
     np.testing.assert_array_equal(h2, h)
 
 
-class _Block(ctypes.Structure):
-    _fields_ = [(k, ctypes.c_void_p) for k in ("ada", "q", "k", "v", "o", "ff1", "ff2")]
-
-
-class _Desc(ctypes.Structure):
-    _fields_ = [(k, ctypes.c_int32) for k in ("dim", "heads", "dim_head", "ff_mult", "depth", "pe_attn_head", "out_dim", "batch",
-                                              "frames", "math")] + \
-               [("blocks", ctypes.POINTER(_Block)), ("norm_out", ctypes.c_void_p), ("proj_out", ctypes.c_void_p)]
+from vox_b200 import _F5Block as _Block, _F5Desc as _Desc  # the C layouts of vox_cuda_f5_block_weights / vox_cuda_f5_desc
 
 
 @pytest.mark.parametrize("field,value", [("dim_head", 15), ("pe_attn_head", 5), ("math", 7), ("depth", 0), ("frames", 0)])
 def test_f5_create_rejects_bad_descriptions(vox_lib, field, value):
     L = vox_lib.lib
     blk = (_Block * 1)(_Block(*([8] * 7)))
-    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8)
+    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8, None, None)
     setattr(d, field, value)
     h = ctypes.c_void_p()
     assert L.vox_cuda_f5_create(ctypes.byref(d), None, ctypes.byref(h)) == -6
@@ -80,8 +73,33 @@ def test_f5_create_rejects_bad_descriptions(vox_lib, field, value):
 def test_f5_create_rejects_null_weights(vox_lib):
     L = vox_lib.lib
     blk = (_Block * 1)(_Block(8, 8, 8, None, 8, 8, 8))
-    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8)
+    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8, None, None)
     h = ctypes.c_void_p()
     assert L.vox_cuda_f5_create(ctypes.byref(d), None, ctypes.byref(h)) == -6
     assert L.vox_cuda_f5_create(None, None, ctypes.byref(h)) == -6
     L.vox_cuda_f5_destroy(None)
+
+
+def f5_golden_model(g):
+    """The golden F5 model (tests/golden/f5.npz, written by make_golden.py from the reference): the residual stream
+    entering the blocks (in_proj of [x, cond, temb]; the position embedding is zero there), ts, and the weights."""
+    keys = ("dim", "depth", "heads", "dim_head", "ff_mult", "text_dim", "text_rows", "mel_dim", "pe_attn_head")
+    dims = dict(zip(keys, (int(v) for v in g["dims"])))
+    B, N, M = g["x"].shape
+    cat = np.concatenate([g["x"], g["cond"], g["temb"]], axis=2).reshape(B * N, -1)
+    h = F5.linear(cat, g["in_proj"], g["in_proj_b"])
+    blocks = [{k: g[f"b{l}_{k}"] for k in ("ada", "q", "k", "v", "o", "ff1", "ff2", "ada_b", "q_b", "k_b", "v_b", "o_b", "ff1_b",
+                                           "ff2_b")} for l in range(dims["depth"])]
+    return dims, B, N, h, blocks
+
+
+def test_dit_matches_reference_dit_forward(golden):
+    """The oracle's DiT from the residual stream to the output equals F5Model::dit_forward of the reference (f32 CPU
+    arithmetic against float64: within 1e-5 of the output's RMS)."""
+    g = golden["f5"]
+    dims, B, N, h, blocks = f5_golden_model(g)
+    out, _ = F5.dit(h, g["ts"], blocks, g["norm_out"], g["proj_out"], heads=dims["heads"], dim_head=dims["dim_head"], batch=B,
+                    frames=N, pe_attn_head=dims["pe_attn_head"], norm_out_b=g["norm_out_b"], proj_out_b=g["proj_out_b"])
+    want = g["out"].reshape(B * N, -1).astype(np.float64)
+    err = np.abs(out - want).max() / np.sqrt(np.mean(want ** 2))
+    assert err <= 1e-5, err

@@ -551,13 +551,15 @@ class Tmod:
 # ------------------------------------------------------------------ F5 DiT step (one CUDA graph)
 
 class _F5Block(ctypes.Structure):
-    _fields_ = [(k, ctypes.c_void_p) for k in ("ada", "q", "k", "v", "o", "ff1", "ff2")]
+    _fields_ = [(k, ctypes.c_void_p) for k in ("ada", "q", "k", "v", "o", "ff1", "ff2", "ada_b", "q_b", "k_b", "v_b", "o_b", "ff1_b",
+                                              "ff2_b")]
 
 
 class _F5Desc(ctypes.Structure):
     _fields_ = [(k, ctypes.c_int32) for k in ("dim", "heads", "dim_head", "ff_mult", "depth", "pe_attn_head", "out_dim", "batch",
                                               "frames", "math")] + \
-               [("blocks", ctypes.POINTER(_F5Block)), ("norm_out", ctypes.c_void_p), ("proj_out", ctypes.c_void_p)]
+               [("blocks", ctypes.POINTER(_F5Block)), ("norm_out", ctypes.c_void_p), ("proj_out", ctypes.c_void_p),
+                ("norm_out_b", ctypes.c_void_p), ("proj_out_b", ctypes.c_void_p)]
 
 
 class _DevView:
@@ -571,15 +573,16 @@ class F5Dit:
     """The transformer of one F5-TTS DiT step (Vox's gpu_f5_step, gpu_f5.cpp:273-332; CPU F5Model::dit,
     f5.cpp:608-724) from the residual stream h after the input embedding to the output projection, captured once as a
     CUDA graph (vox_cuda_f5_create) and replayed by run(). `blocks` is a list of dicts of f32 CUDA tensors
-    {ada [6D][D], q/k/v [H*HD][D], o [D][H*HD], ff1 [F][D], ff2 [D][F]} in Vox's [out][in] layout (no biases);
-    norm_out [2D][D] gives (scale, shift), proj_out [out_dim][D]. `math`: "f32" (CUDA-core GEMMs), "tf32" or "bf16"
-    (tensor cores, f32 accumulation). h, ts and out are the plan's own buffers (torch views)."""
+    {ada [6D][D], q/k/v [H*HD][D], o [D][H*HD], ff1 [F][D], ff2 [D][F]} in Vox's [out][in] layout, each with an
+    optional bias "<name>_b" [out] (absent: zero); norm_out [2D][D] gives (scale, shift), proj_out [out_dim][D], with
+    optional biases norm_out_b, proj_out_b. `math`: "f32" (CUDA-core GEMMs), "tf32" or "bf16" (tensor cores, f32
+    accumulation). h, ts and out are the plan's own buffers (torch views, valid until close())."""
 
     MATH = {"f32": 0, "tf32": 1, "bf16": 2}
     KEYS = ("ada", "q", "k", "v", "o", "ff1", "ff2")
 
     def __init__(self, blocks, norm_out, proj_out, *, heads: int, dim_head: int, batch: int, frames: int,
-                 pe_attn_head: int = 0, math: str = "tf32"):
+                 pe_attn_head: int = 0, math: str = "tf32", norm_out_b=None, proj_out_b=None):
         if math not in self.MATH:
             raise VoxCudaError(-6, f"math must be one of {sorted(self.MATH)}")
         D = int(norm_out.shape[1])
@@ -588,18 +591,26 @@ class F5Dit:
         if not blocks or ff % D:
             raise VoxCudaError(-6, "blocks must be non-empty and ff1 rows a multiple of dim")
         want = {"ada": (6 * D, D), "q": (inner, D), "k": (inner, D), "v": (inner, D), "o": (D, inner), "ff1": (ff, D), "ff2": (D, ff)}
-        for i, b in enumerate(blocks):
-            for k, shp in want.items():
-                t = _dev(b[k], f"blocks[{i}].{k}")
-                if t.dtype != torch.float32 or tuple(t.shape) != shp:
-                    raise VoxCudaError(-6, f"blocks[{i}].{k} must be f32 {shp}")
-        for t, nm, shp in ((norm_out, "norm_out", (2 * D, D)), (proj_out, "proj_out", (out_dim, D))):
+        def check(t, nm, shp):
+            if t is None:
+                return None
             if _dev(t, nm).dtype != torch.float32 or tuple(t.shape) != shp:
                 raise VoxCudaError(-6, f"{nm} must be f32 {shp}")
-        self._keep = (blocks, norm_out, proj_out)  # read by every run
-        arr = (_F5Block * len(blocks))(*[_F5Block(*(b[k].data_ptr() for k in self.KEYS)) for b in blocks])
+            return t.data_ptr()
+
+        for i, b in enumerate(blocks):
+            for k, shp in want.items():
+                check(b[k], f"blocks[{i}].{k}", shp)
+                check(b.get(k + "_b"), f"blocks[{i}].{k}_b", shp[:1])
+        check(norm_out, "norm_out", (2 * D, D))
+        check(proj_out, "proj_out", (out_dim, D))
+        nb, pb = check(norm_out_b, "norm_out_b", (2 * D,)), check(proj_out_b, "proj_out_b", (out_dim,))
+        self._keep = (blocks, norm_out, proj_out, norm_out_b, proj_out_b)  # read by every run
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        arr = (_F5Block * len(blocks))(*[_F5Block(*([b[k].data_ptr() for k in self.KEYS] + [ptr(b.get(k + "_b")) for k in self.KEYS]))
+                                         for b in blocks])
         desc = _F5Desc(D, heads, dim_head, ff // D, len(blocks), pe_attn_head, out_dim, batch, frames, self.MATH[math], arr,
-                       norm_out.data_ptr(), proj_out.data_ptr())
+                       norm_out.data_ptr(), proj_out.data_ptr(), nb, pb)
         h = ctypes.c_void_p()
         _check(lib.vox_cuda_f5_create(ctypes.byref(desc), _stream(norm_out), ctypes.byref(h)))
         self._h = h

@@ -64,14 +64,6 @@ __device__ __forceinline__ float2 gelu_erf_f2(float2 x) {
     const float2 hi = fma2(xq, bc2(-1.0f), x);                    // x - x Q(|x|)
     return make_float2(x.x >= 0.f ? hi.x : xq.x, x.y >= 0.f ? hi.y : xq.y);
 }
-// GELU, tanh form (f5.cpp:93-96): 0.5 x (1 + tanh(k (x + 0.044715 x^3))), tanh(z) = 1 - 2 / (1 + e^(2z)).
-__device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
-    const float2 z = mul2(bc2(0.7978845608028654f), fma2(mul2(bc2(0.044715f), x), mul2(x, x), x));
-    const float2 e = mul2(bc2(2.8853900817779268f), z);  // e^(2z) = 2^(2z log2(e))
-    const float2 d = add2(bc2(1.0f), make_float2(ex2_approx(e.x), ex2_approx(e.y)));
-    const float2 th = fma2(bc2(-2.0f), make_float2(rcp_approx(d.x), rcp_approx(d.y)), bc2(1.0f));
-    return mul2(mul2(bc2(0.5f), x), add2(bc2(1.0f), th));
-}
 
 // sin^2(theta), two elements per call: Cody-Waite reduction by pi (pi = PI1 + PI2 + PI3, PI1 = float(pi)), then
 // u * P(u), u = r^2.

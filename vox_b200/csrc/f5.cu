@@ -47,32 +47,61 @@ __global__ void __launch_bounds__(256) f5_rope_kernel(float *q, float *k, const 
 
 // ------------------------------------------------------------------ fused attention (bf16 math mode, dim_head 64)
 
-// RoPE in place on the bf16 q and k of the fused projection qkv [rows][ld] (q at column 0, k at column inner): four
-// pairs (16 bytes) per thread, each widened to f32, rotated with the rounding of the CPU loop (f5.cpp:696-701) and
-// rounded back to bf16 (RN). quads = rows * rope_heads * hd / 8; hd % 8 == 0.
-__global__ void __launch_bounds__(256) f5_rope_bf16_kernel(uint4 *qkv, uint32_t ld, const float2 *cs, uint32_t quads, uint32_t frames,
-                                                           uint32_t half, uint32_t rope_heads, uint32_t hd, uint32_t inner) {
+// The bf16 q|k|v projection qkv [rows][3 inner] in place: + bias (f32 [3 inner]), then RoPE on the q and k of heads
+// < rope_heads (each pair widened to f32 and rotated with the rounding of the CPU loop, f5.cpp:696-701), rounded back
+// to bf16 (RN); the bias comes first, as matmul adds it (kernels.hpp:83). Eight columns (16 bytes) per thread, hd % 8 == 0.
+__global__ void __launch_bounds__(256) f5_qkv_bias_rope_kernel(uint4 *qkv, const float *bias, const float2 *cs, uint32_t octs,
+                                                               uint32_t frames, uint32_t half, uint32_t rope_heads, uint32_t hd,
+                                                               uint32_t inner) {
     pdl_enter();
-    const uint32_t stride = gridDim.x * blockDim.x, qph = half / 4;  // quads per head
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += stride) {
-        const uint32_t j4 = i % qph, t = i / qph;
-        const uint32_t h = t % rope_heads, r = t / rope_heads;
-        const float4 *c4 = reinterpret_cast<const float4 *>(cs + size_t(r % frames) * half + 4 * j4);
-        const float4 ca = c4[0], cb = c4[1];  // (cos, sin) of pairs 4 j4 .. 4 j4 + 3
-        const float cc[4] = {ca.x, ca.z, cb.x, cb.z}, ss[4] = {ca.y, ca.w, cb.y, cb.w};
-        const size_t e = (size_t(r) * ld + size_t(h) * hd + 8 * j4) / 8;
+    const uint32_t stride = gridDim.x * blockDim.x, row_octs = 3 * inner / 8;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < octs; i += stride) {
+        const uint32_t r = i / row_octs, c = 8 * (i % row_octs);
+        const uint32_t part = c / inner, ci = c % inner, head = ci / hd;
+        uint4 w = qkv[i];
+        uint32_t *wp = &w.x;
+        const float4 b0 = *reinterpret_cast<const float4 *>(bias + c), b1 = *reinterpret_cast<const float4 *>(bias + c + 4);
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        float x[8];
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {
-            uint4 *p = qkv + e + part * (inner / 8);
-            uint4 w = *p;
-            uint32_t *wp = &w.x;
+        for (int k = 0; k < 4; ++k) {
+            x[2 * k] = __fadd_rn(__uint_as_float(wp[k] << 16), bb[2 * k]);
+            x[2 * k + 1] = __fadd_rn(__uint_as_float(wp[k] & 0xFFFF0000u), bb[2 * k + 1]);
+        }
+        if (part < 2 && head < rope_heads) {
+            const float4 *c4 = reinterpret_cast<const float4 *>(cs + size_t(r % frames) * half + (ci % hd) / 2);
+            const float4 ca = c4[0], cb = c4[1];
+            const float cc[4] = {ca.x, ca.z, cb.x, cb.z}, ss[4] = {ca.y, ca.w, cb.y, cb.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float x0 = __uint_as_float(wp[k] << 16), x1 = __uint_as_float(wp[k] & 0xFFFF0000u);
-                wp[k] = pack_bf16(__fsub_rn(__fmul_rn(x0, cc[k]), __fmul_rn(x1, ss[k])), __fadd_rn(__fmul_rn(x1, cc[k]), __fmul_rn(x0, ss[k])));
+                const float x0 = x[2 * k], x1 = x[2 * k + 1];
+                x[2 * k] = __fsub_rn(__fmul_rn(x0, cc[k]), __fmul_rn(x1, ss[k]));
+                x[2 * k + 1] = __fadd_rn(__fmul_rn(x1, cc[k]), __fmul_rn(x0, ss[k]));
             }
-            *p = w;
         }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wp[k] = pack_bf16(x[2 * k], x[2 * k + 1]);
+        qkv[i] = w;
+    }
+}
+
+// ff [rows][F] bf16 in place: gelu_tanh(x + bias) (bias f32 [F]); eight columns per thread, F % 8 == 0.
+__global__ void __launch_bounds__(256) f5_bias_gelu_kernel(uint4 *ff, const float *bias, uint32_t octs, uint32_t F) {
+    pdl_enter();
+    const uint32_t stride = gridDim.x * blockDim.x, row_octs = F / 8;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < octs; i += stride) {
+        const uint32_t c = 8 * (i % row_octs);
+        uint4 w = ff[i];
+        uint32_t *wp = &w.x;
+        const float4 b0 = *reinterpret_cast<const float4 *>(bias + c), b1 = *reinterpret_cast<const float4 *>(bias + c + 4);
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 v = gelu_tanh_f2(make_float2(__fadd_rn(__uint_as_float(wp[k] << 16), bb[2 * k]),
+                                                      __fadd_rn(__uint_as_float(wp[k] & 0xFFFF0000u), bb[2 * k + 1])));
+            wp[k] = pack_bf16(v.x, v.y);
+        }
+        ff[i] = w;
     }
 }
 
@@ -246,12 +275,13 @@ __global__ void __launch_bounds__(256) f5_to_bf16_kernel(const float2 *src, uint
     }
 }
 
-// One warp per row of h [rows][D]: if delta, h += gate * delta (product, then sum, each rounded: gated_add of
-// f5.cpp:670-676); then nrm = LayerNorm(h) * (1 + scale) + shift (no affine, eps; mean and variance two-pass in f32 on
+// One warp per row of h [rows][D]: if delta, h += gate * (delta + dbias) (the projection's bias added first, as
+// matmul does; product, then sum, each rounded: gated_add of f5.cpp:670-676); then nrm = LayerNorm(h) * (1 + scale) + shift (no affine, eps; mean and variance two-pass in f32 on
 // the row in registers) rounded to bf16 for the next projection. Lane l holds columns 4 (l + 32 k), k < VPL.
 template <int VPL>
-__global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *delta, const float *gate, const float *scale,
-                                                        const float *shift, uint2 *nrm, uint32_t rows, uint32_t D, float eps) {
+__global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *delta, const float *dbias, const float *gate,
+                                                        const float *scale, const float *shift, uint2 *nrm, uint32_t rows, uint32_t D,
+                                                        float eps) {
     pdl_enter();
     const uint32_t lane = threadIdx.x & 31, r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= rows) return;
@@ -265,7 +295,9 @@ __global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *d
         if (4 * c < D) {
             x[k] = hr[c];
             if (delta) {
-                const float4 dv = reinterpret_cast<const float4 *>(delta + size_t(r) * D)[c];
+                float4 dv = reinterpret_cast<const float4 *>(delta + size_t(r) * D)[c];
+                const float4 db = reinterpret_cast<const float4 *>(dbias)[c];
+                dv = make_float4(__fadd_rn(dv.x, db.x), __fadd_rn(dv.y, db.y), __fadd_rn(dv.z, db.z), __fadd_rn(dv.w, db.w));
                 const float4 g = reinterpret_cast<const float4 *>(gate)[c];
                 x[k] = make_float4(__fadd_rn(x[k].x, __fmul_rn(g.x, dv.x)), __fadd_rn(x[k].y, __fmul_rn(g.y, dv.y)),
                                    __fadd_rn(x[k].z, __fmul_rn(g.z, dv.z)), __fadd_rn(x[k].w, __fmul_rn(g.w, dv.w)));
@@ -332,6 +364,9 @@ struct F5Plan {
     __nv_bfloat16 *qkv_b = nullptr, *nrm_b = nullptr, *at_b = nullptr, *ff_b = nullptr;
     __nv_bfloat16 *w_qkv = nullptr, *w_o = nullptr, *w_ff1 = nullptr, *w_ff2 = nullptr, *w_proj = nullptr;
     const void **ada_ptrs = nullptr;  // device [3][depth]: W_ada[l], ts, ada_all + l 6D
+    // f32 copies of every bias (zeros where the description has none), made at create: [depth][6D], [depth][3 inner],
+    // [depth][D] (o), [depth][F] (ff1), [depth][D] (ff2), [2D] (norm_out), [out_dim] (proj_out)
+    float *b_ada = nullptr, *b_qkv = nullptr, *b_o = nullptr, *b_ff1 = nullptr, *b_ff2 = nullptr, *b_fin = nullptr, *b_proj = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
 };
@@ -393,41 +428,54 @@ int record(F5Plan &p, cudaStream_t st) {
     const uint32_t half = uint32_t(d.dim_head / 2);
     const uint32_t pairs = uint32_t(R) * rope_heads * half;
     const int rope_grid = grid_for(pairs, 256, 4);
+    auto bias = [&](float *y, const float *b, int64_t rows, int64_t cols) {
+        return b ? vox_cuda_bias_add(y, b, rows, cols, VOX_CUDA_F32, st) : VOX_CUDA_OK;
+    };
     for (const vox_cuda_f5_block_weights &L : p.blocks) {
         F5_TRY(gemm_xwt(p, p.ts, L.ada, p.ada, 1, 6 * D, D));
+        F5_TRY(bias(p.ada, L.ada_b, 1, 6 * D));
         const float *shift_msa = p.ada, *scale_msa = p.ada + D, *gate_msa = p.ada + 2 * D;
         const float *shift_mlp = p.ada + 3 * D, *scale_mlp = p.ada + 4 * D, *gate_mlp = p.ada + 5 * D;
         F5_TRY(vox_cuda_adaln(p.h, shift_msa, scale_msa, nullptr, nullptr, p.nrm, 1, R, D, 1e-6f, VOX_CUDA_F32, st));
         F5_TRY(gemm_xwt(p, p.nrm, L.q, p.q, R, IN, D));
         F5_TRY(gemm_xwt(p, p.nrm, L.k, p.k, R, IN, D));
         F5_TRY(gemm_xwt(p, p.nrm, L.v, p.v, R, IN, D));
+        F5_TRY(bias(p.q, L.q_b, R, IN));
+        F5_TRY(bias(p.k, L.k_b, R, IN));
+        F5_TRY(bias(p.v, L.v_b, R, IN));
         launch_k(f5_rope_kernel, rope_grid, 256, 0, st, p.q, p.k, (const float2 *)p.cs, pairs, uint32_t(d.frames), half, rope_heads,
                  uint32_t(d.dim_head), uint32_t(IN));
         F5_TRY(check_launch("vox_cuda_f5 rope"));
         for (int64_t b = 0; b < d.batch; ++b) F5_TRY(attention(p, b, st));
         F5_TRY(gemm_xwt(p, p.at, L.o, p.o, R, D, IN));
+        F5_TRY(bias(p.o, L.o_b, R, D));
         F5_TRY(vox_cuda_gated_add(p.h, gate_msa, p.o, 1, R, D, VOX_CUDA_F32, st));
         F5_TRY(vox_cuda_adaln(p.h, shift_mlp, scale_mlp, nullptr, nullptr, p.nrm, 1, R, D, 1e-6f, VOX_CUDA_F32, st));
         F5_TRY(gemm_xwt(p, p.nrm, L.ff1, p.ffb, R, FF, D));
+        F5_TRY(bias(p.ffb, L.ff1_b, R, FF));
         F5_TRY(vox_cuda_gelu(p.ffb, p.ffb, R * FF, VOX_CUDA_GELU_TANH, VOX_CUDA_F32, st));
         F5_TRY(gemm_xwt(p, p.ffb, L.ff2, p.o, R, D, FF));
+        F5_TRY(bias(p.o, L.ff2_b, R, D));
         F5_TRY(vox_cuda_gated_add(p.h, gate_mlp, p.o, 1, R, D, VOX_CUDA_F32, st));
     }
     F5_TRY(gemm_xwt(p, p.ts, d.norm_out, p.fin, 1, 2 * D, D));  // fin = [scale, shift] (f5.cpp:720-722)
+    F5_TRY(bias(p.fin, d.norm_out_b, 1, 2 * D));
     F5_TRY(vox_cuda_adaln(p.h, p.fin + D, p.fin, nullptr, nullptr, p.nrm, 1, R, D, 1e-6f, VOX_CUDA_F32, st));
-    return gemm_xwt(p, p.nrm, d.proj_out, p.out, R, d.out_dim, D);
+    F5_TRY(gemm_xwt(p, p.nrm, d.proj_out, p.out, R, d.out_dim, D));
+    return bias(p.out, d.proj_out_b, R, d.out_dim);
 }
 
 // h += gate * delta (if delta), then nrm_b = modulated LayerNorm of h in bf16.
-int resmod(F5Plan &p, const float *delta, const float *gate, const float *scale, const float *shift, cudaStream_t st) {
+int resmod(F5Plan &p, const float *delta, const float *dbias, const float *gate, const float *scale, const float *shift,
+           cudaStream_t st) {
     const uint32_t R = uint32_t(p.R), D = uint32_t(p.d.dim), vpl = (D / 4 + 31) / 32;
     const int g = int((R + 7) / 8);
     uint2 *nrm = reinterpret_cast<uint2 *>(p.nrm_b);
-    if (vpl <= 1) launch_k(f5_resmod_kernel<1>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
-    else if (vpl <= 2) launch_k(f5_resmod_kernel<2>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
-    else if (vpl <= 4) launch_k(f5_resmod_kernel<4>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
-    else if (vpl <= 8) launch_k(f5_resmod_kernel<8>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
-    else launch_k(f5_resmod_kernel<16>, g, 256, 0, st, p.h, delta, gate, scale, shift, nrm, R, D, 1e-6f);
+    if (vpl <= 1) launch_k(f5_resmod_kernel<1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 2) launch_k(f5_resmod_kernel<2>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 4) launch_k(f5_resmod_kernel<4>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 8) launch_k(f5_resmod_kernel<8>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else launch_k(f5_resmod_kernel<16>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
     return check_launch("vox_cuda_f5 residual/modulate");
 }
 
@@ -442,35 +490,40 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
                                           pp + L, CUDA_R_32F, int(D), &zero, (void *const *)(pp + 2 * L), CUDA_R_32F, int(6 * D),
                                           int(L), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
                       "ada (batched)"));
+    F5_TRY(vox_cuda_add(p.ada_all, p.b_ada, p.ada_all, L * 6 * D, VOX_CUDA_F32, st));
     F5_TRY(gemm_xwt(p, p.ts, d.norm_out, p.fin, 1, 2 * D, D));  // fin = [scale, shift] (f5.cpp:720-722)
+    F5_TRY(vox_cuda_add(p.fin, p.b_fin, p.fin, 2 * D, VOX_CUDA_F32, st));
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
-    const uint32_t rquads = uint32_t(R) * rope_heads * uint32_t(d.dim_head / 8);
+    const uint32_t qkv_octs = uint32_t(R * 3 * IN / 8), ff_octs = uint32_t(R * FF / 8);
     const dim3 fg(unsigned((d.frames + kFaRows - 1) / kFaRows), unsigned(d.heads), unsigned(d.batch));
     const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
-    F5_TRY(resmod(p, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
+    F5_TRY(resmod(p, nullptr, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
     for (int64_t l = 0; l < L; ++l) {
         const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
         F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv_b, CUDA_R_16BF, R, 3 * IN, D));
-        launch_k(f5_rope_bf16_kernel, grid_for(rquads, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.qkv_b), uint32_t(3 * IN),
-                 (const float2 *)p.cs, rquads, uint32_t(d.frames), uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head),
-                 uint32_t(IN));
-        F5_TRY(check_launch("vox_cuda_f5 rope (bf16)"));
+        launch_k(f5_qkv_bias_rope_kernel, grid_for(qkv_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.qkv_b),
+                 (const float *)(p.b_qkv + size_t(l) * 3 * IN), (const float2 *)p.cs, qkv_octs, uint32_t(d.frames),
+                 uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
+        F5_TRY(check_launch("vox_cuda_f5 bias/rope (bf16)"));
         launch_k(f5_flash_kernel<true>, fg, kFaThreads, 0, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
                  (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (void *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
         F5_TRY(check_launch("vox_cuda_f5 attention"));
         F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
-        F5_TRY(resmod(p, p.o, A + 2 * D, A + 4 * D, A + 3 * D, st));
+        F5_TRY(resmod(p, p.o, p.b_o + l * D, A + 2 * D, A + 4 * D, A + 3 * D, st));
         F5_TRY(gemm_bf16(p, p.nrm_b, p.w_ff1 + size_t(l) * FF * D, p.ff_b, CUDA_R_16BF, R, FF, D));
-        F5_TRY(vox_cuda_gelu(p.ff_b, p.ff_b, R * FF, VOX_CUDA_GELU_TANH, VOX_CUDA_BF16, st));
+        launch_k(f5_bias_gelu_kernel, grid_for(ff_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.ff_b),
+                 (const float *)(p.b_ff1 + l * FF), ff_octs, uint32_t(FF));
+        F5_TRY(check_launch("vox_cuda_f5 bias/gelu (bf16)"));
         F5_TRY(gemm_bf16(p, p.ff_b, p.w_ff2 + size_t(l) * D * FF, p.o, CUDA_R_32F, R, D, FF));
         if (l + 1 < L) {
             const float *An = A + 6 * D;
-            F5_TRY(resmod(p, p.o, A + 5 * D, An + D, An, st));
+            F5_TRY(resmod(p, p.o, p.b_ff2 + l * D, A + 5 * D, An + D, An, st));
         } else {
-            F5_TRY(resmod(p, p.o, A + 5 * D, p.fin, p.fin + D, st));
+            F5_TRY(resmod(p, p.o, p.b_ff2 + l * D, A + 5 * D, p.fin, p.fin + D, st));
         }
     }
-    return gemm_bf16(p, p.nrm_b, p.w_proj, p.out, CUDA_R_32F, R, d.out_dim, D);
+    F5_TRY(gemm_bf16(p, p.nrm_b, p.w_proj, p.out, CUDA_R_32F, R, d.out_dim, D));
+    return vox_cuda_bias_add(p.out, p.b_proj, R, d.out_dim, VOX_CUDA_F32, st);
 }
 
 void release(F5Plan *p) {
@@ -482,7 +535,8 @@ void release(F5Plan *p) {
     for (void *b : {(void *)p->ws, (void *)p->h, (void *)p->ts, (void *)p->out, (void *)p->nrm, (void *)p->q, (void *)p->k,
                     (void *)p->v, (void *)p->at, (void *)p->o, (void *)p->ffb, (void *)p->s, (void *)p->ada, (void *)p->fin,
                     (void *)p->cs, (void *)p->qkv_b, (void *)p->ada_all, (void *)p->nrm_b, (void *)p->at_b, (void *)p->ff_b, (void *)p->w_qkv, (void *)p->w_o, (void *)p->w_ff1,
-                    (void *)p->w_ff2, (void *)p->w_proj, (void *)p->ada_ptrs})
+                    (void *)p->w_ff2, (void *)p->w_proj, (void *)p->ada_ptrs, (void *)p->b_ada, (void *)p->b_qkv, (void *)p->b_o,
+                    (void *)p->b_ff1, (void *)p->b_ff2, (void *)p->b_fin, (void *)p->b_proj})
         if (b) cudaFree(b);
     if (p->cap) cudaStreamDestroy(p->cap);
     delete p;
@@ -506,7 +560,7 @@ int to_bf16(const float *src, __nv_bfloat16 *dst, size_t n, cudaStream_t st) {
 int build(F5Plan &p, cudaStream_t user) {
     const vox_cuda_f5_desc &d = p.d;
     const size_t R = size_t(p.R), D = size_t(d.dim), IN = size_t(p.inner), FF = size_t(p.ff), N = size_t(d.frames), L = size_t(d.depth);
-    p.bf16 = d.math == VOX_CUDA_F5_MATH_BF16 && d.dim_head == kFaHd && D % 4 == 0 && D <= 2048;
+    p.bf16 = d.math == VOX_CUDA_F5_MATH_BF16 && d.dim_head == kFaHd && D % 4 == 0 && D <= 2048 && FF % 8 == 0;
     F5_TRY(alloc(&p.h, R * D, "h"));
     F5_TRY(alloc(&p.ts, D, "ts"));
     F5_TRY(alloc(&p.out, R * size_t(d.out_dim), "out"));
@@ -536,6 +590,29 @@ int build(F5Plan &p, cudaStream_t user) {
             F5_TRY(to_bf16(B.ff2, p.w_ff2 + l * D * FF, D * FF, user));
         }
         F5_TRY(to_bf16(d.proj_out, p.w_proj, size_t(d.out_dim) * D, user));
+        F5_TRY(alloc(&p.b_ada, L * 6 * D, "ada biases"));
+        F5_TRY(alloc(&p.b_qkv, L * 3 * IN, "q|k|v biases"));
+        F5_TRY(alloc(&p.b_o, L * D, "o biases"));
+        F5_TRY(alloc(&p.b_ff1, L * FF, "ff1 biases"));
+        F5_TRY(alloc(&p.b_ff2, L * D, "ff2 biases"));
+        F5_TRY(alloc(&p.b_fin, 2 * D, "norm_out bias"));
+        F5_TRY(alloc(&p.b_proj, size_t(d.out_dim), "proj_out bias"));
+        auto snap = [&](float *dst, const float *src, size_t n) {  // the bias, or zeros
+            const cudaError_t e = src ? cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, user) : cudaMemsetAsync(dst, 0, n * 4, user);
+            return e == cudaSuccess ? VOX_CUDA_OK : check_launch("vox_cuda_f5_create (biases)");
+        };
+        for (size_t l = 0; l < L; ++l) {
+            const vox_cuda_f5_block_weights &B = p.blocks[l];
+            F5_TRY(snap(p.b_ada + l * 6 * D, B.ada_b, 6 * D));
+            F5_TRY(snap(p.b_qkv + l * 3 * IN, B.q_b, IN));
+            F5_TRY(snap(p.b_qkv + l * 3 * IN + IN, B.k_b, IN));
+            F5_TRY(snap(p.b_qkv + l * 3 * IN + 2 * IN, B.v_b, IN));
+            F5_TRY(snap(p.b_o + l * D, B.o_b, D));
+            F5_TRY(snap(p.b_ff1 + l * FF, B.ff1_b, FF));
+            F5_TRY(snap(p.b_ff2 + l * D, B.ff2_b, D));
+        }
+        F5_TRY(snap(p.b_fin, d.norm_out_b, 2 * D));
+        F5_TRY(snap(p.b_proj, d.proj_out_b, size_t(d.out_dim)));
         std::vector<const void *> ptrs(3 * L);
         for (size_t l = 0; l < L; ++l) {
             ptrs[l] = p.blocks[l].ada;

@@ -172,9 +172,9 @@ class Suite:
                     fn(mats[i], scs[i], gx[:mm], out=gy[:mm])
 
                 add(nm, wbytes + GR * (GC // 32) * 2 + mm * GC * 4 + mm * GR * 4, GR * GC * mm, call, [mats[0], scs[0], gx], [gy])
-        # F5-TTS DiT step (the transformer of gpu_f5_step, one CUDA graph): F5 base (dim 1024, 22 blocks of 16 heads x 64,
-        # ff 2048, mel 100) on 2 sequences (conditional and unconditional) of 1024 frames, seeded random weights and biases; each step
-        # writes the residual stream and time embedding into the plan, then replays the graph
+        # F5-TTS DiT step (gpu_f5_step as one CUDA graph: input embedding, 22 blocks, output head): F5 base (dim 1024, 16
+        # heads x 64, ff 2048, mel 100, text 512) on 2 sequences (conditional and unconditional) of 1024 frames, seeded
+        # random weights and biases; each step writes x, the condition and the time embedding into the plan, then replays
         if any(want_next(f"next_f5_dit_{m}") for m in ("tf32", "bf16")):
             D, H, HD, FFm, L, O, Bq, Nf = 1024, 16, 64, 2, 22, 100, 2, 1024
             IN, FF, Rr = H * HD, FFm * D, Bq * Nf
@@ -187,24 +187,29 @@ class Suite:
                 fb.update({k + "_b": Bv(fb[k].shape[0]) for k in list(fb)})
                 fblocks.append(fb)
             norm_out, proj_out, norm_out_b, proj_out_b = W(2 * D, D, 0.3), W(O, D), Bv(2 * D), Bv(O)
-            h0, ts0 = fill(E(Rr, D), 1, 0, 1, 60), fill(E(D), 1, 0, 1, 61)
+            TDm, KP = 512, 31  # text_dim, position-convolution kernel
+            IND = 2 * O + TDm
+            Wc = lambda: torch.randn(D, D // 16, KP, device=dev, generator=gen) * ((KP * D // 16) ** -0.5)  # noqa: E731
+            fembed = {"in_proj": W(D, IND), "in_proj_b": Bv(D), "pos1_w": Wc(), "pos1_b": Bv(D), "pos2_w": Wc(), "pos2_b": Bv(D)}
+            x0, cond0, ts0 = fill(E(Rr, O), 1, 0, 1, 60), fill(E(Rr, IND - O), 1, 0, 1, 62), fill(E(D), 1, 0, 1, 61)
             fl = L * (2 * 6 * D * D + 3 * 2 * Rr * D * IN + 2 * 2 * Bq * H * Nf * Nf * HD + 2 * Rr * IN * D + 2 * 2 * Rr * D * FF) \
-                + 2 * 2 * D * D + 2 * Rr * D * O
-            wbytes = 4 * (L * (6 * D * D + 4 * D * IN + 2 * D * FF) + 2 * D * D + O * D)
+                + 2 * 2 * D * D + 2 * Rr * D * O + 2 * Rr * D * IND + 2 * 2 * Rr * D * (D // 16) * KP
+            wbytes = 4 * (L * (6 * D * D + 4 * D * IN + 2 * D * FF) + 2 * D * D + O * D + D * IND + 2 * D * (D // 16) * KP)
             for m in ("tf32", "bf16"):
                 nm = f"next_f5_dit_{m}"
                 if not want_next(nm):
                     continue
                 plan = vox.F5Dit(fblocks, norm_out, proj_out, heads=H, dim_head=HD, batch=Bq, frames=Nf, math=m, norm_out_b=norm_out_b,
-                                 proj_out_b=proj_out_b)
+                                 proj_out_b=proj_out_b, embed=fembed)
                 self.f5_plans.append(plan)
 
                 def f5_step(plan=plan):
-                    plan.h.copy_(h0)
+                    plan.x.copy_(x0)
+                    plan.cond.copy_(cond0)
                     plan.ts.copy_(ts0)
                     plan.run()
 
-                add(nm, wbytes + (2 * Rr * D + D + Rr * O) * 4, Rr, f5_step, [h0, ts0], [plan.out], flops=fl)
+                add(nm, wbytes + (Rr * IND + D + Rr * O) * 4, Rr, f5_step, [x0, cond0, ts0], [plan.out], flops=fl)
         # .tmod -> device: a file of Q8 matrices with f32 scales (Qwen3-8B MLP-shaped, [12288][4096] each, about 1.6 GB in
         # all), written once to a temporary directory; one step uploads every blob from the mapped file (page cache)
         if want_next("next_tmod_upload"):

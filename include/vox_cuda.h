@@ -302,18 +302,21 @@ VOX_CUDA_API int vox_cuda_tmod_upload_dequant(vox_cuda_tmod *t, const char *name
 
 /* ---------------------------------------------------------------- F5 DiT step (one CUDA graph) */
 
-/* The transformer of one F5-TTS DiT step as the Vulkan backend records it (gpu_f5_step, gpu_f5.cpp:273-332) and the CPU
- * computes it (F5Model::dit, f5.cpp:608-724), from the residual stream h after the input embedding to the output
- * projection. Per block: ada = W_ada . ts ([shift, scale, gate] of attention, then of the MLP); nrm = LayerNorm(h)
- * (no affine, eps 1e-6) * (1 + scale) + shift; q, k, v = nrm . W^T; RoPE on interleaved pairs (2j, 2j+1) at the
- * frame position, on the first pe_attn_head heads (all heads if 0); attention without mask per sequence and head,
- * softmax(q k^T / sqrt(dim_head)) v; h += gate_msa * (at . W_o^T); the MLP the same way with GELU (tanh form) between
- * ff1 and ff2. Output: fin = W_norm_out . ts = [scale, shift], out = (LayerNorm(h) * (1 + scale) + shift) . W_proj^T.
+/* One F5-TTS DiT step as the Vulkan backend records it (gpu_f5_step, gpu_f5.cpp:273-332) and the CPU computes it
+ * (F5Model::dit_forward, f5.cpp:563-724). Input embedding (when in_proj is given): h = [x, cond, temb] . W_in^T + b
+ * per row, then per sequence h += mish(conv2(mish(conv1(h)))), two grouped (16) 1-D convolutions over time of kernel
+ * 31 with zero padding (Conv1d::forward, f5_ops.cpp:106-145; mish f5.cpp:97-100). Per block: ada = W_ada . ts ([shift,
+ * scale, gate] of attention, then of the MLP); nrm = LayerNorm(h) (no affine, eps 1e-6) * (1 + scale) + shift;
+ * q, k, v = nrm . W^T; RoPE on interleaved pairs (2j, 2j+1) at the frame position, on the first pe_attn_head heads
+ * (all heads if 0); attention without mask per sequence and head, softmax(q k^T / sqrt(dim_head)) v;
+ * h += gate_msa * (at . W_o^T); the MLP the same way with GELU (tanh form) between ff1 and ff2. Output:
+ * fin = W_norm_out . ts = [scale, shift], out = (LayerNorm(h) * (1 + scale) + shift) . W_proj^T.
  * Every linear layer is y = x W^T + b as Vox's matmul computes it (kernels.hpp:83, the bias a Mat carries when the
  * file holds "<name>.bias", f5.cpp:59-84); a NULL bias is zero. Weights and biases are f32 device buffers, weights
- * [out][in] (Vox's Mat layout), owned by the caller and read at every run (the bf16 mode reads its own bf16 copies of
- * the q, k, v, o, ff1, ff2 and proj_out weights, made at create; biases stay f32 and are read at every run). The input embedding (in_proj and the convolutional position
- * embedding, gpu_f5.cpp:284-289) is not part of this entry. */
+ * [out][in] (Vox's Mat layout; convolutions [dim][dim/16][31] as PyTorch stores them), owned by the caller and read at
+ * every run (the bf16 mode reads its own bf16 copies of the q, k, v, o, ff1, ff2 and proj_out weights, made at create,
+ * and its own f32 copies of the biases; the convolution weights are reordered into a copy at create). ts is the
+ * SiLU'd time embedding (F5Model::time_embed, f5.cpp:510-526), computed by the caller. */
 #define VOX_CUDA_F5_MATH_F32 0  /* f32 GEMMs on the CUDA cores (reference accuracy) */
 #define VOX_CUDA_F5_MATH_TF32 1 /* tensor cores, TF32 inputs, f32 accumulation */
 #define VOX_CUDA_F5_MATH_BF16 2 /* tensor cores, bf16 inputs, f32 accumulation; with dim_head 64 (and dim % 4 == 0,
@@ -336,14 +339,22 @@ typedef struct vox_cuda_f5_desc {
     const float *norm_out;  /* [2 dim][dim]: (scale, shift) */
     const float *proj_out;  /* [out_dim][dim] */
     const float *norm_out_b, *proj_out_b; /* their biases, or NULL */
+    /* input embedding, or in_proj NULL (the caller writes h): x [rows][out_dim] and cond [rows][in_dim - out_dim]
+     * (the condition mel then the text embedding) form the in_dim-wide input rows */
+    int32_t in_dim;
+    const float *in_proj, *in_proj_b;                /* [dim][in_dim], [dim] */
+    const float *pos1_w, *pos1_b, *pos2_w, *pos2_b;  /* [dim][dim/16][31], [dim] */
 } vox_cuda_f5_desc;
 typedef struct vox_cuda_f5 vox_cuda_f5;
 /* Allocates the plan's buffers on the current device (h [batch*frames][dim], ts [dim], out [batch*frames][out_dim] and
  * the intermediates), builds the RoPE table as the CPU does (f5.cpp:529-541), runs the step once on `stream` and
  * captures it into a CUDA graph. */
 VOX_CUDA_API int vox_cuda_f5_create(const vox_cuda_f5_desc *desc, void *stream, vox_cuda_f5 **out);
-/* The plan's device buffers: the caller writes h and ts before a run and reads out (and the updated h) after it. */
+/* The plan's device buffers: the caller writes ts and either h (no embedding) or x and cond (embedding; x changes every
+ * step, cond stays for a sequence) before a run, and reads out (and the final h) after it. x and cond are NULL without
+ * an embedding. */
 VOX_CUDA_API int vox_cuda_f5_buffers(vox_cuda_f5 *p, float **h, float **ts, float **out);
+VOX_CUDA_API int vox_cuda_f5_inputs(vox_cuda_f5 *p, float **x, float **cond);
 /* Replays the captured step on `stream` (stream-ordered, asynchronous). */
 VOX_CUDA_API int vox_cuda_f5_run(vox_cuda_f5 *p, void *stream);
 /* Frees the plan (waits for its work). NULL is ignored. */

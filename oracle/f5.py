@@ -1,8 +1,8 @@
 """TEST INFRASTRUCTURE — numpy restatement of the F5-TTS DiT transformer step. Not product code.
 
-Follows Vox's CPU F5Model::dit from the residual stream after the input embedding to the output projection
-(src/f5.cpp:608-724), in float64 except for the quantities the CPU builds in float32 (the RoPE table,
-f5.cpp:529-541). Only tests/ and the CPU-baseline leg of bench.py use it.
+Follows Vox's CPU F5Model::dit_forward (src/f5.cpp:563-724): the input embedding (embed: in_proj and the convolutional
+position embedding with Mish) and the blocks and output head (dit), in float64 except for the quantities the CPU builds in
+float32 (the RoPE table, f5.cpp:529-541). Only tests/ and the CPU-baseline leg of bench.py use it.
 
 Parity of the pieces is pinned elsewhere: the modulated LayerNorm (the adaLN modulate lambda, f5.cpp:617-632), GELU-tanh
 (f5.cpp:93-96) and the row softmax against the reference compiled from its sources (tests/golden); the RoPE here is
@@ -61,6 +61,42 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, batch: int, frames: i
     qh, kh, vh = (a.reshape(shp).transpose(0, 2, 1, 3) for a in (q, k, v))
     p = softmax(qh @ kh.transpose(0, 1, 3, 2), float(np.float32(1.0) / np.sqrt(np.float32(dim_head))))
     return (p @ vh).transpose(0, 2, 1, 3).reshape(batch * frames, heads * dim_head)
+
+
+def mish(x: np.ndarray) -> np.ndarray:
+    """x tanh(softplus(x)), softplus = x past 20 (f5.cpp:97-100)."""
+    sp = np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0))))
+    return x * np.tanh(sp)
+
+
+def conv1d(x: np.ndarray, w: np.ndarray, b, groups: int) -> np.ndarray:
+    """Grouped 1-D convolution over time of x [T][cin], weights [cout][cin/groups][K] (PyTorch layout), zero padding
+    K/2 on both sides, + bias (Conv1d::forward, f5_ops.cpp:106-145)."""
+    T, cin = x.shape
+    cout, cig, K = w.shape
+    cog, pad = cout // groups, K // 2
+    xp = np.zeros((T + 2 * pad, cin))
+    xp[pad:pad + T] = x
+    y = np.zeros((T, cout))
+    for g in range(groups):
+        # windows [T][K][cig] of this group's channels
+        win = np.stack([xp[k:k + T, g * cig:(g + 1) * cig] for k in range(K)], axis=1)
+        wg = np.asarray(w[g * cog:(g + 1) * cog], np.float64)  # [cog][cig][K]
+        y[:, g * cog:(g + 1) * cog] = np.einsum("tki,oik->to", win, wg)
+    return y if b is None else y + np.asarray(b, np.float64)
+
+
+def embed(x, cond, temb, in_proj, in_proj_b, pos1_w, pos1_b, pos2_w, pos2_b, groups: int = 16) -> np.ndarray:
+    """The input embedding of dit_forward (f5.cpp:583-606): h = in_proj([x, cond, temb]) per row, then per sequence
+    h += mish(conv2(mish(conv1(h)))). x, cond [B][N][mel], temb [B][N][text]; returns h [B*N][dim]."""
+    B, N, _ = np.shape(x)
+    cat = np.concatenate([np.asarray(x, np.float64), np.asarray(cond, np.float64), np.asarray(temb, np.float64)], axis=2)
+    h = linear(cat.reshape(B * N, -1), in_proj, in_proj_b)
+    for s in range(B):
+        hs = h[s * N:(s + 1) * N]
+        a = mish(conv1d(hs, pos1_w, pos1_b, groups))
+        hs += mish(conv1d(a, pos2_w, pos2_b, groups))
+    return h
 
 
 def linear(x, w, b=None):

@@ -153,9 +153,8 @@ def main() -> None:
 
 # -- F5 DiT forward (F5Model::dit_forward, f5.cpp:563-724) of a tiny random model written with the reference's own
 #    tmod_write: every linear with a bias, RoPE on the first head only (pe_attn_head 1), no text-encoder or Vocos
-#    layers; the second position-embedding convolution is zero, so the residual stream entering the blocks is exactly
-#    in_proj([x, cond, temb]). Saved: the inputs, the weights the blocks and output head read, the reference's time
-#    embedding ts and its output.
+#    layers. Saved: the inputs, the weights of the input embedding (in_proj, the two grouped position convolutions),
+#    of the blocks and of the output head, the reference's time embedding ts and its output.
 F5_DIMS = dict(dim=32, depth=2, heads=2, dim_head=16, ff_mult=2, text_dim=16, text_rows=4, mel_dim=20, pe_attn_head=1)
 
 
@@ -191,10 +190,11 @@ def f5_golden(P, R) -> None:
     put_lin(d + "time_embed.time_mlp.2", None, D, D)
     put(d + "text_embed.text_embed.weight", nrm((c["text_rows"], TD), 1.0))
     put_lin(d + "input_embed.proj", "in_proj", D, 2 * M + TD)
-    put(d + "input_embed.conv_pos_embed.conv1d.0.weight", nrm((D, D // 16, 31), 0.1))
-    put(d + "input_embed.conv_pos_embed.conv1d.0.bias", nrm((D,), 0.1))
-    put(d + "input_embed.conv_pos_embed.conv1d.2.weight", np.zeros((D, D // 16, 31), np.float32))
-    put(d + "input_embed.conv_pos_embed.conv1d.2.bias", np.zeros((D,), np.float32))
+    for j in (0, 2):  # grouped (16) position convolutions, kernel 31
+        w, b = nrm((D, D // 16, 31), 1.0 / np.sqrt(31 * D // 16)), nrm((D,), 0.1)
+        put(d + f"input_embed.conv_pos_embed.conv1d.{j}.weight", w)
+        put(d + f"input_embed.conv_pos_embed.conv1d.{j}.bias", b)
+        arrays[f"pos{j // 2 + 1}_w"], arrays[f"pos{j // 2 + 1}_b"] = w, b
     names = {"ada": "attn_norm.linear", "q": "attn.to_q", "k": "attn.to_k", "v": "attn.to_v", "o": "attn.to_out.0",
              "ff1": "ff.ff.0.0", "ff2": "ff.ff.2"}
     shapes = {"ada": (6 * D, D), "q": (IN, D), "k": (IN, D), "v": (IN, D), "o": (D, IN), "ff1": (FF, D), "ff2": (D, FF)}

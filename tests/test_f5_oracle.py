@@ -44,6 +44,18 @@ def test_rope_table_is_the_float32_construction():
     assert np.all(c[0] == 1.0) and np.all(s[0] == 0.0)
 
 
+def test_conv1d_matches_a_direct_sum():
+    rng = np.random.default_rng(3)
+    T, cin, groups, K = 9, 8, 2, 5
+    x, w, b = rng.standard_normal((T, cin)), rng.standard_normal((6, cin // groups, K)), rng.standard_normal(6)
+    y = F5.conv1d(x, w, b, groups)
+    for t in range(T):
+        for o in range(6):
+            g = o // 3
+            acc = b[o] + sum(w[o, i, k] * x[t + k - K // 2, g * 4 + i] for i in range(4) for k in range(K) if 0 <= t + k - K // 2 < T)
+            assert abs(y[t, o] - acc) < 1e-12
+
+
 def test_dit_of_zero_blocks_is_the_output_head():
     rng = np.random.default_rng(0)
     R, D, O = 6, 16, 5
@@ -58,11 +70,12 @@ def test_dit_of_zero_blocks_is_the_output_head():
 from vox_b200 import _F5Block as _Block, _F5Desc as _Desc  # the C layouts of vox_cuda_f5_block_weights / vox_cuda_f5_desc
 
 
-@pytest.mark.parametrize("field,value", [("dim_head", 15), ("pe_attn_head", 5), ("math", 7), ("depth", 0), ("frames", 0)])
+@pytest.mark.parametrize("field,value", [("dim_head", 15), ("pe_attn_head", 5), ("math", 7), ("depth", 0), ("frames", 0),
+                                         ("in_proj", 8)])
 def test_f5_create_rejects_bad_descriptions(vox_lib, field, value):
     L = vox_lib.lib
     blk = (_Block * 1)(_Block(*([8] * 7)))
-    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8, None, None)
+    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8, None, None, 0)
     setattr(d, field, value)
     h = ctypes.c_void_p()
     assert L.vox_cuda_f5_create(ctypes.byref(d), None, ctypes.byref(h)) == -6
@@ -73,7 +86,7 @@ def test_f5_create_rejects_bad_descriptions(vox_lib, field, value):
 def test_f5_create_rejects_null_weights(vox_lib):
     L = vox_lib.lib
     blk = (_Block * 1)(_Block(8, 8, 8, None, 8, 8, 8))
-    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8, None, None)
+    d = _Desc(64, 4, 16, 2, 1, 0, 20, 2, 10, 0, blk, 8, 8, None, None, 0)
     h = ctypes.c_void_p()
     assert L.vox_cuda_f5_create(ctypes.byref(d), None, ctypes.byref(h)) == -6
     assert L.vox_cuda_f5_create(None, None, ctypes.byref(h)) == -6
@@ -82,20 +95,19 @@ def test_f5_create_rejects_null_weights(vox_lib):
 
 def f5_golden_model(g):
     """The golden F5 model (tests/golden/f5.npz, written by make_golden.py from the reference): the residual stream
-    entering the blocks (in_proj of [x, cond, temb]; the position embedding is zero there), ts, and the weights."""
+    entering the blocks (the oracle's input embedding of [x, cond, temb]), ts, and the weights."""
     keys = ("dim", "depth", "heads", "dim_head", "ff_mult", "text_dim", "text_rows", "mel_dim", "pe_attn_head")
     dims = dict(zip(keys, (int(v) for v in g["dims"])))
     B, N, M = g["x"].shape
-    cat = np.concatenate([g["x"], g["cond"], g["temb"]], axis=2).reshape(B * N, -1)
-    h = F5.linear(cat, g["in_proj"], g["in_proj_b"])
+    h = F5.embed(g["x"], g["cond"], g["temb"], g["in_proj"], g["in_proj_b"], g["pos1_w"], g["pos1_b"], g["pos2_w"], g["pos2_b"])
     blocks = [{k: g[f"b{l}_{k}"] for k in ("ada", "q", "k", "v", "o", "ff1", "ff2", "ada_b", "q_b", "k_b", "v_b", "o_b", "ff1_b",
                                            "ff2_b")} for l in range(dims["depth"])]
     return dims, B, N, h, blocks
 
 
 def test_dit_matches_reference_dit_forward(golden):
-    """The oracle's DiT from the residual stream to the output equals F5Model::dit_forward of the reference (f32 CPU
-    arithmetic against float64: within 1e-5 of the output's RMS)."""
+    """The oracle's input embedding and DiT equal F5Model::dit_forward of the reference (f32 CPU arithmetic against
+    float64: within 1e-5 of the output's RMS)."""
     g = golden["f5"]
     dims, B, N, h, blocks = f5_golden_model(g)
     out, _ = F5.dit(h, g["ts"], blocks, g["norm_out"], g["proj_out"], heads=dims["heads"], dim_head=dims["dim_head"], batch=B,

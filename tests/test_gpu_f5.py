@@ -111,6 +111,52 @@ def test_f5_bf16_pipeline_matches_oracle(vox, frames, pe_attn_head):
     assert _rel(h_after, want_h) <= 8e-2, _rel(h_after, want_h)
 
 
+@pytest.mark.parametrize("math,bar", [("f32", 2e-5), ("tf32", 2e-2), ("bf16", 8e-2)])
+def test_f5_full_step_matches_reference_dit_forward(vox, golden, math, bar):
+    """The whole dit_forward of the golden F5 model on the device: the input embedding (in_proj over [x, cond, temb],
+    the two grouped position convolutions with Mish) in the same graph as the blocks and the output head."""
+    from test_f5_oracle import f5_golden_model
+
+    g = golden["f5"]
+    dims, B, N, _, blocks = f5_golden_model(g)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()  # noqa: E731
+    embed = {k: t(g[k]) for k in ("in_proj", "in_proj_b", "pos1_w", "pos1_b", "pos2_w", "pos2_b")}
+    plan = vox.F5Dit([{k: t(v) for k, v in b.items()} for b in blocks], t(g["norm_out"]), t(g["proj_out"]), heads=dims["heads"],
+                     dim_head=dims["dim_head"], batch=B, frames=N, pe_attn_head=dims["pe_attn_head"], math=math,
+                     norm_out_b=t(g["norm_out_b"]), proj_out_b=t(g["proj_out_b"]), embed=embed)
+    cond = np.concatenate([g["cond"], g["temb"]], axis=2)
+    out = plan.step(None, t(g["ts"]), x=t(g["x"]), cond=t(cond)).cpu().numpy()
+    plan.close()
+    want = g["out"].reshape(B * N, -1).astype(np.float64)
+    assert _rel(out, want) <= bar, _rel(out, want)
+
+
+def test_f5_bf16_pipeline_with_embedding_matches_oracle(vox):
+    cfg = dict(D=128, H=2, HD=64, FF=256, depth=2, out_dim=24)
+    B, N, TD = 2, 70, 32
+    model = _model(8, **cfg)
+    rng = np.random.default_rng(9)
+    D = cfg["D"]
+    emb = {"in_proj": (rng.standard_normal((D, 2 * cfg["out_dim"] + TD)) * 0.1).astype(np.float32),
+           "in_proj_b": (rng.standard_normal(D) * 0.1).astype(np.float32),
+           "pos1_w": (rng.standard_normal((D, D // 16, 31)) / np.sqrt(31 * D // 16)).astype(np.float32),
+           "pos1_b": (rng.standard_normal(D) * 0.1).astype(np.float32),
+           "pos2_w": (rng.standard_normal((D, D // 16, 31)) / np.sqrt(31 * D // 16)).astype(np.float32),
+           "pos2_b": (rng.standard_normal(D) * 0.1).astype(np.float32)}
+    x = rng.standard_normal((B, N, cfg["out_dim"])).astype(np.float32)
+    cond = rng.standard_normal((B, N, cfg["out_dim"])).astype(np.float32)
+    temb = rng.standard_normal((B, N, TD)).astype(np.float32)
+    ts = rng.standard_normal(D).astype(np.float32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    plan = _plan(vox, _dev(*model), heads=cfg["H"], dim_head=cfg["HD"], batch=B, frames=N, math="bf16",
+                 embed={k: t(v) for k, v in emb.items()})
+    out = plan.step(None, t(ts), x=t(x), cond=t(np.concatenate([cond, temb], axis=2))).cpu().numpy()
+    plan.close()
+    h = F5.embed(x, cond, temb, emb["in_proj"], emb["in_proj_b"], emb["pos1_w"], emb["pos1_b"], emb["pos2_w"], emb["pos2_b"])
+    want, _ = _oracle(model, h, ts, heads=cfg["H"], dim_head=cfg["HD"], batch=B, frames=N)
+    assert _rel(out, want) <= 8e-2, _rel(out, want)
+
+
 def test_f5_replay_is_deterministic_and_reads_fresh_inputs(vox):
     B, N = 2, 33
     model = _model(3, **CFG)

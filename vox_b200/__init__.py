@@ -91,6 +91,7 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_tmod_upload_dequant": ([c_p, ctypes.c_char_p, c_p, c_int, c_p], c_int),
         "vox_cuda_f5_create": ([c_p, c_p, c_p], c_int),
         "vox_cuda_f5_buffers": ([c_p, c_p, c_p, c_p], c_int),
+        "vox_cuda_f5_inputs": ([c_p, c_p, c_p], c_int),
         "vox_cuda_f5_run": ([c_p, c_p], c_int),
         "vox_cuda_f5_destroy": ([c_p], None),
     }
@@ -559,7 +560,8 @@ class _F5Desc(ctypes.Structure):
     _fields_ = [(k, ctypes.c_int32) for k in ("dim", "heads", "dim_head", "ff_mult", "depth", "pe_attn_head", "out_dim", "batch",
                                               "frames", "math")] + \
                [("blocks", ctypes.POINTER(_F5Block)), ("norm_out", ctypes.c_void_p), ("proj_out", ctypes.c_void_p),
-                ("norm_out_b", ctypes.c_void_p), ("proj_out_b", ctypes.c_void_p)]
+                ("norm_out_b", ctypes.c_void_p), ("proj_out_b", ctypes.c_void_p), ("in_dim", ctypes.c_int32)] + \
+               [(k, ctypes.c_void_p) for k in ("in_proj", "in_proj_b", "pos1_w", "pos1_b", "pos2_w", "pos2_b")]
 
 
 class _DevView:
@@ -575,14 +577,17 @@ class F5Dit:
     CUDA graph (vox_cuda_f5_create) and replayed by run(). `blocks` is a list of dicts of f32 CUDA tensors
     {ada [6D][D], q/k/v [H*HD][D], o [D][H*HD], ff1 [F][D], ff2 [D][F]} in Vox's [out][in] layout, each with an
     optional bias "<name>_b" [out] (absent: zero); norm_out [2D][D] gives (scale, shift), proj_out [out_dim][D], with
-    optional biases norm_out_b, proj_out_b. `math`: "f32" (CUDA-core GEMMs), "tf32" or "bf16" (tensor cores, f32
-    accumulation). h, ts and out are the plan's own buffers (torch views, valid until close())."""
+    optional biases norm_out_b, proj_out_b. `embed` (optional) adds the input embedding: a dict {in_proj [D][in_dim],
+    in_proj_b, pos1_w, pos2_w [D][D/16][31], pos1_b, pos2_b}; the step then starts from x [rows][out_dim] and cond
+    [rows][in_dim - out_dim] (condition mel, then text embedding). `math`: "f32" (CUDA-core GEMMs), "tf32" or "bf16"
+    (tensor cores, f32 accumulation). h, ts, out (and x, cond) are the plan's own buffers (torch views, valid until
+    close())."""
 
     MATH = {"f32": 0, "tf32": 1, "bf16": 2}
     KEYS = ("ada", "q", "k", "v", "o", "ff1", "ff2")
 
     def __init__(self, blocks, norm_out, proj_out, *, heads: int, dim_head: int, batch: int, frames: int,
-                 pe_attn_head: int = 0, math: str = "tf32", norm_out_b=None, proj_out_b=None):
+                 pe_attn_head: int = 0, math: str = "tf32", norm_out_b=None, proj_out_b=None, embed: dict | None = None):
         if math not in self.MATH:
             raise VoxCudaError(-6, f"math must be one of {sorted(self.MATH)}")
         D = int(norm_out.shape[1])
@@ -605,12 +610,19 @@ class F5Dit:
         check(norm_out, "norm_out", (2 * D, D))
         check(proj_out, "proj_out", (out_dim, D))
         nb, pb = check(norm_out_b, "norm_out_b", (2 * D,)), check(proj_out_b, "proj_out_b", (out_dim,))
-        self._keep = (blocks, norm_out, proj_out, norm_out_b, proj_out_b)  # read by every run
+        emb = [0] + [None] * 6
+        if embed is not None:
+            in_dim = int(embed["in_proj"].shape[1])
+            cw = (D, D // 16, 31)
+            emb = [in_dim, check(embed["in_proj"], "in_proj", (D, in_dim)), check(embed.get("in_proj_b"), "in_proj_b", (D,)),
+                   check(embed["pos1_w"], "pos1_w", cw), check(embed.get("pos1_b"), "pos1_b", (D,)),
+                   check(embed["pos2_w"], "pos2_w", cw), check(embed.get("pos2_b"), "pos2_b", (D,))]
+        self._keep = (blocks, norm_out, proj_out, norm_out_b, proj_out_b, embed)  # read by every run
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         arr = (_F5Block * len(blocks))(*[_F5Block(*([b[k].data_ptr() for k in self.KEYS] + [ptr(b.get(k + "_b")) for k in self.KEYS]))
                                          for b in blocks])
         desc = _F5Desc(D, heads, dim_head, ff // D, len(blocks), pe_attn_head, out_dim, batch, frames, self.MATH[math], arr,
-                       norm_out.data_ptr(), proj_out.data_ptr(), nb, pb)
+                       norm_out.data_ptr(), proj_out.data_ptr(), nb, pb, *emb)
         h = ctypes.c_void_p()
         _check(lib.vox_cuda_f5_create(ctypes.byref(desc), _stream(norm_out), ctypes.byref(h)))
         self._h = h
@@ -620,14 +632,26 @@ class F5Dit:
         self.h = torch.as_tensor(_DevView(ph.value, (R, D)), device=norm_out.device)
         self.ts = torch.as_tensor(_DevView(pts.value, (D,)), device=norm_out.device)
         self.out = torch.as_tensor(_DevView(po.value, (R, out_dim)), device=norm_out.device)
+        self.x = self.cond = None
+        if embed is not None:
+            px, pc = ctypes.c_void_p(), ctypes.c_void_p()
+            _check(lib.vox_cuda_f5_inputs(self._h, ctypes.byref(px), ctypes.byref(pc)))
+            self.x = torch.as_tensor(_DevView(px.value, (R, out_dim)), device=norm_out.device)
+            self.cond = torch.as_tensor(_DevView(pc.value, (R, emb[0] - out_dim)), device=norm_out.device)
 
     def run(self) -> None:
-        """Replays the step on the current stream: reads h and ts, updates h, writes out."""
+        """Replays the step on the current stream: reads ts and h (or x and cond), updates h, writes out."""
         _check(lib.vox_cuda_f5_run(self._h, _stream(self.h)))
 
-    def step(self, h: torch.Tensor, ts: torch.Tensor) -> torch.Tensor:
-        """Copies h [batch*frames][dim] and ts [dim] in, runs the step, returns a copy of out."""
-        self.h.copy_(h.reshape(self.h.shape))
+    def step(self, h: torch.Tensor | None, ts: torch.Tensor, x: torch.Tensor | None = None,
+             cond: torch.Tensor | None = None) -> torch.Tensor:
+        """Copies the inputs in (h [batch*frames][dim], or x and cond with the embedding), runs the step, returns a
+        copy of out."""
+        if self.x is None:
+            self.h.copy_(h.reshape(self.h.shape))
+        else:
+            self.x.copy_(x.reshape(self.x.shape))
+            self.cond.copy_(cond.reshape(self.cond.shape))
         self.ts.copy_(ts.reshape(self.ts.shape))
         self.run()
         return self.out.clone()

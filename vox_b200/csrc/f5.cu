@@ -1,7 +1,7 @@
 // F5-TTS DiT step on the device, captured as one CUDA graph (vox_cuda_f5_*).
 //
-// The step is the transformer half of Vox's gpu_f5_step (gpu_f5.cpp:273-332; CPU F5Model::dit, f5.cpp:608-724): for
-// each block an ada GEMV, the modulated LayerNorm, the q/k/v projections, RoPE, unmasked attention per sequence and
+// The step is Vox's gpu_f5_step (gpu_f5.cpp:273-332; CPU F5Model::dit_forward, f5.cpp:563-724): the input embedding
+// (in_proj, then two grouped position convolutions with Mish, as im2col + batched GEMMs), then for each block an ada GEMV, the modulated LayerNorm, the q/k/v projections, RoPE, unmasked attention per sequence and
 // head, the output projection and gated residual, then the MLP (ff1, GELU-tanh, ff2) and its gated residual; at the
 // end the final modulation and the output projection. The elementwise and normalisation steps are this library's
 // kernels (vox_cuda_adaln with no gate, vox_cuda_gated_add, vox_cuda_gelu, vox_cuda_softmax_rows) plus the RoPE kernel
@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cmath>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -42,6 +43,51 @@ __global__ void __launch_bounds__(256) f5_rope_kernel(float *q, float *k, const 
         const float2 a = *pq, b = *pk;
         *pq = make_float2(__fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(a.y, c.y)), __fadd_rn(__fmul_rn(a.y, c.x), __fmul_rn(a.x, c.y)));
         *pk = make_float2(__fsub_rn(__fmul_rn(b.x, c.x), __fmul_rn(b.y, c.y)), __fadd_rn(__fmul_rn(b.y, c.x), __fmul_rn(b.x, c.y)));
+    }
+}
+
+// ------------------------------------------------------------------ input embedding (grouped position convolutions)
+
+// Conv weights from PyTorch's [cout][cig][K] into [cout][K][cig] (the order of the im2col columns), once at create.
+__global__ void __launch_bounds__(256) f5_conv_reorder_kernel(const float *w, float *wr, uint32_t n, uint32_t cig, uint32_t K) {
+    pdl_enter();
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+        const uint32_t i = e % cig, t = e / cig, k = t % K, o = t / K;  // e = (o K + k) cig + i
+        wr[e] = w[(size_t(o) * cig + i) * K + k];
+    }
+}
+
+// im2col of x [B][T][cin] for a grouped convolution with zero padding K/2: col [B][groups][T][K cig] with column
+// k cig + i = x[t + k - K/2][g cig + i] (zero outside the sequence); VW channels per thread (4: 16-byte accesses when
+// cig % 4 == 0, else 1).
+template <int VW>
+__global__ void __launch_bounds__(256) f5_im2col_kernel(const float *x, float *col, uint32_t items, uint32_t T, uint32_t cin,
+                                                        uint32_t groups, uint32_t K) {
+    pdl_enter();
+    using V = typename std::conditional<VW == 4, float4, float>::type;
+    const uint32_t cq = cin / groups / VW;  // items per tap of one group
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < items; e += gridDim.x * blockDim.x) {
+        const uint32_t iq = e % cq, r1 = e / cq, k = r1 % K, r2 = r1 / K;  // e = ((sg T + t) K + k) cq + iq
+        const uint32_t t = r2 % T, sg = r2 / T, g = sg % groups, sq = sg / groups;
+        const int tt = int(t) + int(k) - int(K / 2);
+        V v{};
+        if (tt >= 0 && tt < int(T)) v = reinterpret_cast<const V *>(x)[(size_t(sq) * T + uint32_t(tt)) * (cin / VW) + g * cq + iq];
+        reinterpret_cast<V *>(col)[e] = v;
+    }
+}
+
+// mish(x) = x tanh(softplus(x)), softplus = x past 20 (f5.cpp:97-100), with the accurate CUDA functions.
+__device__ __forceinline__ float mish_f(float x) {
+    const float sp = x > 20.f ? x : log1pf(expf(x));
+    return x * tanhf(sp);
+}
+// v = mish(y + bias[col]); y = v (res NULL) or res += v (rounded add); n elements of rows of D.
+__global__ void __launch_bounds__(256) f5_bias_mish_kernel(float *y, const float *bias, float *res, uint32_t n, uint32_t D) {
+    pdl_enter();
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+        const float v = mish_f(__fadd_rn(y[e], bias ? bias[e % D] : 0.f));
+        if (res) res[e] = __fadd_rn(res[e], v);
+        else y[e] = v;
     }
 }
 
@@ -367,6 +413,9 @@ struct F5Plan {
     // f32 copies of every bias (zeros where the description has none), made at create: [depth][6D], [depth][3 inner],
     // [depth][D] (o), [depth][F] (ff1), [depth][D] (ff2), [2D] (norm_out), [out_dim] (proj_out)
     float *b_ada = nullptr, *b_qkv = nullptr, *b_o = nullptr, *b_ff1 = nullptr, *b_ff2 = nullptr, *b_fin = nullptr, *b_proj = nullptr;
+    // input embedding (in_proj given): x [R][out_dim], cond [R][in_dim - out_dim], im2col scratch, reordered conv weights
+    bool embed = false;
+    float *xin = nullptr, *cond = nullptr, *col = nullptr, *ctmp = nullptr, *w1r = nullptr, *w2r = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
 };
@@ -420,10 +469,56 @@ int attention(F5Plan &p, int64_t b, cudaStream_t st) {
                       "attention output");
 }
 
+constexpr int kPosGroups = 16, kPosK = 31;  // F5's position convolutions (f5.cpp:306-307)
+
+// conv of src [R][D] (B sequences of T frames) into dst [R][D]: im2col, then per sequence one GEMM batched over the
+// groups (col [T][K cig] of group g times the group's reordered weights [cog][K cig], into columns g cog of dst).
+int conv_pos(F5Plan &p, const float *src, const float *wr, float *dst, cudaStream_t st) {
+    const vox_cuda_f5_desc &d = p.d;
+    const uint32_t T = uint32_t(d.frames), D = uint32_t(d.dim), cig = D / kPosGroups, J = kPosK * cig;
+    const uint32_t all = uint32_t(d.batch) * kPosGroups * T * J;
+    if (cig % 4 == 0)
+        launch_k(f5_im2col_kernel<4>, grid_for(all / 4, 256, 4), 256, 0, st, src, p.col, all / 4, T, D, uint32_t(kPosGroups), uint32_t(kPosK));
+    else
+        launch_k(f5_im2col_kernel<1>, grid_for(all, 256, 4), 256, 0, st, src, p.col, all, T, D, uint32_t(kPosGroups), uint32_t(kPosK));
+    F5_TRY(check_launch("vox_cuda_f5 im2col"));
+    const float one = 1.0f, zero = 0.0f;
+    for (int64_t b = 0; b < d.batch; ++b)
+        F5_TRY(blas_check(cublasGemmStridedBatchedEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(cig), int(T), int(J), &one, wr, CUDA_R_32F,
+                                                     int(J), int64_t(cig) * J, p.col + size_t(b) * kPosGroups * T * J, CUDA_R_32F,
+                                                     int(J), int64_t(T) * J, &zero, dst + size_t(b) * T * D, CUDA_R_32F, int(D),
+                                                     int64_t(cig), kPosGroups, p.compute, CUBLAS_GEMM_DEFAULT),
+                          "position convolution"));
+    return VOX_CUDA_OK;
+}
+
+// The input embedding into p.h: [x | cond] . W_in^T + b as two accumulating GEMMs over the two column blocks of W_in,
+// then h += mish(conv2(mish(conv1(h) + b1)) + b2).
+int record_embed(F5Plan &p, cudaStream_t st) {
+    const vox_cuda_f5_desc &d = p.d;
+    const int64_t R = p.R, D = d.dim, M = d.out_dim, C = d.in_dim - d.out_dim;
+    const float one = 1.0f, zero = 0.0f;
+    F5_TRY(blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(D), int(R), int(M), &one, d.in_proj, CUDA_R_32F, d.in_dim,
+                                   p.xin, CUDA_R_32F, int(M), &zero, p.h, CUDA_R_32F, int(D), p.compute, CUBLAS_GEMM_DEFAULT),
+                      "in_proj (x)"));
+    F5_TRY(blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(D), int(R), int(C), &one, d.in_proj + M, CUDA_R_32F, d.in_dim,
+                                   p.cond, CUDA_R_32F, int(C), &one, p.h, CUDA_R_32F, int(D), p.compute, CUBLAS_GEMM_DEFAULT),
+                      "in_proj (cond)"));
+    if (d.in_proj_b) F5_TRY(vox_cuda_bias_add(p.h, d.in_proj_b, R, D, VOX_CUDA_F32, st));
+    const uint32_t n = uint32_t(R * D);
+    F5_TRY(conv_pos(p, p.h, p.w1r, p.ctmp, st));
+    launch_k(f5_bias_mish_kernel, grid_for(n, 256, 4), 256, 0, st, p.ctmp, d.pos1_b, (float *)nullptr, n, uint32_t(D));
+    F5_TRY(check_launch("vox_cuda_f5 mish"));
+    F5_TRY(conv_pos(p, p.ctmp, p.w2r, p.o, st));
+    launch_k(f5_bias_mish_kernel, grid_for(n, 256, 4), 256, 0, st, p.o, d.pos2_b, p.h, n, uint32_t(D));
+    return check_launch("vox_cuda_f5 mish");
+}
+
 // The whole step on stream st, f32 / TF32 path (eager or under capture; cuBLAS is bound to the same stream).
 int record(F5Plan &p, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const int64_t R = p.R, D = d.dim, IN = p.inner, FF = p.ff;
+    if (p.embed) F5_TRY(record_embed(p, st));
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
     const uint32_t half = uint32_t(d.dim_head / 2);
     const uint32_t pairs = uint32_t(R) * rope_heads * half;
@@ -485,6 +580,7 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const int64_t R = p.R, D = d.dim, IN = p.inner, FF = p.ff, L = d.depth;
     const float one = 1.0f, zero = 0.0f;
+    if (p.embed) F5_TRY(record_embed(p, st));
     const void *const *pp = p.ada_ptrs;
     F5_TRY(blas_check(cublasGemmBatchedEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(6 * D), 1, int(D), &one, pp, CUDA_R_32F, int(D),
                                           pp + L, CUDA_R_32F, int(D), &zero, (void *const *)(pp + 2 * L), CUDA_R_32F, int(6 * D),
@@ -536,7 +632,8 @@ void release(F5Plan *p) {
                     (void *)p->v, (void *)p->at, (void *)p->o, (void *)p->ffb, (void *)p->s, (void *)p->ada, (void *)p->fin,
                     (void *)p->cs, (void *)p->qkv_b, (void *)p->ada_all, (void *)p->nrm_b, (void *)p->at_b, (void *)p->ff_b, (void *)p->w_qkv, (void *)p->w_o, (void *)p->w_ff1,
                     (void *)p->w_ff2, (void *)p->w_proj, (void *)p->ada_ptrs, (void *)p->b_ada, (void *)p->b_qkv, (void *)p->b_o,
-                    (void *)p->b_ff1, (void *)p->b_ff2, (void *)p->b_fin, (void *)p->b_proj})
+                    (void *)p->b_ff1, (void *)p->b_ff2, (void *)p->b_fin, (void *)p->b_proj, (void *)p->xin, (void *)p->cond,
+                    (void *)p->col, (void *)p->ctmp, (void *)p->w1r, (void *)p->w2r})
         if (b) cudaFree(b);
     if (p->cap) cudaStreamDestroy(p->cap);
     delete p;
@@ -631,6 +728,23 @@ int build(F5Plan &p, cudaStream_t user) {
         F5_TRY(alloc(&p.s, size_t(d.heads) * N * N, "scores"));
         F5_TRY(alloc(&p.ada, 6 * D, "ada"));
     }
+    p.embed = d.in_proj != nullptr;
+    if (p.embed) {
+        const size_t cig = D / kPosGroups, J = size_t(kPosK) * cig, nw = D * J;
+        F5_TRY(alloc(&p.xin, R * size_t(d.out_dim), "x"));
+        F5_TRY(alloc(&p.cond, R * size_t(d.in_dim - d.out_dim), "cond"));
+        F5_TRY(alloc(&p.col, size_t(d.batch) * kPosGroups * N * J, "im2col"));
+        F5_TRY(alloc(&p.ctmp, R * D, "convolution"));
+        F5_TRY(alloc(&p.w1r, nw, "conv1 weights"));
+        F5_TRY(alloc(&p.w2r, nw, "conv2 weights"));
+        if (cudaMemsetAsync(p.xin, 0, R * size_t(d.out_dim) * 4, user) != cudaSuccess ||
+            cudaMemsetAsync(p.cond, 0, R * size_t(d.in_dim - d.out_dim) * 4, user) != cudaSuccess)
+            return check_launch("vox_cuda_f5_create");
+        for (auto [w, wr] : {std::make_pair(d.pos1_w, p.w1r), std::make_pair(d.pos2_w, p.w2r)}) {
+            launch_k(f5_conv_reorder_kernel, grid_for(int64_t(nw), 256, 4), 256, 0, user, w, wr, uint32_t(nw), uint32_t(cig), uint32_t(kPosK));
+            F5_TRY(check_launch("vox_cuda_f5_create (conv weights)"));
+        }
+    }
     // RoPE table as the CPU builds it (f5.cpp:529-541): inv = float(1 / 10000^(2j/hd)) in double, angle = float(i) * inv
     // in float, cos/sin of the float angle.
     const int half = d.dim_head / 2;
@@ -690,6 +804,9 @@ int vox_cuda_f5_create(const vox_cuda_f5_desc *desc, void *stream, vox_cuda_f5 *
     VOX_REQUIRE(d.math == VOX_CUDA_F5_MATH_F32 || d.math == VOX_CUDA_F5_MATH_TF32 || d.math == VOX_CUDA_F5_MATH_BF16,
                 "vox_cuda_f5_create: unknown math mode");
     VOX_REQUIRE(d.blocks && d.norm_out && d.proj_out, "vox_cuda_f5_create: NULL weights");
+    VOX_REQUIRE(!d.in_proj || (d.in_dim > d.out_dim && d.pos1_w && d.pos2_w && d.dim % kPosGroups == 0 &&
+                               int64_t(d.batch) * kPosGroups * d.frames * kPosK * (d.dim / kPosGroups) < (int64_t(1) << 32)),
+                "vox_cuda_f5_create: the input embedding needs in_dim > out_dim, both convolutions and dim % 16 == 0");
     for (int i = 0; i < d.depth; ++i) {
         const vox_cuda_f5_block_weights &L = d.blocks[i];
         VOX_REQUIRE(L.ada && L.q && L.k && L.v && L.o && L.ff1 && L.ff2, "vox_cuda_f5_create: NULL block weights");
@@ -720,6 +837,14 @@ int vox_cuda_f5_buffers(vox_cuda_f5 *plan, float **h, float **ts, float **out) {
     if (h) *h = p->h;
     if (ts) *ts = p->ts;
     if (out) *out = p->out;
+    return VOX_CUDA_OK;
+}
+
+int vox_cuda_f5_inputs(vox_cuda_f5 *plan, float **x, float **cond) {
+    VOX_REQUIRE(plan, "vox_cuda_f5_inputs: NULL plan");
+    F5Plan *p = reinterpret_cast<F5Plan *>(plan);
+    if (x) *x = p->xin;
+    if (cond) *cond = p->cond;
     return VOX_CUDA_OK;
 }
 

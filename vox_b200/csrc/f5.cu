@@ -48,20 +48,22 @@ __global__ void __launch_bounds__(256) f5_rope_kernel(float *q, float *k, const 
 
 // ------------------------------------------------------------------ input embedding (grouped position convolutions)
 
-// Conv weights from PyTorch's [cout][cig][K] into [cout][K][cig] (the order of the im2col columns), once at create.
-__global__ void __launch_bounds__(256) f5_conv_reorder_kernel(const float *w, float *wr, uint32_t n, uint32_t cig, uint32_t K) {
+// Conv weights from PyTorch's [cout][cig][K] into [cout][K][cig] (the order of the im2col columns), f32 or bf16 (RN),
+// once at create.
+template <typename TO>
+__global__ void __launch_bounds__(256) f5_conv_reorder_kernel(const float *w, TO *wr, uint32_t n, uint32_t cig, uint32_t K) {
     pdl_enter();
     for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
         const uint32_t i = e % cig, t = e / cig, k = t % K, o = t / K;  // e = (o K + k) cig + i
-        wr[e] = w[(size_t(o) * cig + i) * K + k];
+        wr[e] = TO(w[(size_t(o) * cig + i) * K + k]);
     }
 }
 
-// im2col of x [B][T][cin] for a grouped convolution with zero padding K/2: col [B][groups][T][K cig] with column
-// k cig + i = x[t + k - K/2][g cig + i] (zero outside the sequence); VW channels per thread (4: 16-byte accesses when
-// cig % 4 == 0, else 1).
-template <int VW>
-__global__ void __launch_bounds__(256) f5_im2col_kernel(const float *x, float *col, uint32_t items, uint32_t T, uint32_t cin,
+// im2col of x [B][T][cin] (f32) for a grouped convolution with zero padding K/2: col [B][groups][T][K cig] with column
+// k cig + i = x[t + k - K/2][g cig + i] (zero outside the sequence), in f32 or rounded to bf16 (RN); VW channels per
+// thread (4 when cig % 4 == 0, else 1).
+template <int VW, bool BF16>
+__global__ void __launch_bounds__(256) f5_im2col_kernel(const float *x, void *col, uint32_t items, uint32_t T, uint32_t cin,
                                                         uint32_t groups, uint32_t K) {
     pdl_enter();
     using V = typename std::conditional<VW == 4, float4, float>::type;
@@ -72,7 +74,13 @@ __global__ void __launch_bounds__(256) f5_im2col_kernel(const float *x, float *c
         const int tt = int(t) + int(k) - int(K / 2);
         V v{};
         if (tt >= 0 && tt < int(T)) v = reinterpret_cast<const V *>(x)[(size_t(sq) * T + uint32_t(tt)) * (cin / VW) + g * cq + iq];
-        reinterpret_cast<V *>(col)[e] = v;
+        if constexpr (!BF16) {
+            reinterpret_cast<V *>(col)[e] = v;
+        } else if constexpr (VW == 4) {
+            reinterpret_cast<uint2 *>(col)[e] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+        } else {
+            reinterpret_cast<__nv_bfloat16 *>(col)[e] = __float2bfloat16_rn(v);
+        }
     }
 }
 
@@ -472,22 +480,30 @@ int attention(F5Plan &p, int64_t b, cudaStream_t st) {
 constexpr int kPosGroups = 16, kPosK = 31;  // F5's position convolutions (f5.cpp:306-307)
 
 // conv of src [R][D] (B sequences of T frames) into dst [R][D]: im2col, then per sequence one GEMM batched over the
-// groups (col [T][K cig] of group g times the group's reordered weights [cog][K cig], into columns g cog of dst).
-int conv_pos(F5Plan &p, const float *src, const float *wr, float *dst, cudaStream_t st) {
+// groups (col [T][K cig] of group g times the group's reordered weights [cog][K cig], into columns g cog of dst); in
+// the bf16 mode columns and weights are bf16 (tensor cores, f32 accumulation).
+int conv_pos(F5Plan &p, const float *src, const void *wr, float *dst, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const uint32_t T = uint32_t(d.frames), D = uint32_t(d.dim), cig = D / kPosGroups, J = kPosK * cig;
     const uint32_t all = uint32_t(d.batch) * kPosGroups * T * J;
-    if (cig % 4 == 0)
-        launch_k(f5_im2col_kernel<4>, grid_for(all / 4, 256, 4), 256, 0, st, src, p.col, all / 4, T, D, uint32_t(kPosGroups), uint32_t(kPosK));
-    else
-        launch_k(f5_im2col_kernel<1>, grid_for(all, 256, 4), 256, 0, st, src, p.col, all, T, D, uint32_t(kPosGroups), uint32_t(kPosK));
+    const uint32_t G = uint32_t(kPosGroups), KK = uint32_t(kPosK);
+    if (cig % 4 == 0) {
+        if (p.bf16) launch_k(f5_im2col_kernel<4, true>, grid_for(all / 4, 256, 4), 256, 0, st, src, (void *)p.col, all / 4, T, D, G, KK);
+        else launch_k(f5_im2col_kernel<4, false>, grid_for(all / 4, 256, 4), 256, 0, st, src, (void *)p.col, all / 4, T, D, G, KK);
+    } else {
+        if (p.bf16) launch_k(f5_im2col_kernel<1, true>, grid_for(all, 256, 4), 256, 0, st, src, (void *)p.col, all, T, D, G, KK);
+        else launch_k(f5_im2col_kernel<1, false>, grid_for(all, 256, 4), 256, 0, st, src, (void *)p.col, all, T, D, G, KK);
+    }
     F5_TRY(check_launch("vox_cuda_f5 im2col"));
     const float one = 1.0f, zero = 0.0f;
+    const cudaDataType_t in_t = p.bf16 ? CUDA_R_16BF : CUDA_R_32F;
+    const size_t esz = p.bf16 ? 2 : 4;
     for (int64_t b = 0; b < d.batch; ++b)
-        F5_TRY(blas_check(cublasGemmStridedBatchedEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(cig), int(T), int(J), &one, wr, CUDA_R_32F,
-                                                     int(J), int64_t(cig) * J, p.col + size_t(b) * kPosGroups * T * J, CUDA_R_32F,
-                                                     int(J), int64_t(T) * J, &zero, dst + size_t(b) * T * D, CUDA_R_32F, int(D),
-                                                     int64_t(cig), kPosGroups, p.compute, CUBLAS_GEMM_DEFAULT),
+        F5_TRY(blas_check(cublasGemmStridedBatchedEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(cig), int(T), int(J), &one, wr, in_t, int(J),
+                                                     int64_t(cig) * J, reinterpret_cast<const char *>(p.col) + size_t(b) * G * T * J * esz,
+                                                     in_t, int(J), int64_t(T) * J, &zero, dst + size_t(b) * T * D, CUDA_R_32F, int(D),
+                                                     int64_t(cig), kPosGroups, p.bf16 ? CUBLAS_COMPUTE_32F : p.compute,
+                                                     CUBLAS_GEMM_DEFAULT),
                           "position convolution"));
     return VOX_CUDA_OK;
 }
@@ -741,7 +757,12 @@ int build(F5Plan &p, cudaStream_t user) {
             cudaMemsetAsync(p.cond, 0, R * size_t(d.in_dim - d.out_dim) * 4, user) != cudaSuccess)
             return check_launch("vox_cuda_f5_create");
         for (auto [w, wr] : {std::make_pair(d.pos1_w, p.w1r), std::make_pair(d.pos2_w, p.w2r)}) {
-            launch_k(f5_conv_reorder_kernel, grid_for(int64_t(nw), 256, 4), 256, 0, user, w, wr, uint32_t(nw), uint32_t(cig), uint32_t(kPosK));
+            if (p.bf16)
+                launch_k(f5_conv_reorder_kernel<__nv_bfloat16>, grid_for(int64_t(nw), 256, 4), 256, 0, user, w,
+                         reinterpret_cast<__nv_bfloat16 *>(wr), uint32_t(nw), uint32_t(cig), uint32_t(kPosK));
+            else
+                launch_k(f5_conv_reorder_kernel<float>, grid_for(int64_t(nw), 256, 4), 256, 0, user, w, wr, uint32_t(nw), uint32_t(cig),
+                         uint32_t(kPosK));
             F5_TRY(check_launch("vox_cuda_f5_create (conv weights)"));
         }
     }

@@ -553,16 +553,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
 constexpr int kRowBatch = 8;              // rows per tensor copy
 constexpr int kRowStages = 3;             // copies in flight per warp
 constexpr int kRowBox = kRowBatch * 512;  // 4 KB
-template <bool SF16> __host__ __device__ constexpr int scale_box() { return kCcRows * 16 * (SF16 ? 2 : 4); }
-template <bool SF16> __host__ __device__ constexpr size_t rows_smem() {
-    return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<SF16>()) + 128;  // + alignment slack
+// Blocks of a 512-byte row chunk: 16 (Q8, 32 bytes a block) or 32 (Q4, 16 bytes a block); their scales for the 32 rows.
+template <bool Q4> __host__ __device__ constexpr int chunk_scales() { return Q4 ? 32 : 16; }
+template <bool Q4, bool SF16> __host__ __device__ constexpr int scale_box() { return kCcRows * chunk_scales<Q4>() * (SF16 ? 2 : 4); }
+template <bool Q4, bool SF16> __host__ __device__ constexpr size_t rows_smem() {
+    return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<Q4, SF16>()) + 128;  // + alignment slack
 }
 
-template <bool SF16, int M>
+// Q8: lane l holds bytes 16 l .. 16 l + 15 of every row of the chunk (codes of half a block); Q4: the same 16 bytes
+// are one whole block (byte j: element j in the low nibble, element j + 16 in the high nibble), so the lane keeps 32
+// activation values and one scale per row.
+template <bool Q4, bool SF16, int M>
 __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap,
                                                                  const __grid_constant__ CUtensorMap smap, GemvArgs a, int C) {
     using ST = typename std::conditional<SF16, __half, float>::type;
-    constexpr int SB = scale_box<SF16>();
+    constexpr int SB = scale_box<Q4, SF16>();
+    constexpr int BPC = chunk_scales<Q4>();  // scales per row of a chunk
+    constexpr int EPL = Q4 ? 32 : 16;        // weights (and activation values) per lane per row
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     __shared__ float red[kWarps][M][kCcRows];
@@ -572,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
     uint8_t *sring = wring + kRowStages * kRowBox;  // two chunks' scales
     const int crank = int(blockIdx.x) % C;
     const int row0 = int(blockIdx.x / C) * kCcRows;  // rows < 2^31 (launcher)
-    const int64_t rowbytes = a.cols;
+    const int64_t rowbytes = Q4 ? a.cols / 2 : a.cols;
     const int nchunk = int((rowbytes + 511) / 512);
     const int c0 = crank * kWarps + warp, cstep = kWarps * C;
     const int nmine = c0 < nchunk ? (nchunk - c0 + cstep - 1) / cstep : 0;  // chunks of this warp
@@ -592,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
             const bool with_scales = u % 4 == 0;
             mbar_arrive_expect_tx(&wbar[s], kRowBox + (with_scales ? SB : 0));
             tensor_g2s_2d(wring + s * kRowBox, &wmap, ci * 128, row0 + (u % 4) * kRowBatch, &wbar[s]);
-            if (with_scales) tensor_g2s_2d(sring + (k & 1) * SB, &smap, ci * 16, row0, &wbar[s]);
+            if (with_scales) tensor_g2s_2d(sring + (k & 1) * SB, &smap, ci * BPC, row0, &wbar[s]);
         }
     };
     for (int u = 0; u < kRowStages && u < units; ++u) issue(u);
@@ -606,16 +613,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
     for (int k = 0; k < nmine && ok; ++k) {
         const int64_t cb = int64_t(c0 + k * cstep) * 512 + lane * 16;  // this lane's 16 bytes of every row
         const bool valid = cb < rowbytes;
-        float2 xv[M][8];
+        const int64_t e0 = Q4 ? 2 * cb : cb;  // its first weight's column
+        float2 xv[M][EPL / 2];
 #pragma unroll
         for (int t = 0; t < M; ++t)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + cb) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < EPL / 4; ++q) {
+                const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + e0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
                 xv[t][2 * q] = make_float2(v.x, v.y);
                 xv[t][2 * q + 1] = make_float2(v.z, v.w);
             }
-        const ST *scs = reinterpret_cast<const ST *>(sring + (k & 1) * SB) + (lane >> 1);  // [32 rows][16 blocks]
+        const ST *scs = reinterpret_cast<const ST *>(sring + (k & 1) * SB) + (Q4 ? lane : lane >> 1);  // [32 rows][BPC blocks]
 #pragma unroll 1
         for (int b = 0; b < kCcRows / kRowBatch; ++b) {
             const int u = k * 4 + b, s = u % kRowStages;
@@ -629,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
 #pragma unroll
             for (int r = 0; r < kRowBatch; ++r) {
                 const uint4 w = *reinterpret_cast<const uint4 *>(st + r * 512);
-                const float sc = float(scs[(b * kRowBatch + r) * 16]);
+                const float sc = float(scs[(b * kRowBatch + r) * BPC]);
                 const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
                 float2 p[M][2];
 #pragma unroll
@@ -637,11 +645,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     float2 c01, c23;
-                    q8_to_f32(wd[i], c01, c23);
+                    if constexpr (Q4) {
+                        float2 h01, h23;
+                        q4_to_f32(wd[i] & 0x0F0F0F0Fu, c01, c23);         // elements 4 i .. 4 i + 3
+                        q4_to_f32((wd[i] >> 4) & 0x0F0F0F0Fu, h01, h23);  // elements 16 + 4 i .. 16 + 4 i + 3
 #pragma unroll
-                    for (int t = 0; t < M; ++t) {
-                        p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
-                        p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                        for (int t = 0; t < M; ++t) {
+                            p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                            p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                            p[t][0] = __ffma2_rn(h01, xv[t][8 + 2 * i], p[t][0]);
+                            p[t][1] = __ffma2_rn(h23, xv[t][8 + 2 * i + 1], p[t][1]);
+                        }
+                    } else {
+                        q8_to_f32(wd[i], c01, c23);
+#pragma unroll
+                        for (int t = 0; t < M; ++t) {
+                            p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                            p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                        }
                     }
                 }
 #pragma unroll
@@ -887,7 +908,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 //   kMmaBoxes: uint8 elements [rows][rowbytes], box 16 rows x 128 bytes, 128-byte swizzle (the MMA path's fragments);
 //   kRowBoxes: 4-byte elements [rows][rowbytes / 4], box 8 rows x 512 bytes (the CUDA-core path reads rows in order);
 //   kScaleBoxes: the block scales [rows][nblk] (2- or 4-byte elements, esize), box 32 rows x 16 blocks.
-enum MapKind { kMmaBoxes = 0, kRowBoxes = 1, kScaleBoxes = 2 };
+enum MapKind { kMmaBoxes = 0, kRowBoxes = 1, kScaleBoxes = 2, kScaleBoxes32 = 3 };
 int weight_map(const void *base, int64_t rows, int64_t width, int kind, int esize, CUtensorMap &map, const char *name) {
     static std::mutex mu;
     static std::map<std::tuple<int, const void *, int64_t, int64_t, int, int>, CUtensorMap> cache;
@@ -913,8 +934,8 @@ int weight_map(const void *base, int64_t rows, int64_t width, int kind, int esiz
     } else if (kind == kRowBoxes) {
         dims[0] = cuuint64_t(width / 4), strides[0] = cuuint64_t(width), box[0] = 128, box[1] = 8;
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
-    } else {
-        dims[0] = cuuint64_t(width), strides[0] = cuuint64_t(width * esize), box[0] = 16, box[1] = 32;
+    } else {  // scales: 16 (Q8) or 32 (Q4) blocks of 32 rows
+        dims[0] = cuuint64_t(width), strides[0] = cuuint64_t(width * esize), box[0] = kind == kScaleBoxes32 ? 32 : 16, box[1] = 32;
         dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
     }
     dims[1] = cuuint64_t(rows);
@@ -936,9 +957,11 @@ bool tma_rows_enabled() {
     return on;
 }
 
-template <bool SF16, int M>
+template <bool Q4, bool SF16, int M>
 int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
-    auto kern = gemv_rows_kernel<SF16, M>;
+    auto kern = gemv_rows_kernel<Q4, SF16, M>;
+    constexpr size_t smem_bytes = rows_smem<Q4, SF16>();
+    const int64_t rowbytes = Q4 ? a.cols / 2 : a.cols;
     static std::mutex mu;
     static std::map<std::tuple<int, int64_t, int64_t>, int> plans;
     int dev = 0;
@@ -951,10 +974,10 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
         if (it != plans.end()) {
             C = it->second;
         } else {
-            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(rows_smem<SF16>())) != cudaSuccess)
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes)) != cudaSuccess)
                 return check_launch(name);
-            const int64_t groups = (a.rows + kCcRows - 1) / kCcRows, nchunk = (a.cols + 511) / 512;
-            int64_t c = resident_blocks((const void *)kern, kThreads, rows_smem<SF16>()) / groups;
+            const int64_t groups = (a.rows + kCcRows - 1) / kCcRows, nchunk = (rowbytes + 511) / 512;
+            int64_t c = resident_blocks((const void *)kern, kThreads, smem_bytes) / groups;
             if (c > nchunk / kWarps) c = nchunk / kWarps;
             C = int(c < 1 ? 1 : c > 8 ? 8 : c);
             while (C > 1) {  // all clusters co-resident
@@ -962,7 +985,7 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
                 cudaLaunchAttribute at;
                 at.id = cudaLaunchAttributeClusterDimension;
                 at.val.clusterDim.x = unsigned(C), at.val.clusterDim.y = 1, at.val.clusterDim.z = 1;
-                q.gridDim = dim3(unsigned(groups * C)), q.blockDim = dim3(kThreads), q.dynamicSmemBytes = rows_smem<SF16>();
+                q.gridDim = dim3(unsigned(groups * C)), q.blockDim = dim3(kThreads), q.dynamicSmemBytes = smem_bytes;
                 q.attrs = &at, q.numAttrs = 1;
                 int clusters = 0;
                 if (cudaOccupancyMaxActiveClusters(&clusters, kern, &q) == cudaSuccess && clusters > 0) break;
@@ -973,14 +996,14 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
         }
     }
     CUtensorMap wmap, smap;
-    int rc = weight_map(a.w, a.rows, a.cols, kRowBoxes, 1, wmap, name);
-    if (rc == VOX_CUDA_OK) rc = weight_map(a.scale, a.rows, a.nblk, kScaleBoxes, SF16 ? 2 : 4, smap, name);
+    int rc = weight_map(a.w, a.rows, rowbytes, kRowBoxes, 1, wmap, name);
+    if (rc == VOX_CUDA_OK) rc = weight_map(a.scale, a.rows, a.nblk, Q4 ? kScaleBoxes32 : kScaleBoxes, SF16 ? 2 : 4, smap, name);
     if (rc != VOX_CUDA_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(unsigned((a.rows + kCcRows - 1) / kCcRows * C));
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = rows_smem<SF16>();
+    cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = st;
     int na = 0;
     attr[na].id = cudaLaunchAttributeClusterDimension;
@@ -1012,11 +1035,15 @@ int launch_gemv(const GemvArgs &base, int64_t m_total, cudaStream_t st, const ch
         a.m = int(m_total - i0 < kTok ? m_total - i0 : kTok);
         a.x = base.x + i0 * base.cols;
         a.y = base.y + i0 * base.ystride;
-        if constexpr (!Q4) {  // Q8 with one or two rows: the CUDA-core path (measured faster; Q4 stays on the MMA path)
-            if (a.m <= 2) {
-                const bool staged = (a.nblk * (SF16 ? 2 : 4)) % 16 == 0 && aligned16(a.scale) && tma_rows_enabled();
-                if (staged) rc = a.m == 1 ? launch_rows<SF16, 1>(a, st, name) : launch_rows<SF16, 2>(a, st, name);
-                else rc = a.m == 1 ? launch_cc<Q4, SF16, 1>(a, st, name) : launch_cc<Q4, SF16, 2>(a, st, name);
+        if (a.m <= 2) {  // one or two activation rows: the CUDA-core path with tensor-copy staging (measured faster)
+            const bool staged = (a.nblk * (SF16 ? 2 : 4)) % 16 == 0 && aligned16(a.scale) && tma_rows_enabled();
+            if (staged) {
+                rc = a.m == 1 ? launch_rows<Q4, SF16, 1>(a, st, name) : launch_rows<Q4, SF16, 2>(a, st, name);
+                if (rc != VOX_CUDA_OK) return rc;
+                continue;
+            }
+            if constexpr (!Q4) {  // register-staged Q8 where the scale rows are not 16-byte strided
+                rc = a.m == 1 ? launch_cc<Q4, SF16, 1>(a, st, name) : launch_cc<Q4, SF16, 2>(a, st, name);
                 if (rc != VOX_CUDA_OK) return rc;
                 continue;
             }

@@ -362,6 +362,26 @@ def test_dequant_config4_bitexact(vox, port):
     assert_bitexact(host(vox.dequant_q4(dev(q4), dev(s32), torch.float32)), want4)
 
 
+def test_dequant_edge_scales_bitexact(vox, port):
+    """f16 scales at the edges of the format: +-0, negative, subnormal, the largest finite, +-inf and NaN, next to
+    ordinary ones; bit-exact against float(code) * scale (kernels.cpp:450, 459-460), NaN where it is NaN."""
+    rows, cols = 7, 4096
+    q8 = port.fill_i8((rows, cols), -128, 127, sid=143)
+    q8[:, :32] = np.arange(-128, 128, 8, dtype=np.int16).astype(np.int8)  # zero and the extremes in block 0
+    q4 = port.fill_u8((rows, cols // 2), sid=144)
+    special = np.array([0.0, -0.0, -0.02, 6e-8, 3e-5, 65504.0, np.inf, -np.inf, np.nan, 0.001, 0.05], np.float16)
+    s16 = port.uniform_arr((rows, cols // 32), 0.001, 0.05, sid=145).astype(np.float16)
+    flat = s16.reshape(-1)
+    flat[::3] = np.resize(special, flat[::3].shape)
+    s32 = port.f16_to_f32(s16.view(np.uint16))
+    for fn, q, want in ((vox.dequant_q8, q8, port.dequant_q8(q8, s32)), (vox.dequant_q4, q4, port.dequant_q4(q4, s32))):
+        for out_dt, ref in ((torch.float32, want), (torch.bfloat16, bf16r(want))):
+            got = host(fn(dev(q), dev(s16), out_dt))
+            nan = np.isnan(ref)
+            np.testing.assert_array_equal(np.isnan(got), nan)
+            assert_bitexact(np.where(nan, 0, got), np.where(nan, 0, ref))
+
+
 def test_dequant_small_shapes(vox, port):
     for rows, cols in ((1, 32), (3, 64), (5, 96), (0, 32)):
         q8 = port.fill_i8((rows, cols), -128, 127, sid=150)

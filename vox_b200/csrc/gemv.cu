@@ -553,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
 constexpr int kRowBatch = 8;              // rows per tensor copy
 constexpr int kRowStages = 3;             // copies in flight per warp
 constexpr int kRowBox = kRowBatch * 512;  // 4 KB
+static_assert(2 * 32 * 4 <= kRowStages * kRowBox, "row partials of two activation rows fit in a warp ring");
 // Blocks of a 512-byte row chunk: 16 (Q8, 32 bytes a block) or 32 (Q4, 16 bytes a block); their scales for the 32 rows.
 template <bool Q4> __host__ __device__ constexpr int chunk_scales() { return Q4 ? 32 : 16; }
 template <bool Q4, bool SF16> __host__ __device__ constexpr int scale_box() { return kCcRows * chunk_scales<Q4>() * (SF16 ? 2 : 4); }
@@ -572,10 +573,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
     constexpr int EPL = Q4 ? 32 : 16;        // weights (and activation values) per lane per row
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    __shared__ float red[kWarps][M][kCcRows];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *wbar = reinterpret_cast<uint64_t *>(smem) + warp * kRowStages;
     uint8_t *wring = smem + 256 + size_t(warp) * (kRowStages * kRowBox + 2 * SB);
+    // the row partials of warp w ([M][32] floats) go to the start of w's ring once its copies have landed: no static
+    // shared memory, so two CTAs (Q8, f16 scales) fit on an SM
+    auto red = [&](int w) { return reinterpret_cast<float *>(smem + 256 + size_t(w) * (kRowStages * kRowBox + 2 * SB)); };
     uint8_t *sring = wring + kRowStages * kRowBox;  // two chunks' scales
     const int crank = int(blockIdx.x) % C;
     const int row0 = int(blockIdx.x / C) * kCcRows;  // rows < 2^31 (launcher)
@@ -705,16 +708,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
 #pragma unroll
         for (int b = 0; b < kCcRows / kRowBatch; ++b)
 #pragma unroll
-            for (int t = 0; t < M; ++t) red[warp][t][b * kRowBatch + lane] = tot[b][t];
+            for (int t = 0; t < M; ++t) red(warp)[t * kCcRows + b * kRowBatch + lane] = tot[b][t];
     }
     __syncthreads();
-    float *cta = &red[0][0][0];
+    float *cta = red(0);
     if (threadIdx.x < M * kCcRows) {
         const int t = threadIdx.x / kCcRows, r = threadIdx.x % kCcRows;
-        float v = red[0][t][r];
+        float v = red(0)[t * kCcRows + r];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) v += red[w][t][r];
-        cta[t * kCcRows + r] = v;
+        for (int w = 1; w < kWarps; ++w) v += red(w)[t * kCcRows + r];
+        cta[t * kCcRows + r] = v;  // red(0) is read above by this thread only
     }
     const bool clustered = C > 1;
     if (clustered) cg::this_cluster().sync();

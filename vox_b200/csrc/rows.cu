@@ -200,7 +200,10 @@ __global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_ke
 #pragma unroll
     for (int t = 0; t < STAGES; ++t)
         if (first + t * kPipeWarps < r1) pending |= 1u << t;
-    // A and C of the range's first batch, while the first rows are in flight
+    // A and C of the range's first batch, while the first rows are in flight. Pairs 2q, 2q + 1 of 16-byte vector v sit
+    // in float4 q * nvec + v, so one epilogue read of the 32 lanes (vectors lane + 32 k) is 512 contiguous bytes: four
+    // shared-memory wavefronts, the minimum for 16 bytes a lane (a vector-major table, lanes 32 bytes apart, took
+    // eight wavefronts for every 8 bytes a lane).
     const int64_t batch0 = r0 < r1 ? int64_t(a.tdiv.div(uint32_t(r0))) : 0;
     if (r0 < r1) {
         const char *scp = reinterpret_cast<const char *>(a.scale) + batch0 * a.n * ES;
@@ -212,9 +215,11 @@ __global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_ke
             unpack2<DT>(ld_param(shp + v * 16), sh);
             unpack2<DT>(ld_param(gp + v * 16), gv);
 #pragma unroll
-            for (int p = 0; p < PW; ++p) {
-                reinterpret_cast<float2 *>(ac)[v * PW + p] = mul2(gv[p], add2(bc2(1.0f), sc[p]));
-                reinterpret_cast<float2 *>(ac + a.n)[v * PW + p] = mul2(gv[p], sh[p]);
+            for (int q = 0; q < PW / 2; ++q) {
+                const float2 a0 = mul2(gv[2 * q], add2(bc2(1.0f), sc[2 * q])), a1 = mul2(gv[2 * q + 1], add2(bc2(1.0f), sc[2 * q + 1]));
+                const float2 c0 = mul2(gv[2 * q], sh[2 * q]), c1 = mul2(gv[2 * q + 1], sh[2 * q + 1]);
+                reinterpret_cast<float4 *>(ac)[q * nvec + v] = make_float4(a0.x, a0.y, a1.x, a1.y);
+                reinterpret_cast<float4 *>(ac + a.n)[q * nvec + v] = make_float4(c0.x, c0.y, c1.x, c1.y);
             }
         }
     }
@@ -279,10 +284,14 @@ __global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_ke
                 if (j < nvec) {
                     float2 rv[PW], o[PW];
                     unpack2<DT>(rres[k], rv);
-                    const float2 *A = reinterpret_cast<const float2 *>(ac) + j * PW;
-                    const float2 *Cc = reinterpret_cast<const float2 *>(ac + a.n) + j * PW;
+                    const float4 *A = reinterpret_cast<const float4 *>(ac) + j;
+                    const float4 *Cc = reinterpret_cast<const float4 *>(ac + a.n) + j;
 #pragma unroll
-                    for (int p = 0; p < PW; ++p) o[p] = add2(fma2(A[p], fma2(xv[k][p], inv2, nmi), Cc[p]), rv[p]);
+                    for (int q = 0; q < PW / 2; ++q) {
+                        const float4 av = A[q * nvec], cv = Cc[q * nvec];
+                        o[2 * q] = add2(fma2(make_float2(av.x, av.y), fma2(xv[k][2 * q], inv2, nmi), make_float2(cv.x, cv.y)), rv[2 * q]);
+                        o[2 * q + 1] = add2(fma2(make_float2(av.z, av.w), fma2(xv[k][2 * q + 1], inv2, nmi), make_float2(cv.z, cv.w)), rv[2 * q + 1]);
+                    }
                     st_stream(yr + j * 16, pack2<DT>(o));
                 }
             }

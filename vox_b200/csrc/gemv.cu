@@ -548,15 +548,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_cc_kernel(GemvArgs a, int C)
 }
 
 // The same arithmetic with the rows and the scales staged by tensor copies (no registers held for bytes in flight,
-// no load latency inside the loop): a warp streams its 512-byte chunk of the CTA's 32 rows as four copies of 8 rows
-// (three in flight) and the chunk's block scales of the 32 rows as one copy issued with the chunk's first rows.
+// no load latency inside the loop): a warp streams its 512-byte chunk of the CTA's 16 rows as two copies of 8 rows
+// (up to three in flight over the warp's chunks) and the chunk's block scales of the 16 rows as one copy issued with
+// the chunk's first rows.
 constexpr int kRowBatch = 8;              // rows per tensor copy
-constexpr int kRowStages = 3;             // copies in flight per warp
+constexpr int kRowsCta = 16;              // rows per CTA: [12288, 4096] makes 768 CTAs, 2.6 waves of 2 per SM
+constexpr int kRowStages = 2;             // copies in flight per warp (a warp of [rows, 4096] Q8 or Q4 has two)
 constexpr int kRowBox = kRowBatch * 512;  // 4 KB
-static_assert(2 * 32 * 4 <= kRowStages * kRowBox, "row partials of two activation rows fit in a warp ring");
-// Blocks of a 512-byte row chunk: 16 (Q8, 32 bytes a block) or 32 (Q4, 16 bytes a block); their scales for the 32 rows.
+constexpr int kRowCopies = kRowsCta / kRowBatch;  // copies per chunk
+static_assert(2 * kRowsCta * 4 <= kRowStages * kRowBox, "row partials of two activation rows fit in a warp ring");
+// Blocks of a 512-byte row chunk: 16 (Q8, 32 bytes a block) or 32 (Q4, 16 bytes a block); their scales for the CTA's rows.
 template <bool Q4> __host__ __device__ constexpr int chunk_scales() { return Q4 ? 32 : 16; }
-template <bool Q4, bool SF16> __host__ __device__ constexpr int scale_box() { return kCcRows * chunk_scales<Q4>() * (SF16 ? 2 : 4); }
+template <bool Q4, bool SF16> __host__ __device__ constexpr int scale_box() { return kRowsCta * chunk_scales<Q4>() * (SF16 ? 2 : 4); }
 template <bool Q4, bool SF16> __host__ __device__ constexpr size_t rows_smem() {
     return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<Q4, SF16>()) + 128;  // + alignment slack
 }
@@ -565,7 +568,7 @@ template <bool Q4, bool SF16> __host__ __device__ constexpr size_t rows_smem() {
 // are one whole block (byte j: element j in the low nibble, element j + 16 in the high nibble), so the lane keeps 32
 // activation values and one scale per row.
 template <bool Q4, bool SF16, int M>
-__global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : 2) gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap,
                                                                  const __grid_constant__ CUtensorMap smap, GemvArgs a, int C) {
     using ST = typename std::conditional<SF16, __half, float>::type;
     constexpr int SB = scale_box<Q4, SF16>();
@@ -576,17 +579,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *wbar = reinterpret_cast<uint64_t *>(smem) + warp * kRowStages;
     uint8_t *wring = smem + 256 + size_t(warp) * (kRowStages * kRowBox + 2 * SB);
-    // the row partials of warp w ([M][32] floats) go to the start of w's ring once its copies have landed: no static
+    // the row partials of warp w ([M][kRowsCta] floats) go to the start of w's ring once its copies have landed: no static
     // shared memory, so two CTAs (Q8, f16 scales) fit on an SM
     auto red = [&](int w) { return reinterpret_cast<float *>(smem + 256 + size_t(w) * (kRowStages * kRowBox + 2 * SB)); };
     uint8_t *sring = wring + kRowStages * kRowBox;  // two chunks' scales
     const int crank = int(blockIdx.x) % C;
-    const int row0 = int(blockIdx.x / C) * kCcRows;  // rows < 2^31 (launcher)
+    const int row0 = int(blockIdx.x / C) * kRowsCta;  // rows < 2^31 (launcher)
     const int64_t rowbytes = Q4 ? a.cols / 2 : a.cols;
     const int nchunk = int((rowbytes + 511) / 512);
     const int c0 = crank * kWarps + warp, cstep = kWarps * C;
     const int nmine = c0 < nchunk ? (nchunk - c0 + cstep - 1) / cstep : 0;  // chunks of this warp
-    const int units = nmine * (kCcRows / kRowBatch);                         // one unit = one copy of 8 rows
+    const int units = nmine * kRowCopies;                                     // one unit = one copy of 8 rows
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kRowStages; ++s) mbar_init(&wbar[s], 1);
@@ -594,21 +597,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
     }
     __syncwarp();
     pdl_enter();
-    // unit u: chunk k = u / 4 (c0 + k cstep), rows row0 + 8 (u % 4) .. + 7, into stage u % kRowStages; the first unit
-    // of a chunk also brings the chunk's scales of the 32 rows into scale buffer k % 2
+    // unit u: chunk k = u / kRowCopies (c0 + k cstep), rows row0 + 8 (u % kRowCopies) .. + 7, into stage u % kRowStages;
+    // the first unit of a chunk also brings the chunk's scales of the CTA's rows into scale buffer k % 2
     auto issue = [&](int u) {
         if (lane == 0) {
-            const int s = u % kRowStages, k = u / 4, ci = c0 + k * cstep;
-            const bool with_scales = u % 4 == 0;
+            const int s = u % kRowStages, k = u / kRowCopies, ci = c0 + k * cstep;
+            const bool with_scales = u % kRowCopies == 0;
             mbar_arrive_expect_tx(&wbar[s], kRowBox + (with_scales ? SB : 0));
-            tensor_g2s_2d(wring + s * kRowBox, &wmap, ci * 128, row0 + (u % 4) * kRowBatch, &wbar[s]);
+            tensor_g2s_2d(wring + s * kRowBox, &wmap, ci * 128, row0 + (u % kRowCopies) * kRowBatch, &wbar[s]);
             if (with_scales) tensor_g2s_2d(sring + (k & 1) * SB, &smap, ci * BPC, row0, &wbar[s]);
         }
     };
     for (int u = 0; u < kRowStages && u < units; ++u) issue(u);
-    float tot[kCcRows / kRowBatch][M];
+    float tot[kRowCopies][M];
 #pragma unroll
-    for (int b = 0; b < kCcRows / kRowBatch; ++b)
+    for (int b = 0; b < kRowCopies; ++b)
 #pragma unroll
         for (int t = 0; t < M; ++t) tot[b][t] = 0.f;
     uint32_t parity = 0;
@@ -626,10 +629,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
                 xv[t][2 * q] = make_float2(v.x, v.y);
                 xv[t][2 * q + 1] = make_float2(v.z, v.w);
             }
-        const ST *scs = reinterpret_cast<const ST *>(sring + (k & 1) * SB) + (Q4 ? lane : lane >> 1);  // [32 rows][BPC blocks]
+        const ST *scs = reinterpret_cast<const ST *>(sring + (k & 1) * SB) + (Q4 ? lane : lane >> 1);  // [kRowsCta rows][BPC blocks]
 #pragma unroll 1
-        for (int b = 0; b < kCcRows / kRowBatch; ++b) {
-            const int u = k * 4 + b, s = u % kRowStages;
+        for (int b = 0; b < kRowCopies; ++b) {
+            const int u = k * kRowCopies + b, s = u % kRowStages;
             if (!mbar_wait_warp(&wbar[s], (parity >> s) & 1u)) {
                 ok = false;
                 break;
@@ -696,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
                 v += __shfl_xor_sync(0xffffffffu, v, 8);
                 v += __shfl_xor_sync(0xffffffffu, v, 16);
 #pragma unroll
-                for (int bb = 0; bb < kCcRows / kRowBatch; ++bb) tot[bb][t] += b == bb ? v : 0.f;
+                for (int bb = 0; bb < kRowCopies; ++bb) tot[bb][t] += b == bb ? v : 0.f;
             }
         }
     }
@@ -706,23 +709,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
     }
     if (lane < kRowBatch) {
 #pragma unroll
-        for (int b = 0; b < kCcRows / kRowBatch; ++b)
+        for (int b = 0; b < kRowCopies; ++b)
 #pragma unroll
-            for (int t = 0; t < M; ++t) red(warp)[t * kCcRows + b * kRowBatch + lane] = tot[b][t];
+            for (int t = 0; t < M; ++t) red(warp)[t * kRowsCta + b * kRowBatch + lane] = tot[b][t];
     }
     __syncthreads();
     float *cta = red(0);
-    if (threadIdx.x < M * kCcRows) {
-        const int t = threadIdx.x / kCcRows, r = threadIdx.x % kCcRows;
-        float v = red(0)[t * kCcRows + r];
+    if (threadIdx.x < M * kRowsCta) {
+        const int t = threadIdx.x / kRowsCta, r = threadIdx.x % kRowsCta;
+        float v = red(0)[t * kRowsCta + r];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) v += red(w)[t * kCcRows + r];
-        cta[t * kCcRows + r] = v;  // red(0) is read above by this thread only
+        for (int w = 1; w < kWarps; ++w) v += red(w)[t * kRowsCta + r];
+        cta[t * kRowsCta + r] = v;  // red(0) is read above by this thread only
     }
     const bool clustered = C > 1;
     if (clustered) cg::this_cluster().sync();
     else __syncthreads();
-    const int lo_r = crank * kCcRows / C, hi_r = (crank + 1) * kCcRows / C, span = hi_r - lo_r;
+    const int lo_r = crank * kRowsCta / C, hi_r = (crank + 1) * kRowsCta / C, span = hi_r - lo_r;
     if (threadIdx.x < M * span) {
         const int t = threadIdx.x / span, r = lo_r + threadIdx.x % span;
         const int64_t grow = row0 + r;
@@ -731,9 +734,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_rows_kernel(const __grid_con
             if (clustered) {
                 cg::cluster_group cl = cg::this_cluster();
                 v = 0.f;
-                for (int q = 0; q < C; ++q) v += cl.map_shared_rank(cta, q)[t * kCcRows + r];
+                for (int q = 0; q < C; ++q) v += cl.map_shared_rank(cta, q)[t * kRowsCta + r];
             } else {
-                v = cta[t * kCcRows + r];
+                v = cta[t * kRowsCta + r];
             }
             float *yp = a.y + int64_t(t) * a.ystride + grow;
             const float out = (a.bias ? __ldg(a.bias + grow) : 0.f) + v;
@@ -910,7 +913,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // The 2-D tensor maps of a weight matrix, cached per device, address, shape and layout (zero fill past the edges):
 //   kMmaBoxes: uint8 elements [rows][rowbytes], box 16 rows x 128 bytes, 128-byte swizzle (the MMA path's fragments);
 //   kRowBoxes: 4-byte elements [rows][rowbytes / 4], box 8 rows x 512 bytes (the CUDA-core path reads rows in order);
-//   kScaleBoxes: the block scales [rows][nblk] (2- or 4-byte elements, esize), box 32 rows x 16 blocks.
+//   kScaleBoxes / kScaleBoxes32: the block scales [rows][nblk] (2- or 4-byte elements, esize), box kRowsCta rows x 16
+//   (Q8) or 32 (Q4) blocks.
 enum MapKind { kMmaBoxes = 0, kRowBoxes = 1, kScaleBoxes = 2, kScaleBoxes32 = 3 };
 int weight_map(const void *base, int64_t rows, int64_t width, int kind, int esize, CUtensorMap &map, const char *name) {
     static std::mutex mu;
@@ -938,7 +942,7 @@ int weight_map(const void *base, int64_t rows, int64_t width, int kind, int esiz
         dims[0] = cuuint64_t(width / 4), strides[0] = cuuint64_t(width), box[0] = 128, box[1] = 8;
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
     } else {  // scales: 16 (Q8) or 32 (Q4) blocks of 32 rows
-        dims[0] = cuuint64_t(width), strides[0] = cuuint64_t(width * esize), box[0] = kind == kScaleBoxes32 ? 32 : 16, box[1] = 32;
+        dims[0] = cuuint64_t(width), strides[0] = cuuint64_t(width * esize), box[0] = kind == kScaleBoxes32 ? 32 : 16, box[1] = kRowsCta;
         dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
     }
     dims[1] = cuuint64_t(rows);
@@ -979,7 +983,7 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
         } else {
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes)) != cudaSuccess)
                 return check_launch(name);
-            const int64_t groups = (a.rows + kCcRows - 1) / kCcRows, nchunk = (rowbytes + 511) / 512;
+            const int64_t groups = (a.rows + kRowsCta - 1) / kRowsCta, nchunk = (rowbytes + 511) / 512;
             int64_t c = resident_blocks((const void *)kern, kThreads, smem_bytes) / groups;
             if (c > nchunk / kWarps) c = nchunk / kWarps;
             C = int(c < 1 ? 1 : c > 8 ? 8 : c);
@@ -1004,7 +1008,7 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
     if (rc != VOX_CUDA_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
-    cfg.gridDim = dim3(unsigned((a.rows + kCcRows - 1) / kCcRows * C));
+    cfg.gridDim = dim3(unsigned((a.rows + kRowsCta - 1) / kRowsCta * C));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = st;

@@ -22,8 +22,17 @@ namespace voxcuda {
 // exposes it through take_device_error() and vox_cuda_device_error() gathers them all.
 static __device__ unsigned int g_device_error = 0;
 constexpr unsigned int kDevErrTimeout = 1u;
-// try_wait polls before a wait gives up (each poll may also suspend the warp for a hardware-chosen time).
-constexpr uint32_t kMaxWaitPolls = 1u << 22;
+// A wait gives up after this much time on the GPU's global timer (ns).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Each try_wait may suspend the thread until the phase completes, for at most this long (ns): a waiting warp then
+// issues a few polls per copy instead of spinning.
+constexpr uint32_t kSuspendHintNs = 100000u;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return uint32_t(__cvta_generic_to_shared(p)); }
 
@@ -38,18 +47,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
 // Bounded wait of a whole warp for the phase of `parity` to complete. Every lane polls (so every lane acquires the
-// phase) and the decision is warp-uniform; false, with the device error flag set, if the phase never completes.
+// phase) and every decision is warp-uniform (the time limit too); false, with the device error flag set, if the phase
+// has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMaxWaitPolls; ++i)
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+        if (__any_sync(0xffffffffu, globaltimer_ns() - t0 > kWaitLimitNs)) break;
+    }
     if ((threadIdx.x & 31) == 0) atomicOr(&g_device_error, kDevErrTimeout);
     return false;
 }

@@ -556,17 +556,20 @@ constexpr int kRowsCta = 16;              // rows per CTA: [12288, 4096] makes 7
 constexpr int kRowStages = 2;             // copies in flight per warp (a warp of [rows, 4096] Q8 or Q4 has two)
 constexpr int kRowBox = kRowBatch * 512;  // 4 KB
 constexpr int kRowCopies = kRowsCta / kRowBatch;  // copies per chunk
-static_assert(2 * kRowsCta * 4 <= kRowStages * kRowBox, "row partials of two activation rows fit in a warp ring");
 // Blocks of a 512-byte row chunk: 16 (Q8, 32 bytes a block) or 32 (Q4, 16 bytes a block); their scales for the CTA's rows.
 template <bool Q4> __host__ __device__ constexpr int chunk_scales() { return Q4 ? 32 : 16; }
 template <bool Q4, bool SF16> __host__ __device__ constexpr int scale_box() { return kRowsCta * chunk_scales<Q4>() * (SF16 ? 2 : 4); }
-template <bool Q4, bool SF16> __host__ __device__ constexpr size_t rows_smem() {
-    return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<Q4, SF16>()) + 128;  // + alignment slack
+template <bool Q4, bool SF16> __host__ __device__ constexpr size_t rows_smem() {  // + row partials of two groups, M <= 2
+    return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<Q4, SF16>()) + size_t(2) * kWarps * 2 * kRowsCta * 4 + 128;
 }
 
 // Q8: lane l holds bytes 16 l .. 16 l + 15 of every row of the chunk (codes of half a block); Q4: the same 16 bytes
 // are one whole block (byte j: element j in the low nibble, element j + 16 in the high nibble), so the lane keeps 32
 // activation values and one scale per row.
+//
+// Row groups of kRowsCta rows: a cluster of C CTAs splits one group's chunks (C > 1, one group per cluster), or a
+// persistent CTA (C = 1) takes groups blockIdx.x, + gridDim.x, ... and each warp's copy stream runs on across its
+// groups, so the copies of the next group are in flight while the current one is reduced and written.
 template <bool Q4, bool SF16, int M>
 __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : 2) gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap,
                                                                  const __grid_constant__ CUtensorMap smap, GemvArgs a, int C) {
@@ -579,17 +582,20 @@ __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : 2) gemv_rows_k
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *wbar = reinterpret_cast<uint64_t *>(smem) + warp * kRowStages;
     uint8_t *wring = smem + 256 + size_t(warp) * (kRowStages * kRowBox + 2 * SB);
-    // the row partials of warp w ([M][kRowsCta] floats) go to the start of w's ring once its copies have landed: no static
-    // shared memory, so two CTAs (Q8, f16 scales) fit on an SM
-    auto red = [&](int w) { return reinterpret_cast<float *>(smem + 256 + size_t(w) * (kRowStages * kRowBox + 2 * SB)); };
-    uint8_t *sring = wring + kRowStages * kRowBox;  // two chunks' scales
+    uint8_t *sring = wring + kRowStages * kRowBox;  // two chunk instances' scales
+    // row partials [2 (group parity)][kWarps][M][kRowsCta], after the rings
+    float *redbuf = reinterpret_cast<float *>(smem + 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * SB));
     const int crank = int(blockIdx.x) % C;
-    const int row0 = int(blockIdx.x / C) * kRowsCta;  // rows < 2^31 (launcher)
+    const int ngroups = int((a.rows + kRowsCta - 1) / kRowsCta);
+    const int gstep = int(gridDim.x) / C;
+    const int g0 = int(blockIdx.x) / C;
+    const int ngm = g0 < ngroups ? (ngroups - g0 + gstep - 1) / gstep : 0;  // groups of this CTA
     const int64_t rowbytes = Q4 ? a.cols / 2 : a.cols;
     const int nchunk = int((rowbytes + 511) / 512);
     const int c0 = crank * kWarps + warp, cstep = kWarps * C;
-    const int nmine = c0 < nchunk ? (nchunk - c0 + cstep - 1) / cstep : 0;  // chunks of this warp
-    const int units = nmine * kRowCopies;                                     // one unit = one copy of 8 rows
+    const int nmine = c0 < nchunk ? (nchunk - c0 + cstep - 1) / cstep : 0;  // chunks of this warp in every group
+    const int upg = nmine * kRowCopies;                                       // units (copies of 8 rows) per group
+    const int units = ngm * upg;
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kRowStages; ++s) mbar_init(&wbar[s], 1);
@@ -597,153 +603,161 @@ __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : 2) gemv_rows_k
     }
     __syncwarp();
     pdl_enter();
-    // unit u: chunk k = u / kRowCopies (c0 + k cstep), rows row0 + 8 (u % kRowCopies) .. + 7, into stage u % kRowStages;
-    // the first unit of a chunk also brings the chunk's scales of the CTA's rows into scale buffer k % 2
+    // unit u: group g0 + (u / upg) gstep, chunk instance ck = u / kRowCopies (chunk c0 + (ck % nmine) cstep), rows
+    // 8 (u % kRowCopies) .. + 7 of the group, into stage u % kRowStages; the first unit of a chunk instance also brings
+    // the chunk's scales of the group's rows into scale buffer ck % 2
     auto issue = [&](int u) {
         if (lane == 0) {
-            const int s = u % kRowStages, k = u / kRowCopies, ci = c0 + k * cstep;
+            const int s = u % kRowStages, ck = u / kRowCopies, ci = c0 + (ck % nmine) * cstep;
+            const int row0 = (g0 + (u / upg) * gstep) * kRowsCta;
             const bool with_scales = u % kRowCopies == 0;
             mbar_arrive_expect_tx(&wbar[s], kRowBox + (with_scales ? SB : 0));
             tensor_g2s_2d(wring + s * kRowBox, &wmap, ci * 128, row0 + (u % kRowCopies) * kRowBatch, &wbar[s]);
-            if (with_scales) tensor_g2s_2d(sring + (k & 1) * SB, &smap, ci * BPC, row0, &wbar[s]);
+            if (with_scales) tensor_g2s_2d(sring + (ck & 1) * SB, &smap, ci * BPC, row0, &wbar[s]);
         }
     };
     for (int u = 0; u < kRowStages && u < units; ++u) issue(u);
-    float tot[kRowCopies][M];
-#pragma unroll
-    for (int b = 0; b < kRowCopies; ++b)
-#pragma unroll
-        for (int t = 0; t < M; ++t) tot[b][t] = 0.f;
     uint32_t parity = 0;
     bool ok = true;
-    for (int k = 0; k < nmine && ok; ++k) {
-        const int64_t cb = int64_t(c0 + k * cstep) * 512 + lane * 16;  // this lane's 16 bytes of every row
-        const bool valid = cb < rowbytes;
-        const int64_t e0 = Q4 ? 2 * cb : cb;  // its first weight's column
-        float2 xv[M][EPL / 2];
-#pragma unroll
-        for (int t = 0; t < M; ++t)
-#pragma unroll
-            for (int q = 0; q < EPL / 4; ++q) {
-                const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + e0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                xv[t][2 * q] = make_float2(v.x, v.y);
-                xv[t][2 * q + 1] = make_float2(v.z, v.w);
-            }
-        const ST *scs = reinterpret_cast<const ST *>(sring + (k & 1) * SB) + (Q4 ? lane : lane >> 1);  // [kRowsCta rows][BPC blocks]
-#pragma unroll 1
-        for (int b = 0; b < kRowCopies; ++b) {
-            const int u = k * kRowCopies + b, s = u % kRowStages;
-            if (!mbar_wait_warp(&wbar[s], (parity >> s) & 1u)) {
-                ok = false;
-                break;
-            }
-            parity ^= 1u << s;
-            const uint8_t *st = wring + s * kRowBox + lane * 16;
-            float acc[kRowBatch][M];
-#pragma unroll
-            for (int r = 0; r < kRowBatch; ++r) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(st + r * 512);
-                const float sc = float(scs[(b * kRowBatch + r) * BPC]);
-                const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-                float2 p[M][2];
-#pragma unroll
-                for (int t = 0; t < M; ++t) p[t][0] = p[t][1] = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float2 c01, c23;
-                    if constexpr (Q4) {
-                        float2 h01, h23;
-                        q4_to_f32(wd[i] & 0x0F0F0F0Fu, c01, c23);         // elements 4 i .. 4 i + 3
-                        q4_to_f32((wd[i] >> 4) & 0x0F0F0F0Fu, h01, h23);  // elements 16 + 4 i .. 16 + 4 i + 3
-#pragma unroll
-                        for (int t = 0; t < M; ++t) {
-                            p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
-                            p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
-                            p[t][0] = __ffma2_rn(h01, xv[t][8 + 2 * i], p[t][0]);
-                            p[t][1] = __ffma2_rn(h23, xv[t][8 + 2 * i + 1], p[t][1]);
-                        }
-                    } else {
-                        q8_to_f32(wd[i], c01, c23);
-#pragma unroll
-                        for (int t = 0; t < M; ++t) {
-                            p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
-                            p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
-                        }
-                    }
-                }
-#pragma unroll
-                for (int t = 0; t < M; ++t) {
-                    const float2 q = __fadd2_rn(p[t][0], p[t][1]);
-                    acc[r][t] = (q.x + q.y) * sc;
-                }
-            }
-            __syncwarp();
-            if (u + kRowStages < units) {
-                if (lane == 0) fence_proxy_async();  // this stage's (and the older scale buffer's) reads precede the refill
-                issue(u + kRowStages);
-            }
-            // transpose butterfly over lane bits 2..0 (lane l keeps row l % 8), then a plain sum over bits 3, 4
-#pragma unroll
-            for (int t = 0; t < M; ++t) {
-#pragma unroll
-                for (int sh = kRowBatch / 2; sh >= 1; sh >>= 1) {
-                    const bool up = (lane & sh) != 0;
-#pragma unroll
-                    for (int j = 0; j < sh; ++j) {
-                        const float send = up ? acc[j][t] : acc[j + sh][t];
-                        const float keep = up ? acc[j + sh][t] : acc[j][t];
-                        acc[j][t] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
-                    }
-                }
-                float v = acc[0][t];
-                v += __shfl_xor_sync(0xffffffffu, v, 8);
-                v += __shfl_xor_sync(0xffffffffu, v, 16);
-#pragma unroll
-                for (int bb = 0; bb < kRowCopies; ++bb) tot[bb][t] += b == bb ? v : 0.f;
-            }
-        }
-    }
-    if (!ok) {
-        // let the warp's copies in flight land (bounded) before the CTA's shared memory can be reused
-        for (int s = 0; s < kRowStages; ++s) mbar_wait_warp(&wbar[s], (parity >> s) & 1u);
-    }
-    if (lane < kRowBatch) {
+    const bool clustered = C > 1;
+    for (int gi = 0; gi < ngm; ++gi) {
+        const int row0 = (g0 + gi * gstep) * kRowsCta;
+        float tot[kRowCopies][M];
 #pragma unroll
         for (int b = 0; b < kRowCopies; ++b)
 #pragma unroll
-            for (int t = 0; t < M; ++t) red(warp)[t * kRowsCta + b * kRowBatch + lane] = tot[b][t];
-    }
-    __syncthreads();
-    float *cta = red(0);
-    if (threadIdx.x < M * kRowsCta) {
-        const int t = threadIdx.x / kRowsCta, r = threadIdx.x % kRowsCta;
-        float v = red(0)[t * kRowsCta + r];
+            for (int t = 0; t < M; ++t) tot[b][t] = 0.f;
+        for (int k = 0; k < nmine && ok; ++k) {
+            const int ck = gi * nmine + k;
+            const int64_t cb = int64_t(c0 + k * cstep) * 512 + lane * 16;  // this lane's 16 bytes of every row
+            const bool valid = cb < rowbytes;
+            const int64_t e0 = Q4 ? 2 * cb : cb;  // its first weight's column
+            float2 xv[M][EPL / 2];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) v += red(w)[t * kRowsCta + r];
-        cta[t * kRowsCta + r] = v;  // red(0) is read above by this thread only
-    }
-    const bool clustered = C > 1;
-    if (clustered) cg::this_cluster().sync();
-    else __syncthreads();
-    const int lo_r = crank * kRowsCta / C, hi_r = (crank + 1) * kRowsCta / C, span = hi_r - lo_r;
-    if (threadIdx.x < M * span) {
-        const int t = threadIdx.x / span, r = lo_r + threadIdx.x % span;
-        const int64_t grow = row0 + r;
-        if (t < a.m && grow < a.rows) {
-            float v;
-            if (clustered) {
-                cg::cluster_group cl = cg::this_cluster();
-                v = 0.f;
-                for (int q = 0; q < C; ++q) v += cl.map_shared_rank(cta, q)[t * kRowsCta + r];
-            } else {
-                v = cta[t * kRowsCta + r];
+            for (int t = 0; t < M; ++t)
+#pragma unroll
+                for (int q = 0; q < EPL / 4; ++q) {
+                    const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + e0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    xv[t][2 * q] = make_float2(v.x, v.y);
+                    xv[t][2 * q + 1] = make_float2(v.z, v.w);
+                }
+            const ST *scs = reinterpret_cast<const ST *>(sring + (ck & 1) * SB) + (Q4 ? lane : lane >> 1);  // [kRowsCta rows][BPC blocks]
+#pragma unroll 1
+            for (int b = 0; b < kRowCopies; ++b) {
+                const int u = ck * kRowCopies + b, s = u % kRowStages;
+                if (!mbar_wait_warp(&wbar[s], (parity >> s) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                parity ^= 1u << s;
+                const uint8_t *st = wring + s * kRowBox + lane * 16;
+                float acc[kRowBatch][M];
+#pragma unroll
+                for (int r = 0; r < kRowBatch; ++r) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(st + r * 512);
+                    const float sc = float(scs[(b * kRowBatch + r) * BPC]);
+                    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+                    float2 p[M][2];
+#pragma unroll
+                    for (int t = 0; t < M; ++t) p[t][0] = p[t][1] = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float2 c01, c23;
+                        if constexpr (Q4) {
+                            float2 h01, h23;
+                            q4_to_f32(wd[i] & 0x0F0F0F0Fu, c01, c23);         // elements 4 i .. 4 i + 3
+                            q4_to_f32((wd[i] >> 4) & 0x0F0F0F0Fu, h01, h23);  // elements 16 + 4 i .. 16 + 4 i + 3
+#pragma unroll
+                            for (int t = 0; t < M; ++t) {
+                                p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                                p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                                p[t][0] = __ffma2_rn(h01, xv[t][8 + 2 * i], p[t][0]);
+                                p[t][1] = __ffma2_rn(h23, xv[t][8 + 2 * i + 1], p[t][1]);
+                            }
+                        } else {
+                            q8_to_f32(wd[i], c01, c23);
+#pragma unroll
+                            for (int t = 0; t < M; ++t) {
+                                p[t][0] = __ffma2_rn(c01, xv[t][2 * i], p[t][0]);
+                                p[t][1] = __ffma2_rn(c23, xv[t][2 * i + 1], p[t][1]);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int t = 0; t < M; ++t) {
+                        const float2 q = __fadd2_rn(p[t][0], p[t][1]);
+                        acc[r][t] = (q.x + q.y) * sc;
+                    }
+                }
+                __syncwarp();
+                if (u + kRowStages < units) {
+                    if (lane == 0) fence_proxy_async();  // this stage's (and the older scale buffer's) reads precede the refill
+                    issue(u + kRowStages);
+                }
+                // transpose butterfly over lane bits 2..0 (lane l keeps row l % 8), then a plain sum over bits 3, 4
+#pragma unroll
+                for (int t = 0; t < M; ++t) {
+#pragma unroll
+                    for (int sh = kRowBatch / 2; sh >= 1; sh >>= 1) {
+                        const bool up = (lane & sh) != 0;
+#pragma unroll
+                        for (int j = 0; j < sh; ++j) {
+                            const float send = up ? acc[j][t] : acc[j + sh][t];
+                            const float keep = up ? acc[j + sh][t] : acc[j][t];
+                            acc[j][t] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
+                        }
+                    }
+                    float v = acc[0][t];
+                    v += __shfl_xor_sync(0xffffffffu, v, 8);
+                    v += __shfl_xor_sync(0xffffffffu, v, 16);
+#pragma unroll
+                    for (int bb = 0; bb < kRowCopies; ++bb) tot[bb][t] += b == bb ? v : 0.f;
+                }
             }
-            float *yp = a.y + int64_t(t) * a.ystride + grow;
-            const float out = (a.bias ? __ldg(a.bias + grow) : 0.f) + v;
-            *yp = a.accumulate ? *yp + out : out;
         }
+        // the group's row sums: warps' partials added in warp order, then (clusters) the CTAs' sums in rank order
+        float *red = redbuf + (gi & 1) * (kWarps * M * kRowsCta);
+        if (lane < kRowBatch) {
+#pragma unroll
+            for (int b = 0; b < kRowCopies; ++b)
+#pragma unroll
+                for (int t = 0; t < M; ++t) red[(warp * M + t) * kRowsCta + b * kRowBatch + lane] = tot[b][t];
+        }
+        __syncthreads();
+        float *cta = red;  // warp 0's slots receive the CTA sums
+        if (threadIdx.x < M * kRowsCta) {
+            const int t = threadIdx.x / kRowsCta, r = threadIdx.x % kRowsCta;
+            float v = red[t * kRowsCta + r];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) v += red[(w * M + t) * kRowsCta + r];
+            cta[t * kRowsCta + r] = v;  // read above by this thread only
+        }
+        if (clustered) cg::this_cluster().sync();
+        else __syncthreads();
+        const int lo_r = crank * kRowsCta / C, hi_r = (crank + 1) * kRowsCta / C, span = hi_r - lo_r;
+        if (threadIdx.x < M * span) {
+            const int t = threadIdx.x / span, r = lo_r + threadIdx.x % span;
+            const int64_t grow = row0 + r;
+            if (t < a.m && grow < a.rows) {
+                float v;
+                if (clustered) {
+                    cg::cluster_group cl = cg::this_cluster();
+                    v = 0.f;
+                    for (int q = 0; q < C; ++q) v += cl.map_shared_rank(cta, q)[t * kRowsCta + r];
+                } else {
+                    v = cta[t * kRowsCta + r];
+                }
+                float *yp = a.y + int64_t(t) * a.ystride + grow;
+                const float out = (a.bias ? __ldg(a.bias + grow) : 0.f) + v;
+                *yp = a.accumulate ? *yp + out : out;
+            }
+        }
+        if (clustered) cg::this_cluster().sync();
     }
-    if (clustered) cg::this_cluster().sync();
+    if (!ok) {
+        // let the warp's copies in flight land (bounded) before the CTA's shared memory can be released
+        for (int s = 0; s < kRowStages; ++s) mbar_wait_warp(&wbar[s], (parity >> s) & 1u);
+    }
 }
 
 struct GemvPlan {
@@ -970,21 +984,24 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
     constexpr size_t smem_bytes = rows_smem<Q4, SF16>();
     const int64_t rowbytes = Q4 ? a.cols / 2 : a.cols;
     static std::mutex mu;
-    static std::map<std::tuple<int, int64_t, int64_t>, int> plans;
+    static std::map<std::tuple<int, int64_t, int64_t>, std::pair<int, int64_t>> plans;  // (C, grid)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return check_launch(name);
     int C = 1;
+    int64_t grid = 1;
     {
         std::lock_guard<std::mutex> lk(mu);
         const auto key = std::make_tuple(dev, a.rows, a.cols);
         auto it = plans.find(key);
         if (it != plans.end()) {
-            C = it->second;
+            C = it->second.first;
+            grid = it->second.second;
         } else {
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes)) != cudaSuccess)
                 return check_launch(name);
             const int64_t groups = (a.rows + kRowsCta - 1) / kRowsCta, nchunk = (rowbytes + 511) / 512;
-            int64_t c = resident_blocks((const void *)kern, kThreads, smem_bytes) / groups;
+            const int64_t slots = resident_blocks((const void *)kern, kThreads, smem_bytes);
+            int64_t c = slots / groups;
             if (c > nchunk / kWarps) c = nchunk / kWarps;
             C = int(c < 1 ? 1 : c > 8 ? 8 : c);
             while (C > 1) {  // all clusters co-resident
@@ -999,7 +1016,9 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
                 cudaGetLastError();
                 --C;
             }
-            plans[key] = C;
+            // one group per cluster (C > 1), or persistent CTAs, one resident wave, over the groups (C = 1)
+            grid = C > 1 ? groups * C : (groups < slots ? groups : (slots > 0 ? slots : 1));
+            plans[key] = std::make_pair(C, grid);
         }
     }
     CUtensorMap wmap, smap;
@@ -1008,7 +1027,7 @@ int launch_rows(const GemvArgs &a, cudaStream_t st, const char *name) {
     if (rc != VOX_CUDA_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
-    cfg.gridDim = dim3(unsigned((a.rows + kRowsCta - 1) / kRowsCta * C));
+    cfg.gridDim = dim3(unsigned(grid));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = st;

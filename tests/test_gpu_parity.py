@@ -220,6 +220,7 @@ def test_softmax_lengths(vox, port, n):
     s = port.normal((2, 21, n), 0.0, 3.0, sid=n)
     assert_close(host(vox.softmax_rows(dev(s), 0.5, 21, 5)), port.softmax_rows(s, 0.5, 21, 5))
     assert_close(host(vox.softmax_rows(dev(s), 0.5, 0, 0)), port.softmax_rows(s, 0.5, 0, 0))
+    assert_close(host(vox.softmax_rows(dev(s), -0.75, 21, 5)), port.softmax_rows(s, -0.75, 21, 5))  # unfolded scale
     xi = dev(s)
     vox.softmax_rows(xi, 0.5, 21, 5, out=xi)
     assert_close(host(xi), port.softmax_rows(s, 0.5, 21, 5))

@@ -353,7 +353,11 @@ __device__ __forceinline__ int64_t visible_len(int64_t r, int64_t n, int64_t q_l
     return v < n ? v : n;
 }
 
-template <int VPL>
+// FOLD (scale positive and finite): s x - max(s x) = s (x - max x), so the maximum is taken on the raw scores and the scale, log2 e
+// and the maximum fold into one multiply-add per pair ahead of the SFU's 2^y: fma(x, s log2e, -max(x) s log2e). The
+// argument differs from the CPU's (s x - max) log2 e by a rounding or two (relative change of the result ~1e-6 at the
+// scores' range), inside the f32 tolerance. Other scales take the multiply, subtract and scale steps.
+template <int VPL, bool FOLD = false>
 struct SoftmaxOp {
     static constexpr int kMinBlocks = 1;
     const float *x;
@@ -389,14 +393,14 @@ struct SoftmaxOp {
             if (128 * (k + 1) <= vis) {  // the whole block of 32 vectors is visible: no mask
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
-                    v[k][p] = mul2(s2, v[k][p]);
+                    if (!FOLD) v[k][p] = mul2(s2, v[k][p]);
                     mx = fmaxf(mx, fmaxf(v[k][p].x, v[k][p].y));
                 }
             } else if (32 * k < vvec) {  // the block holding the end of the visible prefix
                 const int base = (lane + 32 * k) * 4;
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
-                    float2 t = mul2(s2, v[k][p]);
+                    float2 t = FOLD ? v[k][p] : mul2(s2, v[k][p]);
                     t.x = base + 2 * p < vis ? t.x : -INFINITY;
                     t.y = base + 2 * p + 1 < vis ? t.y : -INFINITY;
                     v[k][p] = t;
@@ -406,14 +410,16 @@ struct SoftmaxOp {
         }
         mx = warp_max(mx);
         // exp(x - max) as 2^((x - max) * log2 e) on the SFU (exp of -inf is 0); float sum (kernels.cpp:728-729)
-        const float2 nm = bc2(-mx), l2e = bc2(1.4426950408889634f);
+        constexpr float kLog2e = 1.4426950408889634f;
+        const float sl = FOLD ? scale * kLog2e : kLog2e;
+        const float2 nm = bc2(-mx), l2e = bc2(kLog2e), sl2 = bc2(sl), off = bc2(-(mx * sl));
         float2 sum2 = bc2(0.f);
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             if (32 * k < vvec) {
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
-                    const float2 d = mul2(add2(v[k][p], nm), l2e);
+                    const float2 d = FOLD ? fma2(v[k][p], sl2, off) : mul2(add2(v[k][p], nm), l2e);
                     v[k][p] = make_float2(ex2_approx(d.x), ex2_approx(d.y));
                     sum2 = add2(sum2, v[k][p]);
                 }
@@ -655,11 +661,17 @@ int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float
     const int vpl = int((nvec + 31) / 32);
     const uint32_t stage = uint32_t(n * 4);
     const char *name = "vox_cuda_softmax_rows";
-    if (vpl <= 1) return launch_row_pipe<SoftmaxOp<1>, kStages>(SoftmaxOp<1>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
-    if (vpl <= 2) return launch_row_pipe<SoftmaxOp<2>, kStages>(SoftmaxOp<2>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
-    if (vpl <= 4) return launch_row_pipe<SoftmaxOp<4>, kStages>(SoftmaxOp<4>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
-    if (vpl <= 8) return launch_row_pipe<SoftmaxOp<8>, kStages>(SoftmaxOp<8>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
-    return launch_row_pipe<SoftmaxOp<16>, kStages>(SoftmaxOp<16>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    const bool fold = scale > 0.f && scale <= 3.4e38f;  // positive and finite
+    if (vpl <= 1) return fold ? launch_row_pipe<SoftmaxOp<1, true>, kStages>(SoftmaxOp<1, true>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name)
+                              : launch_row_pipe<SoftmaxOp<1>, kStages>(SoftmaxOp<1>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    if (vpl <= 2) return fold ? launch_row_pipe<SoftmaxOp<2, true>, kStages>(SoftmaxOp<2, true>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name)
+                              : launch_row_pipe<SoftmaxOp<2>, kStages>(SoftmaxOp<2>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    if (vpl <= 4) return fold ? launch_row_pipe<SoftmaxOp<4, true>, kStages>(SoftmaxOp<4, true>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name)
+                              : launch_row_pipe<SoftmaxOp<4>, kStages>(SoftmaxOp<4>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    if (vpl <= 8) return fold ? launch_row_pipe<SoftmaxOp<8, true>, kStages>(SoftmaxOp<8, true>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name)
+                              : launch_row_pipe<SoftmaxOp<8>, kStages>(SoftmaxOp<8>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
+    return fold ? launch_row_pipe<SoftmaxOp<16, true>, kStages>(SoftmaxOp<16, true>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name)
+                       : launch_row_pipe<SoftmaxOp<16>, kStages>(SoftmaxOp<16>{x, y, n, q_len, pos0, scale, qdiv}, rows, stage, st, name);
 }
 
 }  // namespace voxcuda

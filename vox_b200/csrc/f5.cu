@@ -339,40 +339,25 @@ __global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *d
     pdl_enter();
     const uint32_t lane = threadIdx.x & 31, r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= rows) return;
-    float4 x[VPL], dv[VPL];
+    float4 x[VPL];
     float4 *hr = reinterpret_cast<float4 *>(h + size_t(r) * D);
-    // every load of the row before the first store of h (which the compiler must otherwise assume may alias them), so
-    // the row's loads are in flight together instead of one 16-byte step at a time
-#pragma unroll
-    for (int k = 0; k < VPL; ++k) {
-        const uint32_t c = lane + 32 * k;
-        x[k] = dv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (4 * c < D) {
-            x[k] = hr[c];
-            if (delta) dv[k] = reinterpret_cast<const float4 *>(delta + size_t(r) * D)[c];
-        }
-    }
     float sum = 0.f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
         const uint32_t c = lane + 32 * k;
+        x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (4 * c < D) {
+            x[k] = hr[c];
             if (delta) {
+                float4 dv = reinterpret_cast<const float4 *>(delta + size_t(r) * D)[c];
                 const float4 db = reinterpret_cast<const float4 *>(dbias)[c];
-                const float4 d = make_float4(__fadd_rn(dv[k].x, db.x), __fadd_rn(dv[k].y, db.y), __fadd_rn(dv[k].z, db.z),
-                                             __fadd_rn(dv[k].w, db.w));
+                dv = make_float4(__fadd_rn(dv.x, db.x), __fadd_rn(dv.y, db.y), __fadd_rn(dv.z, db.z), __fadd_rn(dv.w, db.w));
                 const float4 g = reinterpret_cast<const float4 *>(gate)[c];
-                x[k] = make_float4(__fadd_rn(x[k].x, __fmul_rn(g.x, d.x)), __fadd_rn(x[k].y, __fmul_rn(g.y, d.y)),
-                                   __fadd_rn(x[k].z, __fmul_rn(g.z, d.z)), __fadd_rn(x[k].w, __fmul_rn(g.w, d.w)));
+                x[k] = make_float4(__fadd_rn(x[k].x, __fmul_rn(g.x, dv.x)), __fadd_rn(x[k].y, __fmul_rn(g.y, dv.y)),
+                                   __fadd_rn(x[k].z, __fmul_rn(g.z, dv.z)), __fadd_rn(x[k].w, __fmul_rn(g.w, dv.w)));
+                hr[c] = x[k];
             }
             sum += (x[k].x + x[k].y) + (x[k].z + x[k].w);
-        }
-    }
-    if (delta) {
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const uint32_t c = lane + 32 * k;
-            if (4 * c < D) hr[c] = x[k];
         }
     }
 #pragma unroll

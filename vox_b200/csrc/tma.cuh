@@ -22,11 +22,9 @@ namespace voxcuda {
 // exposes it through take_device_error() and vox_cuda_device_error() gathers them all.
 static __device__ unsigned int g_device_error = 0;
 constexpr unsigned int kDevErrTimeout = 1u;
-// A wait gives up after this much time on the GPU's global timer (ns).
+// A wait gives up after this much time on the GPU's global timer (ns), read every 32 polls (each try_wait may also
+// suspend the warp for a hardware-chosen time).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-// Each try_wait may suspend the thread until the phase completes, for at most this long (ns): a waiting warp then
-// issues a few polls per copy instead of spinning.
-constexpr uint32_t kSuspendHintNs = 100000u;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
@@ -47,10 +45,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "r"(smem_addr(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -60,9 +58,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (;;) {
+    for (uint32_t i = 1;; ++i) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-        if (__any_sync(0xffffffffu, globaltimer_ns() - t0 > kWaitLimitNs)) break;
+        if ((i & 31u) == 0 && __any_sync(0xffffffffu, globaltimer_ns() - t0 > kWaitLimitNs)) break;
     }
     if ((threadIdx.x & 31) == 0) atomicOr(&g_device_error, kDevErrTimeout);
     return false;

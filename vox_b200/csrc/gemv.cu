@@ -620,6 +620,7 @@ __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : 2) gemv_rows_k
     uint32_t parity = 0;
     bool ok = true;
     const bool clustered = C > 1;
+    float2 xv[M][EPL / 2];  // this lane's activation values of its chunk (kept across groups when the warp has one chunk)
     for (int gi = 0; gi < ngm; ++gi) {
         const int row0 = (g0 + gi * gstep) * kRowsCta;
         float tot[kRowCopies][M];
@@ -632,15 +633,16 @@ __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : 2) gemv_rows_k
             const int64_t cb = int64_t(c0 + k * cstep) * 512 + lane * 16;  // this lane's 16 bytes of every row
             const bool valid = cb < rowbytes;
             const int64_t e0 = Q4 ? 2 * cb : cb;  // its first weight's column
-            float2 xv[M][EPL / 2];
+            if (gi == 0 || nmine > 1) {
 #pragma unroll
-            for (int t = 0; t < M; ++t)
+                for (int t = 0; t < M; ++t)
 #pragma unroll
-                for (int q = 0; q < EPL / 4; ++q) {
-                    const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + e0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    xv[t][2 * q] = make_float2(v.x, v.y);
-                    xv[t][2 * q + 1] = make_float2(v.z, v.w);
-                }
+                    for (int q = 0; q < EPL / 4; ++q) {
+                        const float4 v = valid ? __ldg(reinterpret_cast<const float4 *>(a.x + int64_t(t) * a.cols + e0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        xv[t][2 * q] = make_float2(v.x, v.y);
+                        xv[t][2 * q + 1] = make_float2(v.z, v.w);
+                    }
+            }
             const ST *scs = reinterpret_cast<const ST *>(sring + (ck & 1) * SB) + (Q4 ? lane : lane >> 1);  // [kRowsCta rows][BPC blocks]
 #pragma unroll 1
             for (int b = 0; b < kRowCopies; ++b) {

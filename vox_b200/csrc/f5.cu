@@ -8,8 +8,8 @@
 // below; the projections and the two attention products are cuBLAS GEMMs (f32, or on the tensor cores with TF32 or
 // bf16 inputs and f32 accumulation). In the f32 and TF32 modes attention materialises the score matrix of one
 // sequence at a time ([heads][frames][frames] f32) and normalises it in place with the row softmax; in the bf16 mode
-// (dim_head 64) one fused kernel computes it from the bf16 q|k|v projection without writing the scores (mma.sync
-// bf16, online softmax).
+// (dim_head 64) one fused kernel computes it from the bf16 q|k|v projection without writing the scores (tcgen05
+// bf16 products accumulated in tensor memory, online softmax).
 //
 // The plan records the whole step once eagerly (kernel selection, first-use attributes), then again under stream
 // capture; a run is one cudaGraphLaunch. All buffers are the plan's, so the graph's pointers never change.
@@ -23,6 +23,8 @@
 
 #include "common.cuh"
 #include "sfu.cuh"
+#include "tma.cuh"
+#include "rows.cuh"
 
 namespace voxcuda {
 namespace {
@@ -159,162 +161,218 @@ __global__ void __launch_bounds__(256) f5_bias_gelu_kernel(uint4 *ff, const floa
     }
 }
 
-constexpr int kFaRows = 64;   // query rows per CTA (16 per warp)
-constexpr int kFaKeys = 64;   // keys per staged K/V tile
 constexpr int kFaHd = 64;     // head dimension of the fused kernel
-constexpr int kFaThreads = 128;
 
-// A tile of 64 rows x 64 bf16 (128-byte rows) in shared memory: the 16-byte chunk c of row r sits at chunk c ^ (r % 8),
-// so the 8 row addresses of an ldmatrix phase fall in 8 different bank groups.
+// A tile of rows of 64 bf16 (128-byte rows) in shared memory: the 16-byte chunk c of row r sits at chunk c ^ (r % 8)
+// (the 128-byte swizzle of the tensor cores' shared-memory operands; 8 consecutive rows' chunk c in 8 bank groups).
 __device__ __forceinline__ uint32_t fa_off(int r, int c) { return uint32_t(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // cp.async of one 16-byte chunk; src_bytes 0 fills the chunk with zeros (rows past the sequence end).
 __device__ __forceinline__ void cp16(uint32_t dst, const void *src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
-// Stages rows [row0, row0 + 64) of a head's 64 columns (global row stride `inner` bf16) into a swizzled tile; rows at or
-// past `n` are zero-filled. 512 chunks, 4 per thread.
-__device__ __forceinline__ void fa_stage(uint32_t tile, const __nv_bfloat16 *g, int row0, int n, int inner) {
+// ------------------------------------------------------------------ fused attention on the 5th-generation tensor cores
+
+// softmax(q k^T * scale) v for one sequence and head, 128 query rows per CTA, on tcgen05: S = Q K^T (M 128, N 64 keys, K 64) and each tile's
+// P V (M 128, N 64, K 64 keys) are accumulated in tensor memory (TMEM lane = query row, f32), their operands read
+// from shared memory through matrix descriptors. Q [128 rows][64 bf16], K and V tiles [64 keys][64 bf16] and P
+// [128 rows][64 keys] sit in the 128-byte swizzle (fa_off: 16-byte chunk c of row r at chunk c ^ (r % 8)), which is
+// the canonical K-major SW128 layout for Q, K, P and the MN-major SW128 layout for V (the head dimension is V's N).
+// Thread t of the 4 warps owns query row t: it reads its S row from TMEM (two passes of 32 columns: the maximum, then
+// 2^(s scale log2e - max), rounded to bf16 into P), and after each tile's P V adds that tile's O row to its f32
+// accumulator rescaled by the online-softmax factor. One thread issues the MMAs; their completion arrives on
+// mbarriers (tcgen05.commit); every wait is bounded. K and V of the next tile load by cp.async during this tile.
+// 65 KB of shared memory and 128 TMEM columns a CTA: three CTAs share an SM, so one's softmax overlaps another's MMAs.
+constexpr int kTcRows = 128;
+constexpr int kTcKeys = 64;
+constexpr int kTcThreads = 128;
+constexpr uint32_t kTcQ = 128 * 128;     // Q and P tiles, [128][64] bf16, bytes
+constexpr uint32_t kTcKV = 64 * 128;     // K and V tiles, [64][64] bf16
+constexpr uint32_t kTcCols = 128;        // TMEM columns: S 0..63, P V 64..127
+constexpr size_t kTcSmem = 2 * size_t(kTcQ) + 4 * size_t(kTcKV) + 1024 + 128;  // Q, P, K[2], V[2]; alignment; barriers
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout 2), descriptor version 1: start, leading and stride byte
+// offsets in 16-byte units.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) | (uint64_t((sbo >> 4) & 0x3FFFu) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptors (kind::f16): f32 accumulator (bit 4), bf16 A (bit 7) and B (bit 10), B major-ness (bit 16),
+// N / 8 (bits 17..22), M / 16 (bits 24..28).
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Stages rows [row0, row0 + ROWS) of a head's 64 columns (global row stride ld bf16) into a swizzled tile; rows at
+// or past n are zero-filled. 8 chunks a row, ROWS / 16 per thread.
+template <int ROWS>
+__device__ __forceinline__ void tc_stage(uint32_t tile, const __nv_bfloat16 *g, int row0, int n, int ld) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int idx = threadIdx.x + u * kFaThreads, r = idx >> 3, c = idx & 7;
+    for (int u = 0; u < ROWS / 16; ++u) {
+        const int idx = threadIdx.x + u * kTcThreads, r = idx >> 3, c = idx & 7;
         const int gr = row0 + r;
-        const __nv_bfloat16 *src = g + size_t(gr < n ? gr : n - 1) * inner + c * 8;
-        cp16(tile + fa_off(r, c), src, gr < n ? 16u : 0u);
+        cp16(tile + fa_off(r, c), g + size_t(gr < n ? gr : n - 1) * ld + c * 8, gr < n ? 16u : 0u);
     }
 }
 
-// softmax(q k^T * scale) v for one sequence and head and 64 query rows, online over 64-key tiles (K and V double
-// buffered with cp.async): S and P in registers (P rounded to bf16 for the second product), f32 accumulation, the
-// row maximum and sum in the exp2 domain. q, k, v have row stride ld_in (bf16); at [rows][inner] (f32 or bf16)
-// receives the normalised rows. 4 CTAs per SM, so a 1024-frame, 16-head, 2-sequence step runs in one wave.
-template <bool BF16_OUT>
-__global__ void __launch_bounds__(kFaThreads, 4) f5_flash_kernel(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb, const __nv_bfloat16 *vb,
-                                                              void *at, int n, int ld_in, int inner, float scale_log2) {
-    pdl_enter();
-    __shared__ __align__(128) uint8_t sm[5 * kFaRows * 128];  // Q, K[2], V[2]
-    const uint32_t sQ = uint32_t(__cvta_generic_to_shared(sm)), sK = sQ + 8192, sV = sQ + 3 * 8192;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int q0 = blockIdx.x * kFaRows, head = blockIdx.y;
+__global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb,
+                                                                    const __nv_bfloat16 *vb, __nv_bfloat16 *at, int n, int ld_in,
+                                                                    int inner, float scale_log2) {
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sQ = smem_addr(smem), sP = sQ + kTcQ, sK = sQ + 2 * kTcQ, sV = sK + 2 * kTcKV;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + 2 * kTcQ + 4 * kTcKV);  // [0] S done, [1] P V done
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + 2 * kTcQ + 4 * kTcKV + 16);
+    const int warp = threadIdx.x >> 5, row = threadIdx.x;
+    const int q0 = blockIdx.x * kTcRows, head = blockIdx.y;
     const size_t seq = size_t(blockIdx.z) * size_t(n) * size_t(ld_in) + size_t(head) * kFaHd;
     const __nv_bfloat16 *Q = qb + seq, *K = kb + seq, *V = vb + seq;
-    const int ntiles = (n + kFaKeys - 1) / kFaKeys;
-    fa_stage(sQ, Q, q0, n, ld_in);
-    fa_stage(sK, K, 0, n, ld_in);
-    fa_stage(sV, V, 0, n, ld_in);
+    const int ntiles = (n + kTcKeys - 1) / kTcKeys;
+    pdl_enter();  // the previous grid (and the tensor memory it held) is complete
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)), "r"(kTcCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_stage<kTcRows>(sQ, Q, q0, n, ld_in);
+    tc_stage<kTcKeys>(sK, K, 0, n, ld_in);
+    tc_stage<kTcKeys>(sV, V, 0, n, ld_in);
     asm volatile("cp.async.commit_group;" ::: "memory");
-    float o[8][4];
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);  // this warp's 32 lanes
+    float o[64];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-    uint32_t qa[4][4];
-    for (int kt = 0; kt < ntiles; ++kt) {
+    for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    float mrow = -INFINITY, lrow = 0.f;
+    bool ok = true;
+    for (int kt = 0; kt < ntiles; ++kt) {  // every thread runs every iteration's barriers, ok or not
         const int buf = kt & 1;
-        if (kt + 1 < ntiles) {
-            fa_stage(sK + (buf ^ 1) * 8192, K, (kt + 1) * kFaKeys, n, ld_in);
-            fa_stage(sV + (buf ^ 1) * 8192, V, (kt + 1) * kFaKeys, n, ld_in);
+        const uint32_t tK = sK + buf * kTcKV, tV = sV + buf * kTcKV;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // this thread's tile writes, visible to the MMA
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0 && ok) {
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < 4; ++k)  // 16 of the 64 head dimensions a step: 32 bytes along the swizzled rows
+                umma_bf16(tmem, umma_desc(sQ + 32 * k, 16, 1024), umma_desc(tK + 32 * k, 16, 1024), kIdescS, k > 0);
+            umma_commit(&bar[0]);
+        }
+        if (kt + 1 < ntiles) {  // the other buffers' last readers (tile kt - 1) have completed
+            tc_stage<kTcKeys>(sK + (buf ^ 1) * kTcKV, K, (kt + 1) * kTcKeys, n, ld_in);
+            tc_stage<kTcKeys>(sV + (buf ^ 1) * kTcKV, V, (kt + 1) * kTcKeys, n, ld_in);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        ok = ok && mbar_wait_warp(&bar[0], uint32_t(kt & 1));  // a wait that gives up sets the device error flag
+        tc_fence_after();
+        if (!ok) {  // the MMA never completed: keep the barrier sequence, touch no tensor memory
+            __syncthreads();
+            continue;
+        }
+        const int key0 = kt * kTcKeys;
+        const bool full = key0 + kTcKeys <= n;  // else keys past the sequence end take no weight
+        // pass 1: the row maximum of this tile
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(trow + 32 * c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (full || key0 + 32 * c + i < n) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+        const float mnew = fmaxf(mrow, mx * scale_log2);
+        const float alpha = ex2_approx(mrow - mnew);
+        // pass 2: P = 2^(s scale log2e - max) in bf16 into P, and the row sum of the unrounded values
+        float sum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(trow + 32 * c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {  // 8 keys (one 16-byte chunk) a step
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = 8 * ch + 2 * e, key = key0 + 32 * c + i;
+                    const float p0 = (full || key < n) ? ex2_approx(fmaf(__uint_as_float(r[i]), scale_log2, -mnew)) : 0.f;
+                    const float p1 = (full || key + 1 < n) ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), scale_log2, -mnew)) : 0.f;
+                    sum += p0 + p1;
+                    w[e] = pack_bf16(p0, p1);
+                }
+                const uint32_t dst = sP + fa_off(row, 4 * c + ch);  // key chunk 0..7 of the row
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]) : "memory");
+            }
+        }
+        lrow = lrow * alpha + sum;
+        mrow = mnew;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
+        tc_fence_before();
         __syncthreads();
-        if (kt == 0) {  // this warp's 16 query rows as A fragments, four 16-column steps
+        if (threadIdx.x == 0 && ok) {
+            tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                ldsm_x4(sQ + fa_off(warp * 16 + (lane & 15), 2 * kk + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+            for (int k = 0; k < 4; ++k)  // 16 keys a step: P along its swizzled rows, V by 16 rows (2048 bytes)
+                umma_bf16(tmem + 64, umma_desc(sP + 32 * k, 16, 1024), umma_desc(tV + 2048 * k, 16384, 1024), kIdescO, k > 0);
+            umma_commit(&bar[1]);
         }
-        const uint32_t tK = sK + buf * 8192, tV = sV + buf * 8192;
-        float s[8][4];
+        ok = ok && mbar_wait_warp(&bar[1], uint32_t(kt & 1));
+        tc_fence_after();
+        if (ok) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+            for (int c = 0; c < 2; ++c) {
+                uint32_t r[32];
+                tmem_ld32(trow + 64 + 32 * c, r);
+                tmem_wait_ld();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {  // keys 16 np .. 16 np + 15
-                uint32_t b0, b1, b2, b3;
-                const int mi = lane >> 3;
-                ldsm_x4(tK + fa_off(16 * np + (mi >> 1) * 8 + (lane & 7), 2 * kk + (mi & 1)), b0, b1, b2, b3);
-                mma16816(s[2 * np], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
-                mma16816(s[2 * np + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
-            }
-        const int key0 = kt * kFaKeys;
-        if (key0 + kFaKeys > n) {  // keys past the sequence end take no weight
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (key0 + 8 * j + 2 * t + (c & 1) >= n) s[j][c] = -INFINITY;
-        }
-        // online softmax over this tile: rows g (c = 0, 1) and g + 8 (c = 2, 3) of the warp's 16
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fmaxf(s[j][2 * rr], s[j][2 * rr + 1]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float mnew = fmaxf(mrow[rr], mx * scale_log2);
-            const float alpha = ex2_approx(mrow[rr] - mnew);
-            float sum = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                s[j][2 * rr] = ex2_approx(fmaf(s[j][2 * rr], scale_log2, -mnew));
-                s[j][2 * rr + 1] = ex2_approx(fmaf(s[j][2 * rr + 1], scale_log2, -mnew));
-                sum += s[j][2 * rr] + s[j][2 * rr + 1];
-            }
-            lrow[rr] = lrow[rr] * alpha + sum;
-            mrow[rr] = mnew;
-#pragma unroll
-            for (int d = 0; d < 8; ++d) {
-                o[d][2 * rr] *= alpha;
-                o[d][2 * rr + 1] *= alpha;
+                for (int i = 0; i < 32; ++i) o[32 * c + i] = fmaf(o[32 * c + i], alpha, __uint_as_float(r[i]));
             }
         }
-        // O += P V: P's accumulator layout is the A layout of the next product (keys 16 kk2 .. 16 kk2 + 15)
-#pragma unroll
-        for (int kk2 = 0; kk2 < 4; ++kk2) {
-            const uint32_t a0 = pack_bf16(s[2 * kk2][0], s[2 * kk2][1]), a1 = pack_bf16(s[2 * kk2][2], s[2 * kk2][3]);
-            const uint32_t a2 = pack_bf16(s[2 * kk2 + 1][0], s[2 * kk2 + 1][1]), a3 = pack_bf16(s[2 * kk2 + 1][2], s[2 * kk2 + 1][3]);
-#pragma unroll
-            for (int dp = 0; dp < 4; ++dp) {  // dims 16 dp .. 16 dp + 15
-                uint32_t b0, b1, b2, b3;
-                const int mi = lane >> 3;
-                ldsm_x4_t(tV + fa_off(16 * kk2 + (mi & 1) * 8 + (lane & 7), 2 * dp + (mi >> 1)), b0, b1, b2, b3);
-                mma16816(o[2 * dp], a0, a1, a2, a3, b0, b1);
-                mma16816(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
-            }
-        }
-        __syncthreads();  // the buffer is refilled by the next iteration's copies
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (ok && q0 + row < n) {
+        const float inv = 1.0f / lrow;
+        uint4 *dst = reinterpret_cast<uint4 *>(at + (size_t(blockIdx.z) * size_t(n) + size_t(q0 + row)) * inner + size_t(head) * kFaHd);
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-        float l = lrow[rr];
-        l += __shfl_xor_sync(0xffffffffu, l, 1);
-        l += __shfl_xor_sync(0xffffffffu, l, 2);
-        const float inv = 1.0f / l;
-        const int row = q0 + warp * 16 + g + 8 * rr;
-        if (row < n) {
-            const size_t e = size_t(blockIdx.z) * size_t(n) * size_t(inner) + size_t(row) * inner + size_t(head) * kFaHd + 2 * t;
-#pragma unroll
-            for (int d = 0; d < 8; ++d) {
-                if (BF16_OUT)
-                    reinterpret_cast<uint32_t *>(at)[(e + 8 * d) / 2] = pack_bf16(o[d][2 * rr] * inv, o[d][2 * rr + 1] * inv);
-                else
-                    *reinterpret_cast<float2 *>(static_cast<float *>(at) + e + 8 * d) = make_float2(o[d][2 * rr] * inv, o[d][2 * rr + 1] * inv);
-            }
-        }
+        for (int c = 0; c < 8; ++c)
+            dst[c] = make_uint4(pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv), pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                                pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv), pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
     }
 }
 
@@ -607,7 +665,9 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
     F5_TRY(vox_cuda_add(p.fin, p.b_fin, p.fin, 2 * D, VOX_CUDA_F32, st));
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
     const uint32_t qkv_octs = uint32_t(R * 3 * IN / 8), ff_octs = uint32_t(R * FF / 8);
-    const dim3 fg(unsigned((d.frames + kFaRows - 1) / kFaRows), unsigned(d.heads), unsigned(d.batch));
+    const dim3 fgt(unsigned((d.frames + kTcRows - 1) / kTcRows), unsigned(d.heads), unsigned(d.batch));
+    if (cudaFuncSetAttribute(f5_flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem)) != cudaSuccess)
+        return check_launch("vox_cuda_f5 attention (shared memory)");
     const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
     F5_TRY(resmod(p, nullptr, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
     for (int64_t l = 0; l < L; ++l) {
@@ -617,8 +677,8 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
                  (const float *)(p.b_qkv + size_t(l) * 3 * IN), (const float2 *)p.cs, qkv_octs, uint32_t(d.frames),
                  uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
         F5_TRY(check_launch("vox_cuda_f5 bias/rope (bf16)"));
-        launch_k(f5_flash_kernel<true>, fg, kFaThreads, 0, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
-                 (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (void *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
+        launch_k(f5_flash_tc_kernel, fgt, kTcThreads, kTcSmem, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
+                 (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (__nv_bfloat16 *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
         F5_TRY(check_launch("vox_cuda_f5 attention"));
         F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
         F5_TRY(resmod(p, p.o, p.b_o + l * D, A + 2 * D, A + 4 * D, A + 3 * D, st));
@@ -808,6 +868,9 @@ int build(F5Plan &p, cudaStream_t user) {
 }
 
 }  // namespace
+
+int f5_take_device_error(unsigned int *flags) { return take_device_error(flags); }
+
 }  // namespace voxcuda
 
 using namespace voxcuda;

@@ -52,5 +52,7 @@ int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float
 
 // Reads and clears the quantized GEMV's device error flag into *flags (gemv.cu); VOX_CUDA_OK or VOX_CUDA_ERR_DEVICE.
 int gemv_take_device_error(unsigned int *flags);
+// The same for the F5 step's attention kernel (f5.cu).
+int f5_take_device_error(unsigned int *flags);
 
 }  // namespace voxcuda

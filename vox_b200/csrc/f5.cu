@@ -272,79 +272,87 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
     for (int i = 0; i < 64; ++i) o[i] = 0.f;
     float mrow = -INFINITY, lrow = 0.f;
     bool ok = true;
-    for (int kt = 0; kt < ntiles; ++kt) {  // every thread runs every iteration's barriers, ok or not
-        const int buf = kt & 1;
-        const uint32_t tK = sK + buf * kTcKV, tV = sV + buf * kTcKV;
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // this thread's tile writes, visible to the MMA
-        tc_fence_before();
-        __syncthreads();
-        if (threadIdx.x == 0 && ok) {
-            tc_fence_after();
+    // tile 0's K and V, then its S product; each iteration below issues tile kt's P V together with tile kt + 1's S
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // this thread's tile writes, visible to the MMA
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        tc_fence_after();
 #pragma unroll
-            for (int k = 0; k < 4; ++k)  // 16 of the 64 head dimensions a step: 32 bytes along the swizzled rows
-                umma_bf16(tmem, umma_desc(sQ + 32 * k, 16, 1024), umma_desc(tK + 32 * k, 16, 1024), kIdescS, k > 0);
-            umma_commit(&bar[0]);
-        }
-        if (kt + 1 < ntiles) {  // the other buffers' last readers (tile kt - 1) have completed
+        for (int k = 0; k < 4; ++k)  // 16 of the 64 head dimensions a step: 32 bytes along the swizzled rows
+            umma_bf16(tmem, umma_desc(sQ + 32 * k, 16, 1024), umma_desc(sK + 32 * k, 16, 1024), kIdescS, k > 0);
+        umma_commit(&bar[0]);
+    }
+    for (int kt = 0; kt < ntiles; ++kt) {  // every thread runs every iteration's barrier, ok or not
+        const int buf = kt & 1;
+        if (kt + 1 < ntiles) {  // the other buffers' last readers (tile kt - 1's products) have completed
             tc_stage<kTcKeys>(sK + (buf ^ 1) * kTcKV, K, (kt + 1) * kTcKeys, n, ld_in);
             tc_stage<kTcKeys>(sV + (buf ^ 1) * kTcKV, V, (kt + 1) * kTcKeys, n, ld_in);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
         ok = ok && mbar_wait_warp(&bar[0], uint32_t(kt & 1));  // a wait that gives up sets the device error flag
         tc_fence_after();
-        if (!ok) {  // the MMA never completed: keep the barrier sequence, touch no tensor memory
-            __syncthreads();
-            continue;
-        }
-        const int key0 = kt * kTcKeys;
-        const bool full = key0 + kTcKeys <= n;  // else keys past the sequence end take no weight
-        // pass 1: the row maximum of this tile
-        float mx = -INFINITY;
+        float alpha = 1.f;
+        if (ok) {
+            const int key0 = kt * kTcKeys;
+            const bool full = key0 + kTcKeys <= n;  // else keys past the sequence end take no weight
+            // pass 1: the row maximum of this tile
+            float mx = -INFINITY;
 #pragma unroll 1
-        for (int c = 0; c < kTcKeys / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(trow + 32 * c, r);
-            tmem_wait_ld();
+            for (int c = 0; c < kTcKeys / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(trow + 32 * c, r);
+                tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (full || key0 + 32 * c + i < n) mx = fmaxf(mx, __uint_as_float(r[i]));
-        }
-        const float mnew = fmaxf(mrow, mx * scale_log2);
-        const float alpha = ex2_approx(mrow - mnew);
-        // pass 2: P = 2^(s scale log2e - max) in bf16 into P, and the row sum of the unrounded values
-        float sum = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < kTcKeys / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(trow + 32 * c, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {  // 8 keys (one 16-byte chunk) a step
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = 8 * ch + 2 * e, key = key0 + 32 * c + i;
-                    const float p0 = (full || key < n) ? ex2_approx(fmaf(__uint_as_float(r[i]), scale_log2, -mnew)) : 0.f;
-                    const float p1 = (full || key + 1 < n) ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), scale_log2, -mnew)) : 0.f;
-                    sum += p0 + p1;
-                    w[e] = pack_bf16(p0, p1);
-                }
-                const uint32_t dst = sP + fa_off(row, 4 * c + ch);  // key chunk 0..7 of the row
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]) : "memory");
+                for (int i = 0; i < 32; ++i)
+                    if (full || key0 + 32 * c + i < n) mx = fmaxf(mx, __uint_as_float(r[i]));
             }
+            const float mnew = fmaxf(mrow, mx * scale_log2);
+            alpha = ex2_approx(mrow - mnew);
+            // pass 2: P = 2^(s scale log2e - max) in bf16 into P (tile kt - 1's P V has read it), and the row sum of
+            // the unrounded values
+            float sum = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < kTcKeys / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(trow + 32 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {  // 8 keys (one 16-byte chunk) a step
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int i = 8 * ch + 2 * e, key = key0 + 32 * c + i;
+                        const float p0 = (full || key < n) ? ex2_approx(fmaf(__uint_as_float(r[i]), scale_log2, -mnew)) : 0.f;
+                        const float p1 = (full || key + 1 < n) ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), scale_log2, -mnew)) : 0.f;
+                        sum += p0 + p1;
+                        w[e] = pack_bf16(p0, p1);
+                    }
+                    const uint32_t dst = sP + fa_off(row, 4 * c + ch);  // key chunk 0..7 of the row
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]) : "memory");
+                }
+            }
+            lrow = lrow * alpha + sum;
+            mrow = mnew;
         }
-        lrow = lrow * alpha + sum;
-        mrow = mnew;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
+        asm volatile("cp.async.wait_group 0;" ::: "memory");          // tile kt + 1's K and V
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P and the tile, visible to the MMA
         tc_fence_before();
         __syncthreads();
         if (threadIdx.x == 0 && ok) {
             tc_fence_after();
+            const uint32_t tV = sV + buf * kTcKV, tK1 = sK + (buf ^ 1) * kTcKV;
 #pragma unroll
             for (int k = 0; k < 4; ++k)  // 16 keys a step: P along its swizzled rows, V by 16 rows (2048 bytes)
                 umma_bf16(tmem + 64, umma_desc(sP + 32 * k, 16, 1024), umma_desc(tV + 2048 * k, 16384, 1024), kIdescO, k > 0);
             umma_commit(&bar[1]);
+            if (kt + 1 < ntiles) {  // the next tile's S: every thread has read this tile's S before the barrier
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    umma_bf16(tmem, umma_desc(sQ + 32 * k, 16, 1024), umma_desc(tK1 + 32 * k, 16, 1024), kIdescS, k > 0);
+                umma_commit(&bar[0]);
+            }
         }
         ok = ok && mbar_wait_warp(&bar[1], uint32_t(kt & 1));
         tc_fence_after();

@@ -304,9 +304,14 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
                 uint32_t r[32];
                 tmem_ld32(trow + 32 * c, r);
                 tmem_wait_ld();
+                if (full) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (full || key0 + 32 * c + i < n) mx = fmaxf(mx, __uint_as_float(r[i]));
+                    for (int i = 0; i < 32; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (key0 + 32 * c + i < n) mx = fmaxf(mx, __uint_as_float(r[i]));
+                }
             }
             const float mnew = fmaxf(mrow, mx * scale_log2);
             alpha = ex2_approx(mrow - mnew);
@@ -318,14 +323,20 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
                 uint32_t r[32];
                 tmem_ld32(trow + 32 * c, r);
                 tmem_wait_ld();
+                if (!full) {  // keys past the sequence end: -inf scores, so their weights are 2^-inf = 0
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (key0 + 32 * c + i >= n) r[i] = __float_as_uint(-INFINITY);
+                }
+                const float2 sl2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mnew, -mnew);
 #pragma unroll
                 for (int ch = 0; ch < 4; ++ch) {  // 8 keys (one 16-byte chunk) a step
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const int i = 8 * ch + 2 * e, key = key0 + 32 * c + i;
-                        const float p0 = (full || key < n) ? ex2_approx(fmaf(__uint_as_float(r[i]), scale_log2, -mnew)) : 0.f;
-                        const float p1 = (full || key + 1 < n) ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), scale_log2, -mnew)) : 0.f;
+                        const int i = 8 * ch + 2 * e;
+                        const float2 a = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2, nm2);
+                        const float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
                         sum += p0 + p1;
                         w[e] = pack_bf16(p0, p1);
                     }
@@ -363,7 +374,12 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
                 tmem_ld32(trow + 64 + 32 * c, r);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[32 * c + i] = fmaf(o[32 * c + i], alpha, __uint_as_float(r[i]));
+                for (int i = 0; i < 32; i += 2) {
+                    const float2 v = fma2(make_float2(o[32 * c + i], o[32 * c + i + 1]), make_float2(alpha, alpha),
+                                          make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
+                    o[32 * c + i] = v.x;
+                    o[32 * c + i + 1] = v.y;
+                }
             }
         }
     }

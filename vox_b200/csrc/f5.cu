@@ -297,52 +297,38 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
         if (ok) {
             const int key0 = kt * kTcKeys;
             const bool full = key0 + kTcKeys <= n;  // else keys past the sequence end take no weight
-            // pass 1: the row maximum of this tile
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < kTcKeys / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(trow + 32 * c, r);
-                tmem_wait_ld();
-                if (full) {
+            // the tile's S row: both 32-column loads in flight, one wait
+            uint32_t r[kTcKeys];
+            tmem_ld32(trow, *reinterpret_cast<uint32_t(*)[32]>(r));
+            tmem_ld32(trow + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+            tmem_wait_ld();
+            if (!full) {  // keys past the sequence end: -inf scores, so their weights are 2^-inf = 0
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (key0 + 32 * c + i < n) mx = fmaxf(mx, __uint_as_float(r[i]));
-                }
+                for (int i = 0; i < kTcKeys; ++i)
+                    if (key0 + i >= n) r[i] = __float_as_uint(-INFINITY);
             }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < kTcKeys; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
             const float mnew = fmaxf(mrow, mx * scale_log2);
             alpha = ex2_approx(mrow - mnew);
-            // pass 2: P = 2^(s scale log2e - max) in bf16 into P (tile kt - 1's P V has read it), and the row sum of
-            // the unrounded values
+            // P = 2^(s scale log2e - max) in bf16 into P (tile kt - 1's P V has read it), and the row sum of the
+            // unrounded values
             float sum = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < kTcKeys / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(trow + 32 * c, r);
-                tmem_wait_ld();
-                if (!full) {  // keys past the sequence end: -inf scores, so their weights are 2^-inf = 0
+            const float2 sl2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mnew, -mnew);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (key0 + 32 * c + i >= n) r[i] = __float_as_uint(-INFINITY);
+            for (int ch = 0; ch < kTcKeys / 8; ++ch) {  // 8 keys (one 16-byte chunk) a step
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = 8 * ch + 2 * e;
+                    const float2 a = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2, nm2);
+                    const float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
+                    sum += p0 + p1;
+                    w[e] = pack_bf16(p0, p1);
                 }
-                const float2 sl2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mnew, -mnew);
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {  // 8 keys (one 16-byte chunk) a step
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i = 8 * ch + 2 * e;
-                        const float2 a = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2, nm2);
-                        const float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
-                        sum += p0 + p1;
-                        w[e] = pack_bf16(p0, p1);
-                    }
-                    const uint32_t dst = sP + fa_off(row, 4 * c + ch);  // key chunk 0..7 of the row
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]) : "memory");
-                }
+                const uint32_t dst = sP + fa_off(row, ch);  // key chunk 0..7 of the row
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]) : "memory");
             }
             lrow = lrow * alpha + sum;
             mrow = mnew;

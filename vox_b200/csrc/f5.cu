@@ -86,6 +86,44 @@ __global__ void __launch_bounds__(256) f5_im2col_kernel(const float *x, void *co
     }
 }
 
+// The bf16 im2col with 8 columns (16 bytes) an item: item e of row r = (sq groups + g) T + t is tap k = j / (cig / 8),
+// column block q = j % (cig / 8) (j = e % (K cig / 8)), read as two float4 of x[sq][t + k - K/2][g cig + 8 q ..] (zero
+// past the sequence) and written as one uint4. The divisions by the launch's invariants use FastDiv; kIm2colUnroll
+// items a thread and pass are loaded before any is stored.
+constexpr int kIm2colUnroll = 4;
+__global__ void __launch_bounds__(256) f5_im2col8_kernel(const float *x, uint4 *col, uint32_t items, uint32_t T, uint32_t cin,
+                                                         uint32_t cig, uint32_t K, FastDiv per_row, FastDiv per_tap, FastDiv tdiv,
+                                                         FastDiv gdiv) {
+    pdl_enter();
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t e0 = blockIdx.x * blockDim.x + threadIdx.x; e0 < items; e0 += kIm2colUnroll * stride) {
+        float4 a[kIm2colUnroll], b[kIm2colUnroll];
+#pragma unroll
+        for (int u = 0; u < kIm2colUnroll; ++u) {
+            const uint32_t e = e0 + u * stride;
+            a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < items) {
+                const uint32_t row = per_row.div(e), j = e - row * per_row.d;
+                const uint32_t k = per_tap.div(j), q = j - k * per_tap.d;
+                const uint32_t sg = tdiv.div(row), t = row - sg * T;
+                const uint32_t sq = gdiv.div(sg), g = sg - sq * gdiv.d;
+                const int tt = int(t) + int(k) - int(K / 2);
+                if (tt >= 0 && tt < int(T)) {
+                    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t(sq) * T + uint32_t(tt)) * cin + g * cig + 8 * q);
+                    a[u] = src[0];
+                    b[u] = src[1];
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kIm2colUnroll; ++u) {
+            const uint32_t e = e0 + u * stride;
+            if (e < items)
+                col[e] = make_uint4(pack_bf16(a[u].x, a[u].y), pack_bf16(a[u].z, a[u].w), pack_bf16(b[u].x, b[u].y), pack_bf16(b[u].z, b[u].w));
+        }
+    }
+}
+
 // mish(x) = x tanh(softplus(x)), softplus = x past 20 (f5.cpp:97-100), with the accurate CUDA functions.
 __device__ __forceinline__ float mish_f(float x) {
     const float sp = x > 20.f ? x : log1pf(expf(x));
@@ -555,7 +593,11 @@ int conv_pos(F5Plan &p, const float *src, const void *wr, float *dst, cudaStream
     const uint32_t T = uint32_t(d.frames), D = uint32_t(d.dim), cig = D / kPosGroups, J = kPosK * cig;
     const uint32_t all = uint32_t(d.batch) * kPosGroups * T * J;
     const uint32_t G = uint32_t(kPosGroups), KK = uint32_t(kPosK);
-    if (cig % 4 == 0) {
+    if (p.bf16 && cig % 8 == 0) {
+        const uint32_t items = all / 8;
+        launch_k(f5_im2col8_kernel, grid_for((items + kIm2colUnroll - 1) / kIm2colUnroll, 256, 4), 256, 0, st, src, (uint4 *)p.col, items,
+                 T, D, cig, KK, FastDiv(J / 8), FastDiv(cig / 8), FastDiv(T), FastDiv(G));
+    } else if (cig % 4 == 0) {
         if (p.bf16) launch_k(f5_im2col_kernel<4, true>, grid_for(all / 4, 256, 4), 256, 0, st, src, (void *)p.col, all / 4, T, D, G, KK);
         else launch_k(f5_im2col_kernel<4, false>, grid_for(all / 4, 256, 4), 256, 0, st, src, (void *)p.col, all / 4, T, D, G, KK);
     } else {

@@ -438,21 +438,24 @@ __global__ void __launch_bounds__(256) f5_to_bf16_kernel(const float2 *src, uint
 // One warp per row of h [rows][D]: if delta, h += gate * (delta + dbias) (the projection's bias added first, as
 // matmul does; product, then sum, each rounded: gated_add of f5.cpp:670-676); then nrm = LayerNorm(h) * (1 + scale) + shift (no affine, eps; mean and variance two-pass in f32 on
 // the row in registers) rounded to bf16 for the next projection. Lane l holds columns 4 (l + 32 k), k < VPL.
-template <int VPL>
+// WPR warps share a row (VPL float4 a lane); their partial sums meet in shared memory across a CTA barrier.
+template <int VPL, int WPR>
 __global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *delta, const float *dbias, const float *gate,
                                                         const float *scale, const float *shift, uint2 *nrm, uint32_t rows, uint32_t D,
                                                         float eps) {
     pdl_enter();
-    const uint32_t lane = threadIdx.x & 31, r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (r >= rows) return;
+    __shared__ float part[8][2];  // [warp][sum, squares]
+    const uint32_t warp = threadIdx.x >> 5, r = (blockIdx.x * 8 + warp) / WPR, lane = (warp % WPR) * 32 + (threadIdx.x & 31);
+    const bool live = r < rows;  // (no early exit: the row's warps meet at CTA barriers)
+    if (WPR == 1 && !live) return;
     float4 x[VPL];
     float4 *hr = reinterpret_cast<float4 *>(h + size_t(r) * D);
     float sum = 0.f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
-        const uint32_t c = lane + 32 * k;
+        const uint32_t c = lane + 32 * WPR * k;
         x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (4 * c < D) {
+        if (live && 4 * c < D) {
             x[k] = hr[c];
             if (delta) {
                 float4 dv = reinterpret_cast<const float4 *>(delta + size_t(r) * D)[c];
@@ -468,21 +471,35 @@ __global__ void __launch_bounds__(256) f5_resmod_kernel(float *h, const float *d
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (WPR > 1) {
+        if ((threadIdx.x & 31) == 0) part[warp][0] = sum;
+        __syncthreads();
+        sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPR; ++w) sum += part[warp - warp % WPR + w][0];
+    }
     const float mean = sum / float(D);
     float var = 0.f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k)
-        if (4 * (lane + 32 * k) < D) {
+        if (live && 4 * (lane + 32 * WPR * k) < D) {
             const float a = x[k].x - mean, b = x[k].y - mean, c = x[k].z - mean, e = x[k].w - mean;
             var += (a * a + b * b) + (c * c + e * e);
         }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    if (WPR > 1) {
+        if ((threadIdx.x & 31) == 0) part[warp][1] = var;
+        __syncthreads();
+        var = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPR; ++w) var += part[warp - warp % WPR + w][1];
+    }
     const float inv = rsqrtf(var / float(D) + eps);
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
-        const uint32_t c = lane + 32 * k;
-        if (4 * c < D) {
+        const uint32_t c = lane + 32 * WPR * k;
+        if (live && 4 * c < D) {
             const float4 sc = reinterpret_cast<const float4 *>(scale)[c], sh = reinterpret_cast<const float4 *>(shift)[c];
             const float y0 = fmaf((x[k].x - mean) * inv, 1.f + sc.x, sh.x), y1 = fmaf((x[k].y - mean) * inv, 1.f + sc.y, sh.y);
             const float y2 = fmaf((x[k].z - mean) * inv, 1.f + sc.z, sh.z), y3 = fmaf((x[k].w - mean) * inv, 1.f + sc.w, sh.w);
@@ -690,13 +707,19 @@ int record(F5Plan &p, cudaStream_t st) {
 int resmod(F5Plan &p, const float *delta, const float *dbias, const float *gate, const float *scale, const float *shift,
            cudaStream_t st) {
     const uint32_t R = uint32_t(p.R), D = uint32_t(p.d.dim), vpl = (D / 4 + 31) / 32;
-    const int g = int((R + 7) / 8);
     uint2 *nrm = reinterpret_cast<uint2 *>(p.nrm_b);
-    if (vpl <= 1) launch_k(f5_resmod_kernel<1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
-    else if (vpl <= 2) launch_k(f5_resmod_kernel<2>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
-    else if (vpl <= 4) launch_k(f5_resmod_kernel<4>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
-    else if (vpl <= 8) launch_k(f5_resmod_kernel<8>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
-    else launch_k(f5_resmod_kernel<16>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    if (vpl >= 8 && vpl % 2 == 0) {  // two warps a row: twice the rows' loads in flight for the step's 2 x 1024 rows
+        const int g = int((2 * R + 7) / 8);
+        if (vpl <= 8) launch_k(f5_resmod_kernel<4, 2>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+        else launch_k(f5_resmod_kernel<8, 2>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+        return check_launch("vox_cuda_f5 residual/modulate");
+    }
+    const int g = int((R + 7) / 8);
+    if (vpl <= 1) launch_k(f5_resmod_kernel<1, 1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 2) launch_k(f5_resmod_kernel<2, 1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 4) launch_k(f5_resmod_kernel<4, 1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else if (vpl <= 8) launch_k(f5_resmod_kernel<8, 1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    else launch_k(f5_resmod_kernel<16, 1>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
     return check_launch("vox_cuda_f5 residual/modulate");
 }
 

@@ -708,10 +708,10 @@ int resmod(F5Plan &p, const float *delta, const float *dbias, const float *gate,
            cudaStream_t st) {
     const uint32_t R = uint32_t(p.R), D = uint32_t(p.d.dim), vpl = (D / 4 + 31) / 32;
     uint2 *nrm = reinterpret_cast<uint2 *>(p.nrm_b);
-    if (vpl >= 8 && vpl % 2 == 0) {  // two warps a row: twice the rows' loads in flight for the step's 2 x 1024 rows
-        const int g = int((2 * R + 7) / 8);
-        if (vpl <= 8) launch_k(f5_resmod_kernel<4, 2>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
-        else launch_k(f5_resmod_kernel<8, 2>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+    if (vpl >= 8) {  // four warps a row: four times the rows' loads in flight for the step's 2 x 1024 rows
+        const int g = int((4 * R + 7) / 8);
+        if (vpl <= 8) launch_k(f5_resmod_kernel<2, 4>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
+        else launch_k(f5_resmod_kernel<4, 4>, g, 256, 0, st, p.h, delta, dbias, gate, scale, shift, nrm, R, D, 1e-6f);
         return check_launch("vox_cuda_f5 residual/modulate");
     }
     const int g = int((R + 7) / 8);

@@ -146,7 +146,7 @@ class Suite:
         # quantized decode GEMV (y = W x, m activation rows): Qwen3-8B MLP-up-shaped weights [12288][4096] with f16
         # scales, rotated over enough matrices that the weights stream from HBM (> 126 MB L2) on every call
         for qt in ("q8", "q4"):
-            names = [f"next_gemv_{qt}_m{mm}" for mm in (1, 8)]
+            names = [f"next_gemv_{qt}_m{mm}" for mm in (1, 4, 8)]
             if not any(want_next(nm) for nm in names):
                 continue
             GR, GC = 12288 * K, 4096
@@ -160,7 +160,7 @@ class Suite:
             gy = E(8, GR)
             fn = vox.gemv_q8 if qt == "q8" else vox.gemv_q4
             wbytes = GR * GC if qt == "q8" else GR * GC // 2
-            for mm in (1, 8):
+            for mm in (1, 4, 8):
                 nm = f"next_gemv_{qt}_m{mm}"
                 if not want_next(nm):
                     continue

@@ -53,7 +53,8 @@ def test_gemv_golden(vox, golden):
 
 @pytest.mark.parametrize("q4", [False, True])
 @pytest.mark.parametrize("rows,cols,m", [(4096, 4096, 1), (4096, 4096, 8), (1000, 1024, 3), (11008, 1024, 2),
-                                         (1024, 11008, 5), (130, 64, 16), (7, 32, 1), (12290, 4096, 1)])
+                                         (1024, 11008, 5), (130, 64, 16), (7, 32, 1), (12290, 4096, 1),
+                                         (12290, 4096, 4)])
 def test_gemv_shapes(vox, port, q4, rows, cols, m):
     q, s, x, b = _inputs(port, rows, cols, m, q4)
     for f16, bias in ((False, b), (True, None)):

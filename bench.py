@@ -376,99 +376,200 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------------------------------- CPU reference
 
-def cpu_suite_sample(scale: float = 1.0):
-    """Bounded sample of the suite on the host, through the reference's own CPU operators. Returns (lib, kind, cores, ops)
-    with ops = [(name, bytes, elements, fn)]; byte model identical to the GPU arm's."""
-    from oracle.oracle import port, ref
-
-    R = ref()
-    P = port()
-    kind = "reference" if R is not None else "port"
-    if R is not None:
-        cores = R.set_threads(0)
-    else:
-        cores = 1
-    L = R if R is not None else P
-    f32 = np.float32
-    ops = []
-    x1, w1 = P.normal((512, 1024), sid=1), P.normal((1024,), 1, 0.02, sid=2)
-    g1, u1 = P.normal((512, 3072), sid=3), P.normal((512, 3072), sid=4)
-    ops.append(("cfg1_rmsnorm_f32", 2 * 512 * 1024 * 4 + 1024 * 4, 512 * 1024, lambda: L.rmsnorm(x1, w1, 1e-6)))
-    ops.append(("cfg1_swiglu_f32", 3 * 512 * 3072 * 4, 512 * 3072, lambda: L.silu_mul(g1, u1)))
-    hs = max(1, int(16 * scale))
-    s2 = P.normal((hs, 1024, 1024), 0, 3, sid=5)
-    ops.append(("cfg2_softmax_causal_f32", hs * (1024 * 1025 // 2 * 4 + 1024 * 1024 * 4), hs * 1024 * 1024,
-                lambda: L.softmax_rows(s2, float(1 / np.sqrt(128.0)), 1024, 0)))
-    Bs = max(1, int(8 * scale))
-    x3 = P.normal((Bs, 2048, 1024), sid=6)
-    r3 = P.normal((Bs, 2048, 1024), sid=7)
-    sh3, sc3, g3 = (P.normal((Bs, 1024), 0, 0.1, sid=s) for s in (8, 9, 10))
-    ops.append(("cfg3_adaln_bf16", Bs * (3 * 2048 * 1024 * 2 + 3 * 1024 * 2), Bs * 2048 * 1024,
-                lambda: L.adaln(x3, sh3, sc3, g3, r3)))
-    q8 = P.fill_i8((4096, 4096), -128, 127, sid=11)
-    q4 = P.fill_u8((4096, 2048), sid=12)
-    s4 = P.f16_to_f32(P.uniform_arr((4096, 128), 0.001, 0.05, sid=13).astype(np.float16).view(np.uint16))
-    if R is not None:
-        ops.append(("cfg4_dequant_q8_bf16", 4096 * 4096 * 3 + 4096 * 128 * 2, 4096 * 4096, lambda: P.bf16_round(R.mat_rows(q8, s4))))
-        ops.append(("cfg4_dequant_q4_bf16", 4096 * 2048 + 4096 * 4096 * 2 + 4096 * 128 * 2, 4096 * 4096,
-                    lambda: P.bf16_round(R.mat_rows(q4, s4, q4=True))))
-    else:
-        ops.append(("cfg4_dequant_q8_bf16", 4096 * 4096 * 3 + 4096 * 128 * 2, 4096 * 4096, lambda: P.bf16_round(P.dequant_q8(q8, s4))))
-        ops.append(("cfg4_dequant_q4_bf16", 4096 * 2048 + 4096 * 4096 * 2 + 4096 * 128 * 2, 4096 * 4096,
-                    lambda: P.bf16_round(P.dequant_q4(q4, s4))))
-    Cs = max(4, int(512 * scale / 8))  # snake rows sampled: one batch, Cs channels
-    xs, al = P.normal((1, Cs, 24000), sid=14), P.uniform_arr((Cs,), 0.2, 2.0, sid=15)
-    ops.append(("cfg4_snake_hift_f32", 2 * Cs * 24000 * 4 + Cs * 4, Cs * 24000, lambda: L.snake(xs, al, 0, inner=24000)))
-    n = int(2 ** 24 * scale)
-    a, b = P.normal((n // 4096, 4096), sid=16), P.normal((n // 4096, 4096), sid=18)
-    ops.append(("cfg5_add_f32", 3 * n * 4, n, lambda: L.add(a, b)))
-    ops.append(("cfg5_mul_f32", 3 * n * 4, n, lambda: L.mul(a, b)))
-    ops.append(("cfg5_gelu_f32", 2 * n * 4, n, (lambda: R.gelu_inplace(a)) if R is not None else (lambda: P.gelu(a, 0))))
-    if R is not None:
-        for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
-            ops.append((f"cfg5_{nm}_f32", n * 4 + n // 1024, n, lambda op=op: R.row_reduce(a, op)))
-    else:
-        for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
-            ops.append((f"cfg5_{nm}_f32", n * 4 + n // 1024, n, lambda op=op: P.row_reduce(a, op)))
-    return kind, cores, ops, f32
+def suite_model(sweep_elems: int, scale: int = 1) -> list[tuple[str, int, int]]:
+    """(name, algorithmic bytes, elements) of every op of the default suite per GPU, in launch order: the byte model
+    both arms report against (each input read once, each output written once, at the stated element types)."""
+    K, n = scale, sweep_elems
+    m1, H2, B3, R4, B4 = 512 * K, 16 * K, 8 * K, 4096 * K, 16 * K
+    rows = n // 4096
+    ops = [("cfg1_rmsnorm_f32", 2 * m1 * 1024 * 4 + 1024 * 4, m1 * 1024),
+           ("cfg1_swiglu_f32", 3 * m1 * 3072 * 4, m1 * 3072),
+           ("cfg2_softmax_causal_f32", H2 * 1024 * 1025 // 2 * 4 + H2 * 1024 * 1024 * 4, H2 * 1024 * 1024),
+           ("cfg3_adaln_bf16", 3 * B3 * 2048 * 1024 * 2 + 3 * B3 * 1024 * 2, B3 * 2048 * 1024),
+           ("cfg4_dequant_q8_bf16", R4 * 4096 + R4 * 128 * 2 + R4 * 4096 * 2, R4 * 4096),
+           ("cfg4_dequant_q4_bf16", R4 * 2048 + R4 * 128 * 2 + R4 * 4096 * 2, R4 * 4096),
+           ("cfg4_snake_hift_f32", 2 * B4 * 512 * 24000 * 4 + 512 * 4, B4 * 512 * 24000)]
+    for tag, es in (("f32", 4), ("bf16", 2)):
+        ops += [(f"cfg5_add_{tag}", 3 * n * es, n), (f"cfg5_mul_{tag}", 3 * n * es, n), (f"cfg5_gelu_{tag}", 2 * n * es, n)]
+        ops += [(f"cfg5_{k}_{tag}", n * es + rows * 4, n) for k in ("rowsum", "rowmax", "rowl2")]
+        if es == 4:
+            ops.append(("cfg5_global_sum_f32", n * 4 + rows * 4, n))
+    return ops
 
 
-def time_cpu(ops, reps: int = 1) -> tuple[float, int, int, dict]:
-    """Seconds, bytes and elements over `reps` passes of the sampled suite (after one untimed pass)."""
-    for *_, fn in ops:
-        fn()
-    per = {}
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        for nm, by, el, fn in ops:
-            s = time.perf_counter()
+def suite_config(sweep_elems: int, scale: int = 1) -> dict:
+    """The `config` of the default suite: identical in both arms (the GPU's and the reference CPU's)."""
+    model = suite_model(sweep_elems, scale)
+    nb = sum(b for _, b, _ in model)
+    return {"workload": "vox-hotpath-suite", "ops": [nm for nm, _, _ in model], "sweep_elems_per_gpu": sweep_elems,
+            "bytes_per_step_per_gpu": nb, "elements_per_step_per_gpu": sum(e for _, _, e in model), "scale_cfg1_cfg4": scale,
+            "l2": "no flush: inputs larger than L2 - each step streams %.1f GB per GPU through a 126 MB L2, so every input "
+                  "is evicted by the other ops' traffic between its uses" % (nb / 1e9)}
+
+
+def cpu_model() -> str:
+    try:
+        for ln in subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+class CpuSuite:
+    """The default suite on the host through dariumi/Vox's own CPU operators (oracle/_ref/libvox_ref.so, compiled
+    from the reference sources; the C restatement where that library is absent): the same ops as the GPU suite, at
+    the same shapes and element types in memory (bf16 tensors stay bf16, widened and rounded inside the parallel
+    loops), on the same Philox4x32-10 inputs, with every output preallocated outside the timed region. Threads: all
+    host cores through Vox's own ThreadPool (vox::set_num_threads(0)) with Vox's grains."""
+
+    def __init__(self, sweep_elems: int):
+        from oracle.oracle import port, ref
+
+        P, R = port(), ref()
+        self.kind = "reference" if R is not None else "port"
+        self.cores = R.set_threads(0) if R is not None else 1
+        f32, u16 = np.float32, np.uint16
+        E = lambda *sh, dt=f32: np.empty(sh, dt)  # noqa: E731
+        nrm = lambda sh, sid, m=0.0, sd=1.0: P.fill_into(E(*sh), 1, m, sd, sid=sid)  # noqa: E731
+        uni = lambda sh, sid, lo, hi: P.fill_into(E(*sh), 0, lo, hi, sid=sid)  # noqa: E731
+
+        def nrm16(sh, sid, m=0.0, sd=1.0):
+            return P.bf16_round_into(nrm(sh, sid, m, sd), E(*sh, dt=u16))
+
+        pt = lambda a: a.ctypes.data  # noqa: E731
+        ops = []
+        model = {nm: (b, e) for nm, b, e in suite_model(sweep_elems)}
+
+        def add(name, fn):
+            ops.append((name, model[name][0], model[name][1], fn))
+
+        # cfg1
+        x1, w1, y1 = nrm((512, 1024), 1), nrm((1024,), 2, 1, 0.02), E(512, 1024)
+        g1, u1, h1 = nrm((512, 3072), 3), nrm((512, 3072), 4), E(512, 3072)
+        # cfg2
+        s2, p2 = nrm((16, 1024, 1024), 5, 0, 3), E(16, 1024, 1024)
+        # cfg3 (bf16 activations and parameters)
+        x3, r3 = nrm16((8, 2048, 1024), 6), nrm16((8, 2048, 1024), 7)
+        sh3, sc3, g3 = (nrm16((8, 1024), sid, 0, 0.1) for sid in (8, 9, 10))
+        m3, y3 = E(2048, 1024), E(8, 2048, 1024, dt=u16)
+        # cfg4: f16 scales widened once to the f32 scales Vox's Mat holds
+        s4 = P.f16_to_f32(uni((4096, 128), 13, 0.001, 0.05).astype(np.float16).view(u16))
+        q8, q4 = P.fill_into(E(4096, 4096, dt=np.int8), 2, -128, 127, sid=11), P.fill_into(E(4096, 2048, dt=np.uint8), 3, sid=12)
+        o8, o4 = E(4096, 4096, dt=u16), E(4096, 4096, dt=u16)
+        xs, al, ys = nrm((16, 512, 24000), 14), uni((512,), 15, 0.2, 2.0), E(16, 512, 24000)
+        # cfg5
+        n, rows = sweep_elems, sweep_elems // 4096
+        a5, b5, y5 = nrm((rows, 4096), 16), nrm((rows, 4096), 18), E(rows, 4096)
+        a6, b6, y6 = nrm16((rows, 4096), 17), nrm16((rows, 4096), 19), E(rows, 4096, dt=u16)
+        rr, slots = E(rows), np.empty(840, np.float64)
+        self._keep = [x1, w1, y1, g1, u1, h1, s2, p2, x3, r3, sh3, sc3, g3, m3, y3, s4, q8, q4, o8, o4, xs, al, ys, a5, b5, y5, a6, b6, y6,
+                      rr, slots]
+        sc2 = float(1.0 / np.sqrt(128.0))
+        if R is not None:
+            L = R.L
+            add("cfg1_rmsnorm_f32", lambda: L.vr_rmsnorm_rows(pt(x1), pt(w1), 512, 1024, 1e-6, pt(y1), 1))
+            add("cfg1_swiglu_f32", lambda: L.vr_silu_mul(pt(g1), pt(u1), pt(h1), g1.size))
+            add("cfg2_softmax_causal_f32", lambda: L.vr_softmax_rows(pt(s2), pt(p2), 16 * 1024, 1024, sc2, 1024, 0, 0))
+            add("cfg3_adaln_bf16", lambda: L.vr_adaln_bf16(pt(x3), pt(sh3), pt(sc3), pt(g3), pt(r3), 8, 2048, 1024, pt(m3), pt(y3)))
+            add("cfg4_dequant_q8_bf16", lambda: L.vr_mat_rows_bf16(3, pt(q8), pt(s4), 4096, 4096, pt(o8)))
+            add("cfg4_dequant_q4_bf16", lambda: L.vr_mat_rows_bf16(4, pt(q4), pt(s4), 4096, 4096, pt(o4)))
+            add("cfg4_snake_hift_f32", lambda: L.vr_snake(pt(xs), pt(al), None, pt(ys), xs.size, 512, 24000, 0))
+            add("cfg5_add_f32", lambda: L.vr_add(pt(a5), pt(b5), pt(y5), n))
+            add("cfg5_mul_f32", lambda: L.vr_mul(pt(a5), pt(b5), pt(y5), n))
+            add("cfg5_gelu_f32", lambda: L.vr_gelu_f32(pt(a5), pt(y5), n))
+            for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
+                add(f"cfg5_{nm}_f32", lambda op=op: L.vr_row_reduce(pt(a5), pt(rr), rows, 4096, op))
+            add("cfg5_global_sum_f32", lambda: L.vr_global_sum(pt(a5), rows, 4096, pt(rr), pt(slots)))
+            add("cfg5_add_bf16", lambda: L.vr_add_bf16(pt(a6), pt(b6), pt(y6), n))
+            add("cfg5_mul_bf16", lambda: L.vr_mul_bf16(pt(a6), pt(b6), pt(y6), n))
+            add("cfg5_gelu_bf16", lambda: L.vr_gelu_bf16(pt(a6), pt(y6), n))
+            for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
+                add(f"cfg5_{nm}_bf16", lambda op=op: L.vr_row_reduce_bf16(pt(a6), pt(rr), rows, 4096, op))
+        else:  # the single-threaded C restatement (a machine without the reference library); bf16 tensors widened once
+            from oracle.oracle import bf16_bits_to_f32 as wide
+
+            Q = P.L
+            x3f, r3f, sh3f, sc3f, g3f, y3f = wide(x3), wide(r3), wide(sh3), wide(sc3), wide(g3), E(8, 2048, 1024)
+            a6f, b6f, y6f = wide(a6), wide(b6), E(rows, 4096)
+            self._keep += [x3f, r3f, sh3f, sc3f, g3f, y3f, a6f, b6f, y6f]
+            add("cfg1_rmsnorm_f32", lambda: Q.vo_rmsnorm_rows(pt(x1), pt(w1), 512, 1024, 1e-6, pt(y1)))
+            add("cfg1_swiglu_f32", lambda: Q.vo_silu_mul(pt(g1), pt(u1), pt(h1), g1.size))
+            add("cfg2_softmax_causal_f32", lambda: Q.vo_softmax_rows(pt(s2), pt(p2), 16 * 1024, 1024, sc2, 1024, 0))
+            add("cfg3_adaln_bf16", lambda: Q.vo_adaln(pt(x3f), pt(sh3f), pt(sc3f), pt(g3f), pt(r3f), 8, 2048, 1024, 1e-6, pt(y3f)))
+            add("cfg4_dequant_q8_bf16", lambda: Q.vo_dequant_q8(pt(q8), pt(s4), 4096, 4096, pt(y3f)))
+            add("cfg4_dequant_q4_bf16", lambda: Q.vo_dequant_q4(pt(q4), pt(s4), 4096, 4096, pt(y3f)))
+            add("cfg4_snake_hift_f32", lambda: Q.vo_snake(pt(xs), pt(al), None, pt(ys), xs.size, 512, 24000, 0))
+            for tag, (a, b, y) in (("f32", (a5, b5, y5)), ("bf16", (a6f, b6f, y6f))):
+                add(f"cfg5_add_{tag}", lambda a=a, b=b, y=y: Q.vo_add(pt(a), pt(b), pt(y), n))
+                add(f"cfg5_mul_{tag}", lambda a=a, b=b, y=y: Q.vo_mul(pt(a), pt(b), pt(y), n))
+                add(f"cfg5_gelu_{tag}", lambda a=a, y=y: Q.vo_gelu_erf(pt(a), pt(y), n))
+                for op, nm in ((0, "rowsum"), (1, "rowmax"), (2, "rowl2")):
+                    add(f"cfg5_{nm}_{tag}", lambda op=op, a=a: Q.vo_row_reduce_f64(pt(a), pt(rr), rows, 4096, op))
+            add("cfg5_global_sum_f32", lambda: Q.vo_row_reduce_f64(pt(a5), pt(rr), rows, 4096, 0))
+        order = [nm for nm, _, _ in suite_model(sweep_elems)]
+        ops.sort(key=lambda o: order.index(o[0]))
+        self.ops = ops
+        self.bytes_per_step = sum(o[1] for o in ops)
+        self.elems_per_step = sum(o[2] for o in ops)
+
+    def time(self, steps: int, warmup: int, budget_s: float = 240.0) -> tuple[float, int, int, dict, str]:
+        """Times `steps` steps after `warmup` untimed ones. A step is one pass over every op when (steps + warmup)
+        passes fit in `budget_s`; otherwise each step runs the next op of the suite in turn (a bounded sample whose
+        aggregate over the steps weights the ops as a full pass does). Returns (seconds, bytes, elements, per-op
+        seconds, sample description)."""
+        t0 = time.perf_counter()
+        for *_, fn in self.ops:
             fn()
-            per[nm] = per.get(nm, 0.0) + time.perf_counter() - s
-    dt = time.perf_counter() - t0
-    return dt, reps * sum(o[1] for o in ops), reps * sum(o[2] for o in ops), per
+        one = time.perf_counter() - t0
+        full = (steps + max(warmup - 1, 0)) * one <= budget_s
+        plan = [list(range(len(self.ops))) for _ in range(steps)] if full else \
+            [[k % len(self.ops)] for k in range(steps)]
+        for _ in range(max(warmup - 1, 0)):
+            for i in (range(len(self.ops)) if full else [0]):
+                self.ops[i][3]()
+        per, runs, nbytes, nel = {}, {}, 0, 0
+        t0 = time.perf_counter()
+        for idx in plan:
+            for i in idx:
+                nm, by, el, fn = self.ops[i]
+                s = time.perf_counter()
+                fn()
+                per[nm] = per.get(nm, 0.0) + time.perf_counter() - s
+                runs[nm] = runs.get(nm, 0) + 1
+                nbytes += by
+                nel += el
+        dt = time.perf_counter() - t0
+        sample = ("every step one full pass of the suite: the GPU arm's ops, shapes and element types" if full else
+                  "every step the next op of the suite in turn (a full pass per step would exceed %.0f s)" % budget_s)
+        return dt, nbytes, nel, per, runs, sample
+
+    def op_table(self, per: dict, runs: dict) -> dict:
+        """Per-op GB/s and milliseconds of a timed run."""
+        return {nm: {"gb_s": round(by * runs[nm] / per[nm] / 1e9, 3), "ms": round(per[nm] / runs[nm] * 1e3, 3)}
+                for nm, by, _, _ in self.ops if nm in per}
 
 
 def run_reference(args) -> None:
+    """The reference arm: dariumi/Vox's own CPU operators on the host cores over the GPU arm's suite (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    kind, cores, ops, _ = cpu_suite_sample(1.0)
-    for _ in range(args.warmup):
-        for *_, fn in ops:
-            fn()
-    dt, by, el, per = time_cpu(ops, reps=args.steps)
+    cs = CpuSuite(args.sweep_elems)
+    dt, by, el, per, runs, sample = cs.time(args.steps, args.warmup)
     value = by / dt / 1e9
-    sample = ("per step: cfg1-cfg4 at BASELINE shapes except Snake on 64 of 8192 rows; cfg5 f32 add/mul/GELU/row "
-              "sum/max/L2 on 2^24 elements; bf16 ops computed in f32 and rounded")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (Philox4x32-10 seed 0, BASELINE shapes)",
-        "config": {"workload": "vox-hotpath-suite", "sample": sample},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (Philox4x32-10 seed 0, BASELINE shapes and distributions; the GPU arm's inputs)",
+        "config": suite_config(args.sweep_elems),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cs.cores, "kind": cs.kind, "cpu_model": cpu_model(),
+                         "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "elements_per_s": round(el / dt, 1),
-        "ops": {nm: {"gb_s": round(b * args.steps / per[nm] / 1e9, 3)} for nm, b, _, _ in ops},
+        "ops": cs.op_table(per, runs),
     }
     print(json.dumps(line), flush=True)
 
@@ -566,20 +667,25 @@ def run_ours(args) -> None:
             traffic = None
     cpu = None
     if world == 1 and not args.no_cpu_baseline and not args.only:
-        kind, cores, cops, _ = cpu_suite_sample(1.0)
-        dt, by, el, _ = time_cpu(cops, reps=1)
-        cpu = {"value": round(by / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-               "sample": "one pass: cfg1-cfg4 at BASELINE shapes except Snake on 64 of 8192 rows; cfg5 f32 ops on 2^24 elements"}
+        cs = CpuSuite(args.sweep_elems)
+        dt, by, el, per, runs, _ = cs.time(1, 1)
+        cpu = {"value": round(by / dt / 1e9, 3), "unit": "GB/s", "cores": cs.cores, "kind": cs.kind, "cpu_model": cpu_model(),
+               "sample": "one full pass of the suite after one untimed pass: the GPU arm's ops, shapes and element types",
+               "ops": cs.op_table(per, runs)}
+        del cs
+    if args.only is None and args.scale == 1:
+        config = suite_config(args.sweep_elems)  # the default suite: the reference arm's config
+        assert config["bytes_per_step_per_gpu"] == suite.bytes_per_step and config["ops"] == [o[0] for o in suite.ops]
+    else:
+        config = {"workload": "vox-hotpath-suite" + (f" (ops matching {args.only!r})" if args.only else ""),
+                  "ops": [o[0] for o in suite.ops], "sweep_elems_per_gpu": args.sweep_elems, "bytes_per_step_per_gpu": suite.bytes_per_step,
+                  "elements_per_step_per_gpu": suite.elems_per_step, "scale_cfg1_cfg4": args.scale}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (Philox4x32-10 seed 0 on the device, BASELINE shapes and distributions)",
-        "config": {"workload": "vox-hotpath-suite", "sweep_elems_per_gpu": args.sweep_elems,
-                   "bytes_per_step_per_gpu": suite.bytes_per_step, "elements_per_step_per_gpu": suite.elems_per_step,
-                   "parallelism": f"row shards x{world}, NCCL all-reduce of 840 f64 slots for the global sum",
-                   "scale_cfg1_cfg4": args.scale,
-                   "l2": "no flush: the step streams ~%.1f GB per GPU (> 126 MB L2), so every input is evicted by the other ops' "
-                         "traffic between its uses" % (suite.bytes_per_step / 1e9)},
+        "config": config,
+        "parallelism": f"row shards x{world}, NCCL all-reduce of 840 f64 slots for the global sum",
         "elements_per_s": round(suite.elems_per_step * world / step_s, 1),
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 3), "traffic": traffic, "peak_source": peak_kind},
@@ -730,6 +836,64 @@ def run_sweep(args) -> None:
                           "results": results}), flush=True)
 
 
+def run_copy_roofline(args) -> None:
+    """Size-matched copy roofline of the small BASELINE configs: for each op, the op alone and a plain device copy of
+    the same traffic (a torch copy_ of bytes/2: reads bytes/2, writes bytes/2), both timed the same way - CUDA events
+    around back-to-back launches that rotate over enough buffer sets that the sets total at least 3x the L2 size (so
+    every launch reads HBM) - on one GPU. frac_of_copy = copy time / op time: the fraction of the bandwidth that this
+    size of transfer attains at all. One JSON line."""
+    import torch
+
+    torch.cuda.set_device(0)
+    import vox_b200 as vox
+
+    peak, _ = peaks()
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    names = ["cfg1_rmsnorm_f32", "cfg1_swiglu_f32", "cfg2_softmax_causal_f32", "cfg3_adaln_bf16", "cfg4_dequant_q8_bf16",
+             "cfg4_dequant_q4_bf16", "cfg4_snake_hift_f32"]
+    if args.only:
+        import re
+
+        names = [nm for nm in names if re.search(args.only, nm)]
+    res = {}
+
+    def timed(fns, reps):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for k in range(reps):
+            fns[k % len(fns)]()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3  # us
+
+    for nm in names:
+        nb = dict((o[0], o[1]) for o in suite_model(args.sweep_elems))[nm]
+        sets = max(2, -(-3 * l2 // nb))
+        suites = [Suite(vox, torch, 0, 1, args.sweep_elems, only=f"^{nm}$") for _ in range(sets)]
+        fns = [su.ops[0][3] for su in suites]
+        reps = max(3 * sets, 60)
+        op_us = min(timed(fns, reps) for _ in range(3))
+        del suites, fns
+        torch.cuda.empty_cache()
+        half = nb // 2
+        bufs = [(torch.empty(half, dtype=torch.uint8, device="cuda"), torch.empty(half, dtype=torch.uint8, device="cuda"))
+                for _ in range(sets)]
+        cps = [lambda s=s_, d=d_: d.copy_(s) for s_, d_ in bufs]
+        cp_us = min(timed(cps, reps) for _ in range(3))
+        del bufs, cps
+        torch.cuda.empty_cache()
+        res[nm] = {"bytes": nb, "op_us": round(op_us, 2), "copy_us": round(cp_us, 2), "op_gb_s": round(nb / op_us / 1e3, 1),
+                   "copy_gb_s": round(nb / cp_us / 1e3, 1), "frac_of_copy": round(cp_us / op_us, 3),
+                   "frac_of_peak": round(nb / op_us / 1e3 / peak, 3), "copy_frac_of_peak": round(nb / cp_us / 1e3 / peak, 3),
+                   "buffer_sets": sets}
+    print(json.dumps({"metric": METRIC, "mode": "copy-roofline", "unit": "GB/s", "peak": peak, "l2_bytes": l2,
+                      "config": {"workload": "BASELINE cfg1-cfg4 ops alone against a device copy of the same bytes"},
+                      "results": res}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -742,6 +906,7 @@ def main() -> None:
     ap.add_argument("--only", default=None, help="regex: run only the matching ops (profiling one kernel)")
     ap.add_argument("--sweep", action="store_true", help="BASELINE cfg5 size sweep instead of the suite")
     ap.add_argument("--scale", type=int, default=1, help="multiply the rows/heads/batches of cfg1-cfg4 (1 = BASELINE shapes)")
+    ap.add_argument("--copy-roofline", action="store_true", help="cfg1-cfg4 ops against a size-matched device copy")
     ap.add_argument("--sweep-lo", type=int, default=20)
     ap.add_argument("--sweep-hi", type=int, default=32)
     args = ap.parse_args()
@@ -751,6 +916,8 @@ def main() -> None:
         run_reference(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.copy_roofline:
+        run_copy_roofline(args)
     else:
         run_ours(args)
 

@@ -84,6 +84,13 @@ VOX_CUDA_API int vox_cuda_device_cc(int *cc);
  * its rows unwritten. No counterpart in the reference (Vox's Vulkan backend has no device-side waits). */
 #define VOX_CUDA_DEVERR_TIMEOUT 1u
 VOX_CUDA_API int vox_cuda_device_error(unsigned int *flags);
+/* Test hook of the row operators (RMSNorm, LayerNorm, adaLN, softmax, row reductions, residual + RMSNorm): from the
+ * next launch on, the stage barrier of row `row` (-1 = none) expects 16 bytes more than its copies deliver, so every
+ * copy lands but the wait for that row runs out after wait_limit_ns (0 = the default 2 s); the warp that owns the row
+ * then waits (bounded) for its copies in flight, sets VOX_CUDA_DEVERR_TIMEOUT and stops, leaving that row and its
+ * later rows unwritten. Exercises the give-up path without a fault. Call with (-1, 0) to restore normal operation.
+ * No counterpart in the reference. */
+VOX_CUDA_API int vox_cuda_test_row_stall(int64_t row, uint64_t wait_limit_ns);
 
 /* Seeded synthetic data with Vox's counter-based generator (Philox4x32-10, src/sampling.hpp:16-50).
  * Element i uses counter {i lo, i hi, stream_id, draw}, key {seed lo, seed hi}.
@@ -209,10 +216,13 @@ VOX_CUDA_API int vox_cuda_global_sum_finish(const double *slots, double *out, vo
  * with the row sums and slots kept in a fixed scratch array inside the library instead of caller memory. For callers
  * that cannot call cudaMalloc (a real-time audio callback, where an allocation can block and synchronise the device;
  * a plugin host that owns all device memory apart from the inputs and outputs it passes in).
- * Limit: rows <= 262144 (larger tensors are rejected with VOX_CUDA_ERR_ARG). The scratch array (about 1 MB) is held on
- * every GPU that loads the library until the process exits. The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress); make that first call before any stream capture on that device. All calls share the
- * one array, so calls whose kernels overlap on the GPU (different streams without ordering) race; order them.
+ * Limit: rows <= 262144 (larger tensors are rejected with VOX_CUDA_ERR_ARG). The scratch array (about 1 MB) lives in
+ * the library's device module: it is held on every device where that module is loaded until the process exits (with
+ * CUDA's lazy module loading, from the library's first use on that device, at the latest this entry point's first
+ * call there). The first call in each CUDA context looks up the array's device address (cudaGetSymbolAddress) and may
+ * load the module and block: make it a warm-up call outside the real-time path, before any stream capture, on every
+ * device. A new context of the device (after cudaDeviceReset) is detected and its address looked up again. All calls
+ * share the one array, so calls whose kernels overlap on the GPU (different streams without ordering) race; order them.
  * No counterpart in the reference (Vox has no device-side global sum). */
 VOX_CUDA_API int vox_cuda_global_sum_noalloc(const void *x, int64_t rows, int64_t n, double *out, int dtype, void *stream);
 

@@ -44,12 +44,24 @@ def build_port() -> Path:
     return PORT_SO
 
 
-def build_ref(ref_root: str = "/root/reference") -> Path | None:
-    if not (Path(ref_root) / "src" / "kernels.cpp").exists():
+def reference_dir() -> Path | None:
+    """The reference's source root: $VOX_REFERENCE_DIR, else a directory named ``reference`` beside this repository's
+    root; None where neither holds the reference sources (on a GPU box only the prebuilt oracle/_ref travels)."""
+    import os
+
+    for cand in (os.environ.get("VOX_REFERENCE_DIR"), str(HERE.parent.parent / "reference")):
+        if cand and (Path(cand) / "src" / "kernels.cpp").exists():
+            return Path(cand)
+    return None
+
+
+def build_ref(ref_root: str | Path | None = None) -> Path | None:
+    root = Path(ref_root) if ref_root is not None else reference_dir()
+    if root is None or not (root / "src" / "kernels.cpp").exists():
         return REF_SO if REF_SO.exists() else None
     shim = HERE / "ref_shim.cpp"
     if not REF_SO.exists() or REF_SO.stat().st_mtime < shim.stat().st_mtime:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref_root}"], check=True)
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={root}"], check=True)
     return REF_SO
 
 
@@ -120,6 +132,46 @@ class Port:
 
     def uniform_arr(self, shape, lo, hi, seed=0, sid=0, c0=0):
         return self.fill(int(np.prod(shape)), 0, lo, hi, seed, sid, c0).reshape(shape)
+
+    def fill_into(self, out, dist, a=0.0, b=1.0, seed=0, sid=0, c0=0, threads=None):
+        """Fill a preallocated contiguous array with the numbers of ``fill`` / ``fill_i8`` / ``fill_u8`` (dist 0 / 1:
+        f32, 2: int8 codes in [a, b], 3: bytes), split over host threads (each element depends only on its counter)."""
+        import concurrent.futures as cf
+        import os
+
+        flat = out.reshape(-1)
+        n = flat.size
+        threads = threads or os.cpu_count() or 1
+        step = max(1 << 16, -(-n // (4 * threads)))
+        step += step & 1  # even chunk starts (Box-Muller pairs)
+
+        def one(lo):
+            hi = min(n, lo + step)
+            ptr = flat[lo:hi].ctypes.data_as(_p)
+            if dist in (0, 1):
+                self.L.vo_fill(ptr, hi - lo, dist, a, b, seed, sid, c0 + lo)
+            elif dist == 2:
+                self.L.vo_fill_i8(ptr, hi - lo, int(a), int(b), seed, sid, c0 + lo)
+            else:
+                self.L.vo_fill_u8(ptr, hi - lo, seed, sid, c0 + lo)
+
+        with cf.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(one, range(0, n, step)))
+        return out
+
+    def bf16_round_into(self, x, out, threads=None):
+        """bf16 bits of f32 x into the preallocated uint16 ``out`` (build.py:94-97), split over host threads."""
+        import concurrent.futures as cf
+        import os
+
+        xf, of = x.reshape(-1), out.reshape(-1)
+        n = xf.size
+        threads = threads or os.cpu_count() or 1
+        step = max(1 << 16, -(-n // (4 * threads)))
+        with cf.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(lambda lo: self.L.vo_f32_to_bf16_n(xf[lo:lo + step].ctypes.data_as(_p), of[lo:lo + step].ctypes.data_as(_p),
+                                                           min(step, n - lo)), range(0, n, step)))
+        return out
 
     def fill_i8(self, shape, a, b, seed=0, sid=0, c0=0):
         out = np.empty(int(np.prod(shape)), np.int8)
@@ -384,6 +436,15 @@ class Ref:
         L.vr_tmod_write.restype = _int
         L.vr_tmod_read.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _p, _u64]
         L.vr_tmod_read.restype = _i64
+        for nm, args in (("vr_gelu_f32", [_p, _p, _i64]), ("vr_gelu_bf16", [_p, _p, _i64]), ("vr_add_bf16", [_p, _p, _p, _i64]),
+                         ("vr_mul_bf16", [_p, _p, _p, _i64]), ("vr_row_reduce_bf16", [_p, _p, _i64, _i64, _int]),
+                         ("vr_mat_rows_bf16", [_int, _p, _p, _i64, _i64, _p]),
+                         ("vr_adaln_bf16", [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p])):
+            if hasattr(L, nm):
+                getattr(L, nm).argtypes = args
+        if hasattr(L, "vr_global_sum"):
+            L.vr_global_sum.argtypes = [_p, _i64, _i64, _p, _p]
+            L.vr_global_sum.restype = _d
         if hasattr(L, "vr_f5_dit"):
             L.vr_f5_dit.argtypes = [ctypes.c_char_p, _int, _int, _p, _p, _p, _f, _p, _p, ctypes.c_char_p, _int]
             L.vr_f5_dit.restype = _int

@@ -172,24 +172,34 @@ VR_API void vr_mul(const float *a, const float *b, float *y, int64_t n) {
 // Vox's own fast_sin (nn.hpp:26-40), linked from the header.
 VR_API float vr_fast_sin(float x) { return nn::fast_sin(x); }
 
-// Snake over rows of `inner` elements, channel (i / inner) % C, parallel_for(rows, 256) (cosyvoice.cpp:241,
-// kokoro.cpp:235). kind 0 HiFT (cosyvoice.cpp:239-248), 1 SnakeBeta (qwen3.cpp:86-94, a / inv_b given),
-// 2 Kokoro (kokoro.cpp:233-242). Restated loops (anonymous namespaces), reference helpers.
+// Snake, channel of element i = (i / inner) % C (inner = 1: Vox's [T][C] layout; inner = T: channel-major [B][C][T]).
+// kind 0 HiFT (cosyvoice.cpp:239-248), 1 SnakeBeta (qwen3.cpp:86-94, a / inv_b given), 2 Kokoro (kokoro.cpp:233-242).
+// Restated loops (anonymous namespaces), reference helpers. Vox splits its [T][C] tensor as parallel_for(T, 256)
+// (cosyvoice.cpp:241, kokoro.cpp:235): a task is 256 time steps of all C channels, 256 C elements. The same task size
+// is kept for either layout by splitting the flat element range with a grain of 256 C elements, so a channel-major
+// tensor is spread over all threads along time as Vox spreads its own.
 VR_API void vr_snake(const float *x, const float *alpha, const float *beta, float *y, int64_t n, int64_t C, int64_t inner, int kind) {
-    const int64_t rows = (n + inner - 1) / inner;
-    parallel_for(rows, inner == 1 ? 256 * C : 256, [&](int64_t a, int64_t e) {
-        for (int64_t i = a * inner; i < std::min(n, e * inner); ++i) {
+    parallel_for(n, 256 * C, [&](int64_t a, int64_t e) {
+        for (int64_t i = a; i < e;) {
             const int64_t c = (i / inner) % C;
-            const float v = x[i];
+            const int64_t stop = std::min(e, (i / inner + 1) * inner);  // end of this channel's run
+            const float al = alpha[c];
             if (kind == 0) {
-                const float al = alpha[c], sn = std::sin(al * v);
-                y[i] = v + (1.0f / (al + 1e-9f)) * (sn * sn);
+                for (; i < stop; ++i) {
+                    const float v = x[i], sn = std::sin(al * v);
+                    y[i] = v + (1.0f / (al + 1e-9f)) * (sn * sn);
+                }
             } else if (kind == 1) {
-                const float sn = std::sin(v * alpha[c]);
-                y[i] = v + beta[c] * sn * sn;
+                const float bt = beta[c];
+                for (; i < stop; ++i) {
+                    const float v = x[i], sn = std::sin(v * al);
+                    y[i] = v + bt * sn * sn;
+                }
             } else {
-                const float s = nn::fast_sin(alpha[c] * v);
-                y[i] = v + (1.0f / alpha[c]) * (s * s);
+                for (; i < stop; ++i) {
+                    const float v = x[i], sv = nn::fast_sin(al * v);
+                    y[i] = v + (1.0f / al) * (sv * sv);
+                }
             }
         }
     });
@@ -342,5 +352,134 @@ VR_API int vr_f5_dit(const char *path, int B, int N, const float *x, const float
     } catch (const std::exception &e) {
         std::snprintf(err, size_t(errcap), "%s", e.what());
         return -1;
+    }
+}
+
+// ---------------------------------------------------------------- the CPU arm of the benchmark suite (bench.py)
+//
+// Out-of-place and bf16-I/O forms of the operators above, so the reference's CPU code runs the GPU suite's own
+// workload: same shapes, same element types in memory, outputs preallocated by the caller. Each keeps the reference's
+// arithmetic and its parallel_for grain; bf16 values are widened exactly and rounded to nearest-even once at the store
+// (python/vox/build.py:94-97). A parallel_for whose range fits one grain runs inline in the calling thread
+// (ThreadPool::run, kernels.cpp:56-57), which is how Vox's own in-place operators run on one task's chunk below.
+
+static inline float bf16f(uint16_t h) { return bf16_to_f32(h); }
+static inline uint16_t f32bf(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    return uint16_t((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// y = gelu(x) with vox::nn::gelu_inplace (nn.cpp:87-96) on each parallel_for(n, 8192) task's chunk: the chunk is
+// copied to y (it stays in cache) and transformed in place there.
+VR_API void vr_gelu_f32(const float *x, float *y, int64_t n) {
+    parallel_for(n, 8192, [&](int64_t a, int64_t b) {
+        std::memcpy(y + a, x + a, size_t(b - a) * sizeof(float));
+        nn::gelu_inplace(y + a, b - a);
+    });
+}
+VR_API void vr_gelu_bf16(const uint16_t *x, uint16_t *y, int64_t n) {
+    parallel_for(n, 8192, [&](int64_t a, int64_t b) {
+        float buf[8192];
+        for (int64_t i = a; i < b; ++i) buf[i - a] = bf16f(x[i]);
+        nn::gelu_inplace(buf, b - a);
+        for (int64_t i = a; i < b; ++i) y[i] = f32bf(buf[i - a]);
+    });
+}
+VR_API void vr_add_bf16(const uint16_t *a, const uint16_t *b, uint16_t *y, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t s, int64_t e) {
+        for (int64_t i = s; i < e; ++i) y[i] = f32bf(bf16f(a[i]) + bf16f(b[i]));
+    });
+}
+VR_API void vr_mul_bf16(const uint16_t *a, const uint16_t *b, uint16_t *y, int64_t n) {
+    parallel_for(n, 4096, [&](int64_t s, int64_t e) {
+        for (int64_t i = s; i < e; ++i) y[i] = f32bf(bf16f(a[i]) * bf16f(b[i]));
+    });
+}
+// Row sum / max / L2 of bf16 rows: vr_row_reduce's order on the widened values.
+VR_API void vr_row_reduce_bf16(const uint16_t *x, float *out, int64_t rows, int64_t n, int op) {
+    parallel_for(rows, 16, [&](int64_t a, int64_t b) {
+        for (int64_t r = a; r < b; ++r) {
+            const uint16_t *xr = x + r * n;
+            float acc = op == 1 ? -INFINITY : 0.f;
+            for (int64_t i = 0; i < n; ++i) {
+                const float v = bf16f(xr[i]);
+                acc = op == 1 ? std::max(acc, v) : op == 2 ? acc + v * v : acc + v;
+            }
+            out[r] = op == 2 ? std::sqrt(acc) : acc;
+        }
+    });
+}
+// Global sum of f32 rows [rows][n] (no reference function): row sums as vr_row_reduce, then 840 slot partials in f64
+// (slot s = rows [s rows / 840, (s + 1) rows / 840), in row order) over parallel_for(840, 8), folded in slot order.
+// rowsum: caller scratch of `rows` floats; slots: caller scratch of 840 doubles.
+VR_API double vr_global_sum(const float *x, int64_t rows, int64_t n, float *rowsum, double *slots) {
+    vr_row_reduce(x, rowsum, rows, n, 0);
+    parallel_for(840, 8, [&](int64_t a, int64_t b) {
+        for (int64_t sl = a; sl < b; ++sl) {
+            double acc = 0.0;
+            for (int64_t r = sl * rows / 840; r < (sl + 1) * rows / 840; ++r) acc += double(rowsum[r]);
+            slots[sl] = acc;
+        }
+    });
+    double t = 0.0;
+    for (int s = 0; s < 840; ++s) t += slots[s];
+    return t;
+}
+// Block dequantisation to bf16: vox::mat_gather (kernels.cpp:468-471) of each row into the task's f32 row buffer over
+// parallel_for(rows, 16) (kernels.cpp:665), rounded to bf16 at the store.
+VR_API void vr_mat_rows_bf16(int type, const uint8_t *data, const float *scale, int64_t rows, int64_t cols, uint16_t *out) {
+    Mat M;
+    M.type = type == 4 ? WType::Q4 : WType::Q8;
+    M.data = data;
+    M.scale = scale;
+    M.rows = rows;
+    M.cols = cols;
+    parallel_for(rows, 16, [&](int64_t a, int64_t b) {
+        std::vector<float> row(static_cast<size_t>(cols));
+        for (int64_t r = a; r < b; ++r) {
+            mat_gather(M, r, row.data());
+            uint16_t *o = out + r * cols;
+            for (int64_t i = 0; i < cols; ++i) o[i] = f32bf(row[size_t(i)]);
+        }
+    });
+}
+// The F5 adaLN with bf16 activations: the modulate lambda (f5.cpp:617-632, parallel_for(T, 16)) on the widened x rows
+// into the caller's f32 buffer m [T][D], then the gated_add lambda (f5.cpp:670-676, parallel_for(T, 32)) from the
+// widened residual, rounded to bf16 at the store; per batch b of x [B][T][D]; shift / scale / gate [B][D] bf16.
+VR_API void vr_adaln_bf16(const uint16_t *x, const uint16_t *shift, const uint16_t *scale, const uint16_t *gate, const uint16_t *res,
+                          int64_t B, int64_t T, int64_t D, float *m, uint16_t *out) {
+    for (int64_t bb = 0; bb < B; ++bb) {
+        std::vector<float> sc(static_cast<size_t>(D)), sh(static_cast<size_t>(D)), g(static_cast<size_t>(D));
+        for (int64_t i = 0; i < D; ++i) {
+            sc[size_t(i)] = bf16f(scale[bb * D + i]);
+            sh[size_t(i)] = bf16f(shift[bb * D + i]);
+            g[size_t(i)] = bf16f(gate[bb * D + i]);
+        }
+        const uint16_t *src = x + bb * T * D;
+        parallel_for(T, 16, [&](int64_t r0, int64_t r1) {
+            for (int64_t r = r0; r < r1; ++r) {
+                const uint16_t *xr = src + r * D;
+                double mean = 0;
+                for (int64_t i = 0; i < D; ++i) mean += bf16f(xr[i]);
+                mean /= double(D);
+                double var = 0;
+                for (int64_t i = 0; i < D; ++i) { const double dd = bf16f(xr[i]) - mean; var += dd * dd; }
+                var /= double(D);
+                const float inv = float(1.0 / std::sqrt(var + 1e-6));
+                float *yr = m + r * D;
+                for (int64_t i = 0; i < D; ++i) yr[i] = (bf16f(xr[i]) - float(mean)) * inv * (1.0f + sc[size_t(i)]) + sh[size_t(i)];
+            }
+        });
+        const uint16_t *rb = res + bb * T * D;
+        uint16_t *dst = out + bb * T * D;
+        parallel_for(T, 32, [&](int64_t r0, int64_t r1) {
+            for (int64_t r = r0; r < r1; ++r)
+                for (int64_t i = 0; i < D; ++i) {
+                    float h = bf16f(rb[r * D + i]);
+                    h += g[size_t(i)] * m[r * D + i];
+                    dst[r * D + i] = f32bf(h);
+                }
+        });
     }
 }

@@ -110,6 +110,39 @@ def test_rmsnorm_row_lengths(vox, port, n):
     assert_close(host(vox.rmsnorm(dev(x), dev(w), 1e-6)), port.rmsnorm(x, w, 1e-6))
 
 
+@pytest.mark.parametrize("rows", [64, 1184, 2000])
+@pytest.mark.parametrize("n", [1024, 6144])
+def test_norm_kinds_both_row_paths(vox, port, rows, n):
+    """Every norm kind, f32 and bf16, at row counts that take the CTA-per-row path (few rows: up to 8 per SM) and
+    the warp-per-row pipeline (or, for rows of more than 512 vectors, the general path)."""
+    B = 2 if rows % 2 == 0 else 1
+    T = rows // B
+    x = port.normal((rows, n), 0.3, 1.5, sid=900 + n)
+    w = port.normal((n,), 1.0, 0.1, sid=901)
+    b = port.normal((n,), 0.0, 0.1, sid=902)
+    res = port.normal((rows, n), sid=903)
+    sh, sc, g = (port.normal((B, n), 0.0, 0.1, sid=s) for s in (904, 905, 906))
+    assert_close(host(vox.rmsnorm(dev(x), dev(w), 1e-6)), port.rmsnorm(x, w, 1e-6))
+    assert_close(host(vox.layernorm(dev(x), dev(w), dev(b), 1e-5)), port.layernorm(x, w, b, 1e-5))
+    assert_close(host(vox.layernorm(dev(x), dev(w), dev(b), 1e-6, modulate=True)), port.layernorm(x, w, b, 1e-6, modulate=True))
+    assert_close(host(vox.layernorm(dev(x), None, None, 1e-6)), port.layernorm(x, None, None, 1e-6))
+    X, R = x.reshape(B, T, n), res.reshape(B, T, n)
+    assert_close(host(vox.adaln(dev(X), dev(sh), dev(sc), 1e-6)), port.adaln(X, sh, sc))
+    assert_close(host(vox.adaln(dev(X), dev(sh), dev(sc), 1e-6, dev(g), dev(R))), port.adaln(X, sh, sc, g, R))
+    xb, rb = bf16r(X), bf16r(R)
+    shb, scb, gb = bf16r(sh), bf16r(sc), bf16r(g)
+    d = lambda a: dev(a, torch.bfloat16)  # noqa: E731
+    assert_close(host(vox.rmsnorm(d(xb.reshape(rows, n)), dev(w), 1e-6)), bf16r(port.rmsnorm(xb.reshape(rows, n), w, 1e-6)), BF16_TOL)
+    assert_close(host(vox.adaln(d(xb), d(shb), d(scb), 1e-6, d(gb), d(rb))), bf16r(port.adaln(xb, shb, scb, gb, rb)), BF16_TOL)
+    # in place (y = x) and y = residual
+    xi = dev(X)
+    vox.adaln(xi, dev(sh), dev(sc), 1e-6, dev(g), dev(R), out=xi)
+    assert_close(host(xi), port.adaln(X, sh, sc, g, R))
+    ri = dev(R)
+    vox.adaln(dev(X), dev(sh), dev(sc), 1e-6, dev(g), ri, out=ri)
+    assert_close(host(ri), port.adaln(X, sh, sc, g, R))
+
+
 def test_rmsnorm_bf16(vox, port):
     x = bf16r(port.normal((64, 1024), sid=3))
     w = port.normal((1024,), 1.0, 0.02, sid=4)

@@ -33,11 +33,13 @@ def _reference_path(vox, x):
     return vox.global_sum_finish(vox.global_sum_partials(x, 0, rows)).item()
 
 
+@pytest.mark.parametrize("rows", [3000, 0, 1, 839, 841])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_noalloc_global_sum_matches_the_allocating_entry_point(vox, port, dtype):
+def test_noalloc_global_sum_matches_the_allocating_entry_point(vox, port, dtype, rows):
+    """Row counts below, at and above the 840 slots (most slots empty, one row per slot, a wrapped slot) and none."""
     f = _noalloc(vox)
-    rows, n = 3000, 4096
-    x = torch.from_numpy(port.normal((rows, n), sid=200)).cuda().to(dtype)
+    n = 4096
+    x = torch.from_numpy(port.normal((max(rows, 1), n), sid=200)).cuda().to(dtype)[:rows].contiguous()
     dt = F32 if dtype == torch.float32 else BF16
     want = _reference_path(vox, x)
     stream = torch.cuda.current_stream().cuda_stream
@@ -50,10 +52,26 @@ def test_noalloc_global_sum_matches_the_allocating_entry_point(vox, port, dtype)
         assert abs(got - want) <= 1e-5 * float(x.float().abs().sum())
         assert got == want
     # a smaller tensor after a larger one: stale row sums beyond `rows` must not leak into the result
-    y = x[:777].contiguous()
-    out = torch.empty(1, dtype=torch.float64, device="cuda")
-    vox._check(f(y.data_ptr(), 777, n, out.data_ptr(), dt, stream))
-    assert out.item() == _reference_path(vox, y)
+    if rows > 777:
+        y = x[:777].contiguous()
+        out = torch.empty(1, dtype=torch.float64, device="cuda")
+        vox._check(f(y.data_ptr(), 777, n, out.data_ptr(), dt, stream))
+        assert out.item() == _reference_path(vox, y)
+
+
+def test_noalloc_global_sum_odd_rows_unaligned_bf16(vox, port):
+    """An odd row length at an address off the 16-byte grid: the scalar reduction path, on two calls in a row."""
+    f = _noalloc(vox)
+    rows, n = 1001, 333
+    base = torch.from_numpy(port.normal((rows * n + 1,), sid=201)).cuda().to(torch.bfloat16)
+    x = base[1:].view(rows, n)  # 2 bytes past a 16-byte boundary
+    assert x.data_ptr() % 16 != 0
+    want = _reference_path(vox, x)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        out = torch.full((1,), float("nan"), dtype=torch.float64, device="cuda")
+        vox._check(f(x.data_ptr(), rows, n, out.data_ptr(), BF16, stream))
+        assert out.item() == want
 
 
 def test_noalloc_global_sum_rejects_tensors_over_its_limit(vox):

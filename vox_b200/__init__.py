@@ -57,6 +57,7 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_device_count": ([c_p], c_int),
         "vox_cuda_device_cc": ([c_p], c_int),
         "vox_cuda_device_error": ([c_p], c_int),
+        "vox_cuda_test_row_stall": ([c_i64, c_u64], c_int),
         "vox_cuda_fill_philox": ([c_p, c_i64, c_int, c_f, c_f, c_u64, c_u32, c_i64, c_int, c_p], c_int),
         "vox_cuda_rmsnorm": ([c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
         "vox_cuda_layernorm": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_int, c_p], c_int),
@@ -118,6 +119,13 @@ lib = _Lib()
 
 def version() -> str:
     return lib.vox_cuda_version().decode()
+
+
+def device_error() -> int:
+    """Device-side error bits raised since the last call (bit 0: a bounded wait gave up), then cleared."""
+    flags = ctypes.c_uint(0)
+    _check(lib.vox_cuda_device_error(ctypes.byref(flags)))
+    return flags.value
 
 
 def _check(rc: int) -> None:

@@ -6,10 +6,17 @@
 // its row sums and its 840 slot partials; this variant keeps that scratch in one fixed array in the library's own
 // device memory instead, so the caller passes only the tensor and the output.
 //
-// The scratch array below is a static device variable of this translation unit: every GPU that loads the library
-// holds its kNoAllocScratchBytes (about 1 MB) until the process exits. Host code may not use the array's name as a
-// device address (on the host it is only a stand-in symbol); its device address is looked up once per device with
-// cudaGetSymbolAddress, on that device's first call of the entry point, and passed to the kernels.
+// The scratch array below is a static device variable of this translation unit: it lives in the library's device
+// module, so every device on which that module is loaded holds its kNoAllocScratchBytes (about 1 MB) until the
+// process exits. With CUDA's lazy module loading (the default) the module, and so the array, is loaded on a device
+// the first time the library needs it there, at the latest on this entry point's first call on that device. Host code
+// may not use the array's name as a device address (on the host it is only a stand-in symbol); its device address is
+// looked up with cudaGetSymbolAddress, with the device current, on the first call in each CUDA context, and passed to
+// the kernels. That first call may load the module and block, so it is a warm-up: make it outside any real-time path
+// (and before any stream capture) on every device. The address is kept together with the context it belongs to: a
+// call in another context of the device (after cudaDeviceReset) looks it up again, and a failed lookup is not kept.
+#include <cuda.h>
+
 #include <mutex>
 #include <string>
 
@@ -27,11 +34,29 @@ constexpr size_t kNoAllocScratchBytes = kRowSumBytes + kSlotBytes;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-unsigned char *g_scratch_addr[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
-cudaError_t g_scratch_rc[kMaxDevices];
+struct ScratchSlot {
+    unsigned long long ctx_id = 0;  // unique id of the context the address belongs to (cuCtxGetId; never reused)
+    unsigned char *addr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
+std::mutex g_scratch_mu;
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device, with that device current).
+// The driver's cuCtxGetCurrent and cuCtxGetId, looked up once through the runtime (no link-time dependency on
+// libcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+template <class Fn>
+Fn driver_fn(const char *name) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return reinterpret_cast<Fn>(p);
+}
+
+// Device address of g_noalloc_scratch in the current device's current context.
 int scratch_address(unsigned char **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -39,16 +64,33 @@ int scratch_address(unsigned char **out) {
         return set_error(VOX_CUDA_ERR_DEVICE, std::string("vox_cuda_global_sum_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
     }
     if (dev < 0 || dev >= kMaxDevices) return set_error(VOX_CUDA_ERR_UNSUPPORTED, "vox_cuda_global_sum_noalloc: device index too large");
-    std::call_once(g_scratch_once[dev], [dev] {
+    static const CtxGetCurrentFn get = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+    static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+    if (!get || !get_id) return set_error(VOX_CUDA_ERR_DEVICE, "vox_cuda_global_sum_noalloc: cuCtxGetCurrent / cuCtxGetId not available");
+    CUcontext ctx = nullptr;
+    if (get(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+        // no context current on this thread yet: cudaSetDevice makes the device's primary context current (CUDA 12)
+        if (cudaSetDevice(dev) != cudaSuccess || get(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+            cudaGetLastError();
+            return set_error(VOX_CUDA_ERR_DEVICE, "vox_cuda_global_sum_noalloc: no CUDA context on the current device");
+        }
+    }
+    unsigned long long id = 0;
+    if (get_id(ctx, &id) != CUDA_SUCCESS) return set_error(VOX_CUDA_ERR_DEVICE, "vox_cuda_global_sum_noalloc: cuCtxGetId failed");
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    ScratchSlot &slot = g_scratch[dev];
+    if (slot.ctx_id != id || slot.addr == nullptr) {
         void *p = nullptr;
-        g_scratch_rc[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (g_scratch_rc[dev] != cudaSuccess) cudaGetLastError();
-        g_scratch_addr[dev] = static_cast<unsigned char *>(p);
-    });
-    if (g_scratch_rc[dev] != cudaSuccess || g_scratch_addr[dev] == nullptr)
-        return set_error(VOX_CUDA_ERR_DEVICE, std::string("vox_cuda_global_sum_noalloc: cudaGetSymbolAddress: ") +
-                                                  cudaGetErrorString(g_scratch_rc[dev]));
-    *out = g_scratch_addr[dev];
+        const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (rc != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            slot = ScratchSlot{};  // not kept: the next call tries again
+            return set_error(VOX_CUDA_ERR_DEVICE, std::string("vox_cuda_global_sum_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(rc));
+        }
+        slot.ctx_id = id;
+        slot.addr = static_cast<unsigned char *>(p);
+    }
+    *out = slot.addr;
     return VOX_CUDA_OK;
 }
 

@@ -188,13 +188,16 @@ __global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_ke
     };
     // this warp's rows: r0 + warp, r0 + warp + kPipeWarps, ...
     const int64_t first = r0 + warp;
+    const int64_t stall = lane == 0 ? g_stall_row : -1;  // test hook (-1 in normal use)
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
         mbar_init_fence();
 #pragma unroll
-        for (int s = 0; s < STAGES; ++s)
+        for (int s = 0; s < STAGES; ++s) {
+            if (first + s * kPipeWarps == stall) mbar_expect_tx(&bars[s], 16);
             if (first + s * kPipeWarps < r1) issue(first + s * kPipeWarps, bufs + s * stage_bytes, &bars[s]);
+        }
     }
     uint32_t pending = 0;
 #pragma unroll
@@ -228,8 +231,9 @@ __global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_ke
     int s = 0;
     for (int64_t r = first; r < r1; r += kPipeWarps) {
         if (!mbar_wait_warp(&bars[s], (parity >> s) & 1u)) {
+            // give up: every copy of the warp still in flight lands (bounded), the one waited for included
             for (int t = 0; t < STAGES; ++t)
-                if (t != s && ((pending >> t) & 1u)) mbar_wait_warp(&bars[t], (parity >> t) & 1u);
+                if ((pending >> t) & 1u) mbar_wait_warp(&bars[t], (parity >> t) & 1u);
             return;
         }
         parity ^= 1u << s;
@@ -249,6 +253,7 @@ __global__ void __launch_bounds__(kPipeWarps * 32, VPL <= 4 ? 5 : 3) adaln_ac_ke
         if (r_next < r1) {
             if (lane == 0) {
                 fence_proxy_async();
+                if (r_next == stall) mbar_expect_tx(&bars[s], 16);
                 issue(r_next, buf, &bars[s]);
             }
             pending |= 1u << s;
@@ -561,6 +566,156 @@ int reduce_pipe(const void *x, float *out, int64_t rows, int64_t n, cudaStream_t
                                                        "vox_cuda_row_reduce");
 }
 
+// ------------------------------------------------------------------ few rows: one CTA per row
+
+// For fewer rows than a resident wave has warps (BASELINE cfg1: 512 rows of 1024 on 148 SMs), a warp per row leaves
+// the SMs nearly empty and every row's latency serial. Here a CTA takes one row and each thread VPT of its 16-byte
+// vectors, so all loads of the launch are in flight at once; the statistics are folded by warp butterflies and then
+// across the CTA's warps in warp order through shared memory (a fixed order), with the arithmetic of NormOp.
+constexpr int kCtaRowMaxThreads = 1024;
+
+template <int DT>
+__device__ __forceinline__ float cta_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : 0.f;
+    t = warp_sum(t);
+    __syncthreads();  // red is reused by the next fold
+    return t;
+}
+
+template <int DT, int KIND, int VPT>
+__global__ void __launch_bounds__(kCtaRowMaxThreads) norm_cta_kernel(NormArgs a, uint32_t row_bytes) {
+    pdl_enter();
+    constexpr int W = Vec<DT>::N, PW = W / 2;
+    constexpr int ES = DT == VOX_CUDA_F32 ? 4 : 2;
+    __shared__ float red[32];
+    const int64_t r = blockIdx.x;
+    const int nvec = int(a.n / W), t = threadIdx.x, nt = blockDim.x;
+    const char *xr = reinterpret_cast<const char *>(a.x) + r * int64_t(row_bytes);
+    const char *rr = reinterpret_cast<const char *>(a.res) + r * int64_t(row_bytes);
+    float2 xv[VPT][PW];
+    uint4 rres[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int j = t + nt * k;
+        // coherent loads: y (and the adaLN residual) may alias x; each thread writes only the vectors it read
+        unpack2<DT>(j < nvec ? ld_cg(xr + j * 16) : make_uint4(0, 0, 0, 0), xv[k]);
+        if (KIND == kAdaLnGated) rres[k] = j < nvec ? ld_cg(rr + j * 16) : make_uint4(0, 0, 0, 0);
+    }
+    float2 negmean = bc2(0.f), inv2;
+    if (KIND == kRms) {
+        float2 ss = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k)
+#pragma unroll
+            for (int p = 0; p < PW; ++p) ss = add2(ss, mul2(xv[k][p], xv[k][p]));
+        const float sum = cta_sum<DT>(__fadd_rn(ss.x, ss.y), red);
+        inv2 = bc2(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, float(a.n)), a.eps))));
+    } else {
+        float2 sm = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k)
+#pragma unroll
+            for (int p = 0; p < PW; ++p) sm = add2(sm, xv[k][p]);
+        const float meanf = cta_sum<DT>(__fadd_rn(sm.x, sm.y), red) * a.inv_n;
+        negmean = bc2(-meanf);
+        float2 v = bc2(0.f);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            if (t + nt * k < nvec) {
+#pragma unroll
+                for (int p = 0; p < PW; ++p) {
+                    const float2 d = add2(xv[k][p], negmean);
+                    v = fma2(d, d, v);
+                }
+            }
+        }
+        const float var = cta_sum<DT>(__fadd_rn(v.x, v.y), red) * a.inv_n;
+        inv2 = bc2(rsqrtf(var + a.eps));
+    }
+    const float2 one = bc2(1.0f);
+    const float2 nmi = mul2(negmean, inv2);
+    const int64_t batch = (KIND >= kAdaLn) ? int64_t(a.tdiv.div(uint32_t(r))) : 0;
+    char *yr = reinterpret_cast<char *>(a.y) + r * int64_t(row_bytes);
+    const char *scp = reinterpret_cast<const char *>(a.scale) + batch * a.n * ES;
+    const char *shp = reinterpret_cast<const char *>(a.shift) + batch * a.n * ES;
+    const char *gp = reinterpret_cast<const char *>(a.gate) + batch * a.n * ES;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int j = t + nt * k;
+        if (j >= nvec) continue;
+        float2 o[PW];
+        if (KIND <= kLnMod) {
+            float2 wv[PW], bv[PW];
+#pragma unroll
+            for (int q = 0; q < PW; q += 2) {
+                const uint4 wq = a.w ? ld_param(a.w + j * W + 2 * q) : as_u4(make_float4(1.f, 1.f, 1.f, 1.f));
+                const uint4 bq = a.b ? ld_param(a.b + j * W + 2 * q) : make_uint4(0, 0, 0, 0);
+                unpack2<VOX_CUDA_F32>(wq, wv + q);
+                unpack2<VOX_CUDA_F32>(bq, bv + q);
+            }
+#pragma unroll
+            for (int p = 0; p < PW; ++p) {
+                if (KIND == kRms) {
+                    o[p] = mul2(wv[p], mul2(xv[k][p], inv2));  // kernels.cpp:711, CPU rounding
+                } else {
+                    const float2 nrm = fma2(xv[k][p], inv2, nmi);
+                    if (KIND == kLnMod) o[p] = fma2(add2(one, wv[p]), nrm, bv[p]);  // nn.cpp:262
+                    else if (a.w) o[p] = fma2(nrm, wv[p], bv[p]);               // kernels.cpp:722
+                    else o[p] = a.b ? add2(nrm, bv[p]) : nrm;
+                }
+            }
+        } else {
+            float2 sc[PW], sh[PW], gv[PW], rv[PW];
+            unpack2<DT>(ld_param(scp + j * 16), sc);
+            unpack2<DT>(ld_param(shp + j * 16), sh);
+            if (KIND == kAdaLnGated) {
+                unpack2<DT>(ld_param(gp + j * 16), gv);
+                unpack2<DT>(rres[k], rv);
+            }
+#pragma unroll
+            for (int p = 0; p < PW; ++p) {
+                const float2 nrm = fma2(xv[k][p], inv2, nmi);
+                const float2 m = fma2(nrm, add2(one, sc[p]), sh[p]);  // f5.cpp:630
+                o[p] = KIND == kAdaLnGated ? fma2(gv[p], m, rv[p]) : m;  // f5.cpp:674
+            }
+        }
+        st_stream(yr + j * 16, pack2<DT>(o));
+    }
+}
+
+// VOX_CUDA_NORM_CTA: 0 = never take the CTA-per-row path, 1 = always (where it applies); unset = by row count.
+int norm_cta_mode() {
+    static const int m = [] {
+        const char *e = std::getenv("VOX_CUDA_NORM_CTA");
+        return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : -1;
+    }();
+    return m;
+}
+
+template <int DT, int KIND, int VPT>
+int norm_cta_launch(const NormArgs &a, cudaStream_t st, const char *name) {
+    const int64_t nvec = a.n / Vec<DT>::N;
+    const int threads = int(((nvec + VPT - 1) / VPT + 31) / 32 * 32);
+    launch_k(norm_cta_kernel<DT, KIND, VPT>, dim3(uint32_t(a.rows)), threads, 0, st, a, uint32_t(a.n * (DT == VOX_CUDA_F32 ? 4 : 2)));
+    return check_launch(name);
+}
+
+// The CTA-per-row path where it applies (few rows, at most 2048 vectors a row), else kPipeNotApplicable.
+template <int DT, int KIND>
+int norm_cta(const NormArgs &a, cudaStream_t st, const char *name) {
+    const int mode = norm_cta_mode();
+    const int64_t nvec = a.n / Vec<DT>::N;
+    // a warp per row keeps at most rows warps busy: below a quarter of a resident wave of 32-warp SMs, one CTA a row
+    const bool few = a.rows <= int64_t(sm_count()) * 8;
+    if (mode == 0 || (mode < 0 && !few) || nvec > 2 * kCtaRowMaxThreads || a.rows > 2147483647) return kPipeNotApplicable;
+    if (nvec <= kCtaRowMaxThreads) return norm_cta_launch<DT, KIND, 1>(a, st, name);
+    return norm_cta_launch<DT, KIND, 2>(a, st, name);
+}
+
 template <int DT, int KIND, int VPL>
 int norm_pipe_vpl(const NormArgs &a, cudaStream_t st, const char *name) {
     if constexpr (KIND == kAdaLnGated && (DT == VOX_CUDA_F32 ? VPL <= 8 : VPL <= 4)) {  // rows held in registers
@@ -576,6 +731,8 @@ int norm_pipe_vpl(const NormArgs &a, cudaStream_t st, const char *name) {
 
 template <int DT, int KIND>
 int norm_pipe(const NormArgs &a, cudaStream_t st, const char *name) {
+    const int rc = norm_cta<DT, KIND>(a, st, name);
+    if (rc != kPipeNotApplicable) return rc;
     constexpr int W = Vec<DT>::N;
     const int64_t nvec = a.n / W;
     const int vpl = int((nvec + 31) / 32);
@@ -677,6 +834,12 @@ int launch_softmax_pipe(const float *x, float *y, int64_t rows, int64_t n, float
 }  // namespace voxcuda
 
 using namespace voxcuda;
+
+extern "C" int vox_cuda_test_row_stall(int64_t row, uint64_t wait_limit_ns) {
+    VOX_REQUIRE(row >= -1, "vox_cuda_test_row_stall: row must be >= -1");
+    if (set_wait_test_hook(row, wait_limit_ns) != VOX_CUDA_OK) return check_launch("vox_cuda_test_row_stall");
+    return VOX_CUDA_OK;
+}
 
 extern "C" int vox_cuda_device_error(unsigned int *flags) {
     VOX_REQUIRE(flags != nullptr, "vox_cuda_device_error: flags is NULL");

@@ -9,8 +9,8 @@
 // Each copy lands in the shared memory of the issuing CTA only (a plain shared::cluster destination of a CTA that is
 // a cluster of one); no copy is broadcast to other CTAs.
 // Every wait is bounded: a wait that gives up records VOX_CUDA_DEVERR_TIMEOUT in a device flag, waits (bounded
-// again) for the warp's other copies in flight, and the warp stops; vox_cuda_device_error() reads and clears the
-// flag.
+// again) for every copy of the warp still in flight (the one it gave up on included), and the warp stops;
+// vox_cuda_device_error() reads and clears the flag.
 #pragma once
 
 #include "common.cuh"
@@ -23,8 +23,13 @@ namespace voxcuda {
 static __device__ unsigned int g_device_error = 0;
 constexpr unsigned int kDevErrTimeout = 1u;
 // A wait gives up after this much time on the GPU's global timer (ns), read every 32 polls (each try_wait may also
-// suspend the warp for a hardware-chosen time).
+// suspend the warp for a hardware-chosen time). The limit is a device variable of the translation unit so that a test
+// can shorten it (vox_cuda_test_row_stall); every kernel reads it only once its first poll has failed.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+static __device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+// Test hook of the row pipelines: the row whose stage barrier is told to expect 16 bytes more than its copies
+// deliver (every copy still lands, the phase never completes, the wait runs out); -1 = none.
+static __device__ int64_t g_stall_row = -1;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
@@ -58,12 +63,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = *(volatile uint64_t *)&g_wait_limit_ns;
     for (uint32_t i = 1;; ++i) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-        if ((i & 31u) == 0 && __any_sync(0xffffffffu, globaltimer_ns() - t0 > kWaitLimitNs)) break;
+        if ((i & 31u) == 0 && __any_sync(0xffffffffu, globaltimer_ns() - t0 > limit)) break;
     }
     if ((threadIdx.x & 31) == 0) atomicOr(&g_device_error, kDevErrTimeout);
     return false;
+}
+// Raises the transaction count the current phase of `bar` waits for, without an arrival.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
 }
 // Orders this thread's earlier generic-proxy accesses of shared memory before later async-proxy (TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -99,6 +109,7 @@ __global__ void __launch_bounds__(kPipeWarps * 32, Op::kMinBlocks) row_pipe_kern
     const int64_t gw = int64_t(blockIdx.x) * kPipeWarps + warp;
     const int64_t nw = int64_t(gridDim.x) * kPipeWarps;
     if (gw >= rows) return;
+    const int64_t stall = lane == 0 ? g_stall_row : -1;  // test hook (-1 in normal use)
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
@@ -106,6 +117,7 @@ __global__ void __launch_bounds__(kPipeWarps * 32, Op::kMinBlocks) row_pipe_kern
 #pragma unroll
         for (int s = 0; s < STAGES; ++s) {
             const int64_t r = gw + s * nw;
+            if (r == stall) mbar_expect_tx(&bars[s], 16);
             if (r < rows) op.issue(r, bufs + s * stage_bytes, &bars[s]);
         }
     }
@@ -118,9 +130,10 @@ __global__ void __launch_bounds__(kPipeWarps * 32, Op::kMinBlocks) row_pipe_kern
     int s = 0;
     for (int64_t r = gw; r < rows; r += nw) {
         if (!mbar_wait_warp(&bars[s], (parity >> s) & 1u)) {
-            // give up: let the warp's other copies land (bounded) before the CTA's shared memory can be reused
+            // give up: let every copy of the warp still in flight land (bounded), the one waited for included,
+            // before the CTA's shared memory can be reused
             for (int t = 0; t < STAGES; ++t)
-                if (t != s && ((pending >> t) & 1u)) mbar_wait_warp(&bars[t], (parity >> t) & 1u);
+                if ((pending >> t) & 1u) mbar_wait_warp(&bars[t], (parity >> t) & 1u);
             return;
         }
         parity ^= 1u << s;
@@ -134,6 +147,7 @@ __global__ void __launch_bounds__(kPipeWarps * 32, Op::kMinBlocks) row_pipe_kern
             if (r_next < rows) {
                 if (lane == 0) {
                     fence_proxy_async();
+                    if (r_next == stall) mbar_expect_tx(bar, 16);
                     op.issue(r_next, buf, bar);
                 }
                 pending |= 1u << cur;
@@ -158,14 +172,28 @@ int launch_row_pipe(const Op &op, int64_t rows, uint32_t stage_bytes, cudaStream
     return check_launch(name);
 }
 
-// Reads and clears this translation unit's device error flag (host side). VOX_CUDA_OK or VOX_CUDA_ERR_DEVICE.
+// The flag read and cleared in one atomic step on the device (a flag raised by a kernel still running on another
+// stream is either taken now or left set for the next read, never lost).
+static __device__ unsigned int g_device_error_taken = 0;
+static __global__ void take_device_error_kernel() { g_device_error_taken = atomicExch(&g_device_error, 0u); }
+
+// Reads and clears this translation unit's device error flag (host side; the legacy default stream, so it follows
+// the work of every blocking stream). VOX_CUDA_OK or VOX_CUDA_ERR_DEVICE.
 static inline int take_device_error(unsigned int *flags) {
     unsigned int v = 0;
-    const unsigned int zero = 0;
-    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess ||
-        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess)
+    take_device_error_kernel<<<1, 1>>>();
+    if (cudaGetLastError() != cudaSuccess || cudaMemcpyFromSymbol(&v, g_device_error_taken, sizeof(v)) != cudaSuccess)
         return VOX_CUDA_ERR_DEVICE;
     *flags |= v;
+    return VOX_CUDA_OK;
+}
+
+// Test hook (host side): sets this translation unit's wait limit (ns; 0 restores the default) and stalled row.
+static inline int set_wait_test_hook(int64_t stall_row, uint64_t limit_ns) {
+    const uint64_t lim = limit_ns ? limit_ns : kWaitLimitNs;
+    if (cudaMemcpyToSymbol(g_stall_row, &stall_row, sizeof(stall_row)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof(lim)) != cudaSuccess)
+        return VOX_CUDA_ERR_DEVICE;
     return VOX_CUDA_OK;
 }
 

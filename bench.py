@@ -894,6 +894,51 @@ def run_copy_roofline(args) -> None:
                       "results": res}), flush=True)
 
 
+def run_gemm(args) -> None:
+    """The tcgen05 GEMM (vox_cuda_gemm_bf16) alone on the F5-base projections, a prefill-shaped case and a large square
+    case, against torch's bf16 matmul (cuBLAS) on the same operands: CUDA events around back-to-back launches, one
+    GPU. One JSON line."""
+    import torch
+
+    torch.cuda.set_device(0)
+    import vox_b200 as vox
+
+    tpk, tkind = tensor_peak()
+    shapes = [("f5_qkv", 2048, 3072, 1024), ("f5_o", 2048, 1024, 1024), ("f5_ff1", 2048, 2048, 1024), ("f5_ff2", 2048, 1024, 2048),
+              ("prefill_up", 512, 12288, 4096), ("square_8192", 8192, 8192, 8192)]
+    res = {}
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for nm, m, n, k in shapes:
+        x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+        y = torch.empty(m, n, device="cuda")
+        yb = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        fl = 2 * m * n * k
+        reps = max(5, min(200, int(2e-3 / (fl / 1.2e15))))
+
+        def t(fn):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / reps * 1e3
+
+        ours = min(t(lambda: vox.gemm_bf16(x, w, out=y)) for _ in range(3))
+        ours_b = min(t(lambda: vox.gemm_bf16(x, w, out_dtype=torch.bfloat16, out=yb)) for _ in range(3))
+        ref = min(t(lambda: torch.matmul(x, w.t(), out=yb)) for _ in range(3))
+        res[nm] = {"m": m, "n": n, "k": k, "us_f32_out": round(ours, 2), "us_bf16_out": round(ours_b, 2), "cublas_bf16_us": round(ref, 2),
+                   "tflops": round(fl / ours_b / 1e6, 1), "frac_of_tensor_peak": round(fl / ours_b / 1e6 / tpk, 3),
+                   "cublas_tflops": round(fl / ref / 1e6, 1)}
+        del x, w, y, yb
+    print(json.dumps({"metric": METRIC, "mode": "gemm", "unit": "TFLOP/s", "tensor_peak": f"{tpk} bf16 sustained ({tkind})",
+                      "config": {"workload": "tcgen05 bf16 GEMM vs cuBLAS, F5-base and prefill shapes"}, "results": res}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -907,6 +952,7 @@ def main() -> None:
     ap.add_argument("--sweep", action="store_true", help="BASELINE cfg5 size sweep instead of the suite")
     ap.add_argument("--scale", type=int, default=1, help="multiply the rows/heads/batches of cfg1-cfg4 (1 = BASELINE shapes)")
     ap.add_argument("--copy-roofline", action="store_true", help="cfg1-cfg4 ops against a size-matched device copy")
+    ap.add_argument("--gemm", action="store_true", help="the tcgen05 GEMM alone against cuBLAS")
     ap.add_argument("--sweep-lo", type=int, default=20)
     ap.add_argument("--sweep-hi", type=int, default=32)
     args = ap.parse_args()
@@ -918,6 +964,8 @@ def main() -> None:
         run_sweep(args)
     elif args.copy_roofline:
         run_copy_roofline(args)
+    elif args.gemm:
+        run_gemm(args)
     else:
         run_ours(args)
 

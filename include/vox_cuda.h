@@ -260,6 +260,20 @@ VOX_CUDA_API int vox_cuda_qkv_rope(const float *qkv, const float *q_norm_w, cons
 VOX_CUDA_API int vox_cuda_add_rmsnorm(void *h, const void *delta, const float *layer_scale, const float *w, void *xn, int64_t rows,
                                       int64_t n, float eps, int dtype, void *stream);
 
+/* ---------------------------------------------------------------- GEMM on the tensor cores */
+
+/* Activations fused into the GEMM's epilogue. */
+#define VOX_CUDA_GEMM_NONE 0
+#define VOX_CUDA_GEMM_GELU_ERF 1  /* gemmb.comp flag 2: 0.5 v (1 + erf(v / sqrt 2)) */
+#define VOX_CUDA_GEMM_GELU_TANH 2 /* F5's gelu_tanh, f5.cpp:93-96 */
+
+/* y[m][n] = act(x[m][k] . w[n][k]^T + bias[n]): bf16 x and w (row-major, k a multiple of 8, 16-byte aligned), f32
+ * accumulation on the 5th-generation tensor cores, y f32 or bf16 (out_dtype); bias f32 [n] or NULL.
+ * Replaces the GPU GEMM of Vox's F5 / Vocos linear layers, gemm() in gpu_f5.cpp:287-322 running shaders/gemmb.comp:1-99
+ * with its bias (flag 1) and GELU (flag 2) epilogue; the CPU counterpart is vox::matmul with a bias (kernels.cpp:656-706). */
+VOX_CUDA_API int vox_cuda_gemm_bf16(const void *x, const void *w, const float *bias, void *y, int64_t m, int64_t n, int64_t k, int act,
+                                    int out_dtype, void *stream);
+
 /* ---------------------------------------------------------------- quantized GEMV (decode) */
 
 /* y[i][r] = bias[r] + sum_k W[r][k] * x[i][k] for i < m (accumulate != 0: y[i][r] += that), W[r][k] = code *

@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "Tmod", "F5Dit", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "gemm_bf16", "Tmod", "F5Dit", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -80,6 +80,7 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_rope_table": ([c_p, c_i64, c_i64, c_i64, c_p, c_p], c_int),
         "vox_cuda_qkv_rope": ([c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f, c_p], c_int),
         "vox_cuda_add_rmsnorm": ([c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
+        "vox_cuda_gemm_bf16": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_int, c_p], c_int),
         "vox_cuda_gemv_q8": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
         "vox_cuda_gemv_q4": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
         "vox_cuda_tmod_open": ([ctypes.c_char_p, c_p], c_int),
@@ -444,6 +445,28 @@ def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: floa
     _same(h, out, "h", "out")
     _check(lib.vox_cuda_add_rmsnorm(h.data_ptr(), delta.data_ptr(), _f32(layer_scale, "layer_scale"), _f32(w, "w"),
                                     out.data_ptr(), h.numel() // n, n, eps, dt, _stream(h)))
+    return out
+
+
+# ------------------------------------------------------------------ GEMM on the tensor cores
+
+GEMM_NONE, GEMM_GELU_ERF, GEMM_GELU_TANH = 0, 1, 2
+
+
+def gemm_bf16(x: torch.Tensor, w: torch.Tensor, bias=None, act: int = GEMM_NONE, out_dtype=torch.float32, out=None) -> torch.Tensor:
+    """y [m][n] = act(x [m][k] . w [n][k]^T + bias [n]) on the tensor cores: bf16 x and w, f32 accumulation, y f32 or
+    bf16 (the GEMM of gpu_f5.cpp:287-322 / gemmb.comp with its bias and GELU flags)."""
+    for t, nm in ((x, "x"), (w, "w")):
+        _dev(t, nm)
+        if t.dtype != torch.bfloat16:
+            raise VoxCudaError(-6, f"{nm} must be bfloat16")
+    k = x.shape[-1]
+    if w.dim() != 2 or w.shape[1] != k:
+        raise VoxCudaError(-6, "w must be [n][k] with x's k")
+    m, n = x.numel() // k, w.shape[0]
+    od = F32 if out_dtype == torch.float32 else BF16
+    out = torch.empty(*x.shape[:-1], n, dtype=out_dtype, device=x.device) if out is None else out
+    _check(lib.vox_cuda_gemm_bf16(x.data_ptr(), w.data_ptr(), _f32(bias, "bias"), out.data_ptr(), m, n, k, act, od, _stream(x)))
     return out
 
 

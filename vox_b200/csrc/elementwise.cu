@@ -47,24 +47,6 @@ constexpr int kVecCtasPerSm = 3;
 __device__ __forceinline__ float silu_f(float x) {  // x / (1 + exp(-x)), kernels.hpp:105 (2-ulp division)
     return __fdividef(x, __fadd_rn(1.0f, expf(-x)));
 }
-// GELU, erf form (kernels.hpp:106, nn.cpp:87-96): x * Phi(x), Phi from the normal tail of Abramowitz & Stegun 26.2.17,
-// two elements per call.
-__device__ __forceinline__ float2 gelu_erf_f2(float2 x) {
-    const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
-    const float2 d = fma2(bc2(0.2316419f), a, bc2(1.0f));
-    const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-    // b_k / sqrt(2 pi) of A&S 26.2.17
-    float2 p = fma2(bc2(0.530702714f), t, bc2(-0.726576013f));  // 1.330274429, -1.821255978 (/ sqrt(2 pi))
-    p = fma2(p, t, bc2(0.710706871f));                            // 1.781477937
-    p = fma2(p, t, bc2(-0.142248368f));                           // -0.356563782
-    p = fma2(p, t, bc2(0.127414796f));                            // 0.319381530
-    p = mul2(p, t);
-    const float2 g = mul2(mul2(a, a), bc2(-0.72134752f));         // exp(-a^2 / 2) = 2^(-a^2 log2(e) / 2)
-    const float2 xq = mul2(x, mul2(make_float2(ex2_approx(g.x), ex2_approx(g.y)), p));  // x * Q(|x|)
-    const float2 hi = fma2(xq, bc2(-1.0f), x);                    // x - x Q(|x|)
-    return make_float2(x.x >= 0.f ? hi.x : xq.x, x.y >= 0.f ? hi.y : xq.y);
-}
-
 // sin^2(theta), two elements per call: Cody-Waite reduction by pi (pi = PI1 + PI2 + PI3, PI1 = float(pi)), then
 // u * P(u), u = r^2.
 __device__ __forceinline__ float2 sin2_f2(float2 theta) {

@@ -23,7 +23,8 @@
 
 #include "common.cuh"
 #include "sfu.cuh"
-#include "tma.cuh"
+#include "gemm.cuh"
+#include "tc.cuh"
 #include "rows.cuh"
 
 namespace voxcuda {
@@ -230,36 +231,10 @@ constexpr uint32_t kTcKV = 64 * 128;     // K and V tiles, [64][64] bf16
 constexpr uint32_t kTcCols = 128;        // TMEM columns: S 0..63, P V 64..127
 constexpr size_t kTcSmem = 2 * size_t(kTcQ) + 4 * size_t(kTcKV) + 1024 + 128;  // Q, P, K[2], V[2]; alignment; barriers
 
-// Shared-memory matrix descriptor, 128-byte swizzle (layout 2), descriptor version 1: start, leading and stride byte
-// offsets in 16-byte units.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) | (uint64_t((sbo >> 4) & 0x3FFFu) << 32) |
-           (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-// Instruction descriptors (kind::f16): f32 accumulator (bit 4), bf16 A (bit 7) and B (bit 10), B major-ness (bit 16),
-// N / 8 (bits 17..22), M / 16 (bits 24..28).
-constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t kIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                 : "r"(taddr)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Instruction descriptors of the two products (M 128, N 64): S = Q K^T with both operands K-major, and P V with V
+// MN-major.
+constexpr uint32_t kIdescS = umma_idesc_bf16(128, 64);
+constexpr uint32_t kIdescO = umma_idesc_bf16(128, 64, true);
 
 // Stages rows [row0, row0 + ROWS) of a head's 64 columns (global row stride ld bf16) into a swizzled tile; rows at
 // or past n are zero-filled. 8 chunks a row, ROWS / 16 per thread.
@@ -293,8 +268,7 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
         mbar_init_fence();
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)), "r"(kTcCols) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tmem_alloc(tslot, kTcCols);
     }
     tc_stage<kTcRows>(sQ, Q, q0, n, ld_in);
     tc_stage<kTcKeys>(sK, K, 0, n, ld_in);
@@ -427,6 +401,36 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
 // ------------------------------------------------------------------ bf16 pipeline helpers
 
 // dst = bf16(src) (RN), n / 2 pairs (weights, converted once at plan creation).
+// xc [R][M + C] (bf16, RN) = [x [R][M] | cond [R][C]] (f32): the input of the in_proj GEMM; one element a thread.
+__global__ void __launch_bounds__(256) f5_concat_bf16_kernel(const float *x, const float *cond, __nv_bfloat16 *xc, uint32_t n,
+                                                             uint32_t M, uint32_t C) {
+    pdl_enter();
+    const uint32_t W = M + C;
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+        const uint32_t r = e / W, c = e - r * W;
+        xc[e] = __float2bfloat16_rn(c < M ? x[size_t(r) * M + c] : cond[size_t(r) * C + (c - M)]);
+    }
+}
+
+// y_l[o] = W_l[o] . x + b_l[o] for the L matrices W_l [rows][cols] (f32) of a pointer table (blockIdx.y = l): the ada
+// vectors of every block from one time embedding (f5.cpp:681-682, Vox's per-block matvec). One warp per output row,
+// 16-byte loads, the lanes' partial sums folded by the xor butterfly; cols % 4 == 0.
+__global__ void __launch_bounds__(256) f5_gemv_f32_kernel(const float *const *W, const float *x, const float *bias, float *y,
+                                                          uint32_t rows, uint32_t cols) {
+    pdl_enter();
+    const uint32_t l = blockIdx.y, o = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (o >= rows) return;
+    const float4 *w = reinterpret_cast<const float4 *>(W[l] + size_t(o) * cols);
+    const float4 *xv = reinterpret_cast<const float4 *>(x);
+    float acc = 0.f;
+    for (uint32_t c = lane; c < cols / 4; c += 32) {
+        const float4 a = as_f4(ld_stream(w + c)), b = xv[c];
+        acc = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc))));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[size_t(l) * rows + o] = acc + (bias ? bias[size_t(l) * rows + o] : 0.f);
+}
+
 __global__ void __launch_bounds__(256) f5_to_bf16_kernel(const float2 *src, uint32_t *dst, size_t pairs) {
     pdl_enter();
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs; i += size_t(gridDim.x) * blockDim.x) {
@@ -544,6 +548,12 @@ struct F5Plan {
     // f32 copies of every bias (zeros where the description has none), made at create: [depth][6D], [depth][3 inner],
     // [depth][D] (o), [depth][F] (ff1), [depth][D] (ff2), [2D] (norm_out), [out_dim] (proj_out)
     float *b_ada = nullptr, *b_qkv = nullptr, *b_o = nullptr, *b_ff1 = nullptr, *b_ff2 = nullptr, *b_fin = nullptr, *b_proj = nullptr;
+    // tcgen05 GEMMs of the bf16 path (every K a multiple of 8): built once at create, replayed by the graph; the
+    // in_proj input [x | cond] and weights in bf16
+    bool tc = false;
+    std::vector<GemmPlan> g_qkv, g_o, g_ff1, g_ff2;
+    GemmPlan g_proj, g_in, g_conv1, g_conv2;
+    __nv_bfloat16 *xc_b = nullptr, *w_in = nullptr;
     // input embedding (in_proj given): x [R][out_dim], cond [R][in_dim - out_dim], im2col scratch, reordered conv weights
     bool embed = false;
     float *xin = nullptr, *cond = nullptr, *col = nullptr, *ctmp = nullptr, *w1r = nullptr, *w2r = nullptr;
@@ -605,7 +615,7 @@ constexpr int kPosGroups = 16, kPosK = 31;  // F5's position convolutions (f5.cp
 // conv of src [R][D] (B sequences of T frames) into dst [R][D]: im2col, then per sequence one GEMM batched over the
 // groups (col [T][K cig] of group g times the group's reordered weights [cog][K cig], into columns g cog of dst); in
 // the bf16 mode columns and weights are bf16 (tensor cores, f32 accumulation).
-int conv_pos(F5Plan &p, const float *src, const void *wr, float *dst, cudaStream_t st) {
+int conv_pos(F5Plan &p, const float *src, const void *wr, float *dst, const GemmPlan *gp, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const uint32_t T = uint32_t(d.frames), D = uint32_t(d.dim), cig = D / kPosGroups, J = kPosK * cig;
     const uint32_t all = uint32_t(d.batch) * kPosGroups * T * J;
@@ -622,6 +632,7 @@ int conv_pos(F5Plan &p, const float *src, const void *wr, float *dst, cudaStream
         else launch_k(f5_im2col_kernel<1, false>, grid_for(all, 256, 4), 256, 0, st, src, (void *)p.col, all, T, D, G, KK);
     }
     F5_TRY(check_launch("vox_cuda_f5 im2col"));
+    if (gp) return gemm_run(*gp, st, "vox_cuda_f5 position convolution");  // all sequences and groups in one launch
     const float one = 1.0f, zero = 0.0f;
     const cudaDataType_t in_t = p.bf16 ? CUDA_R_16BF : CUDA_R_32F;
     const size_t esz = p.bf16 ? 2 : 4;
@@ -641,18 +652,26 @@ int record_embed(F5Plan &p, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const int64_t R = p.R, D = d.dim, M = d.out_dim, C = d.in_dim - d.out_dim;
     const float one = 1.0f, zero = 0.0f;
-    F5_TRY(blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(D), int(R), int(M), &one, d.in_proj, CUDA_R_32F, d.in_dim,
-                                   p.xin, CUDA_R_32F, int(M), &zero, p.h, CUDA_R_32F, int(D), p.compute, CUBLAS_GEMM_DEFAULT),
-                      "in_proj (x)"));
-    F5_TRY(blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(D), int(R), int(C), &one, d.in_proj + M, CUDA_R_32F, d.in_dim,
-                                   p.cond, CUDA_R_32F, int(C), &one, p.h, CUDA_R_32F, int(D), p.compute, CUBLAS_GEMM_DEFAULT),
-                      "in_proj (cond)"));
-    if (d.in_proj_b) F5_TRY(vox_cuda_bias_add(p.h, d.in_proj_b, R, D, VOX_CUDA_F32, st));
+    if (p.tc) {  // [x | cond] in bf16, then one GEMM with the bias in its epilogue
+        const uint32_t ne = uint32_t(R * (M + C));
+        launch_k(f5_concat_bf16_kernel, grid_for(ne, 256, 4), 256, 0, st, (const float *)p.xin, (const float *)p.cond, p.xc_b, ne,
+                 uint32_t(M), uint32_t(C));
+        F5_TRY(check_launch("vox_cuda_f5 in_proj input"));
+        F5_TRY(gemm_run(p.g_in, st, "vox_cuda_f5 in_proj"));
+    } else {
+        F5_TRY(blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(D), int(R), int(M), &one, d.in_proj, CUDA_R_32F, d.in_dim,
+                                       p.xin, CUDA_R_32F, int(M), &zero, p.h, CUDA_R_32F, int(D), p.compute, CUBLAS_GEMM_DEFAULT),
+                          "in_proj (x)"));
+        F5_TRY(blas_check(cublasGemmEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(D), int(R), int(C), &one, d.in_proj + M, CUDA_R_32F, d.in_dim,
+                                       p.cond, CUDA_R_32F, int(C), &one, p.h, CUDA_R_32F, int(D), p.compute, CUBLAS_GEMM_DEFAULT),
+                          "in_proj (cond)"));
+        if (d.in_proj_b) F5_TRY(vox_cuda_bias_add(p.h, d.in_proj_b, R, D, VOX_CUDA_F32, st));
+    }
     const uint32_t n = uint32_t(R * D);
-    F5_TRY(conv_pos(p, p.h, p.w1r, p.ctmp, st));
+    F5_TRY(conv_pos(p, p.h, p.w1r, p.ctmp, p.tc ? &p.g_conv1 : nullptr, st));
     launch_k(f5_bias_mish_kernel, grid_for(n, 256, 4), 256, 0, st, p.ctmp, d.pos1_b, (float *)nullptr, n, uint32_t(D));
     F5_TRY(check_launch("vox_cuda_f5 mish"));
-    F5_TRY(conv_pos(p, p.ctmp, p.w2r, p.o, st));
+    F5_TRY(conv_pos(p, p.ctmp, p.w2r, p.o, p.tc ? &p.g_conv2 : nullptr, st));
     launch_k(f5_bias_mish_kernel, grid_for(n, 256, 4), 256, 0, st, p.o, d.pos2_b, p.h, n, uint32_t(D));
     return check_launch("vox_cuda_f5 mish");
 }
@@ -728,16 +747,15 @@ int resmod(F5Plan &p, const float *delta, const float *dbias, const float *gate,
 int record_bf16(F5Plan &p, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const int64_t R = p.R, D = d.dim, IN = p.inner, FF = p.ff, L = d.depth;
-    const float one = 1.0f, zero = 0.0f;
     if (p.embed) F5_TRY(record_embed(p, st));
-    const void *const *pp = p.ada_ptrs;
-    F5_TRY(blas_check(cublasGemmBatchedEx(p.blas, CUBLAS_OP_T, CUBLAS_OP_N, int(6 * D), 1, int(D), &one, pp, CUDA_R_32F, int(D),
-                                          pp + L, CUDA_R_32F, int(D), &zero, (void *const *)(pp + 2 * L), CUDA_R_32F, int(6 * D),
-                                          int(L), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
-                      "ada (batched)"));
-    F5_TRY(vox_cuda_add(p.ada_all, p.b_ada, p.ada_all, L * 6 * D, VOX_CUDA_F32, st));
-    F5_TRY(gemm_xwt(p, p.ts, d.norm_out, p.fin, 1, 2 * D, D));  // fin = [scale, shift] (f5.cpp:720-722)
-    F5_TRY(vox_cuda_add(p.fin, p.b_fin, p.fin, 2 * D, VOX_CUDA_F32, st));
+    // every block's ada vectors (f32 weights, bias added), then fin = [scale, shift] (f5.cpp:720-722)
+    const float *const *wt = reinterpret_cast<const float *const *>(p.ada_ptrs);
+    launch_k(f5_gemv_f32_kernel, dim3(unsigned((6 * D + 7) / 8), unsigned(L)), 256, 0, st, wt, (const float *)p.ts, (const float *)p.b_ada,
+             p.ada_all, uint32_t(6 * D), uint32_t(D));
+    F5_TRY(check_launch("vox_cuda_f5 ada"));
+    launch_k(f5_gemv_f32_kernel, dim3(unsigned((2 * D + 7) / 8), 1u), 256, 0, st, wt + 3 * L, (const float *)p.ts, (const float *)p.b_fin,
+             p.fin, uint32_t(2 * D), uint32_t(D));
+    F5_TRY(check_launch("vox_cuda_f5 norm_out"));
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
     const uint32_t qkv_octs = uint32_t(R * 3 * IN / 8), ff_octs = uint32_t(R * FF / 8);
     const dim3 fgt(unsigned((d.frames + kTcRows - 1) / kTcRows), unsigned(d.heads), unsigned(d.batch));
@@ -747,21 +765,31 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
     F5_TRY(resmod(p, nullptr, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
     for (int64_t l = 0; l < L; ++l) {
         const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
-        F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv_b, CUDA_R_16BF, R, 3 * IN, D));
-        launch_k(f5_qkv_bias_rope_kernel, grid_for(qkv_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.qkv_b),
-                 (const float *)(p.b_qkv + size_t(l) * 3 * IN), (const float2 *)p.cs, qkv_octs, uint32_t(d.frames),
-                 uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
-        F5_TRY(check_launch("vox_cuda_f5 bias/rope (bf16)"));
+        if (p.tc) {  // bias and RoPE in the GEMM's epilogue
+            F5_TRY(gemm_run(p.g_qkv[size_t(l)], st, "vox_cuda_f5 q|k|v"));
+        } else {
+            F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv_b, CUDA_R_16BF, R, 3 * IN, D));
+            launch_k(f5_qkv_bias_rope_kernel, grid_for(qkv_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.qkv_b),
+                     (const float *)(p.b_qkv + size_t(l) * 3 * IN), (const float2 *)p.cs, qkv_octs, uint32_t(d.frames),
+                     uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
+            F5_TRY(check_launch("vox_cuda_f5 bias/rope (bf16)"));
+        }
         launch_k(f5_flash_tc_kernel, fgt, kTcThreads, kTcSmem, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
                  (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (__nv_bfloat16 *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
         F5_TRY(check_launch("vox_cuda_f5 attention"));
-        F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
+        if (p.tc) F5_TRY(gemm_run(p.g_o[size_t(l)], st, "vox_cuda_f5 o"));
+        else F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
         F5_TRY(resmod(p, p.o, p.b_o + l * D, A + 2 * D, A + 4 * D, A + 3 * D, st));
-        F5_TRY(gemm_bf16(p, p.nrm_b, p.w_ff1 + size_t(l) * FF * D, p.ff_b, CUDA_R_16BF, R, FF, D));
-        launch_k(f5_bias_gelu_kernel, grid_for(ff_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.ff_b),
-                 (const float *)(p.b_ff1 + l * FF), ff_octs, uint32_t(FF));
-        F5_TRY(check_launch("vox_cuda_f5 bias/gelu (bf16)"));
-        F5_TRY(gemm_bf16(p, p.ff_b, p.w_ff2 + size_t(l) * D * FF, p.o, CUDA_R_32F, R, D, FF));
+        if (p.tc) {  // bias and GELU-tanh in the ff1 GEMM's epilogue
+            F5_TRY(gemm_run(p.g_ff1[size_t(l)], st, "vox_cuda_f5 ff1"));
+            F5_TRY(gemm_run(p.g_ff2[size_t(l)], st, "vox_cuda_f5 ff2"));
+        } else {
+            F5_TRY(gemm_bf16(p, p.nrm_b, p.w_ff1 + size_t(l) * FF * D, p.ff_b, CUDA_R_16BF, R, FF, D));
+            launch_k(f5_bias_gelu_kernel, grid_for(ff_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.ff_b),
+                     (const float *)(p.b_ff1 + l * FF), ff_octs, uint32_t(FF));
+            F5_TRY(check_launch("vox_cuda_f5 bias/gelu (bf16)"));
+            F5_TRY(gemm_bf16(p, p.ff_b, p.w_ff2 + size_t(l) * D * FF, p.o, CUDA_R_32F, R, D, FF));
+        }
         if (l + 1 < L) {
             const float *An = A + 6 * D;
             F5_TRY(resmod(p, p.o, p.b_ff2 + l * D, A + 5 * D, An + D, An, st));
@@ -769,6 +797,7 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
             F5_TRY(resmod(p, p.o, p.b_ff2 + l * D, A + 5 * D, p.fin, p.fin + D, st));
         }
     }
+    if (p.tc) return gemm_run(p.g_proj, st, "vox_cuda_f5 proj_out");
     F5_TRY(gemm_bf16(p, p.nrm_b, p.w_proj, p.out, CUDA_R_32F, R, d.out_dim, D));
     return vox_cuda_bias_add(p.out, p.b_proj, R, d.out_dim, VOX_CUDA_F32, st);
 }
@@ -784,7 +813,7 @@ void release(F5Plan *p) {
                     (void *)p->cs, (void *)p->qkv_b, (void *)p->ada_all, (void *)p->nrm_b, (void *)p->at_b, (void *)p->ff_b, (void *)p->w_qkv, (void *)p->w_o, (void *)p->w_ff1,
                     (void *)p->w_ff2, (void *)p->w_proj, (void *)p->ada_ptrs, (void *)p->b_ada, (void *)p->b_qkv, (void *)p->b_o,
                     (void *)p->b_ff1, (void *)p->b_ff2, (void *)p->b_fin, (void *)p->b_proj, (void *)p->xin, (void *)p->cond,
-                    (void *)p->col, (void *)p->ctmp, (void *)p->w1r, (void *)p->w2r})
+                    (void *)p->col, (void *)p->ctmp, (void *)p->w1r, (void *)p->w2r, (void *)p->xc_b, (void *)p->w_in})
         if (b) cudaFree(b);
     if (p->cap) cudaStreamDestroy(p->cap);
     delete p;
@@ -805,6 +834,46 @@ int to_bf16(const float *src, __nv_bfloat16 *dst, size_t n, cudaStream_t st) {
     return check_launch("vox_cuda_f5_create (weights to bf16)");
 }
 
+// The tcgen05 GEMMs of the bf16 step, on the plan's own buffers (their tensor maps encode those addresses).
+int build_gemms(F5Plan &p) {
+    const vox_cuda_f5_desc &d = p.d;
+    const int R = int(p.R), D = d.dim, IN = int(p.inner), FF = int(p.ff), L = d.depth;
+    const char *nm = "vox_cuda_f5_create (GEMMs)";
+    auto plan = [&](const void *x, int64_t ldx, const void *w, int64_t ldw, int N, int K, void *y, int64_t ldy, const float *bias, int epi,
+                    GemmPlan &gp) {
+        GemmArgs a;
+        a.M = R, a.N = N, a.K = K, a.y = y, a.ldy = ldy, a.bias = bias;
+        if (epi == kEpiQkvRope) {
+            a.cs = p.cs, a.frames = d.frames, a.rope_heads = d.pe_attn_head > 0 ? d.pe_attn_head : d.heads, a.hd = d.dim_head, a.inner = IN;
+        }
+        return gemm_plan(x, ldx, w, ldw, a, epi, gp, nm);
+    };
+    p.g_qkv.resize(size_t(L)), p.g_o.resize(size_t(L)), p.g_ff1.resize(size_t(L)), p.g_ff2.resize(size_t(L));
+    for (int l = 0; l < L; ++l) {
+        const size_t ls = size_t(l);
+        F5_TRY(plan(p.nrm_b, D, p.w_qkv + ls * 3 * IN * D, D, 3 * IN, D, p.qkv_b, 3 * IN, p.b_qkv + ls * 3 * IN, kEpiQkvRope, p.g_qkv[ls]));
+        F5_TRY(plan(p.at_b, IN, p.w_o + ls * D * IN, IN, D, IN, p.o, D, nullptr, kEpiF32, p.g_o[ls]));
+        F5_TRY(plan(p.nrm_b, D, p.w_ff1 + ls * FF * D, D, FF, D, p.ff_b, FF, p.b_ff1 + ls * FF, kEpiGeluTanh, p.g_ff1[ls]));
+        F5_TRY(plan(p.ff_b, FF, p.w_ff2 + ls * D * FF, FF, D, FF, p.o, D, nullptr, kEpiF32, p.g_ff2[ls]));
+    }
+    F5_TRY(plan(p.nrm_b, D, p.w_proj, D, d.out_dim, D, p.out, d.out_dim, p.b_proj, kEpiF32, p.g_proj));
+    if (p.embed) {
+        F5_TRY(plan(p.xc_b, d.in_dim, p.w_in, d.in_dim, D, d.in_dim, p.h, D, d.in_proj_b, kEpiF32, p.g_in));
+        // position convolutions: x planes [batch][group] of the im2col [T][J], W planes [group][cig][J], y columns g cig
+        const int cig = D / kPosGroups, J = kPosK * cig;
+        const void *wrs[2] = {p.w1r, p.w2r};
+        float *dsts[2] = {p.ctmp, p.o};
+        GemmPlan *gps[2] = {&p.g_conv1, &p.g_conv2};
+        for (int i = 0; i < 2; ++i) {
+            GemmArgs a;
+            a.M = d.frames, a.N = cig, a.K = J, a.batches = d.batch, a.groups = kPosGroups;
+            a.y = dsts[i], a.ldy = D, a.y_bstride = int64_t(d.frames) * D, a.y_gstride = cig;
+            F5_TRY(gemm_plan(p.col, J, wrs[i], J, a, kEpiF32, *gps[i], nm));
+        }
+    }
+    return VOX_CUDA_OK;
+}
+
 int build(F5Plan &p, cudaStream_t user) {
     const vox_cuda_f5_desc &d = p.d;
     const size_t R = size_t(p.R), D = size_t(d.dim), IN = size_t(p.inner), FF = size_t(p.ff), N = size_t(d.frames), L = size_t(d.depth);
@@ -815,7 +884,12 @@ int build(F5Plan &p, cudaStream_t user) {
     F5_TRY(alloc(&p.o, R * D, "o"));
     F5_TRY(alloc(&p.fin, 2 * D, "fin"));
     F5_TRY(alloc(&p.cs, N * size_t(d.dim_head / 2), "rope table"));
-    F5_TRY(alloc(reinterpret_cast<uint8_t **>(&p.ws), kBlasWorkspace, "cuBLAS workspace"));
+    p.embed = d.in_proj != nullptr;
+    {
+        const int64_t cig = d.dim / kPosGroups;
+        p.tc = p.bf16 && D % 8 == 0 && IN % 32 == 0 && FF % 8 == 0 && d.dim_head % 32 == 0 &&
+               (!p.embed || (d.in_dim % 8 == 0 && d.dim % kPosGroups == 0 && cig % 8 == 0));
+    }
     if (p.bf16) {
         F5_TRY(alloc(&p.qkv_b, R * 3 * IN, "q|k|v (bf16)"));
         F5_TRY(alloc(&p.ada_all, L * 6 * D, "ada"));
@@ -827,7 +901,7 @@ int build(F5Plan &p, cudaStream_t user) {
         F5_TRY(alloc(&p.w_ff1, L * FF * D, "ff1 weights (bf16)"));
         F5_TRY(alloc(&p.w_ff2, L * D * FF, "ff2 weights (bf16)"));
         F5_TRY(alloc(&p.w_proj, size_t(d.out_dim) * D, "proj_out weights (bf16)"));
-        F5_TRY(alloc(&p.ada_ptrs, 3 * L, "ada pointers"));
+        F5_TRY(alloc(&p.ada_ptrs, 3 * L + 1, "ada pointers"));
         for (size_t l = 0; l < L; ++l) {
             const vox_cuda_f5_block_weights &B = p.blocks[l];
             F5_TRY(to_bf16(B.q, p.w_qkv + l * 3 * IN * D, IN * D, user));
@@ -861,12 +935,13 @@ int build(F5Plan &p, cudaStream_t user) {
         }
         F5_TRY(snap(p.b_fin, d.norm_out_b, 2 * D));
         F5_TRY(snap(p.b_proj, d.proj_out_b, size_t(d.out_dim)));
-        std::vector<const void *> ptrs(3 * L);
+        std::vector<const void *> ptrs(3 * L + 1);
         for (size_t l = 0; l < L; ++l) {
             ptrs[l] = p.blocks[l].ada;
             ptrs[L + l] = p.ts;
             ptrs[2 * L + l] = p.ada_all + l * 6 * D;
         }
+        ptrs[3 * L] = d.norm_out;
         if (cudaMemcpy(p.ada_ptrs, ptrs.data(), ptrs.size() * sizeof(void *), cudaMemcpyHostToDevice) != cudaSuccess)
             return check_launch("vox_cuda_f5_create");
     } else {
@@ -879,9 +954,13 @@ int build(F5Plan &p, cudaStream_t user) {
         F5_TRY(alloc(&p.s, size_t(d.heads) * N * N, "scores"));
         F5_TRY(alloc(&p.ada, 6 * D, "ada"));
     }
-    p.embed = d.in_proj != nullptr;
     if (p.embed) {
         const size_t cig = D / kPosGroups, J = size_t(kPosK) * cig, nw = D * J;
+        if (p.tc) {
+            F5_TRY(alloc(&p.xc_b, R * size_t(d.in_dim), "in_proj input (bf16)"));
+            F5_TRY(alloc(&p.w_in, D * size_t(d.in_dim), "in_proj weights (bf16)"));
+            F5_TRY(to_bf16(d.in_proj, p.w_in, D * size_t(d.in_dim), user));
+        }
         F5_TRY(alloc(&p.xin, R * size_t(d.out_dim), "x"));
         F5_TRY(alloc(&p.cond, R * size_t(d.in_dim - d.out_dim), "cond"));
         F5_TRY(alloc(&p.col, size_t(d.batch) * kPosGroups * N * J, "im2col"));
@@ -901,6 +980,7 @@ int build(F5Plan &p, cudaStream_t user) {
             F5_TRY(check_launch("vox_cuda_f5_create (conv weights)"));
         }
     }
+    if (p.tc) F5_TRY(build_gemms(p));
     // RoPE table as the CPU builds it (f5.cpp:529-541): inv = float(1 / 10000^(2j/hd)) in double, angle = float(i) * inv
     // in float, cos/sin of the float angle.
     const int half = d.dim_head / 2;
@@ -915,15 +995,18 @@ int build(F5Plan &p, cudaStream_t user) {
     if (cudaMemcpy(p.cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess) return check_launch("vox_cuda_f5_create");
     if (cudaMemsetAsync(p.h, 0, R * D * 4, user) != cudaSuccess || cudaMemsetAsync(p.ts, 0, D * 4, user) != cudaSuccess)
         return check_launch("vox_cuda_f5_create");
-    F5_TRY(blas_check(cublasCreate(&p.blas), "create"));
-    F5_TRY(blas_check(cublasSetMathMode(p.blas, d.math == VOX_CUDA_F5_MATH_F32 ? CUBLAS_PEDANTIC_MATH : CUBLAS_DEFAULT_MATH), "math mode"));
-    p.compute = d.math == VOX_CUDA_F5_MATH_TF32   ? CUBLAS_COMPUTE_32F_FAST_TF32
-                : d.math == VOX_CUDA_F5_MATH_BF16 ? CUBLAS_COMPUTE_32F_FAST_16BF
-                                                  : CUBLAS_COMPUTE_32F_PEDANTIC;
     if (cudaStreamCreateWithFlags(&p.cap, cudaStreamNonBlocking) != cudaSuccess) return check_launch("vox_cuda_f5_create");
-    // stream and workspace set once, outside the capture (no cuBLAS allocation may happen while capturing)
-    F5_TRY(blas_check(cublasSetStream(p.blas, p.cap), "set stream"));
-    F5_TRY(blas_check(cublasSetWorkspace(p.blas, p.ws, kBlasWorkspace), "set workspace"));
+    if (!p.tc) {  // cuBLAS only where a GEMM of the step is not on this library's tcgen05 kernel
+        F5_TRY(alloc(reinterpret_cast<uint8_t **>(&p.ws), kBlasWorkspace, "cuBLAS workspace"));
+        F5_TRY(blas_check(cublasCreate(&p.blas), "create"));
+        F5_TRY(blas_check(cublasSetMathMode(p.blas, d.math == VOX_CUDA_F5_MATH_F32 ? CUBLAS_PEDANTIC_MATH : CUBLAS_DEFAULT_MATH), "math mode"));
+        p.compute = d.math == VOX_CUDA_F5_MATH_TF32   ? CUBLAS_COMPUTE_32F_FAST_TF32
+                    : d.math == VOX_CUDA_F5_MATH_BF16 ? CUBLAS_COMPUTE_32F_FAST_16BF
+                                                      : CUBLAS_COMPUTE_32F_PEDANTIC;
+        // stream and workspace set once, outside the capture (no cuBLAS allocation may happen while capturing)
+        F5_TRY(blas_check(cublasSetStream(p.blas, p.cap), "set stream"));
+        F5_TRY(blas_check(cublasSetWorkspace(p.blas, p.ws, kBlasWorkspace), "set workspace"));
+    }
     // the capture stream starts after the caller's work so far (weight conversion, the table, the zeroed inputs)
     cudaEvent_t ev = nullptr;
     if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return check_launch("vox_cuda_f5_create");

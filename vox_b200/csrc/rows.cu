@@ -18,6 +18,7 @@
 
 #include <cstdlib>
 
+#include "gemm.cuh"
 #include "rows.cuh"
 #include "tma.cuh"
 #include "sfu.cuh"
@@ -844,7 +845,8 @@ extern "C" int vox_cuda_test_row_stall(int64_t row, uint64_t wait_limit_ns) {
 extern "C" int vox_cuda_device_error(unsigned int *flags) {
     VOX_REQUIRE(flags != nullptr, "vox_cuda_device_error: flags is NULL");
     unsigned int v = 0;
-    if (take_device_error(&v) != VOX_CUDA_OK || gemv_take_device_error(&v) != VOX_CUDA_OK || f5_take_device_error(&v) != VOX_CUDA_OK) {
+    if (take_device_error(&v) != VOX_CUDA_OK || gemv_take_device_error(&v) != VOX_CUDA_OK || f5_take_device_error(&v) != VOX_CUDA_OK ||
+        gemm_take_device_error(&v) != VOX_CUDA_OK) {
         const cudaError_t e = cudaGetLastError();
         return set_error(VOX_CUDA_ERR_DEVICE, std::string("vox_cuda_device_error: ") + cudaGetErrorString(e));
     }

@@ -60,15 +60,27 @@ def tensor_peak() -> tuple[float, str]:
 
 # ---------------------------------------------------------------------------------------------------- workload
 
+def make_comm(vox, torch, dist, rank: int, world: int):
+    """The library's communicator over the ranks (None on one GPU): rank 0 draws the id, torch.distributed carries it."""
+    if world <= 1:
+        return None
+    uid = torch.zeros(vox.Comm.ID_BYTES, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(vox.Comm.unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    return vox.Comm(bytes(uid.cpu().numpy()), world, rank)
+
+
 class Suite:
     """Device buffers and the per-op launch list of one step. `ops` entries: (name, bytes, elements, fn).
 
     `only` (a regex) keeps the matching ops and allocates only their buffers (profiling of one kernel)."""
 
-    def __init__(self, vox, torch, rank: int, world: int, sweep_elems: int, dist=None, only: str | None = None, scale: int = 1):
+    def __init__(self, vox, torch, rank: int, world: int, sweep_elems: int, dist=None, only: str | None = None, scale: int = 1, comm=None):
         import re
 
         self.vox, self.t, self.rank, self.world, self.dist = vox, torch, rank, world, dist
+        self.comm = comm
         dev = torch.device("cuda", torch.cuda.current_device())
         f32, bf16 = torch.float32, torch.bfloat16
         E = lambda *s, dt=f32: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
@@ -308,11 +320,10 @@ class Suite:
         return [i for _, idx, _, _ in first + last for i in idx]
 
     def global_sum(self):
-        v = self.vox
-        v.global_sum_partials(self.gsum_x, self.g_row0, self.g_rows_total, slots=self.slots, scratch=self.gscratch)
-        if self.world > 1:
-            self.dist.all_reduce(self.slots)
-        v.global_sum_finish(self.slots, out=self.gout)
+        """One library call: this shard's slot partials, the all-reduce of the 840 slots over the library's own NCCL
+        communicator (world > 1), the fixed-order fold."""
+        self.vox.global_sum_comm(self.gsum_x, self.g_row0, self.g_rows_total, self.comm, slots=self.slots, scratch=self.gscratch,
+                                 out=self.gout)
 
     def step(self, events=None):
         for i, (_, _, _, fn) in enumerate(self.ops):
@@ -590,7 +601,8 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     import vox_b200 as vox
 
-    suite = Suite(vox, torch, rank, world, args.sweep_elems, dist if world > 1 else None, only=args.only, scale=args.scale)
+    comm = make_comm(vox, torch, dist, rank, world)
+    suite = Suite(vox, torch, rank, world, args.sweep_elems, dist if world > 1 else None, only=args.only, scale=args.scale, comm=comm)
     torch.cuda.synchronize()
 
     def barrier():
@@ -638,7 +650,10 @@ def run_ours(args) -> None:
     e2e = run_e2e(suite, torch, dist, world, max(1, min(args.steps, args.e2e_steps))) if args.e2e_steps > 0 else None
 
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -776,6 +791,7 @@ def run_sweep(args) -> None:
     from vox_b200.shard import shard_rows
 
     peak, _ = peaks()
+    comm = make_comm(vox, torch, dist, rank, world)
     results = []
     for lg in range(args.sweep_lo, args.sweep_hi + 1):
         total = 1 << lg
@@ -791,10 +807,7 @@ def run_sweep(args) -> None:
             n = rows * 4096
 
             def gsum():
-                vox.global_sum_partials(a, r0, R, slots=slots, scratch=scratch)
-                if world > 1:
-                    dist.all_reduce(slots)
-                vox.global_sum_finish(slots, out=gout)
+                vox.global_sum_comm(a, r0, R, comm, slots=slots, scratch=scratch, out=gout)
 
             ops = [("add", 3 * es, lambda: vox.add(a, b, out=y)), ("mul", 3 * es, lambda: vox.mul(a, b, out=y)),
                    ("gelu", 2 * es, lambda: vox.gelu(a, vox.GELU_ERF, out=y)),
@@ -827,7 +840,10 @@ def run_sweep(args) -> None:
             del a, b, y, rr
             torch.cuda.empty_cache()
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps({"metric": METRIC, "mode": "sweep", "n_gpus": world, "unit": "GB/s", "peak": peak,

@@ -226,6 +226,33 @@ VOX_CUDA_API int vox_cuda_global_sum_finish(const double *slots, double *out, vo
  * No counterpart in the reference (Vox has no device-side global sum). */
 VOX_CUDA_API int vox_cuda_global_sum_noalloc(const void *x, int64_t rows, int64_t n, double *out, int dtype, void *stream);
 
+/* Cross-GPU global sum in one call. A communicator spans the shards (one rank per GPU; NCCL, loaded at run time):
+ *   vox_cuda_comm_unique_id   rank 0 draws the id (VOX_CUDA_COMM_ID_BYTES bytes) and hands it to every rank;
+ *   vox_cuda_comm_init_rank   each process joins with it (non-blocking communicator; fails with VOX_CUDA_ERR_DEVICE if
+ *                             not every rank joined within timeout_ms, 0 = 30 s);
+ *   vox_cuda_comm_init_all    one process driving ndev GPUs gets one communicator per device;
+ *   vox_cuda_comm_wait        waits (host polling) until the stream's work is done; past timeout_ms (0 = 30 s), or on an
+ *                             NCCL error, the communicator is aborted (its kernels end) and VOX_CUDA_ERR_DEVICE returned:
+ *                             a lost peer is reported to the host instead of hanging;
+ *   vox_cuda_comm_destroy.
+ * vox_cuda_global_sum = vox_cuda_global_sum_partials of this shard (rows [row0, row0 + rows) of the [total_rows][n]
+ * global tensor), then one all-reduce of the 840 f64 slots over comm (comm NULL or of one rank: none), then
+ * vox_cuda_global_sum_finish into out[0]; every rank gets the same bits for any number of ranks 1..8. Stream-ordered;
+ * rowsum_scratch: f32 [rows], slots: f64 [840] (device). With vox_cuda_comm_init_all, wrap the ndev calls (one per
+ * device, each with that device current) in vox_cuda_comm_group_start / _end.
+ * No counterpart in the reference (Vox drives one device per process and has no global reduction). */
+#define VOX_CUDA_COMM_ID_BYTES 128
+typedef struct vox_cuda_comm vox_cuda_comm;
+VOX_CUDA_API int vox_cuda_comm_unique_id(void *id);
+VOX_CUDA_API int vox_cuda_comm_init_rank(const void *id, int nranks, int rank, int timeout_ms, vox_cuda_comm **out);
+VOX_CUDA_API int vox_cuda_comm_init_all(int ndev, const int *devices, vox_cuda_comm **comms);
+VOX_CUDA_API int vox_cuda_comm_group_start(void);
+VOX_CUDA_API int vox_cuda_comm_group_end(void);
+VOX_CUDA_API int vox_cuda_comm_wait(vox_cuda_comm *comm, void *stream, int timeout_ms);
+VOX_CUDA_API void vox_cuda_comm_destroy(vox_cuda_comm *comm);
+VOX_CUDA_API int vox_cuda_global_sum(const void *x, int64_t rows, int64_t n, int64_t row0, int64_t total_rows, float *rowsum_scratch,
+                                     double *slots, double *out, int dtype, vox_cuda_comm *comm, void *stream);
+
 /* ---------------------------------------------------------------- transformer elementwise chain */
 
 /* RoPE table for m positions pos0 .. pos0+m-1: cs[(i*half + p)*2] = cos(f), cs[(i*half + p)*2 + 1] = sin(f),

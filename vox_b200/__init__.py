@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "gemm_bf16", "Tmod", "F5Dit", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "gemm_bf16", "Comm", "global_sum_comm", "Tmod", "F5Dit", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -80,6 +80,11 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_rope_table": ([c_p, c_i64, c_i64, c_i64, c_p, c_p], c_int),
         "vox_cuda_qkv_rope": ([c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f, c_p], c_int),
         "vox_cuda_add_rmsnorm": ([c_p, c_p, c_p, c_p, c_p, c_i64, c_i64, c_f, c_int, c_p], c_int),
+        "vox_cuda_comm_unique_id": ([c_p], c_int),
+        "vox_cuda_comm_init_rank": ([c_p, c_int, c_int, c_int, c_p], c_int),
+        "vox_cuda_comm_wait": ([c_p, c_p, c_int], c_int),
+        "vox_cuda_comm_destroy": ([c_p], None),
+        "vox_cuda_global_sum": ([c_p, c_i64, c_i64, c_i64, c_i64, c_p, c_p, c_p, c_int, c_p, c_p], c_int),
         "vox_cuda_gemm_bf16": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_int, c_p], c_int),
         "vox_cuda_gemv_q8": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
         "vox_cuda_gemv_q4": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
@@ -390,6 +395,56 @@ def global_sum(x: torch.Tensor, row0: int = 0, total_rows: int | None = None, gr
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(slots, op=dist.ReduceOp.SUM, group=group)
     return global_sum_finish(slots)
+
+
+class Comm:
+    """A communicator of the library over the shards' GPUs (vox_cuda_comm_*: NCCL, non-blocking, with deadlines), one
+    rank per process. Rank 0 draws ``Comm.unique_id()`` and hands the bytes to every rank (any channel)."""
+
+    ID_BYTES = 128
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, timeout_ms: int = 30000):
+        buf = ctypes.create_string_buffer(bytes(uid), self.ID_BYTES)
+        h = ctypes.c_void_p()
+        _check(lib.vox_cuda_comm_init_rank(buf, nranks, rank, timeout_ms, ctypes.byref(h)))
+        self.h, self.nranks, self.rank = h, nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(Comm.ID_BYTES)
+        _check(lib.vox_cuda_comm_unique_id(buf))
+        return buf.raw
+
+    def wait(self, timeout_ms: int = 0, stream=None) -> None:
+        """Waits until the current (or given) stream's work is done; raises (and aborts the communicator) past the
+        deadline or on an NCCL error."""
+        st = torch.cuda.current_stream().cuda_stream if stream is None else stream
+        _check(lib.vox_cuda_comm_wait(self.h, st, timeout_ms))
+
+    def close(self) -> None:
+        if self.h:
+            lib.vox_cuda_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def global_sum_comm(x: torch.Tensor, row0: int, total_rows: int, comm: Comm | None, slots=None, scratch=None, out=None) -> torch.Tensor:
+    """The deterministic global sum of a row-sharded tensor in one library call (partials, all-reduce over ``comm``,
+    fold): f64 [1], bitwise identical on every rank and for any number of ranks."""
+    dt = _act(x, "x")
+    n = x.shape[-1]
+    rows = x.numel() // n
+    slots = torch.empty(GLOBAL_SUM_SLOTS, dtype=torch.float64, device=x.device) if slots is None else slots
+    scratch = torch.empty(max(rows, 1), dtype=torch.float32, device=x.device) if scratch is None else scratch
+    out = torch.empty(1, dtype=torch.float64, device=x.device) if out is None else out
+    _check(lib.vox_cuda_global_sum(x.data_ptr(), rows, n, row0, total_rows, scratch.data_ptr(), slots.data_ptr(), out.data_ptr(), dt,
+                                   comm.h if comm is not None else None, _stream(x)))
+    return out
 
 
 # ------------------------------------------------------------------ synthetic data

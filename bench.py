@@ -878,6 +878,8 @@ def run_copy_roofline(args) -> None:
             f()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # a spin kernel holds the GPU while the host enqueues every launch, so no host launch cost is timed
+        torch.cuda._sleep(int(min(max(0.03 * reps, 5.0), 2000.0) * 2.0e6))
         e0.record()
         for k in range(reps):
             fns[k % len(fns)]()
@@ -937,6 +939,7 @@ def run_gemm(args) -> None:
                 fn()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(int(min(max(0.03 * reps, 5.0), 2000.0) * 2.0e6))  # the host enqueues while the GPU spins
             e0.record()
             for _ in range(reps):
                 fn()

@@ -18,6 +18,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -355,7 +356,13 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
         const int64_t cost = (tiles + sms - 1) / sms * bn;
         if (best_cost < 0 || cost < best_cost) best = bn, best_cost = cost;
     }
-    plan.bn = best;
+    // VOX_CUDA_GEMM_BN = 64 / 128 / 256 forces the tile width (for comparisons)
+    static const int forced = [] {
+        const char *e = std::getenv("VOX_CUDA_GEMM_BN");
+        const int v = e ? std::atoi(e) : 0;
+        return v == 64 || v == 128 || v == 256 ? v : 0;
+    }();
+    plan.bn = forced ? forced : best;
     int rc = bf16_map(x, a.K, a.M, z, ldx, kBM, plan.ta, name);
     if (rc != VOX_CUDA_OK) return rc;
     return bf16_map(w, a.K, a.N, a.groups, ldw, plan.bn, plan.tb, name);

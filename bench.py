@@ -956,6 +956,30 @@ def run_gemm(args) -> None:
                    "tflops": round(fl / ours_b / 1e6, 1), "frac_of_tensor_peak": round(fl / ours_b / 1e6 / tpk, 3),
                    "cublas_tflops": round(fl / ref / 1e6, 1)}
         del x, w, y, yb
+    # the quantized prefill GEMM (Q8 / Q4 weights [12288][4096] with f16 scales, 512 f32 activation rows), weights rotated
+    # over enough copies that they stream from HBM
+    m, n, k = 512, 12288, 4096
+    x = torch.randn(m, k, device="cuda", generator=g)
+    y = torch.empty(m, n, device="cuda")
+    fl = 2 * m * n * k
+    for qt in ("q8", "q4"):
+        mats = [vox.fill_philox(torch.empty(n, k if qt == "q8" else k // 2, dtype=torch.int8 if qt == "q8" else torch.uint8, device="cuda"),
+                                2 if qt == "q8" else 3, -128, 127, seed=0, stream_id=70 + i) for i in range(4)]
+        scs = [vox.fill_philox(torch.empty(n, k // 32, device="cuda"), 0, 0.001, 0.05, seed=0, stream_id=80 + i).half() for i in range(4)]
+        fn = vox.gemm_q8 if qt == "q8" else vox.gemm_q4
+        ctr = [0]
+
+        def call(fn=fn, mats=mats, scs=scs, ctr=ctr):
+            i = ctr[0] % 4
+            ctr[0] += 1
+            fn(mats[i], scs[i], x, out=y)
+
+        reps = 40
+        us = min(t(call) for _ in range(3))
+        res[f"prefill_{qt}"] = {"m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(fl / us / 1e6, 1),
+                                "frac_of_tensor_peak": round(fl / us / 1e6 / tpk, 3),
+                                "weight_gb_s": round((n * k * (1 if qt == "q8" else 0.5) + n * k // 32 * 2) / us / 1e3, 1)}
+        del mats, scs
     print(json.dumps({"metric": METRIC, "mode": "gemm", "unit": "TFLOP/s", "tensor_peak": f"{tpk} bf16 sustained ({tkind})",
                       "config": {"workload": "tcgen05 bf16 GEMM vs cuBLAS, F5-base and prefill shapes"}, "results": res}), flush=True)
 

@@ -23,7 +23,7 @@ __all__ = [
     "rmsnorm", "layernorm", "layer_norm", "adaln", "gated_add", "bias_add",
     "softmax_rows", "silu_mul", "swiglu_fused", "gelu", "add", "mul", "snake", "load_snake",
     "dequant_q8", "dequant_q4", "row_reduce", "global_sum_partials", "global_sum_finish", "global_sum",
-    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "gemm_bf16", "Comm", "global_sum_comm", "Tmod", "F5Dit", "F32", "BF16", "F16",
+    "fill_philox", "rope_inv_freq", "rope_table", "qkv_rope", "add_rmsnorm", "gemv_q8", "gemv_q4", "gemm_q8", "gemm_q4", "gemm_bf16", "Comm", "global_sum_comm", "Tmod", "F5Dit", "F32", "BF16", "F16",
 ]
 
 F32, BF16, F16 = 0, 1, 2
@@ -85,6 +85,8 @@ def _load() -> ctypes.CDLL:
         "vox_cuda_comm_wait": ([c_p, c_p, c_int], c_int),
         "vox_cuda_comm_destroy": ([c_p], None),
         "vox_cuda_global_sum": ([c_p, c_i64, c_i64, c_i64, c_i64, c_p, c_p, c_p, c_int, c_p, c_p], c_int),
+        "vox_cuda_gemm_q8": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
+        "vox_cuda_gemm_q4": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
         "vox_cuda_gemm_bf16": ([c_p, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_int, c_p], c_int),
         "vox_cuda_gemv_q8": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
         "vox_cuda_gemv_q4": ([c_p, c_p, c_int, c_p, c_p, c_p, c_i64, c_i64, c_i64, c_int, c_p], c_int),
@@ -552,6 +554,16 @@ def gemv_q8(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, ou
 def gemv_q4(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, out=None, accumulate: bool = False) -> torch.Tensor:
     """As gemv_q8 with Q4 weights: uint8 [rows][cols/2], 16 bytes per 32-block (byte j = code j | code j+16 << 4)."""
     return _gemv(lib.vox_cuda_gemv_q4, True, w, scale, x, bias, out, accumulate)
+
+
+def gemm_q8(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, out=None, accumulate: bool = False) -> torch.Tensor:
+    """The prefill form of gemv_q8 (many activation rows) on the tensor cores in f16: y [m][rows] = W x (+ bias)."""
+    return _gemv(lib.vox_cuda_gemm_q8, False, w, scale, x, bias, out, accumulate)
+
+
+def gemm_q4(w: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, bias=None, out=None, accumulate: bool = False) -> torch.Tensor:
+    """The prefill form of gemv_q4 on the tensor cores in f16."""
+    return _gemv(lib.vox_cuda_gemm_q4, True, w, scale, x, bias, out, accumulate)
 
 
 # ------------------------------------------------------------------ .tmod weight files -> device

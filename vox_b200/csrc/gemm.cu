@@ -38,7 +38,7 @@ template <int BN> struct Cfg {
     static constexpr uint32_t B_BYTES = BN * kBK * 2;
     static constexpr uint32_t STAGE = kABytes + B_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
-    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256;
+    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * 4096;  // + the epilogue warps' staging
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -60,13 +60,20 @@ __device__ __forceinline__ Tile tile_of(int t, int mt, int nt, int groups) {
     return r;
 }
 
-// The epilogue of 32 consecutive columns [c0, c0 + 32) of output row `row` (acc: f32 bit patterns).
+constexpr uint32_t kStageWarpBytes = 32 * 128;  // epilogue staging: a warp's 32 rows x 32 columns (f32), 4 KB
+
+// The epilogue of 32 consecutive columns [c0, c0 + 32) of the warp's 32 output rows m32 .. m32 + 31 (thread lane holds
+// row m32 + lane; acc: f32 bit patterns): bias / RoPE / GELU on the registers, then the block passes through the warp's
+// staging area in shared memory (16-byte chunk c of row r at chunk c ^ (r % 8): conflict-free both ways) so that each
+// store instruction writes whole 128-byte row segments of y instead of 32 scattered pieces.
 template <int EPI>
-__device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&acc)[32], int row, int c0, int zb, int zg) {
+__device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&acc)[32], int m32, int lane, int c0, int zb, int zg,
+                                           uint32_t stg) {
+    const int row = m32 + lane;
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
-    const int nv = min(32, g.N - c0);  // valid columns
+    const int nv = min(32, g.N - c0);  // valid columns (warp-uniform)
     if (g.bias) {
         const float *b = g.bias + int64_t(zg) * g.N + c0;
         if (nv == 32 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0) {
@@ -83,7 +90,7 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&a
     }
     if constexpr (EPI == kEpiQkvRope) {
         const int part = c0 / g.inner, ci = c0 - part * g.inner, head = ci / g.hd;
-        if (part < 2 && head < g.rope_heads) {  // pairs (2j, 2j + 1) of the head, j = (ci % hd) / 2 ..
+        if (part < 2 && head < g.rope_heads && row < g.M) {  // pairs (2j, 2j + 1) of the head, j = (ci % hd) / 2 ..
             const float2 *cs = g.cs + int64_t(row % g.frames) * (g.hd / 2) + (ci % g.hd) / 2;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -106,37 +113,63 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&a
             v[2 * j] = r.x, v[2 * j + 1] = r.y;
         }
     }
-    const int64_t off = int64_t(zb) * g.y_bstride + int64_t(zg) * g.y_gstride + int64_t(row) * g.ldy + c0;
-    if constexpr (EPI == kEpiF32 || EPI == kEpiGeluTanhF32 || EPI == kEpiGeluErfF32) {
-        float *y = reinterpret_cast<float *>(g.y) + off;
-        if (nv == 32 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+    constexpr bool F32OUT = EPI == kEpiF32 || EPI == kEpiGeluTanhF32 || EPI == kEpiGeluErfF32;
+    constexpr int CH = F32OUT ? 8 : 4;             // 16-byte chunks a row
+    constexpr int EPC = F32OUT ? 4 : 8;            // elements a chunk
+    constexpr int RB = CH * 16;                    // staged row bytes
+    // registers -> staging (row = lane)
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    for (int c = 0; c < CH; ++c) {
+        uint4 w;
+        if (F32OUT) w = make_uint4(__float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3]));
+        else w = make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
+                            pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stg + lane * RB + ((c ^ (lane & (CH - 1))) << 4)), "r"(w.x), "r"(w.y),
+                     "r"(w.z), "r"(w.w) : "memory");
+    }
+    __syncwarp();
+    // staging -> y: each instruction covers 32 / CH rows, CH lanes a row (one 16-byte chunk each)
+    constexpr int RPI = 32 / CH;
+    const int c = lane % CH;
+    const int64_t base = int64_t(zb) * g.y_bstride + int64_t(zg) * g.y_gstride + c0 + c * EPC;
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+        const int r = j * RPI + lane / CH;
+        uint4 w;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                     : "r"(stg + r * RB + ((c ^ (r & (CH - 1))) << 4)) : "memory");
+        const int gr = m32 + r;
+        if (gr >= g.M) continue;
+        const int64_t off = base + int64_t(gr) * g.ldy;
+        const int nvc = min(EPC, nv - c * EPC);  // valid elements of this chunk
+        if (nvc <= 0) continue;
+        if (F32OUT) {
+            float *y = reinterpret_cast<float *>(g.y) + off;
+            float f[4] = {__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w)};
+            if (nvc == 4 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
                 if (g.accumulate) {
-                    const float4 p = reinterpret_cast<const float4 *>(y)[q];
-                    o.x += p.x, o.y += p.y, o.z += p.z, o.w += p.w;
+                    const float4 p = *reinterpret_cast<const float4 *>(y);
+                    f[0] += p.x, f[1] += p.y, f[2] += p.z, f[3] += p.w;
                 }
-                reinterpret_cast<float4 *>(y)[q] = o;
+                *reinterpret_cast<float4 *>(y) = make_float4(f[0], f[1], f[2], f[3]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (i < nvc) y[i] = g.accumulate ? y[i] + f[i] : f[i];
             }
         } else {
+            uint16_t *y = reinterpret_cast<uint16_t *>(g.y) + off;
+            if (nvc == 8 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+                *reinterpret_cast<uint4 *>(y) = w;
+            } else {
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (i < nv) y[i] = g.accumulate ? y[i] + v[i] : v[i];
-        }
-    } else {
-        uint16_t *y = reinterpret_cast<uint16_t *>(g.y) + off;
-        if (nv == 32 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                reinterpret_cast<uint4 *>(y)[q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                                                             pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (i < nv) y[i] = to_bf16(v[i]);
+                for (int i = 0; i < 8; ++i)
+                    if (i < nvc) y[i] = uint16_t(ww[i / 2] >> (16 * (i & 1)));
+            }
         }
     }
+    __syncwarp();  // the staging area is reused by the next block
 }
 
 template <int BN, int EPI>
@@ -153,6 +186,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     uint64_t *tempty = tfull + 2;         // [2]: accumulator a has been read out
     uint64_t *drain = tempty + 2;         // wind-down: every MMA issued has completed
     uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
+    const uint32_t STG_BASE = s0 + C::STAGES * C::STAGE + 256;  // the epilogue warps' staging areas (after the barriers)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (g.M + kBM - 1) / kBM, nt = (g.N + BN - 1) / BN;
     const int tiles = mt * nt * g.batches * g.groups, kt = (g.K + kBK - 1) / kBK;
@@ -245,6 +279,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     } else {
         // ---- epilogue: thread = output row 32 (warp % 4) + lane of the tile
         const int q = warp & 3;
+        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
         uint32_t tc = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
@@ -254,7 +289,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             }
             tc_fence_after();
             const Tile tl = tile_of(t, mt, nt, g.groups);
-            const int row = tl.m0 + 32 * q + lane;
             const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + a * BN;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -263,7 +297,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                 uint32_t r[32];
                 tmem_ld32(taddr + uint32_t(c), r);
                 tmem_wait_ld();
-                if (row < g.M) epilogue32<EPI>(g, r, row, c0, tl.zb, tl.zg);
+                epilogue32<EPI>(g, r, tl.m0 + 32 * q, lane, c0, tl.zb, tl.zg, stg);
             }
             tc_fence_before();
             __syncwarp();
@@ -275,6 +309,300 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ quantized prefill GEMM (Q8 / Q4 weights)
+//
+// y[M][N] (+)= bias + x[M][K] . W[N][K]^T with W = code * scale[n][k / 32] (Vox's Q8 / Q4 blocks) and f32 x, on the
+// tensor cores in f16 (kind::f16, f16 A and B, f32 accumulation): the dequantisation is the producer stage. Tile 128
+// activation rows x 256 weight rows, K step 64. Fourteen warps:
+//   warp 0       TMA: the raw tiles of a K step, x [128][64] f32 and the codes [256][64] bytes (Q8) or [256][32] (Q4),
+//                into a two-stage raw ring;
+//   warps 6..13  converters: x to f16, codes to f16 by the exponent trick (0x6400 | u is 1024 + u exactly; minus the
+//                code offset gives the integer code, times the block's scale rounds once to f16), both written as the
+//                128-byte-swizzled K-major operand tiles of a two-stage MMA ring;
+//   warp 1       one thread issues tcgen05.mma (M 128, N 256, K 16) into one of two TMEM accumulators (512 columns);
+//   warps 2..5   the epilogue (bias, accumulate, f32 store) as in the bf16 GEMM.
+// f16 keeps 11 significant bits of x and of code * scale (bf16: 8); |x| must stay below 65504. A code's integer value
+// is exact in f16; its product with an f16 scale is rounded once.
+constexpr int kQBN = 256;
+constexpr int kQThreads = 448;
+constexpr int kQConvWarps = 8;
+constexpr uint32_t kQARaw = kBM * kBK * 4;          // 32 KB f32
+constexpr uint32_t kQAConv = kBM * kBK * 2;         // 16 KB f16
+constexpr uint32_t kQBConv = kQBN * kBK * 2;        // 32 KB f16
+template <bool Q4> struct QCfg {
+    static constexpr uint32_t CODES = Q4 ? kQBN * kBK / 2 : kQBN * kBK;  // raw code bytes a K step
+    static constexpr uint32_t RAW = kQARaw + CODES;
+    static constexpr uint32_t CONV = kQAConv + kQBConv;
+    static constexpr int RS = 2, CS = 2;
+    static constexpr size_t SMEM = size_t(RS) * RAW + size_t(CS) * CONV + 1024 + 256 + 4 * 4096;
+};
+
+// Two codes (bytes b0, b1 of w, already offset to unsigned) as f16x2 1024 + u: prmt puts the code byte under 0x64.
+__device__ __forceinline__ uint32_t f16_pair_1024(uint32_t w, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(w), "r"(0x64646464u), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub_hmul(uint32_t v, uint32_t off2, uint32_t s2) {
+    uint32_t d;
+    asm("{\n\t.reg .b32 t;\n\tsub.rn.f16x2 t, %1, %2;\n\tmul.rn.f16x2 %0, t, %3;\n\t}" : "=r"(d) : "r"(v), "r"(off2), "r"(s2));
+    return d;
+}
+__device__ __forceinline__ uint32_t f16x2_of(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+struct GemmQArgs {
+    int M, N, K, nblk;      // nblk = K / 32
+    const void *scale;      // [N][nblk] f32 or f16
+    GemmArgs g;             // epilogue (kEpiF32: bias, accumulate, y [M][N])
+};
+
+template <bool Q4, bool SF16>
+__global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
+                                                              const GemmQArgs q) {
+    using C = QCfg<Q4>;
+    constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(kQBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);  // f16 A and B, f32 D
+    extern __shared__ uint8_t gq_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gq_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *conv = smem;                                   // [CS][A f16 | B f16], 1024-aligned stages
+    uint8_t *raw = smem + C::CS * C::CONV;                  // [RS][A f32 | codes]
+    uint64_t *raw_full = reinterpret_cast<uint64_t *>(raw + C::RS * C::RAW);
+    uint64_t *raw_empty = raw_full + C::RS;
+    uint64_t *conv_full = raw_empty + C::RS;
+    uint64_t *conv_empty = conv_full + C::CS;
+    uint64_t *tfull = conv_empty + C::CS;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
+    const uint32_t STG_BASE = smem_addr(raw + C::RS * C::RAW) + 256;  // the epilogue warps' staging areas (after the barriers)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = (q.M + kBM - 1) / kBM, nt = (q.N + kQBN - 1) / kQBN;
+    const int tiles = mt * nt, kt = (q.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::RS; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], kQConvWarps);
+        }
+        for (int s = 0; s < C::CS; ++s) {
+            mbar_init(&conv_full[s], kQConvWarps);
+            mbar_init(&conv_empty[s], 1);
+        }
+        mbar_init(&tfull[0], 1);
+        mbar_init(&tfull[1], 1);
+        mbar_init(&tempty[0], 4);
+        mbar_init(&tempty[1], 4);
+        mbar_init(drain, 1);
+        mbar_init_fence();
+        tma_prefetch_desc(&tx);
+        tma_prefetch_desc(&tw);
+    }
+    pdl_enter();
+    if (warp == 0) tmem_alloc(tslot, 2 * kQBN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    bool ok = true;
+
+    if (warp == 0) {
+        // ---- raw tiles
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
+            for (int kc = 0; kc < kt; ++kc, ++it) {
+                const int s = int(it % C::RS);
+                const uint32_t u = it / C::RS;
+                if (!mbar_wait_warp(&raw_empty[s], (u & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t ra = smem_addr(raw + s * C::RAW);
+                    mbar_arrive_expect_tx(&raw_full[s], C::RAW);
+                    tma_load_3d(ra, &tx, kc * kBK, m0, 0, &raw_full[s]);
+                    tma_load_3d(ra + kQARaw, &tw, kc * (Q4 ? kBK / 2 : kBK), n0, 0, &raw_full[s]);
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok) {
+            const uint32_t last = it;
+            for (uint32_t j = last > uint32_t(C::RS) ? last - C::RS : 0; j < last; ++j) mbar_wait_warp(&raw_full[j % C::RS], (j / C::RS) & 1u);
+        }
+    } else if (warp >= 6) {
+        // ---- converters: thread ct of 256
+        const int ct = threadIdx.x - 6 * 32;
+        uint32_t it = 0;
+        const uint32_t off8 = 0x64806480u;   // f16x2 (1152, 1152): 1024 + 128 (Q8 codes offset to unsigned by ^ 0x80)
+        const uint32_t off4 = 0x64086408u;   // f16x2 (1032, 1032): 1024 + 8 (Q4 codes are u - 8)
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
+            (void)m0;
+            for (int kc = 0; kc < kt; ++kc, ++it) {
+                const int rs = int(it % C::RS), cs = int(it % C::CS);
+                const uint32_t ru = it / C::RS, cu = it / C::CS;
+                // the block scales of this thread's weight tasks (global loads, in flight during the waits)
+                constexpr int NT = Q4 ? 2 : 4;  // weight tasks a thread
+                uint32_t s2[NT];
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const int i = ct + 256 * j;
+                    const int row = Q4 ? i >> 1 : i >> 2, blk = kc * 2 + (Q4 ? (i & 1) : ((i & 3) >> 1));
+                    float sc = 0.f;
+                    if (n0 + row < q.N && blk < q.nblk) {
+                        const int64_t e = int64_t(n0 + row) * q.nblk + blk;
+                        sc = SF16 ? __half2float(__ldg(reinterpret_cast<const __half *>(q.scale) + e)) : __ldg(reinterpret_cast<const float *>(q.scale) + e);
+                    }
+                    const __half h = __float2half_rn(sc);
+                    const uint32_t hb = *reinterpret_cast<const uint16_t *>(&h);
+                    s2[j] = hb | (hb << 16);
+                }
+                if (!mbar_wait_warp(&raw_full[rs], ru & 1u) || !mbar_wait_warp(&conv_empty[cs], (cu & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *ra = raw + rs * C::RAW;
+                const uint32_t ca = smem_addr(conv + cs * C::CONV), cb = ca + kQAConv;
+                // x: 8 float4 a thread -> f16, 8 bytes each into the swizzled [128][64] tile
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int i = ct + 256 * j, row = i >> 4, c4 = i & 15;
+                    const float4 v = *reinterpret_cast<const float4 *>(ra + i * 16);
+                    const uint32_t d = ca + row * 128 + (((c4 >> 1) ^ (row & 7)) << 4) + (c4 & 1) * 8;
+                    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(d), "r"(f16x2_of(v.x, v.y)), "r"(f16x2_of(v.z, v.w)) : "memory");
+                }
+                const uint8_t *rc = ra + kQARaw;
+                if constexpr (!Q4) {
+                    // 16 codes a task: row i / 4, 16-code quarter i % 4 (block quarter / 2)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int i = ct + 256 * j, row = i >> 2, qq = i & 3;
+                        const uint4 w = *reinterpret_cast<const uint4 *>(rc + i * 16);
+                        const uint32_t ws[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+                        uint32_t h[8];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            h[2 * k] = hsub_hmul(f16_pair_1024(ws[k], 0x4140u), off8, s2[j]);
+                            h[2 * k + 1] = hsub_hmul(f16_pair_1024(ws[k], 0x4342u), off8, s2[j]);
+                        }
+                        const uint32_t b0 = cb + row * 128;
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b0 + ((((2 * qq) ^ (row & 7))) << 4)), "r"(h[0]), "r"(h[1]),
+                                     "r"(h[2]), "r"(h[3]) : "memory");
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b0 + ((((2 * qq + 1) ^ (row & 7))) << 4)), "r"(h[4]),
+                                     "r"(h[5]), "r"(h[6]), "r"(h[7]) : "memory");
+                    }
+                } else {
+                    // one 16-byte block a task (32 codes): row i / 2, block i % 2; byte j: code j (low), j + 16 (high)
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int i = ct + 256 * j, row = i >> 1, bb = i & 1;
+                        const uint4 w = *reinterpret_cast<const uint4 *>(rc + i * 16);
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                        uint32_t lo[8], hi[8];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t l = ws[k] & 0x0F0F0F0Fu, hh = (ws[k] >> 4) & 0x0F0F0F0Fu;
+                            lo[2 * k] = hsub_hmul(f16_pair_1024(l, 0x4140u), off4, s2[j]);
+                            lo[2 * k + 1] = hsub_hmul(f16_pair_1024(l, 0x4342u), off4, s2[j]);
+                            hi[2 * k] = hsub_hmul(f16_pair_1024(hh, 0x4140u), off4, s2[j]);
+                            hi[2 * k + 1] = hsub_hmul(f16_pair_1024(hh, 0x4342u), off4, s2[j]);
+                        }
+                        const uint32_t b0 = cb + row * 128;
+                        const int c0 = 4 * bb;  // the block's 32 elements: chunks 4 bb .. 4 bb + 3
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b0 + (((c0 + 0) ^ (row & 7)) << 4)), "r"(lo[0]), "r"(lo[1]),
+                                     "r"(lo[2]), "r"(lo[3]) : "memory");
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b0 + (((c0 + 1) ^ (row & 7)) << 4)), "r"(lo[4]), "r"(lo[5]),
+                                     "r"(lo[6]), "r"(lo[7]) : "memory");
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b0 + (((c0 + 2) ^ (row & 7)) << 4)), "r"(hi[0]), "r"(hi[1]),
+                                     "r"(hi[2]), "r"(hi[3]) : "memory");
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b0 + (((c0 + 3) ^ (row & 7)) << 4)), "r"(hi[4]), "r"(hi[5]),
+                                     "r"(hi[6]), "r"(hi[7]) : "memory");
+                    }
+                }
+                fence_proxy_async();  // the generic-proxy writes, visible to the MMA (async proxy)
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&raw_empty[rs]);
+                    mbar_arrive(&conv_full[cs]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue
+        uint32_t it = 0, tc = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+            const uint32_t a = tc & 1u, v = tc >> 1;
+            if (!mbar_wait_warp(&tempty[a], (v & 1u) ^ 1u)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t dcol = tmem + a * kQBN;
+            for (int kc = 0; kc < kt; ++kc, ++it) {
+                const int s = int(it % C::CS);
+                const uint32_t u = it / C::CS;
+                if (!mbar_wait_warp(&conv_full[s], u & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sa = smem_addr(conv + s * C::CONV), sb = sa + kQAConv;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        umma_bf16(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
+                    umma_commit(&conv_empty[s]);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) umma_commit(&tfull[a]);
+            __syncwarp();
+        }
+        if (!ok) {
+            if (lane == 0) umma_commit(drain);
+            __syncwarp();
+            mbar_wait_warp(drain, 0);
+        }
+    } else {
+        // ---- epilogue (warps 2..5)
+        const int qw = warp & 3;
+        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
+        uint32_t tc = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+            const uint32_t a = tc & 1u, v = tc >> 1;
+            if (!mbar_wait_warp(&tfull[a], v & 1u)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
+            const uint32_t taddr = tmem + (uint32_t(32 * qw) << 16) + a * kQBN;
+#pragma unroll 1
+            for (int c = 0; c < kQBN; c += 32) {
+                if (n0 + c >= q.N) break;
+                uint32_t r[32];
+                tmem_ld32(taddr + uint32_t(c), r);
+                tmem_wait_ld();
+                epilogue32<kEpiF32>(q.g, r, m0 + 32 * qw, lane, n0 + c, 0, 0, stg);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[a]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * kQBN);
     }
 }
 
@@ -307,6 +635,38 @@ int bf16_map(const void *base, int64_t cols, int64_t rows, int64_t depth, int64_
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(VOX_CUDA_ERR_ARG, std::string(name) + ": tensor map rejected (code " + std::to_string(int(r)) + ")");
     return VOX_CUDA_OK;
+}
+
+// 3-D map (depth 1) of a row-major [rows][cols] matrix of 1- or 4-byte elements, row pitch ld_bytes, box box_cols x
+// box_rows, no swizzle, zero fill past the edges.
+int plain_map(const void *base, CUtensorMapDataType dt, int64_t cols, int64_t rows, int64_t ld_bytes, int box_cols, int box_rows,
+              CUtensorMap &m, const char *name) {
+    auto fn = encode();
+    if (!fn) return set_error(VOX_CUDA_ERR_DEVICE, std::string(name) + ": cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), 1};
+    const cuuint64_t strides[2] = {cuuint64_t(ld_bytes), cuuint64_t(ld_bytes) * cuuint64_t(rows)};
+    const cuuint32_t box[3] = {uint32_t(box_cols), uint32_t(box_rows), 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = fn(&m, dt, 3, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(VOX_CUDA_ERR_ARG, std::string(name) + ": tensor map rejected (code " + std::to_string(int(r)) + ")");
+    return VOX_CUDA_OK;
+}
+
+template <bool Q4, bool SF16>
+int launch_q(const CUtensorMap &tx, const CUtensorMap &tw, const GemmQArgs &q, cudaStream_t st, const char *name) {
+    auto kern = gemm_q_kernel<Q4, SF16>;
+    static bool attr_set[128] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 128 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(QCfg<Q4>::SMEM)) != cudaSuccess) return check_launch(name);
+        attr_set[dev] = true;
+    }
+    const int64_t tiles = int64_t((q.M + kBM - 1) / kBM) * ((q.N + kQBN - 1) / kQBN);
+    const int grid = int(tiles < sm_count() ? tiles : sm_count());
+    launch_k(kern, grid, kQThreads, QCfg<Q4>::SMEM, st, tx, tw, q);
+    return check_launch(name);
 }
 
 template <int BN, int EPI>
@@ -346,16 +706,11 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
                     std::string(name) + ": RoPE epilogue needs 3 inner columns with inner and hd multiples of 32");
     plan.a = a;
     plan.epi = epi;
-    // tile width: fewest tile columns per SM-wave (ceil(tiles / SMs) * BN), the wider tile on a tie
+    // tile width: the copy engine's feed from L2 bounds these tiles, and a wider tile reads fewer bytes per product, so
+    // 256 columns wherever they still give every SM work for at least half a wave, else 128; 64 for narrow outputs
     const int64_t sms = sm_count(), mt = (a.M + kBM - 1) / kBM, z = int64_t(a.batches) * a.groups;
-    int best = 256;
-    int64_t best_cost = -1;
-    for (int bn : {256, 128, 64}) {
-        if (bn > 64 && a.N <= bn / 2) continue;  // mostly empty tiles
-        const int64_t tiles = mt * ((a.N + bn - 1) / bn) * z;
-        const int64_t cost = (tiles + sms - 1) / sms * bn;
-        if (best_cost < 0 || cost < best_cost) best = bn, best_cost = cost;
-    }
+    const int64_t tiles256 = mt * ((a.N + 255) / 256) * z;
+    const int best = a.N <= 64 ? 64 : (a.N >= 512 && 2 * tiles256 >= sms) ? 256 : 128;
     // VOX_CUDA_GEMM_BN = 64 / 128 / 256 forces the tile width (for comparisons)
     static const int forced = [] {
         const char *e = std::getenv("VOX_CUDA_GEMM_BN");
@@ -378,6 +733,28 @@ int gemm_run(const GemmPlan &p, cudaStream_t st, const char *name) {
         case kEpiGeluTanhF32: return launch_bn<kEpiGeluTanhF32>(p, st, name);
         default: return launch_bn<kEpiGeluErfF32>(p, st, name);
     }
+}
+
+// The quantized prefill GEMM: y[m][rows] (+)= bias + x[m][cols] . W^T with Q8 / Q4 weights (vox_cuda_gemm_q8 / q4).
+int gemm_q(bool q4, const void *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y, int64_t rows,
+           int64_t cols, int64_t m, int accumulate, cudaStream_t st, const char *name) {
+    VOX_REQUIRE(scale_dtype == VOX_CUDA_F32 || scale_dtype == VOX_CUDA_F16, std::string(name) + ": scale dtype must be F32 or F16");
+    VOX_REQUIRE(rows >= 0 && cols > 0 && m >= 0 && cols % 32 == 0, std::string(name) + ": bad shape (cols must be a multiple of 32)");
+    VOX_REQUIRE(rows < (int64_t(1) << 31) && cols < (int64_t(1) << 31) && m < (int64_t(1) << 31), std::string(name) + ": shape too large");
+    if (rows == 0 || m == 0) return VOX_CUDA_OK;
+    VOX_REQUIRE(w && scale && x && y, std::string(name) + ": NULL pointer");
+    VOX_REQUIRE(aligned16(w) && aligned16(x), std::string(name) + ": w and x must be 16-byte aligned");
+    GemmQArgs q{};
+    q.M = int(m), q.N = int(rows), q.K = int(cols), q.nblk = int(cols / 32), q.scale = scale;
+    q.g.M = int(m), q.g.N = int(rows), q.g.K = int(cols), q.g.y = y, q.g.ldy = rows, q.g.bias = bias, q.g.accumulate = accumulate != 0;
+    CUtensorMap tx, tw;
+    int rc = plain_map(x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cols, m, cols * 4, kBK, kBM, tx, name);
+    if (rc != VOX_CUDA_OK) return rc;
+    rc = plain_map(w, CU_TENSOR_MAP_DATA_TYPE_UINT8, q4 ? cols / 2 : cols, rows, q4 ? cols / 2 : cols, q4 ? kBK / 2 : kBK, kQBN, tw, name);
+    if (rc != VOX_CUDA_OK) return rc;
+    const bool f16 = scale_dtype == VOX_CUDA_F16;
+    if (q4) return f16 ? launch_q<true, true>(tx, tw, q, st, name) : launch_q<true, false>(tx, tw, q, st, name);
+    return f16 ? launch_q<false, true>(tx, tw, q, st, name) : launch_q<false, false>(tx, tw, q, st, name);
 }
 
 int gemm_take_device_error(unsigned int *flags) { return take_device_error(flags); }
@@ -404,4 +781,14 @@ extern "C" int vox_cuda_gemm_bf16(const void *x, const void *w, const float *bia
     const int rc = gemm_plan(x, k, w, k, a, epi, p, "vox_cuda_gemm_bf16");
     if (rc != VOX_CUDA_OK) return rc;
     return gemm_run(p, reinterpret_cast<cudaStream_t>(stream), "vox_cuda_gemm_bf16");
+}
+
+extern "C" int vox_cuda_gemm_q8(const int8_t *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y, int64_t rows,
+                                int64_t cols, int64_t m, int accumulate, void *stream) {
+    return gemm_q(false, w, scale, scale_dtype, bias, x, y, rows, cols, m, accumulate, reinterpret_cast<cudaStream_t>(stream), "vox_cuda_gemm_q8");
+}
+
+extern "C" int vox_cuda_gemm_q4(const uint8_t *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y, int64_t rows,
+                                int64_t cols, int64_t m, int accumulate, void *stream) {
+    return gemm_q(true, w, scale, scale_dtype, bias, x, y, rows, cols, m, accumulate, reinterpret_cast<cudaStream_t>(stream), "vox_cuda_gemm_q4");
 }

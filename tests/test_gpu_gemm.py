@@ -4,7 +4,8 @@ y = act(x . w^T + bias) with bf16 x and w: every product of two bf16 values is e
 from the fp32 reference on the same (bf16-valued) operands only by the order of its f32 sums: within 1e-5 of
 sum |x w| per element (f32 output); a bf16 output adds one rounding (2^-8 relative). Shapes cover one row, edges
 that are not multiples of the 128 x BN tiles, K that is not a multiple of the 64-element step (zero fill), every
-tile width (64 / 128 / 256 columns), and the F5-base projections.
+tile width (64 / 128 / 256 columns), the CTA-pair 256 x 256 tiles (m and n of 512 or more, ragged edges included), and
+the F5-base projections.
 """
 
 from __future__ import annotations
@@ -34,7 +35,7 @@ def _bound(x, w, bias):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 64, 64), (100, 100, 712), (257, 257, 136), (300, 1000, 2048), (2048, 3072, 1024),
-                                   (512, 12288, 4096), (2048, 1024, 2048), (130, 520, 64)])
+                                   (512, 12288, 4096), (2048, 1024, 2048), (130, 520, 64), (1000, 1000, 520), (777, 4100, 1024)])
 def test_gemm_bf16_matches_fp32_reference(vox, m, n, k):
     g = torch.Generator(device="cuda").manual_seed(m * 7 + n * 3 + k)
     x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)

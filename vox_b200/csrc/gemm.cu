@@ -214,13 +214,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     bool ok = true;
 
     if (warp == 0) {
-        // ---- tensor copies
+        // ---- tensor copies (and L2 prefetches kPrefetch K steps ahead of them, across this CTA's tiles)
         uint32_t it = 0;
+        constexpr int kPrefetch = 2 * C::STAGES;
+        auto prefetch = [&](uint32_t j) {  // this CTA's j-th K step
+            const int t = blockIdx.x + int(j / uint32_t(kt)) * gridDim.x, kc = int(j % uint32_t(kt));
+            if (t >= tiles) return;
+            const Tile tl = tile_of(t, mt, nt, g.groups);
+            tma_prefetch_l2_3d(&ta, kc * kBK, tl.m0, tl.z);
+            tma_prefetch_l2_3d(&tb, kc * kBK, tl.ni * BN, tl.zg);
+        };
+        if (lane == 0)
+            for (int j = 0; j < kPrefetch; ++j) prefetch(uint32_t(j));
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const Tile tl = tile_of(t, mt, nt, g.groups);
             for (int kc = 0; kc < kt; ++kc, ++it) {
                 const int s = int(it % C::STAGES);
                 const uint32_t u = it / C::STAGES;
+                if (lane == 0) prefetch(it + kPrefetch);
                 if (!mbar_wait_warp(&empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;
@@ -309,6 +320,218 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ CTA pairs (cta_group::2): 256 x 256 output tiles
+//
+// A cluster of two CTAs on two SMs computes one 256 x 256 output tile: CTA r loads rows m0 + 128 r of x and rows
+// n0 + 128 r of W (its half of the tile's W columns) into its own shared memory, and CTA 0's single MMA thread issues
+// tcgen05.mma.cta_group::2 (M 256, N 256, K 16), which reads both CTAs' halves and writes each CTA's 128 output rows
+// (all 256 columns) into that CTA's tensor memory. Per SM and K step the tensor cores then do 128 x 256 x 64 products
+// on 32 KB of shared-memory traffic (128 FLOP a byte; the one-CTA 128 x 256 tile does 85), which is what the L2 feed
+// allows at full tensor rate. Both CTAs' copies complete on CTA 0's full barrier (the barrier's address with the
+// peer bit cleared); the MMA's commits arrive on both CTAs' barriers (tcgen05.commit multicast); each CTA's epilogue
+// reads its own accumulator and releases it on CTA 0's barrier. No copy is broadcast: each CTA loads its own tiles.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairStage = 2 * kABytes;  // x [128][64] + W half [128][64], 32 KB
+constexpr size_t kPairSmem = size_t(kPairStages) * kPairStage + 1024 + 256 + 4 * 4096;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(const void *p, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_addr(p)), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 3-D tiled copy whose completion is counted on the pair's CTA 0 barrier (bar: this CTA's barrier at the same offset).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    const uint32_t b0 = smem_addr(bar) & 0xFEFFFFFFu;  // the peer bit cleared: CTA 0 of the pair
+    asm volatile("cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(b0)
+                 : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+// Arrives on `bar` in both CTAs of the pair when every MMA this thread issued before has completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+                 "h"(uint16_t(3))
+                 : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                                                                   const GemmArgs g) {
+    constexpr int BN = 256;
+    constexpr uint32_t kIdesc = umma_idesc_bf16(256, BN);
+    extern __shared__ uint8_t gemm2_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t s0 = smem_addr(smem);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStage);
+    uint64_t *empty = full + kPairStages;
+    uint64_t *tfull = empty + kPairStages;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
+    const uint32_t STG_BASE = s0 + kPairStages * kPairStage + 256;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int mt = (g.M + 255) / 256, nt = (g.N + BN - 1) / BN;
+    const int tiles = mt * nt * g.batches * g.groups, kt = (g.K + kBK - 1) / kBK;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&tfull[0], 1);
+        mbar_init(&tfull[1], 1);
+        mbar_init(&tempty[0], 8);  // four epilogue warps in each CTA (used on CTA 0)
+        mbar_init(&tempty[1], 8);
+        mbar_init(drain, 1);
+        mbar_init_fence();
+        tma_prefetch_desc(&ta);
+        tma_prefetch_desc(&tb);
+    }
+    pdl_enter();
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)), "r"(2 * BN) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA traffic
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    bool ok = true;
+
+    if (warp == 0) {
+        // ---- tensor copies: this CTA's x rows and W half, completing on CTA 0's full barrier; L2 prefetches ahead
+        uint32_t it = 0;
+        constexpr int kPrefetch = 2 * kPairStages;
+        auto prefetch = [&](uint32_t j) {
+            const int t = pair + int(j / uint32_t(kt)) * npairs, kc = int(j % uint32_t(kt));
+            if (t >= tiles) return;
+            const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zg = z % g.groups;
+            tma_prefetch_l2_3d(&ta, kc * kBK, mi * 256 + 128 * int(rank), z);
+            tma_prefetch_l2_3d(&tb, kc * kBK, ni * BN + 128 * int(rank), zg);
+        };
+        if (lane == 0)
+            for (int j = 0; j < kPrefetch; ++j) prefetch(uint32_t(j));
+        for (int t = pair; t < tiles && ok; t += npairs) {
+            const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zg = z % g.groups;
+            for (int kc = 0; kc < kt; ++kc, ++it) {
+                const int s = int(it % kPairStages);
+                const uint32_t u = it / kPairStages;
+                if (lane == 0) prefetch(it + kPrefetch);
+                if (!mbar_wait_warp(&empty[s], (u & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t sa = s0 + uint32_t(s) * kPairStage;
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * kPairStage);
+                    tma_load_3d_pair(sa, &ta, kc * kBK, mi * 256 + 128 * int(rank), z, &full[s]);
+                    tma_load_3d_pair(sa + kABytes, &tb, kc * kBK, ni * BN + 128 * int(rank), zg, &full[s]);
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok && leader) {
+            const uint32_t last = it;
+            for (uint32_t j = last > uint32_t(kPairStages) ? last - kPairStages : 0; j < last; ++j)
+                mbar_wait_warp(&full[j % kPairStages], (j / kPairStages) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue (CTA 0 only)
+        if (leader) {
+            uint32_t it = 0, tc = 0;
+            for (int t = pair; t < tiles && ok; t += npairs, ++tc) {
+                const uint32_t a = tc & 1u, v = tc >> 1;
+                if (!mbar_wait_warp(&tempty[a], (v & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t dcol = tmem + a * BN;
+                for (int kc = 0; kc < kt; ++kc, ++it) {
+                    const int s = int(it % kPairStages);
+                    const uint32_t u = it / kPairStages;
+                    if (!mbar_wait_warp(&full[s], u & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t sa = s0 + uint32_t(s) * kPairStage, sb = sa + kABytes;
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; ++k)
+                            umma_bf16_pair(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
+                        umma_commit_pair(&empty[s]);  // both CTAs' stage s is free once these MMAs have read it
+                    }
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (lane == 0) umma_commit_pair(&tfull[a]);
+                __syncwarp();
+            }
+            if (!ok) {
+                if (lane == 0) umma_commit_pair(drain);
+                __syncwarp();
+                mbar_wait_warp(drain, 0);
+            }
+        }
+    } else {
+        // ---- epilogue: this CTA's 128 rows of the 256-row tile, all 256 columns
+        const int q = warp & 3;
+        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
+        const uint32_t tempty0 = map_rank(&tempty[0], 0);
+        uint32_t tc = 0;
+        for (int t = pair; t < tiles && ok; t += npairs, ++tc) {
+            const uint32_t a = tc & 1u, v = tc >> 1;
+            if (!mbar_wait_warp(&tfull[a], v & 1u)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zb = z / g.groups, zg = z % g.groups;
+            const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + a * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                const int c0 = ni * BN + c;
+                if (c0 >= g.N) break;
+                uint32_t r[32];
+                tmem_ld32(taddr + uint32_t(c), r);
+                tmem_wait_ld();
+                epilogue32<EPI>(g, r, mi * 256 + 128 * int(rank) + 32 * q, lane, c0, zb, zg, stg);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(tempty0 + a * 8);
+        }
+    }
+    tc_fence_before();
+    cluster_sync();  // the peer's last remote arrivals and reads are done before either CTA releases its memory
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
     }
 }
 
@@ -412,13 +635,23 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     bool ok = true;
 
     if (warp == 0) {
-        // ---- raw tiles
+        // ---- raw tiles (and L2 prefetches of the raw tiles kPrefetch K steps ahead: the ring holds only two)
         uint32_t it = 0;
+        constexpr int kPrefetch = 8;
+        auto prefetch = [&](uint32_t j) {
+            const int t = blockIdx.x + int(j / uint32_t(kt)) * gridDim.x, kc = int(j % uint32_t(kt));
+            if (t >= tiles) return;
+            tma_prefetch_l2_3d(&tx, kc * kBK, (t % mt) * kBM, 0);
+            tma_prefetch_l2_3d(&tw, kc * (Q4 ? kBK / 2 : kBK), (t / mt) * kQBN, 0);
+        };
+        if (lane == 0)
+            for (int j = 0; j < kPrefetch; ++j) prefetch(uint32_t(j));
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
             for (int kc = 0; kc < kt; ++kc, ++it) {
                 const int s = int(it % C::RS);
                 const uint32_t u = it / C::RS;
+                if (lane == 0) prefetch(it + kPrefetch);
                 if (!mbar_wait_warp(&raw_empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;
@@ -687,7 +920,37 @@ int launch(const GemmPlan &p, cudaStream_t st, const char *name) {
 }
 
 template <int EPI>
+int launch_pair(const GemmPlan &p, cudaStream_t st, const char *name) {
+    auto kern = gemm_tc2_kernel<EPI>;
+    static bool attr_set[128] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 128 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPairSmem)) != cudaSuccess) return check_launch(name);
+        attr_set[dev] = true;
+    }
+    const int64_t tiles = int64_t((p.a.M + 255) / 256) * ((p.a.N + 255) / 256) * p.a.batches * p.a.groups;
+    const int64_t pairs = sm_count() / 2;
+    const int grid = 2 * int(tiles < pairs ? tiles : pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = kPairSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    if (cudaLaunchKernelEx(&cfg, kern, p.ta, p.tb, p.a) != cudaSuccess) return check_launch(name);
+    return VOX_CUDA_OK;
+}
+
+template <int EPI>
 int launch_bn(const GemmPlan &p, cudaStream_t st, const char *name) {
+    if (p.pair) return launch_pair<EPI>(p, st, name);
     if (p.bn == 64) return launch<64, EPI>(p, st, name);
     if (p.bn == 256) return launch<256, EPI>(p, st, name);
     return launch<128, EPI>(p, st, name);
@@ -718,9 +981,16 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
         return v == 64 || v == 128 || v == 256 ? v : 0;
     }();
     plan.bn = forced ? forced : best;
+    // CTA pairs (256 x 256 tiles) where both extents fill them; VOX_CUDA_GEMM_PAIR = 0 / 1 forces the choice
+    static const int pair_mode = [] {
+        const char *e = std::getenv("VOX_CUDA_GEMM_PAIR");
+        return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : -1;
+    }();
+    plan.pair = pair_mode == 1 || (pair_mode < 0 && !forced && a.M >= 512 && a.N >= 512);
+    // both kernels read boxes of 128 x rows and of 128 (pair) or BN (one CTA) W rows
     int rc = bf16_map(x, a.K, a.M, z, ldx, kBM, plan.ta, name);
     if (rc != VOX_CUDA_OK) return rc;
-    return bf16_map(w, a.K, a.N, a.groups, ldw, plan.bn, plan.tb, name);
+    return bf16_map(w, a.K, a.N, a.groups, ldw, plan.pair ? 128 : plan.bn, plan.tb, name);
 }
 
 int gemm_run(const GemmPlan &p, cudaStream_t st, const char *name) {

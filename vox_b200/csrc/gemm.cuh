@@ -39,6 +39,7 @@ struct GemmPlan {
     CUtensorMap ta, tb;
     GemmArgs a;
     int bn = 128;
+    bool pair = false;  // a cluster of two CTAs per 256 x 256 tile (tcgen05 cta_group::2)
     int epi = kEpiF32;
 };
 

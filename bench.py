@@ -984,6 +984,71 @@ def run_gemm(args) -> None:
                       "config": {"workload": "tcgen05 bf16 GEMM vs cuBLAS, F5-base and prefill shapes"}, "results": res}), flush=True)
 
 
+def run_probe(args) -> None:
+    """One launch of each operator kernel that the suite does not time (LayerNorm plain and modulate, bias-add, gated
+    add, fused SwiGLU, SnakeBeta and Kokoro Snake, mul f32 / bf16, add bf16, row max and L2, the global sum's slot
+    partials and fold, the Philox fill) on inputs larger than L2 (64 MB a tensor), after one untimed pass, each timed
+    with CUDA events; one JSON line. Under ncu (one GPU, `-k regex:...`) it gives every such kernel's DRAM bytes and
+    throughput in one small capture."""
+    import torch
+
+    torch.cuda.set_device(0)
+    import vox_b200 as vox
+
+    peak, _ = peaks()
+    dev = torch.device("cuda", 0)
+    f32, bf16 = torch.float32, torch.bfloat16
+    fill = lambda t, d=1, a=0.0, b=1.0, sid=0: vox.fill_philox(t, d, a, b, seed=0, stream_id=sid)  # noqa: E731
+    R, D = 16384, 1024                      # 16 M elements: 64 MB f32
+    x = fill(torch.empty(R, D, device=dev), sid=90)
+    xb = fill(torch.empty(R, D, device=dev, dtype=bf16), sid=91)
+    y, yb = torch.empty_like(x), torch.empty_like(xb)
+    w, b = fill(torch.empty(D, device=dev), 1, 1, 0.1, 92), fill(torch.empty(D, device=dev), 1, 0, 0.1, 93)
+    B, T = 8, R // 8
+    g = fill(torch.empty(B, D, device=dev), 1, 0, 0.1, 94)
+    gu = fill(torch.empty(R // 2, 2 * D, device=dev), sid=95)
+    hu = torch.empty(R // 2, D, device=dev)
+    C, Tc = 512, R * D // (16 * 512)
+    xs = fill(torch.empty(16, C, Tc, device=dev), sid=96)
+    al = fill(torch.empty(C, device=dev), 0, 0.2, 2.0, 97)
+    be = fill(torch.empty(C, device=dev), 0, 0.5, 1.5, 98)
+    ys = torch.empty_like(xs)
+    rr = torch.empty(R, device=dev)
+    slots, sc, gout = torch.empty(840, dtype=torch.float64, device=dev), torch.empty(R, device=dev), torch.empty(1, dtype=torch.float64, device=dev)
+    nb = R * D * 4
+    ops = [
+        ("layernorm_f32", 2 * nb, lambda: vox.layernorm(x, w, b, 1e-5, out=y)),
+        ("layernorm_modulate_f32", 2 * nb, lambda: vox.layernorm(x, w, b, 1e-6, modulate=True, out=y)),
+        ("bias_add_f32", 2 * nb, lambda: vox.bias_add(y, b)),
+        ("gated_add_f32", 3 * nb, lambda: vox.gated_add(y.view(B, T, D), g, x.view(B, T, D))),
+        ("swiglu_fused_f32", 3 * nb // 2, lambda: vox.swiglu_fused(gu, out=hu)),
+        ("snake_beta_f32", 2 * nb, lambda: vox.snake(xs, al, vox.SNAKE_BETA, beta=be, out=ys)),
+        ("snake_kokoro_f32", 2 * nb, lambda: vox.snake(xs, al, vox.SNAKE_KOKORO, out=ys)),
+        ("mul_f32", 3 * nb, lambda: vox.mul(x, y, out=y)),
+        ("mul_bf16", 3 * nb // 2, lambda: vox.mul(xb, yb, out=yb)),
+        ("add_bf16", 3 * nb // 2, lambda: vox.add(xb, yb, out=yb)),
+        ("rowmax_f32", nb + R * 4, lambda: vox.row_reduce(x, vox.REDUCE_MAX, out=rr)),
+        ("rowl2_bf16", nb // 2 + R * 4, lambda: vox.row_reduce(xb, vox.REDUCE_L2, out=rr)),
+        ("global_sum_partials_f32", nb + R * 4, lambda: vox.global_sum_partials(x, 0, R, slots=slots, scratch=sc)),
+        ("global_sum_finish", 840 * 8, lambda: vox.global_sum_finish(slots, out=gout)),
+        ("fill_philox_normal_f32", nb, lambda: fill(y, sid=99)),
+    ]
+    for _, _, fn in ops:
+        fn()
+    torch.cuda.synchronize()
+    res = {}
+    for nm, by, fn in ops:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3
+        res[nm] = {"us": round(us, 2), "bytes": by, "gb_s": round(by / us / 1e3, 1), "frac_of_peak": round(by / us / 1e3 / peak, 3)}
+    print(json.dumps({"metric": METRIC, "mode": "probe", "unit": "GB/s", "peak": peak,
+                      "config": {"workload": "one launch of each kernel outside the suite, 64 MB tensors"}, "results": res}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -998,6 +1063,7 @@ def main() -> None:
     ap.add_argument("--scale", type=int, default=1, help="multiply the rows/heads/batches of cfg1-cfg4 (1 = BASELINE shapes)")
     ap.add_argument("--copy-roofline", action="store_true", help="cfg1-cfg4 ops against a size-matched device copy")
     ap.add_argument("--gemm", action="store_true", help="the tcgen05 GEMM alone against cuBLAS")
+    ap.add_argument("--probe", action="store_true", help="one launch of each kernel outside the suite (profiling)")
     ap.add_argument("--sweep-lo", type=int, default=20)
     ap.add_argument("--sweep-hi", type=int, default=32)
     args = ap.parse_args()
@@ -1011,6 +1077,8 @@ def main() -> None:
         run_copy_roofline(args)
     elif args.gemm:
         run_gemm(args)
+    elif args.probe:
+        run_probe(args)
     else:
         run_ours(args)
 

@@ -214,24 +214,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     bool ok = true;
 
     if (warp == 0) {
-        // ---- tensor copies (and L2 prefetches kPrefetch K steps ahead of them, across this CTA's tiles)
+        // ---- tensor copies
         uint32_t it = 0;
-        constexpr int kPrefetch = 2 * C::STAGES;
-        auto prefetch = [&](uint32_t j) {  // this CTA's j-th K step
-            const int t = blockIdx.x + int(j / uint32_t(kt)) * gridDim.x, kc = int(j % uint32_t(kt));
-            if (t >= tiles) return;
-            const Tile tl = tile_of(t, mt, nt, g.groups);
-            tma_prefetch_l2_3d(&ta, kc * kBK, tl.m0, tl.z);
-            tma_prefetch_l2_3d(&tb, kc * kBK, tl.ni * BN, tl.zg);
-        };
-        if (lane == 0)
-            for (int j = 0; j < kPrefetch; ++j) prefetch(uint32_t(j));
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const Tile tl = tile_of(t, mt, nt, g.groups);
             for (int kc = 0; kc < kt; ++kc, ++it) {
                 const int s = int(it % C::STAGES);
                 const uint32_t u = it / C::STAGES;
-                if (lane == 0) prefetch(it + kPrefetch);
                 if (!mbar_wait_warp(&empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;
@@ -423,24 +412,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
     bool ok = true;
 
     if (warp == 0) {
-        // ---- tensor copies: this CTA's x rows and W half, completing on CTA 0's full barrier; L2 prefetches ahead
+        // ---- tensor copies: this CTA's x rows and W half, completing on CTA 0's full barrier
         uint32_t it = 0;
-        constexpr int kPrefetch = 2 * kPairStages;
-        auto prefetch = [&](uint32_t j) {
-            const int t = pair + int(j / uint32_t(kt)) * npairs, kc = int(j % uint32_t(kt));
-            if (t >= tiles) return;
-            const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zg = z % g.groups;
-            tma_prefetch_l2_3d(&ta, kc * kBK, mi * 256 + 128 * int(rank), z);
-            tma_prefetch_l2_3d(&tb, kc * kBK, ni * BN + 128 * int(rank), zg);
-        };
-        if (lane == 0)
-            for (int j = 0; j < kPrefetch; ++j) prefetch(uint32_t(j));
         for (int t = pair; t < tiles && ok; t += npairs) {
             const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zg = z % g.groups;
             for (int kc = 0; kc < kt; ++kc, ++it) {
                 const int s = int(it % kPairStages);
                 const uint32_t u = it / kPairStages;
-                if (lane == 0) prefetch(it + kPrefetch);
                 if (!mbar_wait_warp(&empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;
@@ -635,23 +613,13 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     bool ok = true;
 
     if (warp == 0) {
-        // ---- raw tiles (and L2 prefetches of the raw tiles kPrefetch K steps ahead: the ring holds only two)
+        // ---- raw tiles
         uint32_t it = 0;
-        constexpr int kPrefetch = 8;
-        auto prefetch = [&](uint32_t j) {
-            const int t = blockIdx.x + int(j / uint32_t(kt)) * gridDim.x, kc = int(j % uint32_t(kt));
-            if (t >= tiles) return;
-            tma_prefetch_l2_3d(&tx, kc * kBK, (t % mt) * kBM, 0);
-            tma_prefetch_l2_3d(&tw, kc * (Q4 ? kBK / 2 : kBK), (t / mt) * kQBN, 0);
-        };
-        if (lane == 0)
-            for (int j = 0; j < kPrefetch; ++j) prefetch(uint32_t(j));
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
             for (int kc = 0; kc < kt; ++kc, ++it) {
                 const int s = int(it % C::RS);
                 const uint32_t u = it / C::RS;
-                if (lane == 0) prefetch(it + kPrefetch);
                 if (!mbar_wait_warp(&raw_empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;

@@ -952,9 +952,27 @@ def run_gemm(args) -> None:
         ours = min(t(lambda: vox.gemm_bf16(x, w, out=y)) for _ in range(3))
         ours_b = min(t(lambda: vox.gemm_bf16(x, w, out_dtype=torch.bfloat16, out=yb)) for _ in range(3))
         ref = min(t(lambda: torch.matmul(x, w.t(), out=yb)) for _ in range(3))
+        # weights rotated over copies totalling more than twice the L2, so each launch reads its W from HBM (as the
+        # layers of a model do)
+        ncopy = max(2, -(-300_000_000 // (n * k * 2)))
+        ws = [w.clone() for _ in range(ncopy)] if ncopy <= 64 else None
+        cold = cold_ref = None
+        if ws is not None:
+            ctr = [0]
+
+            def rot(fn):
+                def f():
+                    ctr[0] += 1
+                    fn(ws[ctr[0] % ncopy])
+                return f
+
+            cold = min(t(rot(lambda wi: vox.gemm_bf16(x, wi, out_dtype=torch.bfloat16, out=yb))) for _ in range(3))
+            cold_ref = min(t(rot(lambda wi: torch.matmul(x, wi.t(), out=yb))) for _ in range(3))
+            del ws
         res[nm] = {"m": m, "n": n, "k": k, "us_f32_out": round(ours, 2), "us_bf16_out": round(ours_b, 2), "cublas_bf16_us": round(ref, 2),
                    "tflops": round(fl / ours_b / 1e6, 1), "frac_of_tensor_peak": round(fl / ours_b / 1e6 / tpk, 3),
-                   "cublas_tflops": round(fl / ref / 1e6, 1)}
+                   "cublas_tflops": round(fl / ref / 1e6, 1),
+                   "cold_w_us": None if cold is None else round(cold, 2), "cold_w_cublas_us": None if cold_ref is None else round(cold_ref, 2)}
         del x, w, y, yb
     # the quantized prefill GEMM (Q8 / Q4 weights [12288][4096] with f16 scales, 512 f32 activation rows), weights rotated
     # over enough copies that they stream from HBM

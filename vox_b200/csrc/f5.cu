@@ -16,6 +16,7 @@
 #include <cublas_v2.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <string>
 #include <type_traits>
@@ -569,6 +570,7 @@ struct F5Plan {
     // tcgen05 GEMMs of the bf16 path (every K a multiple of 8): built once at create, replayed by the graph; the
     // in_proj input [x | cond] and weights in bf16
     bool tc = false;
+    int tc_mask = 63;  // which GEMMs run on the tcgen05 kernel when tc (all by default)
     std::vector<GemmPlan> g_qkv, g_o, g_ff1, g_ff2;
     GemmPlan g_proj, g_in, g_conv1, g_conv2;
     __nv_bfloat16 *xc_b = nullptr, *w_in = nullptr;
@@ -670,7 +672,7 @@ int record_embed(F5Plan &p, cudaStream_t st) {
     const vox_cuda_f5_desc &d = p.d;
     const int64_t R = p.R, D = d.dim, M = d.out_dim, C = d.in_dim - d.out_dim;
     const float one = 1.0f, zero = 0.0f;
-    if (p.tc) {  // [x | cond] in bf16, then one GEMM with the bias in its epilogue
+    if (p.tc && (p.tc_mask & 32)) {  // [x | cond] in bf16, then one GEMM with the bias in its epilogue
         const uint32_t ne = uint32_t(R * (M + C));
         launch_k(f5_concat_bf16_kernel, grid_for(ne, 256, 4), 256, 0, st, (const float *)p.xin, (const float *)p.cond, p.xc_b, ne,
                  uint32_t(M), uint32_t(C));
@@ -686,10 +688,10 @@ int record_embed(F5Plan &p, cudaStream_t st) {
         if (d.in_proj_b) F5_TRY(vox_cuda_bias_add(p.h, d.in_proj_b, R, D, VOX_CUDA_F32, st));
     }
     const uint32_t n = uint32_t(R * D);
-    F5_TRY(conv_pos(p, p.h, p.w1r, p.ctmp, p.tc ? &p.g_conv1 : nullptr, st));
+    F5_TRY(conv_pos(p, p.h, p.w1r, p.ctmp, p.tc && (p.tc_mask & 32) ? &p.g_conv1 : nullptr, st));
     launch_k(f5_bias_mish_kernel, grid_for(n, 256, 4), 256, 0, st, p.ctmp, d.pos1_b, (float *)nullptr, n, uint32_t(D));
     F5_TRY(check_launch("vox_cuda_f5 mish"));
-    F5_TRY(conv_pos(p, p.ctmp, p.w2r, p.o, p.tc ? &p.g_conv2 : nullptr, st));
+    F5_TRY(conv_pos(p, p.ctmp, p.w2r, p.o, p.tc && (p.tc_mask & 32) ? &p.g_conv2 : nullptr, st));
     launch_k(f5_bias_mish_kernel, grid_for(n, 256, 4), 256, 0, st, p.o, d.pos2_b, p.h, n, uint32_t(D));
     return check_launch("vox_cuda_f5 mish");
 }
@@ -793,7 +795,7 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
     for (int64_t l = 0; l < L; ++l) {
         const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
         if (p.tc) F5_TRY(prefetch_block(l + 1));  // the next block's weights arrive in L2 during this block
-        if (p.tc) {  // bias and RoPE in the GEMM's epilogue
+        if (p.tc && (p.tc_mask & 1)) {  // bias and RoPE in the GEMM's epilogue
             F5_TRY(gemm_run(p.g_qkv[size_t(l)], st, "vox_cuda_f5 q|k|v"));
         } else {
             F5_TRY(gemm_bf16(p, p.nrm_b, p.w_qkv + size_t(l) * 3 * IN * D, p.qkv_b, CUDA_R_16BF, R, 3 * IN, D));
@@ -805,19 +807,19 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
         launch_k(f5_flash_tc_kernel, fgt, kTcThreads, kTcSmem, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
                  (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (__nv_bfloat16 *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
         F5_TRY(check_launch("vox_cuda_f5 attention"));
-        if (p.tc) F5_TRY(gemm_run(p.g_o[size_t(l)], st, "vox_cuda_f5 o"));
+        if (p.tc && (p.tc_mask & 2)) F5_TRY(gemm_run(p.g_o[size_t(l)], st, "vox_cuda_f5 o"));
         else F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));
         F5_TRY(resmod(p, p.o, p.b_o + l * D, A + 2 * D, A + 4 * D, A + 3 * D, st));
-        if (p.tc) {  // bias and GELU-tanh in the ff1 GEMM's epilogue
+        if (p.tc && (p.tc_mask & 4)) {  // bias and GELU-tanh in the ff1 GEMM's epilogue
             F5_TRY(gemm_run(p.g_ff1[size_t(l)], st, "vox_cuda_f5 ff1"));
-            F5_TRY(gemm_run(p.g_ff2[size_t(l)], st, "vox_cuda_f5 ff2"));
         } else {
             F5_TRY(gemm_bf16(p, p.nrm_b, p.w_ff1 + size_t(l) * FF * D, p.ff_b, CUDA_R_16BF, R, FF, D));
             launch_k(f5_bias_gelu_kernel, grid_for(ff_octs, 256, 4), 256, 0, st, reinterpret_cast<uint4 *>(p.ff_b),
                      (const float *)(p.b_ff1 + l * FF), ff_octs, uint32_t(FF));
             F5_TRY(check_launch("vox_cuda_f5 bias/gelu (bf16)"));
-            F5_TRY(gemm_bf16(p, p.ff_b, p.w_ff2 + size_t(l) * D * FF, p.o, CUDA_R_32F, R, D, FF));
         }
+        if (p.tc && (p.tc_mask & 8)) F5_TRY(gemm_run(p.g_ff2[size_t(l)], st, "vox_cuda_f5 ff2"));
+        else F5_TRY(gemm_bf16(p, p.ff_b, p.w_ff2 + size_t(l) * D * FF, p.o, CUDA_R_32F, R, D, FF));
         if (l + 1 < L) {
             const float *An = A + 6 * D;
             F5_TRY(resmod(p, p.o, p.b_ff2 + l * D, A + 5 * D, An + D, An, st));
@@ -825,7 +827,7 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
             F5_TRY(resmod(p, p.o, p.b_ff2 + l * D, A + 5 * D, p.fin, p.fin + D, st));
         }
     }
-    if (p.tc) return gemm_run(p.g_proj, st, "vox_cuda_f5 proj_out");
+    if (p.tc && (p.tc_mask & 16)) return gemm_run(p.g_proj, st, "vox_cuda_f5 proj_out");
     F5_TRY(gemm_bf16(p, p.nrm_b, p.w_proj, p.out, CUDA_R_32F, R, d.out_dim, D));
     return vox_cuda_bias_add(p.out, p.b_proj, R, d.out_dim, VOX_CUDA_F32, st);
 }
@@ -915,7 +917,13 @@ int build(F5Plan &p, cudaStream_t user) {
     p.embed = d.in_proj != nullptr;
     {
         const int64_t cig = d.dim / kPosGroups;
-        p.tc = p.bf16 && D % 8 == 0 && IN % 32 == 0 && FF % 8 == 0 && d.dim_head % 32 == 0 &&
+        // VOX_CUDA_F5_GEMM=cublas keeps the bf16 step's GEMMs on cuBLAS; VOX_CUDA_F5_TC_MASK (bits: 1 q|k|v, 2 o, 4 ff1,
+        // 8 ff2, 16 proj_out, 32 input embedding) picks the ones on this library's kernel (for comparisons)
+        const char *e = std::getenv("VOX_CUDA_F5_GEMM");
+        const bool cublas = e && std::string(e) == "cublas";
+        const char *mk = std::getenv("VOX_CUDA_F5_TC_MASK");
+        p.tc_mask = mk ? std::atoi(mk) : 63;
+        p.tc = !cublas && p.bf16 && D % 8 == 0 && IN % 32 == 0 && FF % 8 == 0 && d.dim_head % 32 == 0 &&
                (!p.embed || (d.in_dim % 8 == 0 && d.dim % kPosGroups == 0 && cig % 8 == 0));
     }
     if (p.bf16) {
@@ -1024,7 +1032,7 @@ int build(F5Plan &p, cudaStream_t user) {
     if (cudaMemsetAsync(p.h, 0, R * D * 4, user) != cudaSuccess || cudaMemsetAsync(p.ts, 0, D * 4, user) != cudaSuccess)
         return check_launch("vox_cuda_f5_create");
     if (cudaStreamCreateWithFlags(&p.cap, cudaStreamNonBlocking) != cudaSuccess) return check_launch("vox_cuda_f5_create");
-    if (!p.tc) {  // cuBLAS only where a GEMM of the step is not on this library's tcgen05 kernel
+    if (!p.tc || p.tc_mask != 63) {  // cuBLAS only where a GEMM of the step is not on this library's tcgen05 kernel
         F5_TRY(alloc(reinterpret_cast<uint8_t **>(&p.ws), kBlasWorkspace, "cuBLAS workspace"));
         F5_TRY(blas_check(cublasCreate(&p.blas), "create"));
         F5_TRY(blas_check(cublasSetMathMode(p.blas, d.math == VOX_CUDA_F5_MATH_F32 ? CUBLAS_PEDANTIC_MATH : CUBLAS_DEFAULT_MATH), "math mode"));

@@ -38,7 +38,7 @@ template <int BN> struct Cfg {
     static constexpr uint32_t B_BYTES = BN * kBK * 2;
     static constexpr uint32_t STAGE = kABytes + B_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
-    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * 4096;  // + the epilogue warps' staging
+    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * 4096 + 4 * 1024;  // + epilogue staging and bias
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -66,35 +66,53 @@ constexpr uint32_t kStageWarpBytes = 32 * 128;  // epilogue staging: a warp's 32
 // row m32 + lane; acc: f32 bit patterns): bias / RoPE / GELU on the registers, then the block passes through the warp's
 // staging area in shared memory (16-byte chunk c of row r at chunk c ^ (r % 8): conflict-free both ways) so that each
 // store instruction writes whole 128-byte row segments of y instead of 32 scattered pieces.
+// Per-tile inputs of the epilogue, loaded before the accumulator is waited for (so the chunk loop makes no global
+// loads): the tile's bias columns in the warp's shared-memory slot, and (RoPE) the thread's row of the cos / sin table
+// in registers.
+struct EpiPre {
+    const float *bias_s;  // this warp's copy of bias[n0 .. n0 + BN) (shared memory), or nullptr
+    float2 cs[32];        // RoPE: cs[row % frames][0 .. hd / 2) (hd = 64)
+};
+
+template <int EPI>
+__device__ __forceinline__ void epi_prepare(const GemmArgs &g, int n0, int bn, int zg, int row, int lane, float *bias_s, EpiPre &pre) {
+    pre.bias_s = nullptr;
+    if (g.bias) {
+        __syncwarp();  // the previous tile's readers are done with the slot
+        for (int i = lane; i < bn; i += 32) bias_s[i] = n0 + i < g.N ? __ldg(g.bias + int64_t(zg) * g.N + n0 + i) : 0.f;
+        __syncwarp();
+        pre.bias_s = bias_s;
+    }
+    if constexpr (EPI == kEpiQkvRope) {
+        const float2 *cs = g.cs + int64_t((row < g.M ? row : 0) % g.frames) * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pre.cs[j] = __ldg(cs + j);
+    }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&acc)[32], int m32, int lane, int c0, int zb, int zg,
-                                           uint32_t stg) {
+                                           uint32_t stg, const EpiPre &pre, int cb) {
     const int row = m32 + lane;
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
     const int nv = min(32, g.N - c0);  // valid columns (warp-uniform)
-    if (g.bias) {
-        const float *b = g.bias + int64_t(zg) * g.N + c0;
-        if (nv == 32 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0) {
+    if (pre.bias_s) {  // tile columns cb .. cb + 31 (zeros past N)
+        const float4 *b4 = reinterpret_cast<const float4 *>(pre.bias_s + cb);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float4 bb = __ldg(reinterpret_cast<const float4 *>(b) + q);
-                v[4 * q] += bb.x, v[4 * q + 1] += bb.y, v[4 * q + 2] += bb.z, v[4 * q + 3] += bb.w;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (i < nv) v[i] += __ldg(b + i);
+        for (int q = 0; q < 8; ++q) {
+            const float4 bb = b4[q];
+            v[4 * q] += bb.x, v[4 * q + 1] += bb.y, v[4 * q + 2] += bb.z, v[4 * q + 3] += bb.w;
         }
     }
     if constexpr (EPI == kEpiQkvRope) {
         const int part = c0 / g.inner, ci = c0 - part * g.inner, head = ci / g.hd;
         if (part < 2 && head < g.rope_heads && row < g.M) {  // pairs (2j, 2j + 1) of the head, j = (ci % hd) / 2 ..
-            const float2 *cs = g.cs + int64_t(row % g.frames) * (g.hd / 2) + (ci % g.hd) / 2;
+            const bool hi = (ci % g.hd) >= 32;                    // the head's second 32 columns: pairs 16 .. 31
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const float2 c = __ldg(cs + j);
+                const float2 c = hi ? pre.cs[16 + j] : pre.cs[j];
                 const float x0 = v[2 * j], x1 = v[2 * j + 1];
                 v[2 * j] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));  // f5.cpp:696-701, CPU rounding
                 v[2 * j + 1] = __fadd_rn(__fmul_rn(x1, c.x), __fmul_rn(x0, c.y));
@@ -280,15 +298,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         // ---- epilogue: thread = output row 32 (warp % 4) + lane of the tile
         const int q = warp & 3;
         const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
+        float *bias_s = reinterpret_cast<float *>(smem + C::STAGES * C::STAGE + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
         uint32_t tc = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
+            const Tile tl = tile_of(t, mt, nt, g.groups);
+            EpiPre pre;
+            epi_prepare<EPI>(g, tl.ni * BN, BN, tl.zg, tl.m0 + 32 * q + lane, lane, bias_s, pre);
             if (!mbar_wait_warp(&tfull[a], v & 1u)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const Tile tl = tile_of(t, mt, nt, g.groups);
             const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + a * BN;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -297,7 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                 uint32_t r[32];
                 tmem_ld32(taddr + uint32_t(c), r);
                 tmem_wait_ld();
-                epilogue32<EPI>(g, r, tl.m0 + 32 * q, lane, c0, tl.zb, tl.zg, stg);
+                epilogue32<EPI>(g, r, tl.m0 + 32 * q, lane, c0, tl.zb, tl.zg, stg, pre, c);
             }
             tc_fence_before();
             __syncwarp();
@@ -324,7 +345,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 // reads its own accumulator and releases it on CTA 0's barrier. No copy is broadcast: each CTA loads its own tiles.
 constexpr int kPairStages = 6;
 constexpr uint32_t kPairStage = 2 * kABytes;  // x [128][64] + W half [128][64], 32 KB
-constexpr size_t kPairSmem = size_t(kPairStages) * kPairStage + 1024 + 256 + 4 * 4096;
+constexpr size_t kPairSmem = size_t(kPairStages) * kPairStage + 1024 + 256 + 4 * 4096 + 4 * 1024;
 
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
@@ -481,15 +502,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
         const int q = warp & 3;
         const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
         const uint32_t tempty0 = map_rank(&tempty[0], 0);
+        float *bias_s = reinterpret_cast<float *>(smem + kPairStages * kPairStage + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
         uint32_t tc = 0;
         for (int t = pair; t < tiles && ok; t += npairs, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
+            const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zb = z / g.groups, zg = z % g.groups;
+            EpiPre pre;
+            epi_prepare<EPI>(g, ni * BN, BN, zg, mi * 256 + 128 * int(rank) + 32 * q + lane, lane, bias_s, pre);
             if (!mbar_wait_warp(&tfull[a], v & 1u)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int mi = t % mt, rest = t / mt, ni = rest % nt, z = rest / nt, zb = z / g.groups, zg = z % g.groups;
             const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + a * BN;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -498,7 +522,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
                 uint32_t r[32];
                 tmem_ld32(taddr + uint32_t(c), r);
                 tmem_wait_ld();
-                epilogue32<EPI>(g, r, mi * 256 + 128 * int(rank) + 32 * q, lane, c0, zb, zg, stg);
+                epilogue32<EPI>(g, r, mi * 256 + 128 * int(rank) + 32 * q, lane, c0, zb, zg, stg, pre, c);
             }
             tc_fence_before();
             __syncwarp();
@@ -538,7 +562,7 @@ template <bool Q4> struct QCfg {
     static constexpr uint32_t RAW = kQARaw + CODES;
     static constexpr uint32_t CONV = kQAConv + kQBConv;
     static constexpr int RS = 2, CS = 2;
-    static constexpr size_t SMEM = size_t(RS) * RAW + size_t(CS) * CONV + 1024 + 256 + 4 * 4096;
+    static constexpr size_t SMEM = size_t(RS) * RAW + size_t(CS) * CONV + 1024 + 256 + 4 * 4096 + 4 * 1024;
 };
 
 // Two codes (bytes b0, b1 of w, already offset to unsigned) as f16x2 1024 + u: prmt puts the code byte under 0x64.
@@ -776,15 +800,18 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         // ---- epilogue (warps 2..5)
         const int qw = warp & 3;
         const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
+        float *bias_s = reinterpret_cast<float *>(raw + C::RS * C::RAW + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
         uint32_t tc = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
+            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
+            EpiPre pre;
+            epi_prepare<kEpiF32>(q.g, n0, kQBN, 0, m0 + 32 * qw + lane, lane, bias_s, pre);
             if (!mbar_wait_warp(&tfull[a], v & 1u)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
             const uint32_t taddr = tmem + (uint32_t(32 * qw) << 16) + a * kQBN;
 #pragma unroll 1
             for (int c = 0; c < kQBN; c += 32) {
@@ -792,7 +819,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
                 uint32_t r[32];
                 tmem_ld32(taddr + uint32_t(c), r);
                 tmem_wait_ld();
-                epilogue32<kEpiF32>(q.g, r, m0 + 32 * qw, lane, n0 + c, 0, 0, stg);
+                epilogue32<kEpiF32>(q.g, r, m0 + 32 * qw, lane, n0 + c, 0, 0, stg, pre, c);
             }
             tc_fence_before();
             __syncwarp();
@@ -933,8 +960,8 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
                 std::string(name) + ": x and W need 16-byte aligned rows (K and the row pitches multiples of 8)");
     VOX_REQUIRE(epi >= kEpiF32 && epi <= kEpiGeluErfF32, std::string(name) + ": unknown epilogue");
     if (epi == kEpiQkvRope)
-        VOX_REQUIRE(a.cs && a.inner > 0 && a.inner % 32 == 0 && a.hd % 32 == 0 && a.N == 3 * a.inner && a.frames > 0,
-                    std::string(name) + ": RoPE epilogue needs 3 inner columns with inner and hd multiples of 32");
+        VOX_REQUIRE(a.cs && a.inner > 0 && a.inner % 64 == 0 && a.hd == 64 && a.N == 3 * a.inner && a.frames > 0,
+                    std::string(name) + ": RoPE epilogue needs heads of 64 and 3 inner columns");
     plan.a = a;
     plan.epi = epi;
     // tile width: the copy engine's feed from L2 bounds these tiles, and a wider tile reads fewer bytes per product, so

@@ -1003,11 +1003,12 @@ def run_gemm(args) -> None:
 
 
 def run_probe(args) -> None:
-    """One launch of each operator kernel that the suite does not time (LayerNorm plain and modulate, bias-add, gated
-    add, fused SwiGLU, SnakeBeta and Kokoro Snake, mul f32 / bf16, add bf16, row max and L2, the global sum's slot
-    partials and fold, the Philox fill) on inputs larger than L2 (64 MB a tensor), after one untimed pass, each timed
-    with CUDA events; one JSON line. Under ncu (one GPU, `-k regex:...`) it gives every such kernel's DRAM bytes and
-    throughput in one small capture."""
+    """Each operator kernel that the suite does not time (LayerNorm plain and modulate, bias-add, gated add, fused
+    SwiGLU, SnakeBeta and Kokoro Snake, mul f32 / bf16, add bf16, row max and L2, the global sum's slot partials and
+    fold, the Philox fill) on [rows][1024] tensors (default 131072 rows: 512 MB a f32 tensor, four times L2, so no L2
+    flush is needed): `--probe-reps` warm-up launches, then `--probe-reps` launches timed back to back with CUDA events
+    behind a spin kernel (no host launch gaps), mean per launch; one JSON line. With `--probe-reps 1` every kernel
+    launches once after the input fills: the form an ncu launch list or section capture of all of them takes."""
     import torch
 
     torch.cuda.set_device(0)
@@ -1017,7 +1018,7 @@ def run_probe(args) -> None:
     dev = torch.device("cuda", 0)
     f32, bf16 = torch.float32, torch.bfloat16
     fill = lambda t, d=1, a=0.0, b=1.0, sid=0: vox.fill_philox(t, d, a, b, seed=0, stream_id=sid)  # noqa: E731
-    R, D = 16384, 1024                      # 16 M elements: 64 MB f32
+    R, D = args.probe_rows, 1024
     x = fill(torch.empty(R, D, device=dev), sid=90)
     xb = fill(torch.empty(R, D, device=dev, dtype=bf16), sid=91)
     y, yb = torch.empty_like(x), torch.empty_like(xb)
@@ -1051,20 +1052,26 @@ def run_probe(args) -> None:
         ("global_sum_finish", 840 * 8, lambda: vox.global_sum_finish(slots, out=gout)),
         ("fill_philox_normal_f32", nb, lambda: fill(y, sid=99)),
     ]
-    for _, _, fn in ops:
-        fn()
+    reps = max(1, args.probe_reps)
     torch.cuda.synchronize()
     res = {}
     for nm, by, fn in ops:
+        if reps > 1:
+            for _ in range(reps):
+                fn()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000 if reps > 1 else 1000)  # holds the stream while the host enqueues the timed launches
         e0.record()
-        fn()
+        for _ in range(reps):
+            fn()
         e1.record()
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3
+        us = e0.elapsed_time(e1) * 1e3 / reps
         res[nm] = {"us": round(us, 2), "bytes": by, "gb_s": round(by / us / 1e3, 1), "frac_of_peak": round(by / us / 1e3 / peak, 3)}
     print(json.dumps({"metric": METRIC, "mode": "probe", "unit": "GB/s", "peak": peak,
-                      "config": {"workload": "one launch of each kernel outside the suite, 64 MB tensors"}, "results": res}), flush=True)
+                      "config": {"workload": f"each kernel outside the suite on [{R}][{D}] tensors, mean of {reps} back-to-back launches"},
+                      "results": res}), flush=True)
 
 
 def main() -> None:
@@ -1082,6 +1089,8 @@ def main() -> None:
     ap.add_argument("--copy-roofline", action="store_true", help="cfg1-cfg4 ops against a size-matched device copy")
     ap.add_argument("--gemm", action="store_true", help="the tcgen05 GEMM alone against cuBLAS")
     ap.add_argument("--probe", action="store_true", help="one launch of each kernel outside the suite (profiling)")
+    ap.add_argument("--probe-rows", type=int, default=131072, help="--probe: rows of 1024 elements a tensor")
+    ap.add_argument("--probe-reps", type=int, default=20, help="--probe: warm-up and timed launches of each kernel")
     ap.add_argument("--sweep-lo", type=int, default=20)
     ap.add_argument("--sweep-hi", type=int, default=32)
     args = ap.parse_args()

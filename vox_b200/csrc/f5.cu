@@ -401,25 +401,6 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
 
 // ------------------------------------------------------------------ bf16 pipeline helpers
 
-// dst = bf16(src) (RN), n / 2 pairs (weights, converted once at plan creation).
-// Warms L2 with a block's bf16 weights ahead of its GEMMs (the weights of all blocks do not fit in L2, the activations
-// between the kernels do): thread i issues bulk L2 prefetches of buffer i in 1 MB pieces, without waiting for them,
-// then waits for the previous grid like every kernel of the step (so the kernels after it still follow the one before).
-__global__ void __launch_bounds__(32) f5_l2_prefetch_kernel(const char *b0, uint64_t n0, const char *b1, uint64_t n1, const char *b2,
-                                                            uint64_t n2, const char *b3, uint64_t n3) {
-    const char *bs[4] = {b0, b1, b2, b3};
-    const uint64_t ns[4] = {n0, n1, n2, n3};
-    if (threadIdx.x < 4) {
-        const char *b = bs[threadIdx.x];
-        const uint64_t n = ns[threadIdx.x] & ~uint64_t(15);
-        for (uint64_t o = 0; o < n; o += (1u << 20)) {
-            const uint32_t sz = uint32_t(n - o < (1u << 20) ? n - o : (1u << 20));
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + o), "r"(sz) : "memory");
-        }
-    }
-    pdl_enter();
-}
-
 // xc [R][M + C] (bf16, RN) = [x [R][M] | cond [R][C]] (f32): the input of the in_proj GEMM; one element a thread.
 __global__ void __launch_bounds__(256) f5_concat_bf16_kernel(const float *x, const float *cond, __nv_bfloat16 *xc, uint32_t n,
                                                              uint32_t M, uint32_t C) {
@@ -450,6 +431,7 @@ __global__ void __launch_bounds__(256) f5_gemv_f32_kernel(const float *const *W,
     if (lane == 0) y[size_t(l) * rows + o] = acc + (bias ? bias[size_t(l) * rows + o] : 0.f);
 }
 
+// dst = bf16(src) (RN), n / 2 pairs (weights, converted once at plan creation).
 __global__ void __launch_bounds__(256) f5_to_bf16_kernel(const float2 *src, uint32_t *dst, size_t pairs) {
     pdl_enter();
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs; i += size_t(gridDim.x) * blockDim.x) {
@@ -783,18 +765,8 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
         return check_launch("vox_cuda_f5 attention (shared memory)");
     const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
     F5_TRY(resmod(p, nullptr, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
-    auto prefetch_block = [&](int64_t l) {  // block l's bf16 weights into L2 (16 MB at F5 base)
-        if (l >= L) return VOX_CUDA_OK;
-        const size_t ls = size_t(l);
-        launch_k(f5_l2_prefetch_kernel, 1, 32, 0, st, (const char *)(p.w_qkv + ls * 3 * IN * D), uint64_t(3 * IN * D * 2),
-                 (const char *)(p.w_o + ls * D * IN), uint64_t(D * IN * 2), (const char *)(p.w_ff1 + ls * FF * D), uint64_t(FF * D * 2),
-                 (const char *)(p.w_ff2 + ls * D * FF), uint64_t(D * FF * 2));
-        return check_launch("vox_cuda_f5 weight prefetch");
-    };
-    if (p.tc) F5_TRY(prefetch_block(0));
     for (int64_t l = 0; l < L; ++l) {
         const float *A = p.ada_all + l * 6 * D;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
-        if (p.tc) F5_TRY(prefetch_block(l + 1));  // the next block's weights arrive in L2 during this block
         if (p.tc && (p.tc_mask & 1)) {  // bias and RoPE in the GEMM's epilogue
             F5_TRY(gemm_run(p.g_qkv[size_t(l)], st, "vox_cuda_f5 q|k|v"));
         } else {

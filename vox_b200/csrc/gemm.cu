@@ -34,11 +34,12 @@ constexpr int kGemmThreads = 192;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 
 template <int BN> struct Cfg {
-    static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 6 : 8;
+    static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 5 : 7;
+    static constexpr uint32_t SWB = BN == 256 ? 4096 : 8192;  // epilogue staging bytes a warp
     static constexpr uint32_t B_BYTES = BN * kBK * 2;
     static constexpr uint32_t STAGE = kABytes + B_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
-    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * 4096 + 4 * 1024;  // + epilogue staging and bias
+    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * SWB + 4 * 1024;  // + epilogue staging and bias
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -60,7 +61,7 @@ __device__ __forceinline__ Tile tile_of(int t, int mt, int nt, int groups) {
     return r;
 }
 
-constexpr uint32_t kStageWarpBytes = 32 * 128;  // epilogue staging: a warp's 32 rows x 32 columns (f32), 4 KB
+constexpr uint32_t kStageWarpBytes = 32 * 128;  // one epilogue staging block: a warp's 32 rows x 32 columns (f32), 4 KB
 
 // The epilogue of 32 consecutive columns [c0, c0 + 32) of the warp's 32 output rows m32 .. m32 + 31 (thread lane holds
 // row m32 + lane; acc: f32 bit patterns): bias / RoPE / GELU on the registers, then the block passes through the warp's
@@ -90,9 +91,11 @@ __device__ __forceinline__ void epi_prepare(const GemmArgs &g, int n0, int bn, i
     }
 }
 
-template <int EPI>
-__device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&acc)[32], int m32, int lane, int c0, int zb, int zg,
-                                           uint32_t stg, const EpiPre &pre, int cb) {
+// SWB: the warp's staging bytes; tensor stores rotate through SWB / block-size blocks (seq counts the warp's stores),
+// so a block waits only for the store that used its buffer SWB / block-size stores before.
+template <int EPI, uint32_t SWB>
+__device__ __forceinline__ void epilogue32(const GemmArgs &g, const CUtensorMap *ty, const uint32_t (&acc)[32], int m32, int lane, int c0, int zb,
+                                           int zg, uint32_t stg, uint32_t &seq, const EpiPre &pre, int cb) {
     const int row = m32 + lane;
     float v[32];
 #pragma unroll
@@ -135,15 +138,33 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&a
     constexpr int CH = F32OUT ? 8 : 4;             // 16-byte chunks a row
     constexpr int EPC = F32OUT ? 4 : 8;            // elements a chunk
     constexpr int RB = CH * 16;                    // staged row bytes
-    // registers -> staging (row = lane)
+    const bool tst = g.tma_store != 0;
+    constexpr uint32_t BOX = 32 * RB;              // staged block bytes
+    constexpr int NB = int(SWB / BOX);             // staging buffers for tensor stores
+    if (tst) {  // the store that last used this buffer has finished reading it (a no-op in lanes without stores)
+        stg += (seq % uint32_t(NB)) * BOX;
+        bulk_wait_read<NB - 1>();
+        __syncwarp();
+    }
+    // registers -> staging (row = lane). For a tensor store the layout is the map's swizzle: 16-byte chunk c of row r at
+    // c ^ (r % 8) (f32, 128-byte rows: the 128-byte swizzle) or c ^ ((r / 2) % 4) (bf16, 64-byte rows: the 64-byte
+    // swizzle); both are free of bank conflicts for these writes.
+    const int sw = F32OUT ? (lane & 7) : tst ? ((lane >> 1) & 3) : (lane & 3);
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
         uint4 w;
         if (F32OUT) w = make_uint4(__float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3]));
         else w = make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
                             pack_bf16(v[8 * c + 6], v[8 * c + 7]));
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stg + lane * RB + ((c ^ (lane & (CH - 1))) << 4)), "r"(w.x), "r"(w.y),
-                     "r"(w.z), "r"(w.w) : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stg + lane * RB + ((c ^ sw) << 4)), "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w)
+                     : "memory");
+    }
+    if (tst) {  // one tensor store (or add) of the 32 x 32 block; rows >= M and columns past the map's extent are clipped
+        fence_proxy_async();
+        __syncwarp();
+        tma_store_3d_warp(ty, stg, int(int64_t(zg) * g.y_gstride) + c0, m32, zb, F32OUT && g.accumulate);
+        ++seq;
+        return;
     }
     __syncwarp();
     // staging -> y: each instruction covers 32 / CH rows, CH lanes a row (one 16-byte chunk each)
@@ -190,21 +211,36 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &g, const uint32_t (&a
     __syncwarp();  // the staging area is reused by the next block
 }
 
+// The epilogue of one accumulator: its 32-column chunks [0, nch) (thread = row m32 + lane; taddr: this warp's lanes,
+// column 0), each loaded from tensor memory, finished and stored in turn. (Loading the next chunk while the current
+// one is stored measured slower.)
+template <int EPI, uint32_t SWB>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &g, const CUtensorMap *ty, uint32_t taddr, int nch, int m32, int lane, int n0,
+                                              int zb, int zg, uint32_t stg, uint32_t &seq, const EpiPre &pre) {
+#pragma unroll 1
+    for (int c = 0; c < nch; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + uint32_t(32 * c), r);
+        tmem_wait_ld(r);
+        epilogue32<EPI, SWB>(g, ty, r, m32, lane, n0 + 32 * c, zb, zg, stg, seq, pre, 32 * c);
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                                                                  const GemmArgs g) {
+                                                                  const __grid_constant__ CUtensorMap ty, const GemmArgs g) {
     using C = Cfg<BN>;
     constexpr uint32_t kIdesc = umma_idesc_bf16(kBM, BN);
     extern __shared__ uint8_t gemm_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t s0 = smem_addr(smem);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE + 4 * C::SWB);
     uint64_t *empty = full + C::STAGES;
     uint64_t *tfull = empty + C::STAGES;  // [2]: accumulator a holds a finished tile
     uint64_t *tempty = tfull + 2;         // [2]: accumulator a has been read out
     uint64_t *drain = tempty + 2;         // wind-down: every MMA issued has completed
     uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
-    const uint32_t STG_BASE = s0 + C::STAGES * C::STAGE + 256;  // the epilogue warps' staging areas (after the barriers)
+    const uint32_t STG_BASE = s0 + C::STAGES * C::STAGE;  // the epilogue warps' staging areas (1024-byte aligned), then the barriers
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (g.M + kBM - 1) / kBM, nt = (g.N + BN - 1) / BN;
     const int tiles = mt * nt * g.batches * g.groups, kt = (g.K + kBK - 1) / kBK;
@@ -223,11 +259,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         tma_prefetch_desc(&ta);
         tma_prefetch_desc(&tb);
     }
-    pdl_enter();  // the previous grid (its outputs, and the tensor memory it held) is complete
-    if (warp == 0) tmem_alloc(tslot, C::TMEM_COLS);
+    if (warp == 0) tmem_alloc(tslot, C::TMEM_COLS);  // (no kernel of this library co-resides with a GEMM CTA: shared memory)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_enter();  // the previous grid is complete before the first read of its outputs and the first write of y
     const uint32_t tmem = *tslot;
     bool ok = true;
 
@@ -243,12 +279,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                     ok = false;
                     break;
                 }
-                if (lane == 0) {
-                    const uint32_t sa = s0 + uint32_t(s) * C::STAGE;
-                    mbar_arrive_expect_tx(&full[s], C::STAGE);
-                    tma_load_3d(sa, &ta, kc * kBK, tl.m0, tl.z, &full[s]);
-                    tma_load_3d(sa + kABytes, &tb, kc * kBK, tl.ni * BN, tl.zg, &full[s]);
-                }
+                const uint32_t sa = s0 + uint32_t(s) * C::STAGE;
+                tma_stage_warp(&full[s], C::STAGE, sa, &ta, kc * kBK, tl.m0, tl.z, sa + kABytes, &tb, kc * kBK, tl.ni * BN, tl.zg);
                 __syncwarp();
             }
         }
@@ -276,29 +308,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                     break;
                 }
                 tc_fence_after();
-                if (lane == 0) {
+                {  // the whole warp, one lane elected to issue (operands warp-uniform)
                     const uint32_t sa = s0 + uint32_t(s) * C::STAGE, sb = sa + kABytes;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
-                        umma_bf16(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
-                    umma_commit(&empty[s]);  // the stage returns to the copy warp when these MMAs have read it
+                        umma_bf16_warp(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
+                    umma_commit_warp(&empty[s]);  // the stage returns to the copy warp when these MMAs have read it
                 }
                 __syncwarp();
             }
             if (!ok) break;
-            if (lane == 0) umma_commit(&tfull[a]);
+            umma_commit_warp(&tfull[a]);
             __syncwarp();
         }
         if (!ok) {  // wind-down: every MMA issued completes before the tensor memory is released
-            if (lane == 0) umma_commit(drain);
+            umma_commit_warp(drain);
             __syncwarp();
             mbar_wait_warp(drain, 0);
         }
     } else {
         // ---- epilogue: thread = output row 32 (warp % 4) + lane of the tile
         const int q = warp & 3;
-        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
-        float *bias_s = reinterpret_cast<float *>(smem + C::STAGES * C::STAGE + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
+        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * C::SWB;
+        float *bias_s = reinterpret_cast<float *>(smem + C::STAGES * C::STAGE + 4 * C::SWB + 256) + (warp - 2) * 256;
+        uint32_t seq = 0;
         uint32_t tc = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
@@ -310,19 +343,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                 break;
             }
             tc_fence_after();
-            const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + a * BN;
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                const int c0 = tl.ni * BN + c;
-                if (c0 >= g.N) break;  // warp-uniform
-                uint32_t r[32];
-                tmem_ld32(taddr + uint32_t(c), r);
-                tmem_wait_ld();
-                epilogue32<EPI>(g, r, tl.m0 + 32 * q, lane, c0, tl.zb, tl.zg, stg, pre, c);
-            }
+            const int n0 = tl.ni * BN, nch = min(BN, g.N - n0 + 31) / 32;  // chunks holding columns < N
+            epilogue_tile<EPI, C::SWB>(g, &ty, tmem + (uint32_t(32 * q) << 16) + a * BN, nch, tl.m0 + 32 * q, lane, n0, tl.zb, tl.zg, stg, seq, pre);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[a]);
+        }
+        if (g.tma_store) {  // the tensor stores complete before the CTA's shared memory is released
+            bulk_wait_all();
+            __syncwarp();
         }
     }
     tc_fence_before();
@@ -333,19 +362,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     }
 }
 
-// ------------------------------------------------------------------ CTA pairs (cta_group::2): 256 x 256 output tiles
+// ------------------------------------------------------------------ CTA pairs (cta_group::2): 256 x BN output tiles
 //
-// A cluster of two CTAs on two SMs computes one 256 x 256 output tile: CTA r loads rows m0 + 128 r of x and rows
-// n0 + 128 r of W (its half of the tile's W columns) into its own shared memory, and CTA 0's single MMA thread issues
-// tcgen05.mma.cta_group::2 (M 256, N 256, K 16), which reads both CTAs' halves and writes each CTA's 128 output rows
-// (all 256 columns) into that CTA's tensor memory. Per SM and K step the tensor cores then do 128 x 256 x 64 products
-// on 32 KB of shared-memory traffic (128 FLOP a byte; the one-CTA 128 x 256 tile does 85), which is what the L2 feed
-// allows at full tensor rate. Both CTAs' copies complete on CTA 0's full barrier (the barrier's address with the
-// peer bit cleared); the MMA's commits arrive on both CTAs' barriers (tcgen05.commit multicast); each CTA's epilogue
-// reads its own accumulator and releases it on CTA 0's barrier. No copy is broadcast: each CTA loads its own tiles.
-constexpr int kPairStages = 6;
-constexpr uint32_t kPairStage = 2 * kABytes;  // x [128][64] + W half [128][64], 32 KB
-constexpr size_t kPairSmem = size_t(kPairStages) * kPairStage + 1024 + 256 + 4 * 4096 + 4 * 1024;
+// A cluster of two CTAs on two SMs computes one 256 x BN output tile (BN 128, 192 or 256): CTA r loads rows
+// m0 + 128 r of x and rows n0 + (BN / 2) r of W (its half of the tile's W columns) into its own shared memory, and
+// CTA 0's single MMA thread issues tcgen05.mma.cta_group::2 (M 256, N BN, K 16), which reads both CTAs' halves and
+// writes each CTA's 128 output rows (all BN columns) into that CTA's tensor memory. Per SM and K step the tensor cores
+// then do 128 x BN x 64 products on 16 KB + BN x 64 B of shared-memory traffic (at BN 256: 128 FLOP a byte; the
+// one-CTA 128 x 256 tile does 85), which is what the L2 feed allows at full tensor rate. Both CTAs' copies complete on
+// CTA 0's full barrier (the barrier's address with the peer bit cleared); the MMA's commits arrive on both CTAs'
+// barriers (tcgen05.commit multicast); each CTA's epilogue reads its own accumulator and releases it on CTA 0's
+// barrier. No copy is broadcast: each CTA loads its own tiles.
+template <int BN> struct PairCfg {
+    static constexpr uint32_t STAGE = kABytes + uint32_t(BN / 2) * kBK * 2;  // x [128][64] + W half [BN / 2][64]
+    static constexpr int STAGES = BN == 256 ? 6 : 7;
+    static constexpr uint32_t SWB = BN == 128 ? 8192 : 4096;  // epilogue staging bytes a warp
+    static constexpr uint32_t ACC = BN == 192 ? 256 : BN;                    // column offset of the second accumulator
+    static constexpr uint32_t TMEM_COLS = 2 * ACC;                           // two accumulators (a power of two)
+    static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * SWB + 4 * 1024;
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
@@ -364,42 +399,52 @@ __device__ __forceinline__ uint32_t map_rank(const void *p, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
-// 3-D tiled copy whose completion is counted on the pair's CTA 0 barrier (bar: this CTA's barrier at the same offset).
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
-    const uint32_t b0 = smem_addr(bar) & 0xFEFFFFFFu;  // the peer bit cleared: CTA 0 of the pair
-    asm volatile("cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-                 ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(b0)
+// One stage's copies of a pair CTA, issued by a whole converged warp through one elected lane: CTA 0's lane arrives
+// on its full barrier expecting both CTAs' bytes; each CTA's two copies complete on CTA 0's barrier.
+__device__ __forceinline__ void tma_stage_pair_warp(uint64_t *bar, bool leader, uint32_t bytes, uint32_t dst_a, const CUtensorMap *ma, int xa, int ya,
+                                                    int za, uint32_t dst_b, const CUtensorMap *mb, int xb, int yb, int zb) {
+    const uint32_t b = smem_addr(bar), b0 = b & 0xFEFFFFFFu;
+    asm volatile("{\n\t.reg .pred e, l;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.and.b32 l, %13, 0, e;\n\t"
+                 "@l mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t"
+                 "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%3, {%4, %5, %6}], [%12];\n\t"
+                 "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%7], [%8, {%9, %10, %11}], [%12];\n\t}"
+                 ::"r"(b), "r"(bytes), "r"(dst_a), "l"(ma), "r"(xa), "r"(ya), "r"(za), "r"(dst_b), "l"(mb), "r"(xb), "r"(yb), "r"(zb), "r"(b0),
+                 "r"(uint32_t(leader))
                  : "memory");
 }
+// tcgen05.mma.cta_group::2 issued by a whole converged warp, one lane elected (as umma_bf16_warp).
 __device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
-        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u)
+        "{\n\t.reg .pred e, p;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// Arrives on `bar` in both CTAs of the pair when every MMA this thread issued before has completed.
+// Arrives on `bar` in both CTAs of the pair when every MMA the elected lane issued before has completed (whole warp).
 __device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+    asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(smem_addr(bar)),
                  "h"(uint16_t(3))
                  : "memory");
 }
 
-template <int EPI>
+template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                                                                   const GemmArgs g) {
-    constexpr int BN = 256;
+                                                                   const __grid_constant__ CUtensorMap ty, const GemmArgs g) {
+    using P = PairCfg<BN>;
+    constexpr int kPairStages = P::STAGES;
+    constexpr uint32_t kPairStage = P::STAGE;
     constexpr uint32_t kIdesc = umma_idesc_bf16(256, BN);
     extern __shared__ uint8_t gemm2_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t s0 = smem_addr(smem);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStage);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStage + 4 * P::SWB);
     uint64_t *empty = full + kPairStages;
     uint64_t *tfull = empty + kPairStages;
     uint64_t *tempty = tfull + 2;
     uint64_t *drain = tempty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
-    const uint32_t STG_BASE = s0 + kPairStages * kPairStage + 256;
+    const uint32_t STG_BASE = s0 + kPairStages * kPairStage;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
@@ -421,14 +466,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
         tma_prefetch_desc(&ta);
         tma_prefetch_desc(&tb);
     }
-    pdl_enter();
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)), "r"(2 * BN) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)), "r"(P::TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
     cluster_sync();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA traffic
     tc_fence_after();
+    pdl_enter();
     const uint32_t tmem = *tslot;
     bool ok = true;
 
@@ -444,12 +489,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
                     ok = false;
                     break;
                 }
-                if (lane == 0) {
-                    const uint32_t sa = s0 + uint32_t(s) * kPairStage;
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * kPairStage);
-                    tma_load_3d_pair(sa, &ta, kc * kBK, mi * 256 + 128 * int(rank), z, &full[s]);
-                    tma_load_3d_pair(sa + kABytes, &tb, kc * kBK, ni * BN + 128 * int(rank), zg, &full[s]);
-                }
+                const uint32_t sa = s0 + uint32_t(s) * kPairStage;
+                tma_stage_pair_warp(&full[s], leader, 2 * kPairStage, sa, &ta, kc * kBK, mi * 256 + 128 * int(rank), z, sa + kABytes, &tb, kc * kBK,
+                                    ni * BN + (BN / 2) * int(rank), zg);
                 __syncwarp();
             }
         }
@@ -469,7 +511,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
                     break;
                 }
                 tc_fence_after();
-                const uint32_t dcol = tmem + a * BN;
+                const uint32_t dcol = tmem + a * P::ACC;
                 for (int kc = 0; kc < kt; ++kc, ++it) {
                     const int s = int(it % kPairStages);
                     const uint32_t u = it / kPairStages;
@@ -478,7 +520,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
                         break;
                     }
                     tc_fence_after();
-                    if (lane == 0) {
+                    {
                         const uint32_t sa = s0 + uint32_t(s) * kPairStage, sb = sa + kABytes;
 #pragma unroll
                         for (int k = 0; k < kBK / 16; ++k)
@@ -488,11 +530,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
                     __syncwarp();
                 }
                 if (!ok) break;
-                if (lane == 0) umma_commit_pair(&tfull[a]);
+                umma_commit_pair(&tfull[a]);
                 __syncwarp();
             }
             if (!ok) {
-                if (lane == 0) umma_commit_pair(drain);
+                umma_commit_pair(drain);
                 __syncwarp();
                 mbar_wait_warp(drain, 0);
             }
@@ -500,9 +542,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
     } else {
         // ---- epilogue: this CTA's 128 rows of the 256-row tile, all 256 columns
         const int q = warp & 3;
-        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
+        const uint32_t stg = STG_BASE + uint32_t(warp - 2) * P::SWB;
+        uint32_t seq = 0;
         const uint32_t tempty0 = map_rank(&tempty[0], 0);
-        float *bias_s = reinterpret_cast<float *>(smem + kPairStages * kPairStage + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
+        float *bias_s = reinterpret_cast<float *>(smem + kPairStages * kPairStage + 4 * P::SWB + 256) + (warp - 2) * 256;
         uint32_t tc = 0;
         for (int t = pair; t < tiles && ok; t += npairs, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
@@ -514,26 +557,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
                 break;
             }
             tc_fence_after();
-            const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + a * BN;
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                const int c0 = ni * BN + c;
-                if (c0 >= g.N) break;
-                uint32_t r[32];
-                tmem_ld32(taddr + uint32_t(c), r);
-                tmem_wait_ld();
-                epilogue32<EPI>(g, r, mi * 256 + 128 * int(rank) + 32 * q, lane, c0, zb, zg, stg, pre, c);
-            }
+            const int n0 = ni * BN, nch = min(BN, g.N - n0 + 31) / 32;
+            epilogue_tile<EPI, P::SWB>(g, &ty, tmem + (uint32_t(32 * q) << 16) + a * P::ACC, nch, mi * 256 + 128 * int(rank) + 32 * q, lane, n0, zb,
+                                       zg, stg, seq, pre);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tempty0 + a * 8);
+        }
+        if (g.tma_store) {
+            bulk_wait_all();
+            __syncwarp();
         }
     }
     tc_fence_before();
     cluster_sync();  // the peer's last remote arrivals and reads are done before either CTA releases its memory
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TMEM_COLS) : "memory");
     }
 }
 
@@ -628,11 +668,11 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         tma_prefetch_desc(&tx);
         tma_prefetch_desc(&tw);
     }
-    pdl_enter();
     if (warp == 0) tmem_alloc(tslot, 2 * kQBN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_enter();
     const uint32_t tmem = *tslot;
     bool ok = true;
 
@@ -778,21 +818,21 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
                     break;
                 }
                 tc_fence_after();
-                if (lane == 0) {
+                {
                     const uint32_t sa = smem_addr(conv + s * C::CONV), sb = sa + kQAConv;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
-                        umma_bf16(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
-                    umma_commit(&conv_empty[s]);
+                        umma_bf16_warp(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
+                    umma_commit_warp(&conv_empty[s]);
                 }
                 __syncwarp();
             }
             if (!ok) break;
-            if (lane == 0) umma_commit(&tfull[a]);
+            umma_commit_warp(&tfull[a]);
             __syncwarp();
         }
         if (!ok) {
-            if (lane == 0) umma_commit(drain);
+            umma_commit_warp(drain);
             __syncwarp();
             mbar_wait_warp(drain, 0);
         }
@@ -801,6 +841,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         const int qw = warp & 3;
         const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
         float *bias_s = reinterpret_cast<float *>(raw + C::RS * C::RAW + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
+        uint32_t qseq = 0;
         uint32_t tc = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
             const uint32_t a = tc & 1u, v = tc >> 1;
@@ -812,15 +853,9 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
                 break;
             }
             tc_fence_after();
-            const uint32_t taddr = tmem + (uint32_t(32 * qw) << 16) + a * kQBN;
-#pragma unroll 1
-            for (int c = 0; c < kQBN; c += 32) {
-                if (n0 + c >= q.N) break;
-                uint32_t r[32];
-                tmem_ld32(taddr + uint32_t(c), r);
-                tmem_wait_ld();
-                epilogue32<kEpiF32>(q.g, r, m0 + 32 * qw, lane, n0 + c, 0, 0, stg, pre, c);
-            }
+            const int nch = min(kQBN, q.N - n0 + 31) / 32;
+            epilogue_tile<kEpiF32, kStageWarpBytes>(q.g, nullptr, tmem + (uint32_t(32 * qw) << 16) + a * kQBN, nch, m0 + 32 * qw, lane, n0, 0, 0, stg,
+                                                    qseq, pre);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[a]);
@@ -881,6 +916,24 @@ int plain_map(const void *base, CUtensorMapDataType dt, int64_t cols, int64_t ro
     return VOX_CUDA_OK;
 }
 
+// 3-D map of the GEMM output y: planes [depth][rows][cols] of f32 or bf16 (row pitch ld_bytes, plane pitch
+// plane_bytes), box 32 x 32 x 1 in the swizzle the epilogue stages with (128-byte rows: 128-byte swizzle; 64-byte
+// rows: 64-byte swizzle).
+int y_map(const void *base, bool f32, int64_t cols, int64_t rows, int64_t depth, int64_t ld_bytes, int64_t plane_bytes, CUtensorMap &m,
+          const char *name) {
+    auto fn = encode();
+    if (!fn) return set_error(VOX_CUDA_ERR_DEVICE, std::string(name) + ": cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(depth)};
+    const cuuint64_t strides[2] = {cuuint64_t(ld_bytes), cuuint64_t(plane_bytes)};
+    const cuuint32_t box[3] = {32, 32, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = fn(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides,
+                          box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(VOX_CUDA_ERR_ARG, std::string(name) + ": output tensor map rejected (code " + std::to_string(int(r)) + ")");
+    return VOX_CUDA_OK;
+}
+
 template <bool Q4, bool SF16>
 int launch_q(const CUtensorMap &tx, const CUtensorMap &tw, const GemmQArgs &q, cudaStream_t st, const char *name) {
     auto kern = gemm_q_kernel<Q4, SF16>;
@@ -910,13 +963,14 @@ int launch(const GemmPlan &p, cudaStream_t st, const char *name) {
     const int mt = (p.a.M + kBM - 1) / kBM, nt = (p.a.N + BN - 1) / BN;
     const int64_t tiles = int64_t(mt) * nt * p.a.batches * p.a.groups;
     const int grid = int(tiles < sm_count() ? tiles : sm_count());
-    launch_k(kern, grid, kGemmThreads, Cfg<BN>::SMEM, st, p.ta, p.tb, p.a);
+    launch_k(kern, grid, kGemmThreads, Cfg<BN>::SMEM, st, p.ta, p.tb, p.ty, p.a);
     return check_launch(name);
 }
 
-template <int EPI>
+template <int BN, int EPI>
 int launch_pair(const GemmPlan &p, cudaStream_t st, const char *name) {
-    auto kern = gemm_tc2_kernel<EPI>;
+    auto kern = gemm_tc2_kernel<BN, EPI>;
+    constexpr size_t kPairSmem = PairCfg<BN>::SMEM;
     static bool attr_set[128] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -924,7 +978,7 @@ int launch_pair(const GemmPlan &p, cudaStream_t st, const char *name) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPairSmem)) != cudaSuccess) return check_launch(name);
         attr_set[dev] = true;
     }
-    const int64_t tiles = int64_t((p.a.M + 255) / 256) * ((p.a.N + 255) / 256) * p.a.batches * p.a.groups;
+    const int64_t tiles = int64_t((p.a.M + 255) / 256) * ((p.a.N + BN - 1) / BN) * p.a.batches * p.a.groups;
     const int64_t pairs = sm_count() / 2;
     const int grid = 2 * int(tiles < pairs ? tiles : pairs);
     cudaLaunchConfig_t cfg = {};
@@ -939,13 +993,17 @@ int launch_pair(const GemmPlan &p, cudaStream_t st, const char *name) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    if (cudaLaunchKernelEx(&cfg, kern, p.ta, p.tb, p.a) != cudaSuccess) return check_launch(name);
+    if (cudaLaunchKernelEx(&cfg, kern, p.ta, p.tb, p.ty, p.a) != cudaSuccess) return check_launch(name);
     return VOX_CUDA_OK;
 }
 
 template <int EPI>
 int launch_bn(const GemmPlan &p, cudaStream_t st, const char *name) {
-    if (p.pair) return launch_pair<EPI>(p, st, name);
+    if (p.pair) {
+        if (p.bn == 128) return launch_pair<128, EPI>(p, st, name);
+        if (p.bn == 192) return launch_pair<192, EPI>(p, st, name);
+        return launch_pair<256, EPI>(p, st, name);
+    }
     if (p.bn == 64) return launch<64, EPI>(p, st, name);
     if (p.bn == 256) return launch<256, EPI>(p, st, name);
     return launch<128, EPI>(p, st, name);
@@ -964,28 +1022,60 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
                     std::string(name) + ": RoPE epilogue needs heads of 64 and 3 inner columns");
     plan.a = a;
     plan.epi = epi;
-    // tile width: the copy engine's feed from L2 bounds these tiles, and a wider tile reads fewer bytes per product, so
-    // 256 columns wherever they still give every SM work for at least half a wave, else 128; 64 for narrow outputs
-    const int64_t sms = sm_count(), mt = (a.M + kBM - 1) / kBM, z = int64_t(a.batches) * a.groups;
-    const int64_t tiles256 = mt * ((a.N + 255) / 256) * z;
-    const int best = a.N <= 64 ? 64 : (a.N >= 512 && 2 * tiles256 >= sms) ? 256 : 128;
-    // VOX_CUDA_GEMM_BN = 64 / 128 / 256 forces the tile width (for comparisons)
-    static const int forced = [] {
-        const char *e = std::getenv("VOX_CUDA_GEMM_BN");
-        const int v = e ? std::atoi(e) : 0;
-        return v == 64 || v == 128 || v == 256 ? v : 0;
-    }();
-    plan.bn = forced ? forced : best;
-    // CTA pairs (256 x 256 tiles) where both extents fill them; VOX_CUDA_GEMM_PAIR = 0 / 1 forces the choice
-    static const int pair_mode = [] {
-        const char *e = std::getenv("VOX_CUDA_GEMM_PAIR");
-        return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : -1;
-    }();
-    plan.pair = pair_mode == 1 || (pair_mode < 0 && !forced && a.M >= 512 && a.N >= 512);
-    // both kernels read boxes of 128 x rows and of 128 (pair) or BN (one CTA) W rows
+    // Tile shape: each candidate's time is estimated as waves x (K steps x t_step + t_wave) + t_fixed (+ t_f32 for an
+    // f32 output), with waves = ceil(tiles / CTAs that fit: the SM count, or half of it for pairs), and the cheapest is
+    // taken. The constants (us) are least-squares fits of measured launches on B200 (F5-base projections, a
+    // 512 x 12288 x 4096 prefill GEMM; bf16 and f32 outputs): a K step of 64 costs 0.26 us on 128 x 128 tiles (the
+    // copy and MMA issue rate), 0.40 us on 128 x 256 (the tensor cores); pairs halve the W bytes per CTA but pay a
+    // larger fixed cost (cluster launch and first copies). The 128 x 64 tile's constants are scaled from the 128 x 128
+    // tile's. VOX_CUDA_GEMM_BN (64 / 128 / 192 / 256) and VOX_CUDA_GEMM_PAIR (0 / 1) restrict the candidates (for
+    // comparisons and tests; read at every plan).
+    const int64_t sms = sm_count(), z = int64_t(a.batches) * a.groups, kt = (a.K + kBK - 1) / kBK;
+    const char *ebn = std::getenv("VOX_CUDA_GEMM_BN"), *epair = std::getenv("VOX_CUDA_GEMM_PAIR");
+    const int fv = ebn ? std::atoi(ebn) : 0;
+    const int forced = fv == 64 || fv == 128 || fv == 192 || fv == 256 ? fv : 0;
+    const int pair_mode = epair && epair[0] == '0' ? 0 : epair && epair[0] == '1' ? 1 : -1;
+    const bool f32y = epi == kEpiF32 || epi == kEpiGeluTanhF32 || epi == kEpiGeluErfF32;
+    struct Cand {
+        bool pair;
+        int bn;
+        double step, wave, fixed, f32;
+    };
+    static constexpr Cand kCands[] = {{false, 64, 0.20, 0.20, 1.9, 0.6},   {false, 128, 0.261, 0.275, 2.0, 1.12},
+                                      {false, 256, 0.395, 0.856, 2.46, 1.77}, {true, 128, 0.225, 0.542, 4.9, 0.81},
+                                      {true, 192, 0.275, 1.473, 3.43, 1.29},  {true, 256, 0.316, 0.717, 5.56, 1.41}};
+    double best = -1;
+    for (const Cand &c : kCands) {
+        if ((forced && c.bn != forced) || (pair_mode >= 0 && c.pair != (pair_mode == 1))) continue;
+        const int64_t units = ((a.M + (c.pair ? 255 : 127)) / (c.pair ? 256 : 128)) * ((a.N + c.bn - 1) / c.bn) * z;
+        const int64_t slots = c.pair ? sms / 2 : sms, waves = (units + slots - 1) / slots;
+        const double cost = double(waves) * (double(kt) * c.step + c.wave) + c.fixed + (f32y ? c.f32 : 0.0);
+        if (best < 0 || cost < best) best = cost, plan.pair = c.pair, plan.bn = c.bn;
+    }
+    if (best < 0) plan.pair = forced == 192, plan.bn = forced ? forced : 128;  // contradictory overrides
+    // x boxes of 128 rows; W boxes of BN rows (one CTA) or BN / 2 (each CTA of a pair)
     int rc = bf16_map(x, a.K, a.M, z, ldx, kBM, plan.ta, name);
     if (rc != VOX_CUDA_OK) return rc;
-    return bf16_map(w, a.K, a.N, a.groups, ldw, plan.pair ? 128 : plan.bn, plan.tb, name);
+    rc = bf16_map(w, a.K, a.N, a.groups, ldw, plan.pair ? plan.bn / 2 : plan.bn, plan.tb, name);
+    if (rc != VOX_CUDA_OK) return rc;
+    // y by tensor stores of 32 x 32 blocks where its layout allows: planes [batches][M][columns] with 16-byte aligned
+    // rows, group g's columns at g * y_gstride (whole 32-column blocks, so no block of one group reaches the next);
+    // otherwise by the threads' own stores. VOX_CUDA_GEMM_TMA_STORE=0 selects the latter (for comparisons).
+    const bool f32out = epi == kEpiF32 || epi == kEpiGeluTanhF32 || epi == kEpiGeluErfF32;
+    const int64_t es = f32out ? 4 : 2;
+    const char *ets = std::getenv("VOX_CUDA_GEMM_TMA_STORE");
+    const bool tma_ok = !(ets && ets[0] == '0') && aligned16(a.y) && (a.ldy * es) % 16 == 0 && a.ldy >= a.N &&
+                        (a.batches == 1 || (a.y_bstride * es) % 16 == 0) &&
+                        (a.groups == 1 || (a.N % 32 == 0 && (a.y_gstride * es) % 16 == 0)) && (!a.accumulate || f32out);
+    plan.a.tma_store = 0;
+    if (tma_ok) {
+        const int64_t cols = int64_t(a.groups - 1) * a.y_gstride + a.N;
+        const int64_t bstride = a.batches > 1 ? a.y_bstride : int64_t(a.M) * a.ldy;
+        rc = y_map(a.y, f32out, cols, a.M, a.batches, a.ldy * es, bstride * es, plan.ty, name);
+        if (rc != VOX_CUDA_OK) return rc;
+        plan.a.tma_store = 1;
+    }
+    return VOX_CUDA_OK;
 }
 
 int gemm_run(const GemmPlan &p, cudaStream_t st, const char *name) {

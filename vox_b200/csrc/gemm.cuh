@@ -31,12 +31,14 @@ struct GemmArgs {
     // kEpiQkvRope: y [M][3 inner]; row r at position r % frames; heads < rope_heads of q and k rotate with cs[pos][hd/2]
     const float2 *cs = nullptr;
     int frames = 1, rope_heads = 0, hd = 64, inner = 0;
+    int tma_store = 0;                // set by gemm_plan: y is written by tensor stores (GemmPlan::ty)
 };
 
-// A prepared GEMM: its two tensor maps (x planes [z][M][K], W planes [g][N][K], bf16, 128-byte swizzle), the tile
-// width and the epilogue. Built once per operand set; launching it allocates nothing.
+// A prepared GEMM: its tensor maps (x planes [z][M][K], W planes [g][N][K], bf16, 128-byte swizzle; y in 32 x 32
+// boxes where its layout allows tensor stores), the tile shape and the epilogue. Built once per operand set;
+// launching it allocates nothing.
 struct GemmPlan {
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, ty;
     GemmArgs a;
     int bn = 128;
     bool pair = false;  // a cluster of two CTAs per 256 x 256 tile (tcgen05 cta_group::2)

@@ -91,11 +91,11 @@ def test_f5_step_matches_oracle(vox, math, bar, pe_attn_head):
     assert _rel(h_after, want_h) <= bar, _rel(h_after, want_h)
 
 
-@pytest.mark.parametrize("frames,pe_attn_head", [(70, 1), (128, 0), (300, 1)])
+@pytest.mark.parametrize("frames,pe_attn_head", [(70, 1), (128, 0), (300, 1), (520, 1)])
 def test_f5_bf16_pipeline_matches_oracle(vox, frames, pe_attn_head):
     """dim_head 64 in bf16 mode: bf16 weight copies, fused q|k|v projection, the fused attention kernel (128-row query
-    tiles, 64-key tiles; 70 and 300 frames leave a ragged last tile of keys and of queries, 300 runs three query tiles
-    and five key tiles through the double-buffered pipeline), residual and modulation fused."""
+    tiles, 64-key tiles; 70, 300 and 520 frames leave a ragged last tile of keys and of queries, 300 runs three query tiles
+    and five key tiles, 520 nine key tiles: the key/value buffers rotate several times), residual and modulation fused."""
     cfg = dict(D=128, H=2, HD=64, FF=256, depth=2, out_dim=24)
     B = 2
     model = _model(6, **cfg)

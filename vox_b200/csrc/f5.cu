@@ -239,11 +239,11 @@ constexpr uint32_t kIdescO = umma_idesc_bf16(128, 64, true);
 
 // Stages rows [row0, row0 + ROWS) of a head's 64 columns (global row stride ld bf16) into a swizzled tile; rows at
 // or past n are zero-filled. 8 chunks a row, ROWS / 16 per thread.
-template <int ROWS>
+template <int ROWS, int THREADS = kTcThreads>
 __device__ __forceinline__ void tc_stage(uint32_t tile, const __nv_bfloat16 *g, int row0, int n, int ld) {
 #pragma unroll
-    for (int u = 0; u < ROWS / 16; ++u) {
-        const int idx = threadIdx.x + u * kTcThreads, r = idx >> 3, c = idx & 7;
+    for (int u = 0; u < ROWS * 8 / THREADS; ++u) {
+        const int idx = threadIdx.x + u * THREADS, r = idx >> 3, c = idx & 7;
         const int gr = row0 + r;
         cp16(tile + fa_off(r, c), g + size_t(gr < n ? gr : n - 1) * ld + c * 8, gr < n ? 16u : 0u);
     }
@@ -400,6 +400,172 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
 }
 
 // ------------------------------------------------------------------ bf16 pipeline helpers
+
+// The same attention with two threads a query row: 8 warps, warp w reads TMEM lanes 32 (w % 4) .. (its 32 query rows)
+// and takes keys 32 h .. 32 h + 31 of each S tile and head dimensions 32 h .. 32 h + 31 of each P V tile, h = w / 4.
+// The two halves of a row exchange their partial maxima through shared memory (a named barrier per pair of warps)
+// and add their partial row sums once at the end; both halves apply the same running maximum, so their sums and
+// output columns share one scale. Each thread's serial softmax chain is half as long (and split into four independent
+// max and sum chains) and twice as many warps share an SM as with one thread a row. Warp 0 issues the MMAs through an
+// elected lane (operands warp-uniform). Measured against the alternatives on B200 (F5 base, 2 x 1024 frames, 16
+// heads): 28.9 us a launch against 31.2 us for one thread a row; keeping two S and two P V buffers in tensor memory
+// so that P V of a tile is waited for one tile later measured 33.5 us, and the same with a ninth warp issuing the
+// MMAs (no CTA-wide barrier in the loop) 37.0 us.
+constexpr int kTc2Threads = 256;
+constexpr size_t kTc2Smem = kTcSmem + 2 * 128 * sizeof(float);  // + the partial maxima / sums of the two halves
+
+__global__ void __launch_bounds__(kTc2Threads, 2) f5_flash_tc2_kernel(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb,
+                                                                      const __nv_bfloat16 *vb, __nv_bfloat16 *at, int n, int ld_in,
+                                                                      int inner, float scale_log2) {
+    extern __shared__ uint8_t tc2_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc2_smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sQ = smem_addr(smem), sP = sQ + kTcQ, sK = sQ + 2 * kTcQ, sV = sK + 2 * kTcKV;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + 2 * kTcQ + 4 * kTcKV);  // [0] S done, [1] P V done, [2] drain
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + 2 * kTcQ + 4 * kTcKV + 32);
+    float *red = reinterpret_cast<float *>(smem + 2 * kTcQ + 4 * kTcKV + 128);  // [2][128]: half h's value for row r
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, quad = warp & 3, half = warp >> 2;
+    const int row = 32 * quad + lane;  // query row within the tile
+    const int q0 = blockIdx.x * kTcRows, head = blockIdx.y;
+    const size_t seq = size_t(blockIdx.z) * size_t(n) * size_t(ld_in) + size_t(head) * kFaHd;
+    const __nv_bfloat16 *Q = qb + seq, *K = kb + seq, *V = vb + seq;
+    const int ntiles = (n + kTcKeys - 1) / kTcKeys;
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory"); };  // the row's two warps
+    pdl_enter();  // the previous grid (and the tensor memory it held) is complete
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+        mbar_init_fence();
+    }
+    if (warp == 0) tmem_alloc(tslot, kTcCols);
+    tc_stage<kTcRows, kTc2Threads>(sQ, Q, q0, n, ld_in);
+    tc_stage<kTcKeys, kTc2Threads>(sK, K, 0, n, ld_in);
+    tc_stage<kTcKeys, kTc2Threads>(sV, V, 0, n, ld_in);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16);  // this warp's 32 lanes
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    float mrow = -INFINITY, lrow = 0.f;
+    bool ok = true;
+    if (warp == 0) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            umma_bf16_warp(tmem, umma_desc(sQ + 32 * k, 16, 1024), umma_desc(sK + 32 * k, 16, 1024), kIdescS, k > 0);
+        umma_commit_warp(&bar[0]);
+    }
+    for (int kt = 0; kt < ntiles; ++kt) {  // every thread runs every iteration's barriers, ok or not
+        const int buf = kt & 1;
+        if (kt + 1 < ntiles) {  // the other buffers' last readers (tile kt - 1's products) have completed
+            tc_stage<kTcKeys, kTc2Threads>(sK + (buf ^ 1) * kTcKV, K, (kt + 1) * kTcKeys, n, ld_in);
+            tc_stage<kTcKeys, kTc2Threads>(sV + (buf ^ 1) * kTcKV, V, (kt + 1) * kTcKeys, n, ld_in);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        ok = ok && mbar_wait_warp(&bar[0], uint32_t(kt & 1));
+        tc_fence_after();
+        float alpha = 1.f;
+        uint32_t r[32];
+        float mx = -INFINITY;
+        if (ok) {
+            const int key0 = kt * kTcKeys + 32 * half;
+            tmem_ld32(trow + 32 * half, r);
+            tmem_wait_ld(r);
+            if (key0 + 32 > n) {  // keys past the sequence end: -inf scores, weight 2^-inf = 0
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (key0 + i >= n) r[i] = __float_as_uint(-INFINITY);
+            }
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
+#pragma unroll
+            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(r[i]));
+            mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+            red[half * 128 + row] = mx;
+        }
+        pair_sync();
+        if (ok) {
+            mx = fmaxf(mx, red[(half ^ 1) * 128 + row]);
+            const float mnew = fmaxf(mrow, mx * scale_log2);
+            alpha = ex2_approx(mrow - mnew);
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+            const float2 sl2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mnew, -mnew);
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {  // key chunks 4 h .. 4 h + 3 of the row (8 keys each)
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = 8 * ch + 2 * e;
+                    const float2 a = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2, nm2);
+                    const float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
+                    s4[e] += p0 + p1;
+                    w[e] = pack_bf16(p0, p1);
+                }
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP + fa_off(row, 4 * half + ch)), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                             "r"(w[3])
+                             : "memory");
+            }
+            lrow = lrow * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+            mrow = mnew;
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");          // tile kt + 1's K and V
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P and the tile, visible to the MMA
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0 && ok) {
+            tc_fence_after();
+            const uint32_t tV = sV + buf * kTcKV, tK1 = sK + (buf ^ 1) * kTcKV;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                umma_bf16_warp(tmem + 64, umma_desc(sP + 32 * k, 16, 1024), umma_desc(tV + 2048 * k, 16384, 1024), kIdescO, k > 0);
+            umma_commit_warp(&bar[1]);
+            if (kt + 1 < ntiles) {  // the next tile's S: every thread has read this tile's S before the barrier
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    umma_bf16_warp(tmem, umma_desc(sQ + 32 * k, 16, 1024), umma_desc(tK1 + 32 * k, 16, 1024), kIdescS, k > 0);
+                umma_commit_warp(&bar[0]);
+            }
+        }
+        __syncwarp();
+        ok = ok && mbar_wait_warp(&bar[1], uint32_t(kt & 1));
+        tc_fence_after();
+        if (ok) {
+            uint32_t v[32];
+            tmem_ld32(trow + 64 + 32 * half, v);
+            tmem_wait_ld(v);
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                const float2 t = fma2(make_float2(o[i], o[i + 1]), make_float2(alpha, alpha), make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
+                o[i] = t.x;
+                o[i + 1] = t.y;
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    // the row sum: this half's plus the other's (same running maximum)
+    red[half * 128 + row] = lrow;
+    pair_sync();
+    const float ltot = lrow + red[(half ^ 1) * 128 + row];
+    if (ok && q0 + row < n) {
+        const float inv = 1.0f / ltot;
+        uint4 *dst = reinterpret_cast<uint4 *>(at + (size_t(blockIdx.z) * size_t(n) + size_t(q0 + row)) * inner + size_t(head) * kFaHd + 32 * half);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            dst[c] = make_uint4(pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv), pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                                pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv), pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {  // every MMA issued has completed (a wait above may have given up) before the memory is released
+        tc_fence_after();
+        umma_commit_warp(&bar[2]);
+        __syncwarp();
+        mbar_wait_warp(&bar[2], 0);
+        tmem_dealloc(tmem, kTcCols);
+    }
+}
 
 // xc [R][M + C] (bf16, RN) = [x [R][M] | cond [R][C]] (f32): the input of the in_proj GEMM; one element a thread.
 __global__ void __launch_bounds__(256) f5_concat_bf16_kernel(const float *x, const float *cond, __nv_bfloat16 *xc, uint32_t n,
@@ -761,7 +927,11 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
     const uint32_t rope_heads = uint32_t(d.pe_attn_head > 0 ? d.pe_attn_head : d.heads);
     const uint32_t qkv_octs = uint32_t(R * 3 * IN / 8), ff_octs = uint32_t(R * FF / 8);
     const dim3 fgt(unsigned((d.frames + kTcRows - 1) / kTcRows), unsigned(d.heads), unsigned(d.batch));
-    if (cudaFuncSetAttribute(f5_flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem)) != cudaSuccess)
+    // two threads a query row (VOX_CUDA_F5_ATTN=1: one thread a row, for comparisons)
+    const char *eattn = std::getenv("VOX_CUDA_F5_ATTN");
+    const bool attn1 = eattn && eattn[0] == '1';
+    if (cudaFuncSetAttribute(f5_flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem)) != cudaSuccess ||
+        cudaFuncSetAttribute(f5_flash_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTc2Smem)) != cudaSuccess)
         return check_launch("vox_cuda_f5 attention (shared memory)");
     const float scale_log2 = float(1.4426950408889634 / std::sqrt(double(d.dim_head)));
     F5_TRY(resmod(p, nullptr, nullptr, nullptr, p.ada_all + D, p.ada_all, st));
@@ -776,8 +946,12 @@ int record_bf16(F5Plan &p, cudaStream_t st) {
                      uint32_t(d.dim_head / 2), rope_heads, uint32_t(d.dim_head), uint32_t(IN));
             F5_TRY(check_launch("vox_cuda_f5 bias/rope (bf16)"));
         }
-        launch_k(f5_flash_tc_kernel, fgt, kTcThreads, kTcSmem, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
-                 (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (__nv_bfloat16 *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
+        if (attn1)
+            launch_k(f5_flash_tc_kernel, fgt, kTcThreads, kTcSmem, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
+                     (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (__nv_bfloat16 *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
+        else
+            launch_k(f5_flash_tc2_kernel, fgt, kTc2Threads, kTc2Smem, st, (const __nv_bfloat16 *)p.qkv_b, (const __nv_bfloat16 *)(p.qkv_b + IN),
+                     (const __nv_bfloat16 *)(p.qkv_b + 2 * IN), (__nv_bfloat16 *)p.at_b, int(d.frames), int(3 * IN), int(IN), scale_log2);
         F5_TRY(check_launch("vox_cuda_f5 attention"));
         if (p.tc && (p.tc_mask & 2)) F5_TRY(gemm_run(p.g_o[size_t(l)], st, "vox_cuda_f5 o"));
         else F5_TRY(gemm_bf16(p, p.at_b, p.w_o + size_t(l) * D * IN, p.o, CUDA_R_32F, R, D, IN));

@@ -42,9 +42,6 @@ template <int BN> struct Cfg {
     static constexpr size_t SMEM = size_t(STAGES) * STAGE + 1024 + 256 + 4 * SWB + 4 * 1024;  // + epilogue staging and bias
 };
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
 
 // Output tile t: row block t % mt (the fastest, so neighbouring CTAs share a W tile), column block ni, plane z.
 struct Tile {

@@ -1015,10 +1015,24 @@ int build_gemms(F5Plan &p) {
     const vox_cuda_f5_desc &d = p.d;
     const int R = int(p.R), D = d.dim, IN = int(p.inner), FF = int(p.ff), L = d.depth;
     const char *nm = "vox_cuda_f5_create (GEMMs)";
+    // VOX_CUDA_F5_TILES="qkv=1192,o=128,ff1=256,ff2=128" fixes a projection's tile (1000 * pair + columns; for
+    // comparisons), else gemm_plan chooses
+    const char *et = std::getenv("VOX_CUDA_F5_TILES");
+    auto tile_of = [&](const char *key) {
+        if (!et) return 0;
+        const std::string t(et), k = std::string(key) + "=";
+        size_t i = t.find(k);
+        while (i != std::string::npos && i > 0 && t[i - 1] != ',') i = t.find(k, i + 1);
+        return i == std::string::npos ? 0 : std::atoi(t.c_str() + i + k.size());
+    };
     auto plan = [&](const void *x, int64_t ldx, const void *w, int64_t ldw, int N, int K, void *y, int64_t ldy, const float *bias, int epi,
                     GemmPlan &gp) {
         GemmArgs a;
         a.M = R, a.N = N, a.K = K, a.y = y, a.ldy = ldy, a.bias = bias;
+        a.tile = tile_of(epi == kEpiQkvRope ? "qkv" : epi == kEpiGeluTanh ? "ff1" : y == p.o && K == FF ? "ff2" : y == p.o ? "o" : "other");
+        // the fused q|k|v projection on 128 x 256 tiles: in the step it measured faster than the shape gemm_plan picks
+        // alone (256 x 192 pairs; 2.213 against 2.238 ms a step, same box), its RoPE epilogue being the difference
+        if (epi == kEpiQkvRope && !a.tile && N % 256 == 0) a.tile = 256;
         if (epi == kEpiQkvRope) {
             a.cs = p.cs, a.frames = d.frames, a.rope_heads = d.pe_attn_head > 0 ? d.pe_attn_head : d.heads, a.hd = d.dim_head, a.inner = IN;
         }

@@ -3,18 +3,22 @@
 // GPU F5 step (gpu_f5.cpp:287-322, gemm(): shaders/gemmb.comp:1-99, with its bias and GELU flags) and the grouped
 // position convolutions' GEMMs (shaders/convgemm.comp).
 //
-// One CTA per SM, persistent over output tiles of 128 rows x BN columns (BN 64, 128 or 256), tiles with the same W
-// columns taken by neighbouring CTAs so a weight tile is read from HBM once and then from L2. Six warps:
+// One CTA per SM (or a CTA pair on two SMs), persistent over output tiles of 128 rows x BN columns (BN 64, 128 or 256;
+// pairs: 256 x 128 / 192 / 256), tiles with the same W columns taken by neighbouring CTAs so a weight tile is read from
+// HBM once and then from L2. Six warps:
 //   warp 0      tensor copies (TMA): for every K step of 64, the x tile [128][64] and the W tile [BN][64], both in the
 //               128-byte swizzle, into a ring of STAGES shared-memory stages (mbarrier full/empty pairs);
-//   warp 1      one thread issues tcgen05.mma (M 128, N BN, K 16; four per K step) into one of two TMEM accumulators
-//               and commits each stage back to the copy warp, and each finished tile to the epilogue;
+//   warp 1      issues tcgen05.mma (M 128, N BN, K 16; four per K step) through one elected lane into one of two TMEM
+//               accumulators and commits each stage back to the copy warp, and each finished tile to the epilogue;
 //   warps 2..5  the epilogue: each thread reads its output row from TMEM (warp w reads lanes 32 (w % 4) ..), applies
-//               bias / RoPE / GELU and stores it; the accumulator goes back to the MMA thread, which meanwhile has
-//               started the next tile in the other accumulator.
-// Every wait is bounded; a wait that gives up sets the device error flag and the CTA winds down (its copies and MMAs
-// in flight are waited for, bounded, before its shared and tensor memory are released). No copy is broadcast across
-// a cluster.
+//               bias / RoPE / GELU, stages the block in shared memory and writes it with a tensor store; the
+//               accumulator goes back to the MMA warp, which meanwhile has started the next tile in the other
+//               accumulator.
+// Copies and MMAs are issued by the whole converged warp with one elected lane (measured: 347 -> 149 clocks to issue
+// a K step's four MMAs and commit, against a single-lane branch). Eight epilogue warps (two a lane quadrant, alternate
+// 32-column chunks) measured no faster in the F5 step and slower on long K (fewer copy stages fit). Every wait is
+// bounded; a wait that gives up sets the device error flag and the CTA winds down (its copies and MMAs in flight are
+// waited for, bounded, before its shared and tensor memory are released). No copy is broadcast across a cluster.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -1044,6 +1048,7 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
     double best = -1;
     for (const Cand &c : kCands) {
         if ((forced && c.bn != forced) || (pair_mode >= 0 && c.pair != (pair_mode == 1))) continue;
+        if (a.tile && (c.bn != a.tile % 1000 || c.pair != (a.tile >= 1000))) continue;
         const int64_t units = ((a.M + (c.pair ? 255 : 127)) / (c.pair ? 256 : 128)) * ((a.N + c.bn - 1) / c.bn) * z;
         const int64_t slots = c.pair ? sms / 2 : sms, waves = (units + slots - 1) / slots;
         const double cost = double(waves) * (double(kt) * c.step + c.wave) + c.fixed + (f32y ? c.f32 : 0.0);

@@ -31,6 +31,7 @@ struct GemmArgs {
     // kEpiQkvRope: y [M][3 inner]; row r at position r % frames; heads < rope_heads of q and k rotate with cs[pos][hd/2]
     const float2 *cs = nullptr;
     int frames = 1, rope_heads = 0, hd = 64, inner = 0;
+    int tile = 0;                     // 0: gemm_plan picks the tile; else 1000 * pair + BN (128, 256, 1128, 1192, ...)
     int tma_store = 0;                // set by gemm_plan: y is written by tensor stores (GemmPlan::ty)
 };
 

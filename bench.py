@@ -926,6 +926,9 @@ def run_gemm(args) -> None:
     tpk, tkind = tensor_peak()
     shapes = [("f5_qkv", 2048, 3072, 1024), ("f5_o", 2048, 1024, 1024), ("f5_ff1", 2048, 2048, 1024), ("f5_ff2", 2048, 1024, 2048),
               ("prefill_up", 512, 12288, 4096), ("square_8192", 8192, 8192, 8192)]
+    if args.gemm_shape:  # one shape only (profiling a single kernel)
+        m, n, k = (int(v) for v in args.gemm_shape.lower().split("x"))
+        shapes = [(f"gemm_{m}x{n}x{k}", m, n, k)]
     res = {}
     g = torch.Generator(device="cuda").manual_seed(0)
     for nm, m, n, k in shapes:
@@ -1089,6 +1092,7 @@ def main() -> None:
     ap.add_argument("--copy-roofline", action="store_true", help="cfg1-cfg4 ops against a size-matched device copy")
     ap.add_argument("--gemm", action="store_true", help="the tcgen05 GEMM alone against cuBLAS")
     ap.add_argument("--probe", action="store_true", help="one launch of each kernel outside the suite (profiling)")
+    ap.add_argument("--gemm-shape", default=None, help="--gemm: one MxNxK shape only")
     ap.add_argument("--probe-rows", type=int, default=131072, help="--probe: rows of 1024 elements a tensor")
     ap.add_argument("--probe-reps", type=int, default=20, help="--probe: warm-up and timed launches of each kernel")
     ap.add_argument("--sweep-lo", type=int, default=20)

@@ -337,15 +337,50 @@ class Suite:
 # ---------------------------------------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) during the timed region: median SM MHz under load and throttle reasons."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU during the timed region, read (never set) through
+    NVML in a thread every 2 ms, so that even a timed region of a few tens of ms holds samples; nvidia-smi at 200 ms
+    (`-lms 200`) where NVML is not importable. Median SM MHz under load, the maximum SM MHz, the reasons seen."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h): SW power cap, HW slowdown, SW thermal, HW thermal
+    BITS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40))
 
     def __init__(self, gpu_index: int):
         self.idx, self.proc, self.lines = gpu_index, None, []
+        self.nv, self.h, self.samples, self.mask, self.max_mhz, self.stop = None, None, [], 0, None, threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:  # the device torch sees as this index (CUDA_VISIBLE_DEVICES may renumber)
+            uuid = str(torch.cuda.get_device_properties(self.idx).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
 
     def __enter__(self):
+        try:
+            self.nv, self.h = self._nvml_handle()
+            self.max_mhz = float(self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            reasons = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append(float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)))
+                        self.mask |= int(reasons(self.h))
+                    except Exception:
+                        pass
+                    self.stop.wait(0.002)
+
+            self.th = threading.Thread(target=poll, daemon=True)
+            self.th.start()
+            return self
+        except Exception:
+            self.nv = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -360,6 +395,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        self.stop.set()
+        if self.nv is not None:
+            self.th.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -368,6 +406,10 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        if self.nv is not None:
+            reasons = sorted(nm for nm, bit in self.BITS if self.mask & bit)
+            return {"sm_mhz": float(np.median(self.samples)) if self.samples else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml"}
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for ln in self.lines:
@@ -382,7 +424,8 @@ class ClockSampler:
             for nm, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------------------------------- CPU reference

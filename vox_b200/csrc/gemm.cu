@@ -581,29 +581,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
 // ------------------------------------------------------------------ quantized prefill GEMM (Q8 / Q4 weights)
 //
 // y[M][N] (+)= bias + x[M][K] . W[N][K]^T with W = code * scale[n][k / 32] (Vox's Q8 / Q4 blocks) and f32 x, on the
-// tensor cores in f16 (kind::f16, f16 A and B, f32 accumulation): the dequantisation is the producer stage. Tile 128
-// activation rows x 256 weight rows, K step 64. Fourteen warps:
-//   warp 0       TMA: the raw tiles of a K step, x [128][64] f32 and the codes [256][64] bytes (Q8) or [256][32] (Q4),
-//                into a two-stage raw ring;
-//   warps 6..13  converters: x to f16, codes to f16 by the exponent trick (0x6400 | u is 1024 + u exactly; minus the
-//                code offset gives the integer code, times the block's scale rounds once to f16), both written as the
-//                128-byte-swizzled K-major operand tiles of a two-stage MMA ring;
-//   warp 1       one thread issues tcgen05.mma (M 128, N 256, K 16) into one of two TMEM accumulators (512 columns);
+// tensor cores in f16 (kind::f16, f16 A and B, f32 accumulation). x is rounded to f16 once, by a small kernel before
+// the GEMM (q_x_to_f16_kernel); the codes are converted inside the GEMM. Tile 128 activation rows x 256 weight rows,
+// K step 64, one ring of three stages, each holding the x tile (f16, loaded by TMA straight into the 128-byte-swizzled
+// MMA operand layout), the raw codes and the converted weight tile. Fourteen warps:
+//   warp 0       TMA: a stage's x tile [128][64] f16 and codes [256][64] bytes (Q8) or [256][32] (Q4);
+//   warps 6..13  converters: codes to f16 by the exponent trick (0x6400 | u is 1024 + u exactly; minus the code offset
+//                gives the integer code, times the block's scale rounds once to f16), written as the 128-byte-swizzled
+//                K-major weight tile of the same stage;
+//   warp 1       issues tcgen05.mma (M 128, N 256, K 16) through an elected lane into one of two TMEM accumulators
+//                (512 columns) and frees the stage when its MMAs have read it;
 //   warps 2..5   the epilogue (bias, accumulate, f32 store) as in the bf16 GEMM.
-// f16 keeps 11 significant bits of x and of code * scale (bf16: 8); |x| must stay below 65504. A code's integer value
-// is exact in f16; its product with an f16 scale is rounded once.
+// Measured at 512 x 12288 x 4096 (Q8 / Q4): converting x inside the GEMM (an f32 raw ring beside the f16 one, two
+// stages each) took 144 / 141 us; this ring 118 / 98 us. Not kept: a separate code ring loaded up to three steps ahead
+// with the x copies started by the converters (122 / 115 us), and the next step's block scales loaded while the
+// current one converts (142 / 132 us). f16 keeps 11 significant bits of x and of code * scale (bf16: 8); |x| must stay
+// below 65504. A code's integer value is exact in f16; its product with an f16 scale is rounded once.
 constexpr int kQBN = 256;
 constexpr int kQThreads = 448;
 constexpr int kQConvWarps = 8;
-constexpr uint32_t kQARaw = kBM * kBK * 4;          // 32 KB f32
-constexpr uint32_t kQAConv = kBM * kBK * 2;         // 16 KB f16
-constexpr uint32_t kQBConv = kQBN * kBK * 2;        // 32 KB f16
+constexpr uint32_t kQA = kBM * kBK * 2;             // x tile, 16 KB f16
+constexpr uint32_t kQB = kQBN * kBK * 2;            // weight tile, 32 KB f16
 template <bool Q4> struct QCfg {
     static constexpr uint32_t CODES = Q4 ? kQBN * kBK / 2 : kQBN * kBK;  // raw code bytes a K step
-    static constexpr uint32_t RAW = kQARaw + CODES;
-    static constexpr uint32_t CONV = kQAConv + kQBConv;
-    static constexpr int RS = 2, CS = 2;
-    static constexpr size_t SMEM = size_t(RS) * RAW + size_t(CS) * CONV + 1024 + 256 + 4 * 4096 + 4 * 1024;
+    static constexpr uint32_t STAGE = kQA + kQB + CODES;                 // 64 KB (Q8), 56 KB (Q4); multiples of 1024
+    static constexpr int S = 3;
+    static constexpr size_t SMEM = size_t(S) * STAGE + 1024 + 256 + 4 * 4096 + 4 * 1024;
 };
 
 // Two codes (bytes b0, b1 of w, already offset to unsigned) as f16x2 1024 + u: prmt puts the code byte under 0x64.
@@ -623,6 +626,15 @@ __device__ __forceinline__ uint32_t f16x2_of(float lo, float hi) {
     return d;
 }
 
+// xh = f16(x) (round to nearest), four elements a thread and pass (n a multiple of 4; x and xh 16- and 8-byte aligned).
+__global__ void __launch_bounds__(256) q_x_to_f16_kernel(const float4 *x, uint2 *xh, int64_t n4) {
+    pdl_enter();
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+        const float4 v = __ldg(x + i);
+        xh[i] = make_uint2(f16x2_of(v.x, v.y), f16x2_of(v.z, v.w));
+    }
+}
+
 struct GemmQArgs {
     int M, N, K, nblk;      // nblk = K / 32
     const void *scale;      // [N][nblk] f32 or f16
@@ -636,29 +648,24 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(kQBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);  // f16 A and B, f32 D
     extern __shared__ uint8_t gq_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gq_smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *conv = smem;                                   // [CS][A f16 | B f16], 1024-aligned stages
-    uint8_t *raw = smem + C::CS * C::CONV;                  // [RS][A f32 | codes]
-    uint64_t *raw_full = reinterpret_cast<uint64_t *>(raw + C::RS * C::RAW);
-    uint64_t *raw_empty = raw_full + C::RS;
-    uint64_t *conv_full = raw_empty + C::RS;
-    uint64_t *conv_empty = conv_full + C::CS;
-    uint64_t *tfull = conv_empty + C::CS;
+    // stages [S][x f16 (A) | weights f16 (B) | codes], 1024-aligned; then the barriers, staging and bias slots
+    uint64_t *raw_full = reinterpret_cast<uint64_t *>(smem + C::S * C::STAGE);  // x and codes landed (TMA)
+    uint64_t *conv_full = raw_full + C::S;                                      // weights converted (8 warps)
+    uint64_t *stage_empty = conv_full + C::S;                                   // the stage's MMAs have completed
+    uint64_t *tfull = stage_empty + C::S;
     uint64_t *tempty = tfull + 2;
     uint64_t *drain = tempty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
-    const uint32_t STG_BASE = smem_addr(raw + C::RS * C::RAW) + 256;  // the epilogue warps' staging areas (after the barriers)
+    const uint32_t STG_BASE = smem_addr(smem + C::S * C::STAGE) + 256;  // the epilogue warps' staging areas (after the barriers)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (q.M + kBM - 1) / kBM, nt = (q.N + kQBN - 1) / kQBN;
     const int tiles = mt * nt, kt = (q.K + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::RS; ++s) {
+        for (int s = 0; s < C::S; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], kQConvWarps);
-        }
-        for (int s = 0; s < C::CS; ++s) {
             mbar_init(&conv_full[s], kQConvWarps);
-            mbar_init(&conv_empty[s], 1);
+            mbar_init(&stage_empty[s], 1);
         }
         mbar_init(&tfull[0], 1);
         mbar_init(&tfull[1], 1);
@@ -678,29 +685,25 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     bool ok = true;
 
     if (warp == 0) {
-        // ---- raw tiles
+        // ---- copies: a stage's x tile (into its MMA operand slot) and codes
         uint32_t it = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
             for (int kc = 0; kc < kt; ++kc, ++it) {
-                const int s = int(it % C::RS);
-                const uint32_t u = it / C::RS;
-                if (!mbar_wait_warp(&raw_empty[s], (u & 1u) ^ 1u)) {
+                const int s = int(it % C::S);
+                const uint32_t u = it / C::S;
+                if (!mbar_wait_warp(&stage_empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;
                 }
-                if (lane == 0) {
-                    const uint32_t ra = smem_addr(raw + s * C::RAW);
-                    mbar_arrive_expect_tx(&raw_full[s], C::RAW);
-                    tma_load_3d(ra, &tx, kc * kBK, m0, 0, &raw_full[s]);
-                    tma_load_3d(ra + kQARaw, &tw, kc * (Q4 ? kBK / 2 : kBK), n0, 0, &raw_full[s]);
-                }
+                const uint32_t sa = smem_addr(smem + s * C::STAGE);
+                tma_stage_warp(&raw_full[s], kQA + C::CODES, sa, &tx, kc * kBK, m0, 0, sa + kQA + kQB, &tw, kc * (Q4 ? kBK / 2 : kBK), n0, 0);
                 __syncwarp();
             }
         }
         if (!ok) {
             const uint32_t last = it;
-            for (uint32_t j = last > uint32_t(C::RS) ? last - C::RS : 0; j < last; ++j) mbar_wait_warp(&raw_full[j % C::RS], (j / C::RS) & 1u);
+            for (uint32_t j = last > uint32_t(C::S) ? last - C::S : 0; j < last; ++j) mbar_wait_warp(&raw_full[j % C::S], (j / C::S) & 1u);
         }
     } else if (warp >= 6) {
         // ---- converters: thread ct of 256
@@ -709,11 +712,10 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         const uint32_t off8 = 0x64806480u;   // f16x2 (1152, 1152): 1024 + 128 (Q8 codes offset to unsigned by ^ 0x80)
         const uint32_t off4 = 0x64086408u;   // f16x2 (1032, 1032): 1024 + 8 (Q4 codes are u - 8)
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
-            (void)m0;
+            const int n0 = (t / mt) * kQBN;
             for (int kc = 0; kc < kt; ++kc, ++it) {
-                const int rs = int(it % C::RS), cs = int(it % C::CS);
-                const uint32_t ru = it / C::RS, cu = it / C::CS;
+                const int rs = int(it % C::S);
+                const uint32_t ru = it / C::S;
                 // the block scales of this thread's weight tasks (global loads, in flight during the waits)
                 constexpr int NT = Q4 ? 2 : 4;  // weight tasks a thread
                 uint32_t s2[NT];
@@ -730,21 +732,14 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
                     const uint32_t hb = *reinterpret_cast<const uint16_t *>(&h);
                     s2[j] = hb | (hb << 16);
                 }
-                if (!mbar_wait_warp(&raw_full[rs], ru & 1u) || !mbar_wait_warp(&conv_empty[cs], (cu & 1u) ^ 1u)) {
+                // the stage was reloaded only after its previous MMAs completed, so its weight tile is free
+                if (!mbar_wait_warp(&raw_full[rs], ru & 1u)) {
                     ok = false;
                     break;
                 }
-                const uint8_t *ra = raw + rs * C::RAW;
-                const uint32_t ca = smem_addr(conv + cs * C::CONV), cb = ca + kQAConv;
-                // x: 8 float4 a thread -> f16, 8 bytes each into the swizzled [128][64] tile
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int i = ct + 256 * j, row = i >> 4, c4 = i & 15;
-                    const float4 v = *reinterpret_cast<const float4 *>(ra + i * 16);
-                    const uint32_t d = ca + row * 128 + (((c4 >> 1) ^ (row & 7)) << 4) + (c4 & 1) * 8;
-                    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(d), "r"(f16x2_of(v.x, v.y)), "r"(f16x2_of(v.z, v.w)) : "memory");
-                }
-                const uint8_t *rc = ra + kQARaw;
+                const uint8_t *sp = smem + rs * C::STAGE;
+                const uint32_t cb = smem_addr(sp) + kQA;
+                const uint8_t *rc = sp + kQA + kQB;
                 if constexpr (!Q4) {
                     // 16 codes a task: row i / 4, 16-code quarter i % 4 (block quarter / 2)
 #pragma unroll
@@ -794,10 +789,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
                 }
                 fence_proxy_async();  // the generic-proxy writes, visible to the MMA (async proxy)
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&raw_empty[rs]);
-                    mbar_arrive(&conv_full[cs]);
-                }
+                if (lane == 0) mbar_arrive(&conv_full[rs]);
             }
         }
     } else if (warp == 1) {
@@ -812,19 +804,20 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
             tc_fence_after();
             const uint32_t dcol = tmem + a * kQBN;
             for (int kc = 0; kc < kt; ++kc, ++it) {
-                const int s = int(it % C::CS);
-                const uint32_t u = it / C::CS;
-                if (!mbar_wait_warp(&conv_full[s], u & 1u)) {
+                const int s = int(it % C::S);
+                const uint32_t u = it / C::S;
+                // the x tile (TMA) and the converted weights
+                if (!mbar_wait_warp(&raw_full[s], u & 1u) || !mbar_wait_warp(&conv_full[s], u & 1u)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 {
-                    const uint32_t sa = smem_addr(conv + s * C::CONV), sb = sa + kQAConv;
+                    const uint32_t sa = smem_addr(smem + s * C::STAGE), sb = sa + kQA;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
                         umma_bf16_warp(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
-                    umma_commit_warp(&conv_empty[s]);
+                    umma_commit_warp(&stage_empty[s]);  // the stage returns to the copy warp when these MMAs have read it
                 }
                 __syncwarp();
             }
@@ -841,7 +834,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         // ---- epilogue (warps 2..5)
         const int qw = warp & 3;
         const uint32_t stg = STG_BASE + uint32_t(warp - 2) * kStageWarpBytes;
-        float *bias_s = reinterpret_cast<float *>(raw + C::RS * C::RAW + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
+        float *bias_s = reinterpret_cast<float *>(smem + C::S * C::STAGE + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
         uint32_t qseq = 0;
         uint32_t tc = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
@@ -885,16 +878,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode() {
     return fn;
 }
 
-// 3-D bf16 map of planes [depth][rows][cols] (row pitch ld elements, plane pitch rows * ld), box 64 x box_rows x 1,
-// 128-byte swizzle, zero fill past every edge.
-int bf16_map(const void *base, int64_t cols, int64_t rows, int64_t depth, int64_t ld, int box_rows, CUtensorMap &m, const char *name) {
+// 3-D bf16 (or f16: dt) map of planes [depth][rows][cols] (row pitch ld elements, plane pitch rows * ld), box 64 x
+// box_rows x 1, 128-byte swizzle, zero fill past every edge.
+int bf16_map(const void *base, int64_t cols, int64_t rows, int64_t depth, int64_t ld, int box_rows, CUtensorMap &m, const char *name,
+             CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
     auto fn = encode();
     if (!fn) return set_error(VOX_CUDA_ERR_DEVICE, std::string(name) + ": cuTensorMapEncodeTiled is not available");
     const cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(depth)};
     const cuuint64_t strides[2] = {cuuint64_t(ld) * 2, cuuint64_t(ld) * 2 * cuuint64_t(rows)};
     const cuuint32_t box[3] = {uint32_t(kBK), uint32_t(box_rows), 1};
     const cuuint32_t es[3] = {1, 1, 1};
-    const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+    const CUresult r = fn(&m, dt, 3, const_cast<void *>(base), dims, strides, box, es,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(VOX_CUDA_ERR_ARG, std::string(name) + ": tensor map rejected (code " + std::to_string(int(r)) + ")");
@@ -1104,14 +1098,24 @@ int gemm_q(bool q4, const void *w, const void *scale, int scale_dtype, const flo
     GemmQArgs q{};
     q.M = int(m), q.N = int(rows), q.K = int(cols), q.nblk = int(cols / 32), q.scale = scale;
     q.g.M = int(m), q.g.N = int(rows), q.g.K = int(cols), q.g.y = y, q.g.ldy = rows, q.g.bias = bias, q.g.accumulate = accumulate != 0;
+    // x rounded to f16 once, into stream-ordered scratch from the device's memory pool (freed, stream-ordered, after
+    // the GEMM)
+    void *xh = nullptr;
+    const int64_t n4 = m * cols / 4;
+    if (cudaMallocAsync(&xh, size_t(m * cols * 2), st) != cudaSuccess) return check_launch(name);
+    launch_k(q_x_to_f16_kernel, grid_for(n4, 256, 4), 256, 0, st, reinterpret_cast<const float4 *>(x), reinterpret_cast<uint2 *>(xh), n4);
+    int rc = check_launch(name);
     CUtensorMap tx, tw;
-    int rc = plain_map(x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cols, m, cols * 4, kBK, kBM, tx, name);
-    if (rc != VOX_CUDA_OK) return rc;
-    rc = plain_map(w, CU_TENSOR_MAP_DATA_TYPE_UINT8, q4 ? cols / 2 : cols, rows, q4 ? cols / 2 : cols, q4 ? kBK / 2 : kBK, kQBN, tw, name);
-    if (rc != VOX_CUDA_OK) return rc;
-    const bool f16 = scale_dtype == VOX_CUDA_F16;
-    if (q4) return f16 ? launch_q<true, true>(tx, tw, q, st, name) : launch_q<true, false>(tx, tw, q, st, name);
-    return f16 ? launch_q<false, true>(tx, tw, q, st, name) : launch_q<false, false>(tx, tw, q, st, name);
+    if (rc == VOX_CUDA_OK) rc = bf16_map(xh, cols, m, 1, cols, kBM, tx, name, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    if (rc == VOX_CUDA_OK)
+        rc = plain_map(w, CU_TENSOR_MAP_DATA_TYPE_UINT8, q4 ? cols / 2 : cols, rows, q4 ? cols / 2 : cols, q4 ? kBK / 2 : kBK, kQBN, tw, name);
+    if (rc == VOX_CUDA_OK) {
+        const bool f16 = scale_dtype == VOX_CUDA_F16;
+        if (q4) rc = f16 ? launch_q<true, true>(tx, tw, q, st, name) : launch_q<true, false>(tx, tw, q, st, name);
+        else rc = f16 ? launch_q<false, true>(tx, tw, q, st, name) : launch_q<false, false>(tx, tw, q, st, name);
+    }
+    cudaFreeAsync(xh, st);
+    return rc;
 }
 
 int gemm_take_device_error(unsigned int *flags) { return take_device_error(flags); }

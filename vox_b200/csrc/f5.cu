@@ -1033,6 +1033,7 @@ int build_gemms(F5Plan &p) {
         // the fused q|k|v projection on 128 x 256 tiles: in the step it measured faster than the shape gemm_plan picks
         // alone (256 x 192 pairs; 2.213 against 2.238 ms a step, same box), its RoPE epilogue being the difference
         if (epi == kEpiQkvRope && !a.tile && N % 256 == 0) a.tile = 256;
+        a.w_early = 1;  // the plan's bf16 weight snapshots: no kernel of the step writes them
         if (epi == kEpiQkvRope) {
             a.cs = p.cs, a.frames = d.frames, a.rope_heads = d.pe_attn_head > 0 ? d.pe_attn_head : d.heads, a.hd = d.dim_head, a.inner = IN;
         }

@@ -212,6 +212,16 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &g, const CUtensorMap 
     __syncwarp();  // the staging area is reused by the next block
 }
 
+// One tiled copy issued by a whole converged warp through an elected lane, completing on `bar`; with expect_bytes > 0
+// the lane first arrives on `bar` expecting that many bytes (the whole stage).
+__device__ __forceinline__ void tma_one_warp(uint64_t *bar, uint32_t expect_bytes, uint32_t dst, const CUtensorMap *map, int x, int y, int z) {
+    asm volatile("{\n\t.reg .pred e, f;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.and.b32 f, %1, 0, e;\n\t"
+                 "@f mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t"
+                 "@e cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%3, {%4, %5, %6}], [%0];\n\t}"
+                 ::"r"(smem_addr(bar)), "r"(expect_bytes), "r"(dst), "l"(map), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 // The epilogue of one accumulator: its 32-column chunks [0, nch) (thread = row m32 + lane; taddr: this warp's lanes,
 // column 0), each loaded from tensor memory, finished and stored in turn. (Loading the next chunk while the current
 // one is stored measured slower.)
@@ -264,23 +274,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    pdl_enter();  // the previous grid is complete before the first read of its outputs and the first write of y
+    // the previous grid is complete before the first read of its outputs and the first write of y (the copy warp waits
+    // below, after its early weight copies)
+    if (warp != 0 || !g.w_early) pdl_enter();
     const uint32_t tmem = *tslot;
     bool ok = true;
 
     if (warp == 0) {
-        // ---- tensor copies
+        // ---- tensor copies. With w_early, the W tiles of the first tile's first STAGES K steps are requested before
+        // the previous grid has ended (W is none of its outputs), so their latency overlaps that grid's tail.
+        int pre = 0;
+        if (g.w_early) {
+            if (int(blockIdx.x) < tiles) {
+                const Tile tl = tile_of(int(blockIdx.x), mt, nt, g.groups);
+                pre = kt < C::STAGES ? kt : C::STAGES;
+                for (int kc = 0; kc < pre; ++kc)
+                    tma_one_warp(&full[kc], C::STAGE, s0 + uint32_t(kc) * C::STAGE + kABytes, &tb, kc * kBK, tl.ni * BN, tl.zg);
+                __syncwarp();
+            }
+            pdl_enter();
+        }
         uint32_t it = 0;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const Tile tl = tile_of(t, mt, nt, g.groups);
             for (int kc = 0; kc < kt; ++kc, ++it) {
                 const int s = int(it % C::STAGES);
                 const uint32_t u = it / C::STAGES;
+                const uint32_t sa = s0 + uint32_t(s) * C::STAGE;
+                if (int(it) < pre) {  // its W copy is in flight already (the stage's bytes expected): x only
+                    tma_one_warp(&full[s], 0, sa, &ta, kc * kBK, tl.m0, tl.z);
+                    __syncwarp();
+                    continue;
+                }
                 if (!mbar_wait_warp(&empty[s], (u & 1u) ^ 1u)) {
                     ok = false;
                     break;
                 }
-                const uint32_t sa = s0 + uint32_t(s) * C::STAGE;
                 tma_stage_warp(&full[s], C::STAGE, sa, &ta, kc * kBK, tl.m0, tl.z, sa + kABytes, &tb, kc * kBK, tl.ni * BN, tl.zg);
                 __syncwarp();
             }
@@ -1063,6 +1092,8 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
     const bool tma_ok = !(ets && ets[0] == '0') && aligned16(a.y) && (a.ldy * es) % 16 == 0 && a.ldy >= a.N &&
                         (a.batches == 1 || (a.y_bstride * es) % 16 == 0) &&
                         (a.groups == 1 || (a.N % 32 == 0 && (a.y_gstride * es) % 16 == 0)) && (!a.accumulate || f32out);
+    const char *ewe = std::getenv("VOX_CUDA_GEMM_W_EARLY");  // 0: no early weight copies (for comparisons)
+    if (ewe && ewe[0] == '0') plan.a.w_early = 0;
     plan.a.tma_store = 0;
     if (tma_ok) {
         const int64_t cols = int64_t(a.groups - 1) * a.y_gstride + a.N;

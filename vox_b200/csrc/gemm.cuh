@@ -32,6 +32,8 @@ struct GemmArgs {
     const float2 *cs = nullptr;
     int frames = 1, rope_heads = 0, hd = 64, inner = 0;
     int tile = 0;                     // 0: gemm_plan picks the tile; else 1000 * pair + BN (128, 256, 1128, 1192, ...)
+    int w_early = 0;                  // 1: W is not written by the previous kernel of the stream (weights of a plan), so
+                                      // its first copies may start before that kernel has ended (one-CTA tiles)
     int tma_store = 0;                // set by gemm_plan: y is written by tensor stores (GemmPlan::ty)
 };
 

@@ -105,21 +105,26 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &g, const CUtensorMap 
     if (pre.bias_s) {  // tile columns cb .. cb + 31 (zeros past N)
         const float4 *b4 = reinterpret_cast<const float4 *>(pre.bias_s + cb);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 8; ++q) {  // packed f32x2 adds (each rounded as the scalar add)
             const float4 bb = b4[q];
-            v[4 * q] += bb.x, v[4 * q + 1] += bb.y, v[4 * q + 2] += bb.z, v[4 * q + 3] += bb.w;
+            const float2 lo = add2(make_float2(v[4 * q], v[4 * q + 1]), make_float2(bb.x, bb.y));
+            const float2 hi = add2(make_float2(v[4 * q + 2], v[4 * q + 3]), make_float2(bb.z, bb.w));
+            v[4 * q] = lo.x, v[4 * q + 1] = lo.y, v[4 * q + 2] = hi.x, v[4 * q + 3] = hi.y;
         }
     }
     if constexpr (EPI == kEpiQkvRope) {
-        const int part = c0 / g.inner, ci = c0 - part * g.inner, head = ci / g.hd;
-        if (part < 2 && head < g.rope_heads && row < g.M) {  // pairs (2j, 2j + 1) of the head, j = (ci % hd) / 2 ..
-            const bool hi = (ci % g.hd) >= 32;                    // the head's second 32 columns: pairs 16 .. 31
+        // q, k or v part, and the head (hd is 64 for this epilogue: gemm_plan checks it), without divisions
+        const int part = c0 >= 2 * g.inner ? 2 : c0 >= g.inner ? 1 : 0, ci = c0 - part * g.inner, head = ci >> 6;
+        if (part < 2 && head < g.rope_heads && row < g.M) {  // pairs (2j, 2j + 1) of the head, j = (ci % 64) / 2 ..
+            const bool hi = (ci & 63) >= 32;                      // the head's second 32 columns: pairs 16 .. 31
+            // (x0, x1) -> (x0 c - x1 s, x1 c + x0 s) (f5.cpp:696-701) as one packed multiply and one packed FMA a pair:
+            // each output rounded once instead of three times; the bf16 output rounding is far larger than the difference
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const float2 c = hi ? pre.cs[16 + j] : pre.cs[j];
-                const float x0 = v[2 * j], x1 = v[2 * j + 1];
-                v[2 * j] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));  // f5.cpp:696-701, CPU rounding
-                v[2 * j + 1] = __fadd_rn(__fmul_rn(x1, c.x), __fmul_rn(x0, c.y));
+                const float2 x = make_float2(v[2 * j], v[2 * j + 1]);
+                const float2 r = fma2(x, make_float2(c.x, c.x), mul2(make_float2(x.y, x.x), make_float2(-c.y, c.y)));
+                v[2 * j] = r.x, v[2 * j + 1] = r.y;
             }
         }
     } else if constexpr (EPI == kEpiGeluTanh || EPI == kEpiGeluTanhF32) {

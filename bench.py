@@ -957,6 +957,85 @@ def run_copy_roofline(args) -> None:
                       "results": res}), flush=True)
 
 
+def run_gemv_sweep(args) -> None:
+    """The quantized decode GEMV (one activation row, [rows][4096] weights with f16 scales) over a range of matrix
+    heights, on one GPU, each size timed three ways: an event pair around every launch (as the suite's per-op numbers),
+    back-to-back launches (the mean; consecutive launches may overlap their set-up), and a plain device copy of the
+    same bytes (a torch copy_ of bytes/2, back to back). Every timing rotates over enough matrices that they total at
+    least 3x the L2 size, so every launch reads HBM. A least-squares line through the two largest sizes splits the
+    per-launch time into a fixed part (us) and a marginal rate (GB/s). One JSON line."""
+    import torch
+
+    torch.cuda.set_device(0)
+    import vox_b200 as vox
+
+    peak, _ = peaks()
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    cols, res = 4096, {}
+    for qt in ("q8", "q4"):
+        fn = vox.gemv_q8 if qt == "q8" else vox.gemv_q4
+        pts = []
+        for rows in (3072, 6144, 12288, 24576, 49152):
+            wb = rows * cols if qt == "q8" else rows * cols // 2
+            nb = wb + rows * (cols // 32) * 2 + cols * 4 + rows * 4
+            sets = max(2, -(-3 * l2 // nb))
+            gen = torch.Generator(device="cuda").manual_seed(rows)
+            if qt == "q8":
+                mats = [torch.randint(-128, 128, (rows, cols), dtype=torch.int8, device="cuda", generator=gen) for _ in range(sets)]
+            else:
+                mats = [torch.randint(0, 256, (rows, cols // 2), dtype=torch.uint8, device="cuda", generator=gen) for _ in range(sets)]
+            scs = [(torch.rand(rows, cols // 32, device="cuda", generator=gen) * 0.05 + 0.001).half() for _ in range(sets)]
+            x = torch.randn(1, cols, device="cuda", generator=gen)
+            y = torch.empty(1, rows, device="cuda")
+            calls = [lambda i=i: fn(mats[i], scs[i], x, out=y) for i in range(sets)]
+            reps = max(3 * sets, 60)
+            for c in calls:
+                c()
+            torch.cuda.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            torch.cuda._sleep(int(min(max(0.06 * reps, 5.0), 2000.0) * 2.0e6))  # the host enqueues while the GPU spins
+            for k in range(reps):
+                ev[k][0].record()
+                calls[k % sets]()
+                ev[k][1].record()
+            torch.cuda.synchronize()
+            per_launch = float(np.mean([a.elapsed_time(b) for a, b in ev])) * 1e3
+
+            def b2b(fns):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(int(min(max(0.03 * reps, 5.0), 2000.0) * 2.0e6))
+                e0.record()
+                for k in range(reps):
+                    fns[k % len(fns)]()
+                e1.record()
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) / reps * 1e3
+
+            back = min(b2b(calls) for _ in range(3))
+            del mats, scs, calls
+            torch.cuda.empty_cache()
+            bufs = [(torch.empty(nb // 2, dtype=torch.uint8, device="cuda"), torch.empty(nb // 2, dtype=torch.uint8, device="cuda"))
+                    for _ in range(sets)]
+            cps = [lambda s=s_, d=d_: d.copy_(s) for s_, d_ in bufs]
+            for c in cps:
+                c()
+            cp = min(b2b(cps) for _ in range(3))
+            del bufs, cps
+            torch.cuda.empty_cache()
+            pts.append((nb, per_launch))
+            res[f"{qt}_{rows}x{cols}"] = {"bytes": nb, "per_launch_us": round(per_launch, 2), "back_to_back_us": round(back, 2),
+                                          "copy_us": round(cp, 2), "per_launch_frac_of_peak": round(nb / per_launch / 1e3 / peak, 3),
+                                          "back_to_back_frac_of_peak": round(nb / back / 1e3 / peak, 3),
+                                          "copy_frac_of_peak": round(nb / cp / 1e3 / peak, 3), "frac_of_copy": round(cp / back, 3)}
+        (b1, t1), (b2, t2) = pts[-2], pts[-1]
+        slope = (t2 - t1) / (b2 - b1)  # us per byte
+        res[f"{qt}_fit"] = {"fixed_us": round(t1 - slope * b1, 2), "marginal_gb_s": round(1.0 / slope / 1e3, 1),
+                            "marginal_frac_of_peak": round(1.0 / slope / 1e3 / peak, 3)}
+    print(json.dumps({"metric": METRIC, "mode": "gemv-sweep", "unit": "GB/s", "peak": peak, "l2_bytes": l2,
+                      "config": {"workload": "quantized decode GEMV, 1 activation row, [rows][4096] with f16 scales"},
+                      "results": res}), flush=True)
+
+
 def run_gemm(args) -> None:
     """The tcgen05 GEMM (vox_cuda_gemm_bf16) alone on the F5-base projections, a prefill-shaped case and a large square
     case, against torch's bf16 matmul (cuBLAS) on the same operands: CUDA events around back-to-back launches, one
@@ -1133,6 +1212,7 @@ def main() -> None:
     ap.add_argument("--sweep", action="store_true", help="BASELINE cfg5 size sweep instead of the suite")
     ap.add_argument("--scale", type=int, default=1, help="multiply the rows/heads/batches of cfg1-cfg4 (1 = BASELINE shapes)")
     ap.add_argument("--copy-roofline", action="store_true", help="cfg1-cfg4 ops against a size-matched device copy")
+    ap.add_argument("--gemv-sweep", action="store_true", help="the decode GEMV over matrix heights, against a same-bytes copy")
     ap.add_argument("--gemm", action="store_true", help="the tcgen05 GEMM alone against cuBLAS")
     ap.add_argument("--probe", action="store_true", help="one launch of each kernel outside the suite (profiling)")
     ap.add_argument("--gemm-shape", default=None, help="--gemm: one MxNxK shape only")
@@ -1149,6 +1229,8 @@ def main() -> None:
         run_sweep(args)
     elif args.copy_roofline:
         run_copy_roofline(args)
+    elif args.gemv_sweep:
+        run_gemv_sweep(args)
     elif args.gemm:
         run_gemm(args)
     elif args.probe:

@@ -558,6 +558,23 @@ constexpr int kRowBox = kRowBatch * 512;  // 4 KB
 constexpr int kRowCopies = kRowsCta / kRowBatch;  // copies per chunk
 // Blocks of a 512-byte row chunk: 16 (Q8, 32 bytes a block) or 32 (Q4, 16 bytes a block); their scales for the CTA's rows.
 template <bool Q4> __host__ __device__ constexpr int chunk_scales() { return Q4 ? 32 : 16; }
+// shared-memory reads by address (ld.shared): the staging rings sit behind a realigned pointer
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+template <typename ST> __device__ __forceinline__ float lds_scale(uint32_t a);
+template <> __device__ __forceinline__ float lds_scale<__half>(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return __half2float(__ushort_as_half(v));
+}
+template <> __device__ __forceinline__ float lds_scale<float>(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
 template <bool Q4, bool SF16> __host__ __device__ constexpr int scale_box() { return kRowsCta * chunk_scales<Q4>() * (SF16 ? 2 : 4); }
 template <bool Q4, bool SF16, int M> __host__ __device__ constexpr size_t rows_smem() {  // + row partials of two groups
     return 256 + size_t(kWarps) * (kRowStages * kRowBox + 2 * scale_box<Q4, SF16>()) + size_t(2) * kWarps * M * kRowsCta * 4 + 128;
@@ -643,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : M <= 2 ? 2 : 1
                         xv[t][2 * q + 1] = make_float2(v.z, v.w);
                     }
             }
-            const ST *scs = reinterpret_cast<const ST *>(sring + (ck & 1) * SB) + (Q4 ? lane : lane >> 1);  // [kRowsCta rows][BPC blocks]
+            const uint32_t scs = smem_addr(reinterpret_cast<const ST *>(sring + (ck & 1) * SB) + (Q4 ? lane : lane >> 1));  // [kRowsCta rows][BPC blocks]
 #pragma unroll 1
             for (int b = 0; b < kRowCopies; ++b) {
                 const int u = ck * kRowCopies + b, s = u % kRowStages;
@@ -652,12 +669,12 @@ __global__ void __launch_bounds__(kThreads, (!Q4 && M == 1) ? 3 : M <= 2 ? 2 : 1
                     break;
                 }
                 parity ^= 1u << s;
-                const uint8_t *st = wring + s * kRowBox + lane * 16;
+                const uint32_t st = smem_addr(wring + s * kRowBox + lane * 16);
                 float acc[kRowBatch][M];
 #pragma unroll
                 for (int r = 0; r < kRowBatch; ++r) {
-                    const uint4 w = *reinterpret_cast<const uint4 *>(st + r * 512);
-                    const float sc = float(scs[(b * kRowBatch + r) * BPC]);
+                    const uint4 w = lds_v4(st + r * 512);
+                    const float sc = lds_scale<ST>(scs + uint32_t((b * kRowBatch + r) * BPC * sizeof(ST)));
                     const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
                     float2 p[M][2];
 #pragma unroll

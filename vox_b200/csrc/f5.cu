@@ -410,7 +410,10 @@ __global__ void __launch_bounds__(kTcThreads, 3) f5_flash_tc_kernel(const __nv_b
 // elected lane (operands warp-uniform). Measured against the alternatives on B200 (F5 base, 2 x 1024 frames, 16
 // heads): 28.9 us a launch against 31.2 us for one thread a row; keeping two S and two P V buffers in tensor memory
 // so that P V of a tile is waited for one tile later measured 33.5 us, and the same with a ninth warp issuing the
-// MMAs (no CTA-wide barrier in the loop) 37.0 us.
+// MMAs (no CTA-wide barrier in the loop) 37.0 us. In the step (same box, 22 launches): the next tile's S issued before
+// this tile's P V, P V folded into the output after the next tile's exponentials and K / V in three buffers took the
+// step from 2.200 to 2.272 ms; a quarter of the exponentials from a cubic on the FMA pipe (beside the MUFU ex2), from
+// 2.203 to 2.215 ms.
 constexpr int kTc2Threads = 256;
 constexpr size_t kTc2Smem = kTcSmem + 2 * 128 * sizeof(float);  // + the partial maxima / sums of the two halves
 

@@ -1051,8 +1051,25 @@ def run_gemm(args) -> None:
     if args.gemm_shape:  # one shape only (profiling a single kernel)
         m, n, k = (int(v) for v in args.gemm_shape.lower().split("x"))
         shapes = [(f"gemm_{m}x{n}x{k}", m, n, k)]
+    if args.gemm_quant:  # the quantized prefill GEMM only
+        shapes = []
     res = {}
     g = torch.Generator(device="cuda").manual_seed(0)
+    reps = 40
+
+    def t(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(int(min(max(0.03 * reps, 5.0), 2000.0) * 2.0e6))  # the host enqueues while the GPU spins
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3
+
     for nm, m, n, k in shapes:
         x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
         w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
@@ -1060,19 +1077,6 @@ def run_gemm(args) -> None:
         yb = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
         fl = 2 * m * n * k
         reps = max(5, min(200, int(2e-3 / (fl / 1.2e15))))
-
-        def t(fn):
-            for _ in range(3):
-                fn()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda._sleep(int(min(max(0.03 * reps, 5.0), 2000.0) * 2.0e6))  # the host enqueues while the GPU spins
-            e0.record()
-            for _ in range(reps):
-                fn()
-            e1.record()
-            torch.cuda.synchronize()
-            return e0.elapsed_time(e1) / reps * 1e3
 
         ours = min(t(lambda: vox.gemm_bf16(x, w, out=y)) for _ in range(3))
         ours_b = min(t(lambda: vox.gemm_bf16(x, w, out_dtype=torch.bfloat16, out=yb)) for _ in range(3))
@@ -1099,30 +1103,34 @@ def run_gemm(args) -> None:
                    "cublas_tflops": round(fl / ref / 1e6, 1),
                    "cold_w_us": None if cold is None else round(cold, 2), "cold_w_cublas_us": None if cold_ref is None else round(cold_ref, 2)}
         del x, w, y, yb
-    # the quantized prefill GEMM (Q8 / Q4 weights [12288][4096] with f16 scales, 512 f32 activation rows), weights rotated
-    # over enough copies that they stream from HBM
-    m, n, k = 512, 12288, 4096
-    x = torch.randn(m, k, device="cuda", generator=g)
-    y = torch.empty(m, n, device="cuda")
-    fl = 2 * m * n * k
-    for qt in ("q8", "q4"):
-        mats = [vox.fill_philox(torch.empty(n, k if qt == "q8" else k // 2, dtype=torch.int8 if qt == "q8" else torch.uint8, device="cuda"),
-                                2 if qt == "q8" else 3, -128, 127, seed=0, stream_id=70 + i) for i in range(4)]
-        scs = [vox.fill_philox(torch.empty(n, k // 32, device="cuda"), 0, 0.001, 0.05, seed=0, stream_id=80 + i).half() for i in range(4)]
-        fn = vox.gemm_q8 if qt == "q8" else vox.gemm_q4
-        ctr = [0]
+    # the quantized prefill GEMM (Q8 / Q4 weights [n][4096] with f16 scales, 512 f32 activation rows), weights rotated
+    # over enough copies that they stream from HBM; also timed with whole tiles only (VOX_CUDA_GEMMQ_SPLIT=0, read by
+    # the library at every call) for the K-range split's share
+    for m, n, k in ((512, 12288, 4096), (512, 4096, 4096)):
+        x = torch.randn(m, k, device="cuda", generator=g)
+        y = torch.empty(m, n, device="cuda")
+        fl = 2 * m * n * k
+        for qt in ("q8", "q4"):
+            mats = [vox.fill_philox(torch.empty(n, k if qt == "q8" else k // 2, dtype=torch.int8 if qt == "q8" else torch.uint8, device="cuda"),
+                                    2 if qt == "q8" else 3, -128, 127, seed=0, stream_id=70 + i) for i in range(4)]
+            scs = [vox.fill_philox(torch.empty(n, k // 32, device="cuda"), 0, 0.001, 0.05, seed=0, stream_id=80 + i).half() for i in range(4)]
+            fn = vox.gemm_q8 if qt == "q8" else vox.gemm_q4
+            ctr = [0]
 
-        def call(fn=fn, mats=mats, scs=scs, ctr=ctr):
-            i = ctr[0] % 4
-            ctr[0] += 1
-            fn(mats[i], scs[i], x, out=y)
+            def call(fn=fn, mats=mats, scs=scs, ctr=ctr):
+                i = ctr[0] % 4
+                ctr[0] += 1
+                fn(mats[i], scs[i], x, out=y)
 
-        reps = 40
-        us = min(t(call) for _ in range(3))
-        res[f"prefill_{qt}"] = {"m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(fl / us / 1e6, 1),
-                                "frac_of_tensor_peak": round(fl / us / 1e6 / tpk, 3),
-                                "weight_gb_s": round((n * k * (1 if qt == "q8" else 0.5) + n * k // 32 * 2) / us / 1e3, 1)}
-        del mats, scs
+            reps = 40
+            us = min(t(call) for _ in range(3))
+            os.environ["VOX_CUDA_GEMMQ_SPLIT"] = "0"
+            us_whole = min(t(call) for _ in range(3))
+            del os.environ["VOX_CUDA_GEMMQ_SPLIT"]
+            res[f"prefill_{qt}" + ("" if n == 12288 else f"_{m}x{n}x{k}")] = {
+                "m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "frac_of_tensor_peak": round(fl / us / 1e6 / tpk, 3),
+                "weight_gb_s": round((n * k * (1 if qt == "q8" else 0.5) + n * k // 32 * 2) / us / 1e3, 1), "us_whole_tiles": round(us_whole, 2)}
+            del mats, scs
     print(json.dumps({"metric": METRIC, "mode": "gemm", "unit": "TFLOP/s", "tensor_peak": f"{tpk} bf16 sustained ({tkind})",
                       "config": {"workload": "tcgen05 bf16 GEMM vs cuBLAS, F5-base and prefill shapes"}, "results": res}), flush=True)
 
@@ -1216,6 +1224,7 @@ def main() -> None:
     ap.add_argument("--gemm", action="store_true", help="the tcgen05 GEMM alone against cuBLAS")
     ap.add_argument("--probe", action="store_true", help="one launch of each kernel outside the suite (profiling)")
     ap.add_argument("--gemm-shape", default=None, help="--gemm: one MxNxK shape only")
+    ap.add_argument("--gemm-quant", action="store_true", help="--gemm: the quantized prefill GEMM only")
     ap.add_argument("--probe-rows", type=int, default=131072, help="--probe: rows of 1024 elements a tensor")
     ap.add_argument("--probe-reps", type=int, default=20, help="--probe: warm-up and timed launches of each kernel")
     ap.add_argument("--sweep-lo", type=int, default=20)

@@ -673,7 +673,28 @@ struct GemmQArgs {
     int M, N, K, nblk;      // nblk = K / 32
     const void *scale;      // [N][nblk] f32 or f16
     GemmArgs g;             // epilogue (kEpiF32: bias, accumulate, y [M][N])
+    // Work items (one CTA takes items blockIdx.x, + gridDim.x, ...): items 0 .. full - 1 are whole output tiles, the
+    // rest are `splits` K-ranges of each of the last `rem` tiles (piece p of tail tile i is item full + p * rem + i),
+    // whose f32 partials go to part[item - full][128][256] and are summed in piece order by gemm_q_fixup_kernel.
+    int full, rem, splits, items;
+    float *part;
 };
+
+// Tile, K-step range and partial slot (-1: the whole tile, finished into y) of work item w.
+struct QItem {
+    int t, kb, ke, slot;
+};
+__device__ __forceinline__ QItem q_item(const GemmQArgs &q, int w, int kt) {
+    QItem r;
+    if (w < q.full) {
+        r.t = w, r.kb = 0, r.ke = kt, r.slot = -1;
+        return r;
+    }
+    const int j = w - q.full, p = j / q.rem;
+    r.t = q.full + (j - p * q.rem), r.slot = j;
+    r.kb = int(int64_t(p) * kt / q.splits), r.ke = int(int64_t(p + 1) * kt / q.splits);  // splits <= kt: never empty
+    return r;
+}
 
 template <bool Q4, bool SF16>
 __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
@@ -692,8 +713,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
     const uint32_t STG_BASE = smem_addr(smem + C::S * C::STAGE) + 256;  // the epilogue warps' staging areas (after the barriers)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = (q.M + kBM - 1) / kBM, nt = (q.N + kQBN - 1) / kQBN;
-    const int tiles = mt * nt, kt = (q.K + kBK - 1) / kBK;
+    const int mt = (q.M + kBM - 1) / kBM, kt = (q.K + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::S; ++s) {
@@ -721,9 +741,10 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     if (warp == 0) {
         // ---- copies: a stage's x tile (into its MMA operand slot) and codes
         uint32_t it = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
-            for (int kc = 0; kc < kt; ++kc, ++it) {
+        for (int w = blockIdx.x; w < q.items && ok; w += gridDim.x) {
+            const QItem wi = q_item(q, w, kt);
+            const int m0 = (wi.t % mt) * kBM, n0 = (wi.t / mt) * kQBN;
+            for (int kc = wi.kb; kc < wi.ke; ++kc, ++it) {
                 const int s = int(it % C::S);
                 const uint32_t u = it / C::S;
                 if (!mbar_wait_warp(&stage_empty[s], (u & 1u) ^ 1u)) {
@@ -745,9 +766,10 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         uint32_t it = 0;
         const uint32_t off8 = 0x64806480u;   // f16x2 (1152, 1152): 1024 + 128 (Q8 codes offset to unsigned by ^ 0x80)
         const uint32_t off4 = 0x64086408u;   // f16x2 (1032, 1032): 1024 + 8 (Q4 codes are u - 8)
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            const int n0 = (t / mt) * kQBN;
-            for (int kc = 0; kc < kt; ++kc, ++it) {
+        for (int w = blockIdx.x; w < q.items && ok; w += gridDim.x) {
+            const QItem wi = q_item(q, w, kt);
+            const int n0 = (wi.t / mt) * kQBN;
+            for (int kc = wi.kb; kc < wi.ke; ++kc, ++it) {
                 const int rs = int(it % C::S);
                 const uint32_t ru = it / C::S;
                 // the block scales of this thread's weight tasks (global loads, in flight during the waits)
@@ -829,7 +851,8 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     } else if (warp == 1) {
         // ---- MMA issue
         uint32_t it = 0, tc = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        for (int w = blockIdx.x; w < q.items && ok; w += gridDim.x, ++tc) {
+            const QItem wi = q_item(q, w, kt);
             const uint32_t a = tc & 1u, v = tc >> 1;
             if (!mbar_wait_warp(&tempty[a], (v & 1u) ^ 1u)) {
                 ok = false;
@@ -837,7 +860,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
             }
             tc_fence_after();
             const uint32_t dcol = tmem + a * kQBN;
-            for (int kc = 0; kc < kt; ++kc, ++it) {
+            for (int kc = wi.kb; kc < wi.ke; ++kc, ++it) {
                 const int s = int(it % C::S);
                 const uint32_t u = it / C::S;
                 // the x tile (TMA) and the converted weights
@@ -850,7 +873,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
                     const uint32_t sa = smem_addr(smem + s * C::STAGE), sb = sa + kQA;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
-                        umma_bf16_warp(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, (kc | k) != 0);
+                        umma_bf16_warp(dcol, umma_desc(sa + 32 * k, 16, 1024), umma_desc(sb + 32 * k, 16, 1024), kIdesc, kc != wi.kb || k != 0);
                     umma_commit_warp(&stage_empty[s]);  // the stage returns to the copy warp when these MMAs have read it
                 }
                 __syncwarp();
@@ -871,18 +894,27 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
         float *bias_s = reinterpret_cast<float *>(smem + C::S * C::STAGE + 256 + 4 * kStageWarpBytes) + (warp - 2) * 256;
         uint32_t qseq = 0;
         uint32_t tc = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        for (int w = blockIdx.x; w < q.items && ok; w += gridDim.x, ++tc) {
+            const QItem wi = q_item(q, w, kt);
             const uint32_t a = tc & 1u, v = tc >> 1;
-            const int m0 = (t % mt) * kBM, n0 = (t / mt) * kQBN;
+            const int m0 = (wi.t % mt) * kBM, n0 = (wi.t / mt) * kQBN;
+            // a K-range piece stores its raw f32 partial in its [128][256] slot (no bias, no accumulate): y is addressed
+            // as slot - (m0 row pitch + n0) so that the epilogue's absolute rows and columns land inside the slot
+            GemmArgs ga = q.g;
+            if (wi.slot >= 0) {
+                ga.bias = nullptr, ga.accumulate = 0, ga.ldy = kQBN;
+                ga.y = reinterpret_cast<void *>(reinterpret_cast<uintptr_t>(q.part) +
+                                                uintptr_t((int64_t(wi.slot) * kBM * kQBN - int64_t(m0) * kQBN - n0) * int64_t(sizeof(float))));
+            }
             EpiPre pre;
-            epi_prepare<kEpiF32>(q.g, n0, kQBN, 0, m0 + 32 * qw + lane, lane, bias_s, pre);
+            epi_prepare<kEpiF32>(ga, n0, kQBN, 0, m0 + 32 * qw + lane, lane, bias_s, pre);
             if (!mbar_wait_warp(&tfull[a], v & 1u)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int nch = min(kQBN, q.N - n0 + 31) / 32;
-            epilogue_tile<kEpiF32, kStageWarpBytes>(q.g, nullptr, tmem + (uint32_t(32 * qw) << 16) + a * kQBN, nch, m0 + 32 * qw, lane, n0, 0, 0, stg,
+            epilogue_tile<kEpiF32, kStageWarpBytes>(ga, nullptr, tmem + (uint32_t(32 * qw) << 16) + a * kQBN, nch, m0 + 32 * qw, lane, n0, 0, 0, stg,
                                                     qseq, pre);
             tc_fence_before();
             __syncwarp();
@@ -894,6 +926,40 @@ __global__ void __launch_bounds__(kQThreads, 1) gemm_q_kernel(const __grid_const
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, 2 * kQBN);
+    }
+}
+
+// The tail tiles of a split schedule: y = (sum of the tile's K-range partials, in piece order) + bias (+ y), each element
+// added in the order the whole-tile epilogue uses, so the result is the same run to run. Four columns a thread.
+__global__ void __launch_bounds__(256) gemm_q_fixup_kernel(const GemmQArgs q) {
+    pdl_enter();
+    constexpr int kQuads = kBM * kQBN / 4;
+    const int mt = (q.M + kBM - 1) / kBM;
+    const size_t slot = size_t(q.rem) * kBM * kQBN;  // floats between piece p and piece p + 1 of one tile
+    const int64_t total = int64_t(q.rem) * kQuads;
+    float *y = reinterpret_cast<float *>(q.g.y);
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int ti = int(i / kQuads), e = int(i - int64_t(ti) * kQuads);
+        const int r = e / (kQBN / 4), c = (e % (kQBN / 4)) * 4;
+        const int t = q.full + ti;
+        const int gm = (t % mt) * kBM + r, gn = (t / mt) * kQBN + c;
+        if (gm >= q.M || gn >= q.N) continue;
+        const float *pp = q.part + size_t(ti) * kBM * kQBN + size_t(r) * kQBN + c;
+        float4 a = *reinterpret_cast<const float4 *>(pp);
+        for (int p = 1; p < q.splits; ++p) {
+            const float4 b = *reinterpret_cast<const float4 *>(pp + p * slot);
+            a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+        }
+        const float v[4] = {a.x, a.y, a.z, a.w};
+        float *yr = y + int64_t(gm) * q.g.ldy + gn;
+        const int nv = min(4, q.N - gn);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (j >= nv) break;
+            float f = v[j];
+            if (q.g.bias) f += __ldg(q.g.bias + gn + j);
+            yr[j] = q.g.accumulate ? f + yr[j] : f;
+        }
     }
 }
 
@@ -973,10 +1039,14 @@ int launch_q(const CUtensorMap &tx, const CUtensorMap &tw, const GemmQArgs &q, c
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(QCfg<Q4>::SMEM)) != cudaSuccess) return check_launch(name);
         attr_set[dev] = true;
     }
-    const int64_t tiles = int64_t((q.M + kBM - 1) / kBM) * ((q.N + kQBN - 1) / kQBN);
-    const int grid = int(tiles < sm_count() ? tiles : sm_count());
+    const int grid = q.items < sm_count() ? q.items : sm_count();
     launch_k(kern, grid, kQThreads, QCfg<Q4>::SMEM, st, tx, tw, q);
-    return check_launch(name);
+    int rc = check_launch(name);
+    if (rc == VOX_CUDA_OK && q.splits > 1) {
+        launch_k(gemm_q_fixup_kernel, grid_for(int64_t(q.rem) * kBM * kQBN / 4, 256, 8), 256, 0, st, q);
+        rc = check_launch(name);
+    }
+    return rc;
 }
 
 template <int BN, int EPI>
@@ -1134,11 +1204,32 @@ int gemm_q(bool q4, const void *w, const void *scale, int scale_dtype, const flo
     GemmQArgs q{};
     q.M = int(m), q.N = int(rows), q.K = int(cols), q.nblk = int(cols / 32), q.scale = scale;
     q.g.M = int(m), q.g.N = int(rows), q.g.K = int(cols), q.g.y = y, q.g.ldy = rows, q.g.bias = bias, q.g.accumulate = accumulate != 0;
-    // x rounded to f16 once, into stream-ordered scratch from the device's memory pool (freed, stream-ordered, after
-    // the GEMM)
+    // Work split. T output tiles of 128 x 256 on P (the SM count) persistent CTAs leave the last wave T % P tiles wide
+    // (512 x 12288: 192 tiles, 44 of 148 CTAs busy in the second wave; 512 x 4096: 64 tiles, one wave of 64). The T % P
+    // tail tiles are cut instead into s = min(P / (T % P), K steps / 4, 8) K-ranges each, so every CTA takes its whole
+    // tiles and at most one piece; the pieces' f32 partials are summed in a fixed order by gemm_q_fixup_kernel.
+    // VOX_CUDA_GEMMQ_SPLIT=0 keeps whole tiles.
+    {
+        const int64_t mt = (m + kBM - 1) / kBM, nt = (rows + kQBN - 1) / kQBN, tiles = mt * nt, kt = (cols + kBK - 1) / kBK;
+        const int64_t P = sm_count();
+        const int64_t full = tiles / P * P, rem = tiles - full;
+        int64_t s = rem ? P / rem : 1;
+        if (s > kt / 4) s = kt / 4;
+        if (s > 8) s = 8;
+        const char *es = std::getenv("VOX_CUDA_GEMMQ_SPLIT");
+        if (es && es[0] == '0') s = 1;
+        VOX_REQUIRE(tiles < (int64_t(1) << 30), std::string(name) + ": shape too large");
+        if (s >= 2) q.full = int(full), q.rem = int(rem), q.splits = int(s), q.items = int(full + rem * s);
+        else q.full = int(tiles), q.rem = 1, q.splits = 1, q.items = int(tiles);
+    }
+    // x rounded to f16 once, and the pieces' partials, in stream-ordered scratch from the device's memory pool (freed,
+    // stream-ordered, after the GEMM)
     void *xh = nullptr;
     const int64_t n4 = m * cols / 4;
-    if (cudaMallocAsync(&xh, size_t(m * cols * 2), st) != cudaSuccess) return check_launch(name);
+    const size_t xh_bytes = (size_t(m * cols * 2) + 255) & ~size_t(255);
+    const size_t part_bytes = q.splits > 1 ? size_t(q.rem) * q.splits * kBM * kQBN * sizeof(float) : 0;
+    if (cudaMallocAsync(&xh, xh_bytes + part_bytes, st) != cudaSuccess) return check_launch(name);
+    q.part = part_bytes ? reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xh) + xh_bytes) : nullptr;
     launch_k(q_x_to_f16_kernel, grid_for(n4, 256, 4), 256, 0, st, reinterpret_cast<const float4 *>(x), reinterpret_cast<uint2 *>(xh), n4);
     int rc = check_launch(name);
     CUtensorMap tx, tw;

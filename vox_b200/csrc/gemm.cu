@@ -629,8 +629,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_
 // Measured at 512 x 12288 x 4096 (Q8 / Q4): converting x inside the GEMM (an f32 raw ring beside the f16 one, two
 // stages each) took 144 / 141 us; this ring 118 / 98 us. Not kept: a separate code ring loaded up to three steps ahead
 // with the x copies started by the converters (122 / 115 us), and the next step's block scales loaded while the
-// current one converts (142 / 132 us). f16 keeps 11 significant bits of x and of code * scale (bf16: 8); |x| must stay
-// below 65504. A code's integer value is exact in f16; its product with an f16 scale is rounded once.
+// current one converts (142 / 132 us). With the last wave split into K-ranges (q_item, gemm_q_fixup_kernel): 90.0 /
+// 79.1 us; not kept there: CTA pairs on 256 x 256 tiles (cta_group::2, each CTA converting 128 weight rows: 131 / 127
+// us) and the block scales loaded one K step ahead (99 / 88 us). f16 keeps 11 significant bits of x and of code *
+// scale (bf16: 8); |x| must stay below 65504. A code's integer value is exact in f16; its product with an f16 scale is
+// rounded once.
 constexpr int kQBN = 256;
 constexpr int kQThreads = 448;
 constexpr int kQConvWarps = 8;

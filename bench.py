@@ -1104,8 +1104,9 @@ def run_gemm(args) -> None:
                    "cold_w_us": None if cold is None else round(cold, 2), "cold_w_cublas_us": None if cold_ref is None else round(cold_ref, 2)}
         del x, w, y, yb
     # the quantized prefill GEMM (Q8 / Q4 weights [n][4096] with f16 scales, 512 f32 activation rows), weights rotated
-    # over enough copies that they stream from HBM; also timed with whole tiles only (VOX_CUDA_GEMMQ_SPLIT=0, read by
-    # the library at every call) for the K-range split's share
+    # over enough copies that they stream from HBM; `us` is the default form (two passes from 256 rows of x), also
+    # timed in one pass (VOX_CUDA_GEMMQ_TWOPASS=0) and in one pass on whole tiles (VOX_CUDA_GEMMQ_SPLIT=0); the
+    # library reads both at every call
     for m, n, k in ((512, 12288, 4096), (512, 4096, 4096)):
         x = torch.randn(m, k, device="cuda", generator=g)
         y = torch.empty(m, n, device="cuda")
@@ -1124,12 +1125,14 @@ def run_gemm(args) -> None:
 
             reps = 40
             us = min(t(call) for _ in range(3))
+            os.environ["VOX_CUDA_GEMMQ_TWOPASS"] = "0"
+            us_one = min(t(call) for _ in range(3))
             os.environ["VOX_CUDA_GEMMQ_SPLIT"] = "0"
             us_whole = min(t(call) for _ in range(3))
-            del os.environ["VOX_CUDA_GEMMQ_SPLIT"]
+            del os.environ["VOX_CUDA_GEMMQ_SPLIT"], os.environ["VOX_CUDA_GEMMQ_TWOPASS"]
             res[f"prefill_{qt}" + ("" if n == 12288 else f"_{m}x{n}x{k}")] = {
                 "m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "frac_of_tensor_peak": round(fl / us / 1e6 / tpk, 3),
-                "weight_gb_s": round((n * k * (1 if qt == "q8" else 0.5) + n * k // 32 * 2) / us / 1e3, 1), "us_whole_tiles": round(us_whole, 2)}
+                "weight_gb_s": round((n * k * (1 if qt == "q8" else 0.5) + n * k // 32 * 2) / us / 1e3, 1), "us_one_pass": round(us_one, 2), "us_one_pass_whole_tiles": round(us_whole, 2)}
             del mats, scs
     print(json.dumps({"metric": METRIC, "mode": "gemm", "unit": "TFLOP/s", "tensor_peak": f"{tpk} bf16 sustained ({tkind})",
                       "config": {"workload": "tcgen05 bf16 GEMM vs cuBLAS, F5-base and prefill shapes"}, "results": res}), flush=True)

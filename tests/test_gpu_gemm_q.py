@@ -57,17 +57,20 @@ def test_gemm_q_golden(vox, golden):
 @pytest.mark.parametrize("q4", [False, True])
 @pytest.mark.parametrize("rows,cols,m", [(4096, 4096, 512), (1000, 1024, 130), (300, 96, 9), (257, 4064, 200), (12288, 1024, 64),
                                          (12288, 1024, 512), (10000, 512, 520), (20000, 512, 300)])
-def test_gemm_q_shapes(vox, port, q4, rows, cols, m):
-    """Tile edges in every dimension (rows and m not multiples of 256 / 128, cols an odd number of 32-blocks), and
-    every work schedule on 148 SMs: one partial wave cut into K-ranges (4096 x 512: 64 tiles, 2 pieces each), whole
+def test_gemm_q_shapes(vox, port, q4, rows, cols, m, monkeypatch):
+    """Tile edges in every dimension (rows and m not multiples of 256 / 128, cols an odd number of 32-blocks), both
+    forms (one pass; two passes: W to f16, then the f16 GEMM, the default from 256 rows of x), and every one-pass work
+    schedule on 148 SMs: one partial wave cut into K-ranges (4096 x 512: 64 tiles, 2 pieces each), whole
     tiles plus K-range pieces of the tail (12288 x 512: 192 tiles, the last 44 in 3 pieces; 10000 x 520: 200 tiles,
     the last 52 in 2 pieces with ragged rows and columns), whole tiles only (20000 x 300: 237 tiles), tiny K unsplit."""
     q, s, x, b = _inputs(port, rows, cols, m, q4)
     for f16, bias in ((False, b), (True, None)):
         sc = s.astype(np.float16).astype(np.float32) if f16 else s
-        y = host(_gpu(vox, q, sc, x, bias, q4, f16=f16))
         want, bound = port.gemv(q, sc, x, bias, q4=q4)
-        _check(y, want, bound)
+        for two in ("0", "1"):  # one pass (codes converted in the GEMM) and two passes (f16 W, then the f16 GEMM)
+            monkeypatch.setenv("VOX_CUDA_GEMMQ_TWOPASS", two)
+            y = host(_gpu(vox, q, sc, x, bias, q4, f16=f16))
+            _check(y, want, bound)
     assert vox.device_error() == 0
 
 
@@ -87,21 +90,19 @@ def test_gemm_q_accumulate_and_determinism(vox, port, q4):
 
 @pytest.mark.parametrize("q4", [False, True])
 def test_gemm_q_split_schedule_matches_whole_tiles(vox, port, q4, monkeypatch):
-    """The K-range pieces and their fixed-order sum agree with whole tiles (VOX_CUDA_GEMMQ_SPLIT=0) to the oracle's
-    bound, accumulate into y as whole tiles do, and repeat bit for bit."""
+    """The one-pass K-range pieces and their fixed-order sum agree with whole tiles (VOX_CUDA_GEMMQ_SPLIT=0) and the
+    two-pass form to the oracle's bound, each accumulates into y, and each repeats bit for bit."""
     rows, cols, m = 12288, 1024, 512
     q, s, x, b = _inputs(port, rows, cols, m, q4, sid=230)
     y0 = port.normal((m, rows), sid=235)
     want, bound = port.gemv(q, s, x, b, y=y0, q4=q4)
-    outs = []
-    for split in ("1", "0"):
+    for two, split in (("0", "1"), ("0", "0"), ("1", "1")):
+        monkeypatch.setenv("VOX_CUDA_GEMMQ_TWOPASS", two)
         monkeypatch.setenv("VOX_CUDA_GEMMQ_SPLIT", split)
         out = dev(y0)
         _gpu(vox, q, s, x, b, q4, out=out, accumulate=True)
-        outs.append(host(out))
-        _check(outs[-1], want, bound + np.abs(y0))
-    monkeypatch.delenv("VOX_CUDA_GEMMQ_SPLIT")
-    r1 = host(_gpu(vox, q, s, x, b, q4))
-    r2 = host(_gpu(vox, q, s, x, b, q4))
-    np.testing.assert_array_equal(r1.view(np.uint32), r2.view(np.uint32))
+        _check(host(out), want, bound + np.abs(y0))
+        r1 = host(_gpu(vox, q, s, x, b, q4))
+        r2 = host(_gpu(vox, q, s, x, b, q4))
+        np.testing.assert_array_equal(r1.view(np.uint32), r2.view(np.uint32))
     assert vox.device_error() == 0

@@ -242,11 +242,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &g, const CUtensorM
     }
 }
 
-template <int BN, int EPI>
+// F16: f16 x and W instead of bf16 (the quantized GEMM's two-pass form); same kernel, the MMA's operand type differs.
+template <int BN, int EPI, bool F16 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                                                                   const __grid_constant__ CUtensorMap ty, const GemmArgs g) {
     using C = Cfg<BN>;
-    constexpr uint32_t kIdesc = umma_idesc_bf16(kBM, BN);
+    constexpr uint32_t kIdesc = F16 ? umma_idesc_f16(kBM, BN) : umma_idesc_bf16(kBM, BN);
     extern __shared__ uint8_t gemm_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t s0 = smem_addr(smem);
@@ -463,13 +464,13 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
                  : "memory");
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool F16 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                                                                    const __grid_constant__ CUtensorMap ty, const GemmArgs g) {
     using P = PairCfg<BN>;
     constexpr int kPairStages = P::STAGES;
     constexpr uint32_t kPairStage = P::STAGE;
-    constexpr uint32_t kIdesc = umma_idesc_bf16(256, BN);
+    constexpr uint32_t kIdesc = F16 ? umma_idesc_f16(256, BN) : umma_idesc_bf16(256, BN);
     extern __shared__ uint8_t gemm2_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t s0 = smem_addr(smem);
@@ -669,6 +670,40 @@ __global__ void __launch_bounds__(256) q_x_to_f16_kernel(const float4 *x, uint2 
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
         const float4 v = __ldg(x + i);
         xh[i] = make_uint2(f16x2_of(v.x, v.y), f16x2_of(v.z, v.w));
+    }
+}
+
+// The two-pass form's weight pass: w16[e] = f16(code(e)) * f16(scale[e / 32]) for the flat element e of W [N][K]
+// (K a multiple of 32, so a 32-block is the flat e / 32), with the converters' arithmetic of gemm_q_kernel (the code
+// exact in f16 by the 0x64 exponent pattern, one rounding of the product): the f16 operands are the same either way.
+// Eight weights a thread and pass: Q8 bytes e .. e + 7; Q4 the low (e % 32 < 16) or high nibbles of the block's bytes
+// (e % 16) .. (e % 16) + 7 (Vox's order: byte j holds elements j and j + 16).
+template <bool Q4, bool SF16>
+__global__ void __launch_bounds__(256) q_w_to_f16_kernel(const uint8_t *w, const void *scale, uint4 *w16, int64_t n8) {
+    pdl_enter();
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t e = 8 * i, blk = e >> 5;
+        const float sc = SF16 ? __half2float(__ldg(reinterpret_cast<const __half *>(scale) + blk)) : __ldg(reinterpret_cast<const float *>(scale) + blk);
+        const __half h = __float2half_rn(sc);
+        const uint32_t hb = *reinterpret_cast<const uint16_t *>(&h), s2 = hb | (hb << 16);
+        uint32_t c[2], off;
+        if constexpr (Q4) {
+            const int p = int(e & 31);
+            const uint2 v = __ldg(reinterpret_cast<const uint2 *>(w + blk * 16 + (p & 15)));
+            const int sh = p < 16 ? 0 : 4;
+            c[0] = (v.x >> sh) & 0x0F0F0F0Fu, c[1] = (v.y >> sh) & 0x0F0F0F0Fu;
+            off = 0x64086408u;  // f16x2 (1032, 1032): 1024 + 8
+        } else {
+            const uint2 v = __ldg(reinterpret_cast<const uint2 *>(w + e));
+            c[0] = v.x ^ 0x80808080u, c[1] = v.y ^ 0x80808080u;
+            off = 0x64806480u;  // f16x2 (1152, 1152): 1024 + 128
+        }
+        uint4 o;
+        o.x = hsub_hmul(f16_pair_1024(c[0], 0x4140u), off, s2);
+        o.y = hsub_hmul(f16_pair_1024(c[0], 0x4342u), off, s2);
+        o.z = hsub_hmul(f16_pair_1024(c[1], 0x4140u), off, s2);
+        o.w = hsub_hmul(f16_pair_1024(c[1], 0x4342u), off, s2);
+        w16[i] = o;
     }
 }
 
@@ -1052,9 +1087,9 @@ int launch_q(const CUtensorMap &tx, const CUtensorMap &tw, const GemmQArgs &q, c
     return rc;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool F16 = false>
 int launch(const GemmPlan &p, cudaStream_t st, const char *name) {
-    auto kern = gemm_tc_kernel<BN, EPI>;
+    auto kern = gemm_tc_kernel<BN, EPI, F16>;
     static bool attr_set[128] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1069,9 +1104,9 @@ int launch(const GemmPlan &p, cudaStream_t st, const char *name) {
     return check_launch(name);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool F16 = false>
 int launch_pair(const GemmPlan &p, cudaStream_t st, const char *name) {
-    auto kern = gemm_tc2_kernel<BN, EPI>;
+    auto kern = gemm_tc2_kernel<BN, EPI, F16>;
     constexpr size_t kPairSmem = PairCfg<BN>::SMEM;
     static bool attr_set[128] = {};
     int dev = 0;
@@ -1099,16 +1134,16 @@ int launch_pair(const GemmPlan &p, cudaStream_t st, const char *name) {
     return VOX_CUDA_OK;
 }
 
-template <int EPI>
+template <int EPI, bool F16 = false>
 int launch_bn(const GemmPlan &p, cudaStream_t st, const char *name) {
     if (p.pair) {
-        if (p.bn == 128) return launch_pair<128, EPI>(p, st, name);
-        if (p.bn == 192) return launch_pair<192, EPI>(p, st, name);
-        return launch_pair<256, EPI>(p, st, name);
+        if (p.bn == 128) return launch_pair<128, EPI, F16>(p, st, name);
+        if (p.bn == 192) return launch_pair<192, EPI, F16>(p, st, name);
+        return launch_pair<256, EPI, F16>(p, st, name);
     }
-    if (p.bn == 64) return launch<64, EPI>(p, st, name);
-    if (p.bn == 256) return launch<256, EPI>(p, st, name);
-    return launch<128, EPI>(p, st, name);
+    if (p.bn == 64) return launch<64, EPI, F16>(p, st, name);
+    if (p.bn == 256) return launch<256, EPI, F16>(p, st, name);
+    return launch<128, EPI, F16>(p, st, name);
 }
 
 }  // namespace
@@ -1119,6 +1154,7 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
     VOX_REQUIRE(a.K % 8 == 0 && ldx % 8 == 0 && ldw % 8 == 0 && ldx >= a.K && ldw >= a.K && aligned16(x) && aligned16(w),
                 std::string(name) + ": x and W need 16-byte aligned rows (K and the row pitches multiples of 8)");
     VOX_REQUIRE(epi >= kEpiF32 && epi <= kEpiGeluErfF32, std::string(name) + ": unknown epilogue");
+    VOX_REQUIRE(!a.f16 || epi == kEpiF32, std::string(name) + ": f16 operands take the f32 epilogue only");
     if (epi == kEpiQkvRope)
         VOX_REQUIRE(a.cs && a.inner > 0 && a.inner % 64 == 0 && a.hd == 64 && a.N == 3 * a.inner && a.frames > 0,
                     std::string(name) + ": RoPE epilogue needs heads of 64 and 3 inner columns");
@@ -1157,9 +1193,10 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
     }
     if (best < 0) plan.pair = forced == 192, plan.bn = forced ? forced : 128;  // contradictory overrides
     // x boxes of 128 rows; W boxes of BN rows (one CTA) or BN / 2 (each CTA of a pair)
-    int rc = bf16_map(x, a.K, a.M, z, ldx, kBM, plan.ta, name);
+    const CUtensorMapDataType odt = a.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    int rc = bf16_map(x, a.K, a.M, z, ldx, kBM, plan.ta, name, odt);
     if (rc != VOX_CUDA_OK) return rc;
-    rc = bf16_map(w, a.K, a.N, a.groups, ldw, plan.pair ? plan.bn / 2 : plan.bn, plan.tb, name);
+    rc = bf16_map(w, a.K, a.N, a.groups, ldw, plan.pair ? plan.bn / 2 : plan.bn, plan.tb, name, odt);
     if (rc != VOX_CUDA_OK) return rc;
     // y by tensor stores of 32 x 32 blocks where its layout allows: planes [batches][M][columns] with 16-byte aligned
     // rows, group g's columns at g * y_gstride (whole 32-column blocks, so no block of one group reaches the next);
@@ -1184,6 +1221,7 @@ int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const Gemm
 }
 
 int gemm_run(const GemmPlan &p, cudaStream_t st, const char *name) {
+    if (p.a.f16) return launch_bn<kEpiF32, true>(p, st, name);  // (gemm_plan admits f16 operands with kEpiF32 only)
     switch (p.epi) {
         case kEpiF32: return launch_bn<kEpiF32>(p, st, name);
         case kEpiBf16: return launch_bn<kEpiBf16>(p, st, name);
@@ -1207,6 +1245,43 @@ int gemm_q(bool q4, const void *w, const void *scale, int scale_dtype, const flo
     GemmQArgs q{};
     q.M = int(m), q.N = int(rows), q.K = int(cols), q.nblk = int(cols / 32), q.scale = scale;
     q.g.M = int(m), q.g.N = int(rows), q.g.K = int(cols), q.g.y = y, q.g.ldy = rows, q.g.bias = bias, q.g.accumulate = accumulate != 0;
+    // Two passes for prefill batches of 256 rows or more: W dequantised to f16 once (an HBM-bound pass of 3 bytes a Q8
+    // weight), then the tcgen05 GEMM on f16 x and W, whose CTAs share converted weights through L2 instead of each
+    // converting its tile (the one-pass kernel converts every weight tile once per 128 activation rows). The
+    // operands are the one-pass kernel's, rounded the same way. VOX_CUDA_GEMMQ_TWOPASS=0 / 1 forces a form.
+    bool two = m >= 256;
+    if (const char *et = std::getenv("VOX_CUDA_GEMMQ_TWOPASS")) two = et[0] == '1';
+    if (two) {
+        void *buf = nullptr;
+        const size_t xb = (size_t(m * cols * 2) + 255) & ~size_t(255), wb = size_t(rows) * size_t(cols) * 2;
+        if (cudaMallocAsync(&buf, xb + wb, st) != cudaSuccess) return check_launch(name);
+        void *xh = buf, *w16 = reinterpret_cast<uint8_t *>(buf) + xb;
+        const int64_t n4 = m * cols / 4, n8 = rows * cols / 8;
+        launch_k(q_x_to_f16_kernel, grid_for(n4, 256, 4), 256, 0, st, reinterpret_cast<const float4 *>(x), reinterpret_cast<uint2 *>(xh), n4);
+        int rc = check_launch(name);
+        if (rc == VOX_CUDA_OK) {
+            const bool f16s = scale_dtype == VOX_CUDA_F16;
+            const uint8_t *wu = reinterpret_cast<const uint8_t *>(w);
+            uint4 *wo = reinterpret_cast<uint4 *>(w16);
+            if (q4) {
+                if (f16s) launch_k(q_w_to_f16_kernel<true, true>, grid_for(n8, 256, 8), 256, 0, st, wu, scale, wo, n8);
+                else launch_k(q_w_to_f16_kernel<true, false>, grid_for(n8, 256, 8), 256, 0, st, wu, scale, wo, n8);
+            } else {
+                if (f16s) launch_k(q_w_to_f16_kernel<false, true>, grid_for(n8, 256, 8), 256, 0, st, wu, scale, wo, n8);
+                else launch_k(q_w_to_f16_kernel<false, false>, grid_for(n8, 256, 8), 256, 0, st, wu, scale, wo, n8);
+            }
+            rc = check_launch(name);
+        }
+        if (rc == VOX_CUDA_OK) {
+            GemmArgs a = q.g;
+            a.f16 = 1;
+            GemmPlan p;
+            rc = gemm_plan(xh, cols, w16, cols, a, kEpiF32, p, name);
+            if (rc == VOX_CUDA_OK) rc = gemm_run(p, st, name);
+        }
+        cudaFreeAsync(buf, st);
+        return rc;
+    }
     // Work split. T output tiles of 128 x 256 on P (the SM count) persistent CTAs leave the last wave T % P tiles wide
     // (512 x 12288: 192 tiles, 44 of 148 CTAs busy in the second wave; 512 x 4096: 64 tiles, one wave of 64). The T % P
     // tail tiles are cut instead into s = min(P / (T % P), K steps / 4, 8) K-ranges each, so every CTA takes its whole

@@ -35,6 +35,7 @@ struct GemmArgs {
     int w_early = 0;                  // 1: W is not written by the previous kernel of the stream (weights of a plan), so
                                       // its first copies may start before that kernel has ended (one-CTA tiles)
     int tma_store = 0;                // set by gemm_plan: y is written by tensor stores (GemmPlan::ty)
+    int f16 = 0;                      // 1: x and W are f16, not bf16 (kEpiF32 only)
 };
 
 // A prepared GEMM: its tensor maps (x planes [z][M][K], W planes [g][N][K], bf16, 128-byte swizzle; y in 32 x 32
@@ -48,8 +49,8 @@ struct GemmPlan {
     int epi = kEpiF32;
 };
 
-// Builds a plan for x (bf16, [batches * groups][M][K] planes, row pitch ldx elements) and W (bf16, [groups][N][K],
-// row pitch ldw): K % 8 == 0, ldx and ldw multiples of 8, x and W 16-byte aligned. VOX_CUDA_OK or an error status.
+// Builds a plan for x (bf16, or f16 with a.f16, [batches * groups][M][K] planes, row pitch ldx elements) and W (the
+// same type, [groups][N][K], row pitch ldw): K % 8 == 0, ldx and ldw multiples of 8, x and W 16-byte aligned. VOX_CUDA_OK or an error status.
 int gemm_plan(const void *x, int64_t ldx, const void *w, int64_t ldw, const GemmArgs &a, int epi, GemmPlan &plan, const char *name);
 // Launches a prepared GEMM on stream st.
 int gemm_run(const GemmPlan &plan, cudaStream_t st, const char *name);

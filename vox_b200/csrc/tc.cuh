@@ -22,6 +22,8 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(uint32_t m, uint32_t n, bool b_mn = false) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
+// The same with f16 A and B (type fields 0), both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t m, uint32_t n) { return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24); }
 
 // D[tmem] (+)= A[smem] . B[smem] for one instruction of K = 16 (bf16), issued by one thread.
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {

@@ -320,12 +320,14 @@ VOX_CUDA_API int vox_cuda_gemv_q4(const uint8_t *w, const void *scale, int scale
 
 /* The prefill form of the same product (many activation rows): y[i][r] (+)= bias[r] + sum_k W[r][k] x[i][k] for i < m,
  * same arguments and weight layouts as vox_cuda_gemv_q8 / q4, on the 5th-generation tensor cores in f16: the weight
- * codes are dequantised to f16 (code * scale, one rounding) inside the kernel and x rounded to f16 once before it,
- * products accumulated in f32. Error within about 1e-3 of sum |w x| (f16 keeps 11 significant bits); |x| must stay
- * below 65504. The weights stream from HBM once per 128 activation rows. Where the output tiles do not fill the SMs
- * evenly, the last wave's tiles are split into K-ranges whose f32 partials are added in a fixed order: results are
- * identical run to run. Scratch (the f16 x, the partials: at most 128 KB per SM) comes from the device's default
- * memory pool, stream-ordered (cudaMallocAsync / cudaFreeAsync on `stream`). Replaces, for m > 8, Vox's dequantise-then-f32-matmul path
+ * codes are dequantised to f16 (code * scale, one rounding) and x rounded to f16 once, products accumulated in f32.
+ * Error within about 1e-3 of sum |w x| (f16 keeps 11 significant bits); |x| must stay below 65504. Results are
+ * identical run to run. Two forms with the same operands: below 256 rows of x one pass (the codes converted inside
+ * the GEMM kernel; where the output tiles do not fill the SMs evenly the last wave's tiles are split into K-ranges
+ * whose f32 partials are added in a fixed order); from 256 rows two passes (W dequantised to f16 once, then the f16
+ * GEMM). Scratch comes from the device's default memory pool, stream-ordered (cudaMallocAsync / cudaFreeAsync on
+ * `stream`): m * cols * 2 bytes for x, plus at most 128 KB per SM of partials (one pass) or rows * cols * 2 bytes for
+ * the f16 weights (two passes). Replaces, for m > 8, Vox's dequantise-then-f32-matmul path
  * (kernels.cpp:661-688) and its GPU tiled GEMM on q8 weights (shaders/gemmb.comp:1-99 WTYPE 3). */
 VOX_CUDA_API int vox_cuda_gemm_q8(const int8_t *w, const void *scale, int scale_dtype, const float *bias, const float *x, float *y,
                                   int64_t rows, int64_t cols, int64_t m, int accumulate, void *stream);
